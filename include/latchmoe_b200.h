@@ -1,0 +1,178 @@
+/*
+ * latchmoe_b200.h -- C ABI of liblatchmoe_b200.so, the B200 (sm_100a) data path of the
+ * slot-bank MoE layer: router -> expert histogram -> pair grouping (permute) -> grouped
+ * gate_up GEMM with fused SiLU*mul -> grouped down GEMM -> weighted top-k combine, plus the
+ * host->device expert staging copy.
+ *
+ * Conventions shared by every entry point
+ *   - All tensor arguments are raw DEVICE pointers unless the parameter name ends in
+ *     `_host`. bf16 tensors are passed as `uint16_t*` (raw bf16 bit patterns).
+ *   - `stream` is a cudaStream_t passed as `void*` (NULL = legacy default stream).
+ *   - Every function returns LM_OK (0) or a negative LM_ERR_* code. No C++ exception
+ *     crosses the ABI. On error `lm_last_error()` returns a message for this thread.
+ *   - The library never allocates device memory on the hot path: the caller owns and
+ *     pre-allocates every buffer (slot banks, permute/offset tables, scratch). Captured
+ *     CUDA graphs may therefore replay these launches as long as the buffers stay put.
+ *   - `err_word` (int32, device) receives the first device-side error code
+ *     (LM_DEVERR_*); the host reads it outside graph capture. Kernels never trap: an
+ *     out-of-range expert id or an unmapped expert is recorded and the pair is skipped,
+ *     and every spin-wait is bounded.
+ *
+ * The reference (vllm_moe_offload_ascend) ships no native code; each entry point below
+ * replaces a device operation that its Python call sites delegate to the Ascend stack.
+ * The "Replaces" line names that call site (file:line within the reference project).
+ */
+#ifndef LATCHMOE_B200_H
+#define LATCHMOE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LM_ABI_VERSION 1
+
+#define LM_OK 0
+#define LM_ERR_INVALID_ARGUMENT (-1)
+#define LM_ERR_CUDA (-2)
+#define LM_ERR_UNSUPPORTED (-3)
+#define LM_ERR_DEVICE (-4)
+
+/* Device-side error codes written to `err_word` (first error wins). */
+#define LM_DEVERR_NONE 0
+#define LM_DEVERR_BAD_EXPERT_ID 1   /* top-k id outside [0, num_experts) */
+#define LM_DEVERR_UNMAPPED_EXPERT 2 /* expert routed but its group/slot entry is -1 */
+#define LM_DEVERR_WAIT_TIMEOUT 3    /* a bounded mbarrier wait gave up */
+#define LM_DEVERR_BAD_GROUP 4       /* group table inconsistent with the pair table */
+
+/* Scoring functions accepted by lm_route_topk (reference `scoring_func`). */
+#define LM_SCORING_SOFTMAX 0
+#define LM_SCORING_SIGMOID 1
+
+/* Staging copy directions accepted by lm_stage_copy. */
+#define LM_COPY_H2D 1
+#define LM_COPY_D2D 3
+
+/* ABI version (LM_ABI_VERSION of the built library). */
+int lm_abi_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* lm_last_error(void);
+
+/*
+ * K1 router: scores(logits) -> (optional grouped) top-k -> optional renormalisation
+ * w / max(sum w, FLT_EPSILON) -> x routed_scaling_factor -> cast to bf16.
+ * Selection ties go to the lower expert id. Softmax/sigmoid are monotone, so without a
+ * correction bias the selection runs on the logits themselves (exact on the inputs).
+ * logits [T, E] fp32 row-major; topk_weights_bf16 [T, k] (required); topk_weights_f32
+ * [T, k] (optional, may be NULL); topk_ids [T, k] int32. E <= 256, k <= 32.
+ * e_score_correction_bias [E] fp32 or NULL. num_expert_group/topk_group <= 1 disable
+ * group-limited selection.
+ * Replaces: ops/fused_moe/moe_router_op.py:98-124 (select_experts) and the CANN gating
+ * fallback patches/patch_fused_moe.py:597-637.
+ */
+int lm_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts,
+                  int32_t top_k, int32_t scoring_func, int32_t renormalize,
+                  float routed_scaling_factor, const float* e_score_correction_bias,
+                  int32_t num_expert_group, int32_t topk_group,
+                  uint16_t* topk_weights_bf16, float* topk_weights_f32,
+                  int32_t* topk_ids, void* stream);
+
+/*
+ * K2 active-expert histogram: counts[e] = #pairs routed to expert e (counts is
+ * overwritten). Invalid ids set LM_DEVERR_BAD_EXPERT_ID in err_word (may be NULL).
+ * Replaces: ops/fused_moe/moe_offload_stage_op.py:297-302,474-508 (D2H of all top-k ids
+ * + host counting) and moe_offload/phase_split.py:479-492.
+ */
+int lm_expert_histogram(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
+                        int32_t* counts, int32_t* err_word, void* stream);
+
+/* Scratch (int32 elements) lm_build_groups needs for `num_pairs` pairs and `num_groups`. */
+int64_t lm_build_groups_scratch_elems(int64_t num_pairs, int32_t num_groups);
+
+/*
+ * K4/K9 pair grouping (stable counting sort): pair p = t*k + j goes to group
+ * g = expert_to_group[topk_ids[p]]. Rows of group g are [group_offsets[g],
+ * group_offsets[g+1]) and keep the original flat pair order inside the group.
+ * Outputs: group_offsets [G+1], pair_to_row [P] (row of pair p, -1 if unmapped),
+ * row_to_pair [P] (pair of row r; rows past group_offsets[G] are left untouched).
+ * With expert_to_group = log2phy this is the decode slot remap; with the wave table it is
+ * the multi-wave pair planner.
+ * Replaces: moe_offload/slot_mapping.py:116-141 (log2phy[topk_ids]), the CANN
+ * npu_moe_init_routing_v2 call patches/patch_fused_moe.py:645-711, and
+ * moe_offload/phase_split.py:1224-1385 (build_b2_device_wave_microbatch_plans).
+ */
+int lm_build_groups(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
+                    const int32_t* expert_to_group, int32_t num_groups,
+                    int32_t* group_offsets, int32_t* pair_to_row, int32_t* row_to_pair,
+                    int32_t* scratch, int64_t scratch_elems, int32_t* err_word,
+                    void* stream);
+
+/*
+ * Row gather: x_perm[r, :] = hidden[row_to_pair[r] / top_k, :] for r < num_rows.
+ * hidden [T, H] bf16, x_perm [num_rows, H] bf16; H % 8 == 0.
+ * Replaces: the token-permute half of npu_moe_init_routing_v2
+ * (patches/patch_fused_moe.py:688-702).
+ */
+int lm_permute_rows(const uint16_t* hidden, int32_t hidden_size, const int32_t* row_to_pair,
+                    int32_t top_k, int64_t num_rows, uint16_t* x_perm, void* stream);
+
+/*
+ * Grouped expert MLP over groups [group_begin, group_end).
+ * Weights live in a "bank": w13_bank [bank_rows, 2I, H] (rows 0..I-1 = gate, I..2I-1 = up,
+ * K-major) and w2_bank [bank_rows, H, I] (K-major); group g reads bank row
+ * group_bank_row[g]. x_perm [R, H] bf16 (rows in group order), act [R, I] bf16 (written),
+ * y_perm [R, H] bf16 (written). R = total rows (= group_offsets[num_groups]).
+ *   act[r, j]  = silu(x_r . w13[j]) * (x_r . w13[I + j])    (fp32 accumulate)
+ *   y_perm[r]  = act_r . w2^T                                (fp32 accumulate)
+ * lm_moe_mlp_decode: bandwidth-bound GEMV path for small groups (reads hidden rows through
+ *   row_to_pair directly; x_perm is not needed). Requires H % 32 == 0, I % 32 == 0.
+ * lm_moe_mlp_prefill: tcgen05/TMEM grouped GEMM fed by TMA (128x256x64 tiles, persistent
+ *   CTAs). Requires H % 256 == 0, I % 128 == 0, 16-byte aligned bases.
+ * Replaces: the two npu_grouped_matmul calls and npu_swiglu inside the host
+ * unified_apply_mlp (patches/patch_fused_moe.py:4249-4302, moe_offload/phase_split.py:2167).
+ */
+int lm_moe_mlp_decode(const uint16_t* hidden, int32_t top_k, const int32_t* row_to_pair,
+                      const int32_t* group_offsets, const int32_t* group_bank_row,
+                      int32_t group_begin, int32_t group_end, int32_t max_rows_per_group,
+                      const uint16_t* w13_bank, const uint16_t* w2_bank, int64_t bank_rows,
+                      int32_t hidden_size, int32_t intermediate_size,
+                      uint16_t* act, uint16_t* y_perm, int32_t* err_word, void* stream);
+
+int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
+                       const int32_t* group_offsets, const int32_t* group_bank_row,
+                       int32_t group_begin, int32_t group_end,
+                       const uint16_t* w13_bank, const uint16_t* w2_bank, int64_t bank_rows,
+                       int32_t hidden_size, int32_t intermediate_size,
+                       uint16_t* act, uint16_t* y_perm, int32_t* err_word, void* stream);
+
+/*
+ * K8 weighted combine in the original flattened top-k pair order:
+ *   out[t, :] = bf16( sum_{j<k} f32(topk_weights[t, j]) * f32(y_perm[pair_to_row[t*k+j], :]) )
+ * accumulated in fp32 in j order (deterministic, no atomics). pair_to_row < 0 contributes 0.
+ * Replaces: the single native token_combine after all waves
+ * (patches/patch_fused_moe.py:3340-3366, moe_offload/phase_split.py:1765-1856).
+ */
+int lm_moe_combine(const uint16_t* y_perm, const int32_t* pair_to_row,
+                   const uint16_t* topk_weights_bf16, int64_t num_tokens, int32_t top_k,
+                   int32_t hidden_size, uint16_t* out, void* stream);
+
+/*
+ * K10 expert staging: for i < n, copy bytes_per_expert bytes from
+ * src + src_rows_host[i]*src_row_stride to dst + dst_rows_host[i]*dst_row_stride with
+ * cudaMemcpyAsync on `stream`, coalescing runs where both row sequences are consecutive
+ * into one copy. kind = LM_COPY_H2D (src is pinned host memory) or LM_COPY_D2D.
+ * Returns the number of cudaMemcpyAsync calls issued (>= 0) or a negative error.
+ * Replaces: moe_offload/transfer_engine.py:139-187,205-228,246-303 (load_many_async,
+ * _copy_loads, _try_batch_view).
+ */
+int lm_stage_copy(void* dst, int64_t dst_row_stride, const void* src, int64_t src_row_stride,
+                  const int32_t* src_rows_host, const int32_t* dst_rows_host, int32_t n,
+                  int64_t bytes_per_expert, int32_t kind, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LATCHMOE_B200_H */

@@ -1,0 +1,221 @@
+"""Generate golden control-plane vectors by running the REFERENCE's own Python code.
+
+Run in a container that has the reference checkout (read-only) at REFERENCE_ROOT:
+
+    python tests/golden/make_golden.py [REFERENCE_ROOT]
+
+It imports ``vllm_moe_offload_ascend`` (slot bank, runtime, phase_split) with a two-module
+stand-in for ``vllm_ascend.envs`` (the reference reads its settings through that module;
+the stand-in answers from the reference's own ``env_registry``), drives it on seeded
+inputs with the slot bank on the CPU (as the reference's unit tests do), and writes the
+results as JSON next to this script. Tests never import the reference; they compare the
+oracle and the product host logic against these files.
+"""
+
+from __future__ import annotations
+
+import json
+import random
+import sys
+import types
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+
+
+def _install_reference(root: str) -> None:
+    sys.path.insert(0, root)
+    from importlib import import_module
+
+    envreg = import_module("vllm_moe_offload_ascend.env_registry")
+
+    class _Envs(types.ModuleType):
+        def __getattr__(self, name):
+            loader = envreg.ENVIRONMENT_VARIABLES.get(name)
+            if loader is None:
+                raise AttributeError(name)
+            return loader()
+
+    pkg = types.ModuleType("vllm_ascend")
+    envs = _Envs("vllm_ascend.envs")
+    pkg.envs = envs
+    sys.modules["vllm_ascend"] = pkg
+    sys.modules["vllm_ascend.envs"] = envs
+
+
+def _wave_cases(ps):
+    rng = random.Random(1234)
+    cases = [({1: 10, 2: 9, 3: 8, 4: 1, 5: 1}, 2), ({1: 10, 2: 9, 3: 8, 4: 7}, 4),
+             ({5: 100, 1: 90, 2: 80, 4: 70}, 4), ({1: 10, 2: 100, 5: 90}, 3),
+             ({e: 1 for e in range(128)}, 32), ({0: 5}, 1)]
+    for _ in range(60):
+        E = rng.choice([8, 64, 128])
+        S = rng.choice([1, 2, 3, 7, 24, 32])
+        counts = {e: rng.choice([0, 0, 1, 2, 3, 10, 50, rng.randint(1, 4096)]) for e in range(E)}
+        cases.append((counts, S))
+    # routing histograms of the seeded benchmark configurations
+    import torch
+
+    sys.path.insert(0, str(REPO))
+    from oracle import router as orouter
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+    for name in ("c1_decode", "c2_prefill", "c4_shared", "c5_ep"):
+        cfg = syn.CONFIGS[name]
+        logits = syn.make_router_logits(cfg, seed=0)
+        _, _, ids = orouter.route(logits.numpy(), cfg.top_k, renormalize=cfg.renormalize)
+        counts = torch.bincount(torch.from_numpy(ids.reshape(-1)).long(), minlength=cfg.num_experts)
+        cases.append(({e: int(c) for e, c in enumerate(counts.tolist())}, cfg.num_slots))
+    out = []
+    for counts, S in cases:
+        plan = ps.plan_balanced_b2_waves(counts, S)
+        out.append({"counts": {str(k): int(v) for k, v in counts.items()}, "num_slots": S,
+                    "waves": [list(w) for w in plan.waves]})
+    return out
+
+
+def _schedule_cases(ps):
+    rng = random.Random(99)
+    out = []
+    for _ in range(40):
+        n = rng.randint(1, 6)
+        waves = tuple(tuple(range(i * 4, i * 4 + rng.randint(1, 4))) for i in range(n))
+        ready = {e: rng.random() < 0.4 for w in waves for e in w}
+        kw = dict(prefetch_depth=rng.randint(0, 3), buffer_count=rng.randint(1, 3),
+                  h2d_bytes_by_wave={i: rng.randint(0, 10) * 1000 for i in range(n)},
+                  compute_cost_by_wave={i: float(rng.randint(0, 9)) for i in range(n)},
+                  transfer_aware=rng.random() < 0.6)
+        sched = ps.plan_b2_prefill_async_schedule(waves, slot_readiness=ready, **kw)
+        out.append({
+            "waves": [list(w) for w in waves],
+            "readiness": {str(k): v for k, v in ready.items()},
+            "kwargs": {**kw, "h2d_bytes_by_wave": {str(k): v for k, v in kw["h2d_bytes_by_wave"].items()},
+                       "compute_cost_by_wave": {str(k): v for k, v in kw["compute_cost_by_wave"].items()}},
+            "schedule": sched.to_jsonable(),
+            "issue_log": [list(x) for x in ps.simulate_b2_prefill_issue_log(sched)],
+        })
+    return out
+
+
+def _slot_traces():
+    import torch
+    from vllm_moe_offload_ascend.moe_offload.config import MoeOffloadConfig
+    from vllm_moe_offload_ascend.moe_offload.runtime import MoeOffloadRuntime
+
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+    class Layer(torch.nn.Module):
+        def __init__(self, E):
+            super().__init__()
+            self.layer_id = 3
+            self.w13_weight = torch.nn.Parameter(torch.zeros(E, 2, 3))
+            self.w2_weight = torch.nn.Parameter(torch.zeros(E, 3, 2))
+
+    traces = []
+    rng = random.Random(7)
+    seqs = [
+        ("reference_test_S4", 5, 4, [(0, 1), (2, 3, 4)]),
+        ("locality_k8_S32", 128, 32,
+         syn.locality_topk_sequence(syn.CONFIGS["c1_decode"], 64, keep_prob=0.7, seed=0)),
+        ("random_S8", 32, 8, [tuple(sorted(rng.sample(range(32), rng.randint(1, 8))))
+                              for _ in range(50)]),
+        ("evict_later_active_S3", 8, 3, [(5, 6, 7), (0, 5), (1, 2, 6), (0, 1, 7)]),
+    ]
+    for name, E, S, steps in seqs:
+        rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=S, async_load=False,
+                                                graph_compatible_offload=True))
+        rt.register_layer_for_fixed_slots(Layer(E), slot_device=torch.device("cpu"))
+        rec = []
+        for active in steps:
+            prepared = rt.stage_fixed_slot_plan(layer_id=3, active_experts=tuple(active),
+                                                num_logical_experts=E)
+            rec.append({"active": list(active),
+                        "active_slot_ids": list(prepared.mapping.active_slot_ids),
+                        "log2phy": rt.log2phy_buffer(3).tolist()})
+        traces.append({"name": name, "num_experts": E, "num_slots": S, "steps": rec})
+    return traces
+
+
+def _pair_plans(ps):
+    import torch
+
+    rng = random.Random(5)
+    out = []
+    cases = [(torch.tensor([[3, 1], [2, 3], [0, 2]]), ((0, 3), (1, 2)))]
+    for _ in range(12):
+        E = rng.choice([8, 16, 128])
+        k = rng.choice([1, 2, 6, 8])
+        T = rng.randint(1, 40)
+        ids = torch.tensor([rng.sample(range(E), k) for _ in range(T)])
+        counts = {int(e): int(c) for e, c in zip(*torch.unique(ids, return_counts=True))}
+        waves = ps.plan_balanced_b2_waves(counts, rng.choice([1, 2, 4, 8])).waves
+        cases.append((ids, waves))
+    for ids, waves in cases:
+        E = int(ids.max()) + 1
+        active = tuple(sorted(set(ids.reshape(-1).tolist())))
+        plans = ps.build_b2_device_wave_microbatch_plans(
+            ids, waves, num_logical_experts=E, active_experts=active,
+            wave_pair_counts=tuple(int(sum(int((ids == e).sum()) for e in w)) for w in waves))
+        out.append({"topk_ids": ids.tolist(), "waves": [list(w) for w in waves],
+                    "plans": [{"flat_pair_offsets": p.flat_pair_offsets.tolist(),
+                               "token_indices": p.token_indices.tolist(),
+                               "physical_slot_ids": p.physical_slot_ids.tolist()} for p in plans]})
+    return out
+
+
+def _combine_index(ps):
+    import torch
+    from dataclasses import dataclass
+
+    @dataclass(frozen=True)
+    class Meta:
+        x: int = 0
+
+    rng = random.Random(11)
+    out = []
+    for case in range(10):
+        total = rng.randint(1, 24)
+        perm = list(range(total))
+        rng.shuffle(perm)
+        n_w = rng.randint(1, min(4, total))
+        cuts = sorted(rng.sample(range(1, total), n_w - 1)) if n_w > 1 else []
+        parts = [perm[a:b] for a, b in zip([0] + cuts, cuts + [total])]
+        payloads = []
+        for w, offs in enumerate(parts):
+            local = list(range(len(offs)))
+            rng.shuffle(local)
+            payloads.append(ps.B2DirectScatterPayload(
+                permuted_tokens=torch.arange(len(offs), dtype=torch.float32).reshape(-1, 1),
+                expanded_row_idx=torch.tensor(local, dtype=torch.int32),
+                topk_weights=torch.ones(len(offs), 1),
+                restore_token_indices=torch.zeros(len(offs), dtype=torch.long),
+                pair_offsets=torch.tensor(sorted(offs)), combine_metadata=Meta(), wave_index=w))
+        _, index, _ = ps.build_b2_native_combine_inputs(tuple(payloads), total_pairs=total)
+        out.append({"total_pairs": total,
+                    "waves": [{"pair_offsets": sorted(o), "local": p.expanded_row_idx.tolist()}
+                              for o, p in zip(parts, payloads)],
+                    "index": index.tolist()})
+    return out
+
+
+def main() -> None:
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    _install_reference(root)
+    sys.path.insert(0, str(REPO))
+    from vllm_moe_offload_ascend.moe_offload import phase_split as ps
+
+    blobs = {
+        "waves.json": _wave_cases(ps),
+        "schedules.json": _schedule_cases(ps),
+        "slot_traces.json": _slot_traces(),
+        "pair_plans.json": _pair_plans(ps),
+        "combine_index.json": _combine_index(ps),
+    }
+    for name, data in blobs.items():
+        (HERE / name).write_text(json.dumps(data, separators=(",", ":")) + "\n")
+        print(name, len(data))
+
+
+if __name__ == "__main__":
+    main()

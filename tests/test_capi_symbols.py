@@ -1,0 +1,38 @@
+"""The C-ABI library loads without a GPU and exports every symbol include/*.h declares."""
+
+import ctypes
+import re
+from pathlib import Path
+
+from vllm_ascend_hust_latchmoe_b200 import _build, _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(lm_[a-z0-9_]+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    path = _build.build()
+    lib = ctypes.CDLL(str(path))
+    names = declared_symbols()
+    assert len(names) >= 10
+    for name in sorted(names):
+        assert hasattr(lib, name), name
+    assert names == set(_lib.SIGNATURES), names ^ set(_lib.SIGNATURES)
+
+
+def test_abi_version_and_error_strings_without_gpu():
+    lib = _lib.load()
+    assert lib.lm_abi_version() == 1
+    # argument validation happens on the host, before any CUDA call
+    rc = lib.lm_route_topk(None, 4, 999, 8, 0, 1, 1.0, None, 0, 0, None, None, None, None)
+    assert rc == -1
+    assert b"num_experts" in lib.lm_last_error()
+    rc = lib.lm_stage_copy(None, 16, None, 16, None, None, 1, 16, 7, None)
+    assert rc == -1 and b"kind" in lib.lm_last_error()

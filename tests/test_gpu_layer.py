@@ -1,0 +1,101 @@
+"""GPU parity of the whole slot-bank MoE layer (router -> stage -> MLP -> combine).
+
+Routing ids and the slot assignment are bit-exact against the oracle (the slot allocator
+oracle is pinned to the reference's own control plane); layer outputs are within the bf16
+tolerance of the fp32-accumulating oracle.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import control as ocontrol
+from oracle import mlp as omlp
+from oracle import router as orouter
+from oracle.bf16 import bf16_bits_to_f32
+from tests.helpers import MAX_REL_ERR, MIN_COSINE, bits, build_layer
+from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_layer(cfg, hidden, logits, w13, w2):
+    wb, _, ids = orouter.route(logits.numpy(), cfg.top_k, renormalize=cfg.renormalize,
+                               routed_scaling_factor=cfg.routed_scaling_factor,
+                               scoring_func=cfg.scoring_func,
+                               num_expert_group=cfg.num_expert_group, topk_group=cfg.topk_group)
+    out = omlp.moe_layer(bits(hidden), ids, wb, bits(w13), bits(w2))
+    return ids, wb, out
+
+
+def _check(out, ref):
+    m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)
+    assert m["max_rel_err"] <= MAX_REL_ERR and m["cosine"] >= MIN_COSINE, m
+
+
+def test_decode_slots_path_matches_oracle_and_slot_order(cuda):
+    """Batch-8 decode steps (working set <= S): slots staged in sorted order, LRU reuse."""
+    cfg = syn.CONFIGS["c1_decode"].with_tokens(4)
+    layer, rt, (w13, w2) = build_layer(cfg, max_tokens=4)
+    alloc = ocontrol.SlotAllocator(cfg.num_slots, cfg.num_experts)
+    for step in range(6):
+        hidden = syn.make_hidden(cfg, seed=step)
+        logits = syn.make_router_logits(cfg, seed=step)
+        ids_ref, _, ref = _oracle_layer(cfg, hidden, logits, w13, w2)
+        out = layer.forward(hidden.to(cuda), logits.to(cuda))
+        torch.cuda.synchronize()
+        layer.check_device_errors()
+        assert np.array_equal(layer.topk_ids[:4].cpu().numpy(), ids_ref)
+        exp = alloc.stage(tuple(sorted(set(ids_ref.reshape(-1).tolist()))))
+        assert np.array_equal(rt.log2phy_buffer(0).cpu().numpy(), exp["log2phy"])
+        _check(out, ref)
+
+
+@pytest.mark.parametrize("store_on_device", [False, True])
+def test_c1_decode_overflow_runs_waves(cuda, store_on_device):
+    """C1: 16 tokens route to more experts than the 32 slots -> multi-wave + one combine."""
+    cfg = syn.CONFIGS["c1_decode"]
+    layer, rt, (w13, w2) = build_layer(cfg, store_on_device=store_on_device)
+    hidden = syn.make_hidden(cfg)
+    logits = syn.make_router_logits(cfg)
+    ids_ref, _, ref = _oracle_layer(cfg, hidden, logits, w13, w2)
+    out = layer.forward(hidden.to(cuda), logits.to(cuda))
+    torch.cuda.synchronize()
+    layer.check_device_errors()
+    assert np.array_equal(layer.topk_ids[:16].cpu().numpy(), ids_ref)
+    counts = np.bincount(ids_ref.reshape(-1), minlength=cfg.num_experts)
+    waves = ocontrol.plan_balanced_waves({e: int(c) for e, c in enumerate(counts)}, cfg.num_slots)
+    assert layer.last_waves.waves == waves and len(waves) >= 2
+    _check(out, ref)
+
+
+@pytest.mark.parametrize("store_on_device", [False, True])
+def test_prefill_waves_tcgen05_matches_oracle(cuda, store_on_device):
+    """C2-shaped multi-wave prefill on a 1024-token slice (>= 4 waves, one combine)."""
+    cfg = syn.CONFIGS["c2_prefill"].with_tokens(1024)
+    layer, rt, (w13, w2) = build_layer(cfg, store_on_device=store_on_device)
+    hidden = syn.make_hidden(cfg)
+    logits = syn.make_router_logits(cfg)
+    ids_ref, _, ref = _oracle_layer(cfg, hidden, logits, w13, w2)
+    out = layer.forward(hidden.to(cuda), logits.to(cuda))
+    torch.cuda.synchronize()
+    layer.check_device_errors()
+    assert len(layer.last_waves.waves) >= 4
+    _check(out, ref)
+    # Second call reuses every buffer and stage bank: same result.
+    out2 = layer.forward(hidden.to(cuda), logits.to(cuda))
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+
+
+def test_c4_deepseek_shaped_layer(cuda):
+    cfg = syn.CONFIGS["c4_shared"]
+    layer, rt, (w13, w2) = build_layer(cfg)
+    hidden = syn.make_hidden(cfg)
+    logits = syn.make_router_logits(cfg)
+    ids_ref, _, ref = _oracle_layer(cfg, hidden, logits, w13, w2)
+    out = layer.forward(hidden.to(cuda), logits.to(cuda))
+    torch.cuda.synchronize()
+    layer.check_device_errors()
+    assert np.array_equal(layer.topk_ids[:64].cpu().numpy(), ids_ref)
+    _check(out, ref)

@@ -1,0 +1,131 @@
+"""Host logic of the product (planners, slot bank, runtime staging order) against the
+reference's golden vectors, with the slot bank on the CPU as in the reference's tests."""
+
+import json
+from pathlib import Path
+
+import pytest
+import torch
+
+from tests.helpers import ExpertLayer
+from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
+from vllm_ascend_hust_latchmoe_b200.moe_offload import phase_split as ps
+from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
+from vllm_ascend_hust_latchmoe_b200.moe_offload.slot_bank import SlotState
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def load(name):
+    return json.loads((GOLDEN / name).read_text())
+
+
+def test_plan_balanced_b2_waves_golden():
+    for case in load("waves.json"):
+        counts = {int(k): v for k, v in case["counts"].items()}
+        plan = ps.plan_balanced_b2_waves(counts, case["num_slots"], slot_readiness={1: True})
+        assert [list(w) for w in plan.waves] == case["waves"]
+
+
+def test_async_schedule_golden():
+    for case in load("schedules.json"):
+        kw = dict(case["kwargs"])
+        kw["h2d_bytes_by_wave"] = {int(k): v for k, v in kw["h2d_bytes_by_wave"].items()}
+        kw["compute_cost_by_wave"] = {int(k): v for k, v in kw["compute_cost_by_wave"].items()}
+        waves = tuple(tuple(w) for w in case["waves"])
+        sched = ps.plan_b2_prefill_async_schedule(
+            waves, slot_readiness={int(k): v for k, v in case["readiness"].items()}, **kw)
+        assert sched.to_jsonable() == case["schedule"]
+        assert [list(x) for x in ps.simulate_b2_prefill_issue_log(sched)] == case["issue_log"]
+
+
+def _runtime(E, S):
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=S, async_load=False,
+                                            graph_compatible_offload=True))
+    layer = ExpertLayer(3, torch.zeros(E, 2, 3), torch.zeros(E, 3, 2))
+    rt.register_layer_for_fixed_slots(layer, slot_device=torch.device("cpu"))
+    return rt
+
+
+def test_runtime_slot_traces_golden():
+    for trace in load("slot_traces.json"):
+        rt = _runtime(trace["num_experts"], trace["num_slots"])
+        for step in trace["steps"]:
+            prepared = rt.stage_fixed_slot_plan(layer_id=3, active_experts=tuple(step["active"]),
+                                                num_logical_experts=trace["num_experts"])
+            assert list(prepared.mapping.active_slot_ids) == step["active_slot_ids"], trace["name"]
+            assert rt.log2phy_buffer(3).tolist() == step["log2phy"], trace["name"]
+
+
+def test_stage_copies_expert_rows_into_slots():
+    E = 6
+    w13 = torch.arange(E * 2 * 3, dtype=torch.float32).reshape(E, 2, 3)
+    w2 = -torch.arange(E * 3 * 2, dtype=torch.float32).reshape(E, 3, 2)
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=3))
+    rt.register_layer_for_fixed_slots(ExpertLayer(1, w13, w2), slot_device=torch.device("cpu"))
+    p = rt.stage_fixed_slot_plan(layer_id=1, active_experts=(4, 1), num_logical_experts=E)
+    for e, s in zip(p.mapping.active_experts, p.mapping.active_slot_ids):
+        assert torch.equal(p.w1[s], w13[e]) and torch.equal(p.w2[s], w2[e])
+
+
+def test_compute_protected_eviction_and_lease_checks():
+    rt = _runtime(8, 2)
+    p = rt.stage_fixed_slot_plan(layer_id=3, active_experts=(0, 1), num_logical_experts=8)
+    handle = rt.begin_slot_compute(p)
+    bank = rt.slot_bank(3)
+    assert all(s.state == SlotState.COMPUTING for s in bank.slots)
+    rt.end_slot_compute(handle)  # CPU bank: completion is immediate
+    assert all(s.state == SlotState.READY for s in bank.slots)
+    p2 = rt.stage_fixed_slot_plan(layer_id=3, active_experts=(2,), num_logical_experts=8)
+    assert p2.mapping.active_slot_ids == (0,)  # LRU tie -> lowest slot id
+    with pytest.raises(RuntimeError, match="exceeds num_slots"):
+        rt.stage_fixed_slot_plan(layer_id=3, active_experts=(3, 4, 5), num_logical_experts=8)
+    with pytest.raises(ValueError):
+        rt.stage_fixed_slot_plan(layer_id=3, active_experts=(9,), num_logical_experts=8)
+
+
+def test_address_lock_rejects_reregistration():
+    rt = _runtime(8, 2)
+    assert rt.capture_safe_slot_weights(layer_id=3) is not None
+    with pytest.raises(RuntimeError, match="already captured"):
+        rt.register_layer_for_fixed_slots(ExpertLayer(3, torch.zeros(8, 2, 3), torch.zeros(8, 3, 2)),
+                                          slot_device=torch.device("cpu"))
+
+
+def test_pinned_shared_suffix_and_log2phy():
+    w13 = torch.randn(6, 2, 3)
+    w2 = torch.randn(6, 3, 2)
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=2))
+    rt.register_layer_for_fixed_slots(ExpertLayer(0, w13, w2, shared=2), slot_device=torch.device("cpu"))
+    bank = rt.slot_bank(0)
+    assert bank.physical_expert_count == 4 and bank.pinned_slot_ids == (2, 3)
+    assert rt.log2phy_buffer(0).tolist() == [-1, -1, -1, -1, 2, 3]
+    assert torch.equal(bank.w13_slots[2:], w13[4:])
+    p = rt.stage_fixed_slot_plan(layer_id=0, active_experts=(3,), num_logical_experts=4)
+    assert p.mapping.slot_to_expert == (3, None, 4, 5)
+
+
+def test_prefill_stage_plan_positional_slots_and_d2d_hits():
+    E = 8
+    w13 = torch.arange(E * 2 * 3, dtype=torch.float32).reshape(E, 2, 3)
+    w2 = torch.arange(E * 3 * 2, dtype=torch.float32).reshape(E, 3, 2)
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=3, b2_wave_prefill=True))
+    rt.register_layer_for_fixed_slots(ExpertLayer(2, w13, w2), slot_device=torch.device("cpu"))
+    rt.stage_fixed_slot_plan(layer_id=2, active_experts=(5,), num_logical_experts=E)
+    stage, ready = rt.prepare_prefill_stage_plan(layer_id=2, active_experts=(1, 5, 7), buffer_index=1)
+    rt.wait_prefill_stage_plan(ready)
+    for pos, e in enumerate((1, 5, 7)):
+        assert torch.equal(stage.w13_slots[pos], w13[e])
+        assert stage.slots[pos].state == SlotState.READY
+    with pytest.raises(ValueError):
+        rt.prefill_stage_bank(2, 5)
+
+
+def test_should_use_b2_pair_waves_gate():
+    rt = _runtime(8, 2)
+    assert not rt.should_use_b2_pair_waves(layer_id=3, active_expert_count=5)
+    rt2 = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=2, b2_wave_prefill=True))
+    rt2.register_layer_for_fixed_slots(ExpertLayer(3, torch.zeros(8, 2, 3), torch.zeros(8, 3, 2)),
+                                       slot_device=torch.device("cpu"))
+    assert rt2.should_use_b2_pair_waves(layer_id=3, active_expert_count=3)
+    assert not rt2.should_use_b2_pair_waves(layer_id=3, active_expert_count=2)

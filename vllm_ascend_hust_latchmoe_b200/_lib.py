@@ -1,0 +1,273 @@
+"""ctypes binding of liblatchmoe_b200.so (the C ABI declared in include/latchmoe_b200.h).
+
+Every wrapper takes torch tensors, passes raw pointers and the current CUDA stream across
+the C boundary, and raises ``RuntimeError`` with the library's message on a negative
+return code. There is no fallback: if the library is missing the import of this module
+fails loudly, so no CPU or eager path can silently stand in for the kernels.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+from ._build import LIB_PATH
+
+LM_OK = 0
+LM_SCORING_SOFTMAX = 0
+LM_SCORING_SIGMOID = 1
+LM_COPY_H2D = 1
+LM_COPY_D2D = 3
+
+DEVERR_NAMES = {
+    0: "none",
+    1: "top-k id outside [0, num_experts)",
+    2: "expert routed but unmapped (log2phy/group entry is -1)",
+    3: "bounded device wait timed out",
+    4: "group table inconsistent with the pair table",
+}
+
+# Every symbol include/latchmoe_b200.h declares, with (restype, argtypes).
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+_F32 = ctypes.c_float
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "lm_abi_version": (ctypes.c_int, []),
+    "lm_last_error": (ctypes.c_char_p, []),
+    "lm_route_topk": (
+        ctypes.c_int,
+        [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _P, _P, _P, _P],
+    ),
+    "lm_expert_histogram": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _P]),
+    "lm_build_groups_scratch_elems": (ctypes.c_int64, [_I64, _I32]),
+    "lm_build_groups": (
+        ctypes.c_int,
+        [_P, _I64, _I32, _P, _I32, _P, _P, _P, _P, _I64, _P, _P],
+    ),
+    "lm_permute_rows": (ctypes.c_int, [_P, _I32, _P, _I32, _I64, _P, _P]),
+    "lm_moe_mlp_decode": (
+        ctypes.c_int,
+        [_P, _I32, _P, _P, _P, _I32, _I32, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
+    ),
+    "lm_moe_mlp_prefill": (
+        ctypes.c_int,
+        [_P, _I64, _P, _P, _I32, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
+    ),
+    "lm_moe_combine": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P, _P]),
+    "lm_stage_copy": (
+        ctypes.c_int,
+        [_P, _I64, _P, _I64, _P, _P, _I32, _I64, _I32, _P],
+    ),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load(path: str | Path | None = None) -> ctypes.CDLL:
+    """Load the library once and bind every declared symbol (raises if absent)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        lib_path = Path(path) if path is not None else LIB_PATH
+        if not lib_path.exists():
+            raise RuntimeError(
+                f"{lib_path.name} is not built at {lib_path}; run "
+                "`python -c 'import __graft_entry__ as g; g.build()'` (nvcc, sm_100a). "
+                "There is no CPU fallback for the MoE data path."
+            )
+        lib = ctypes.CDLL(str(lib_path))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        if lib.lm_abi_version() != 1:
+            raise RuntimeError("liblatchmoe_b200.so ABI version mismatch")
+        _lib = lib
+        return lib
+
+
+def lib() -> ctypes.CDLL:
+    return _lib if _lib is not None else load()
+
+
+def _check(name: str, rc: int) -> int:
+    if rc < 0:
+        msg = lib().lm_last_error().decode(errors="replace")
+        raise RuntimeError(f"{name} failed ({rc}): {msg}")
+    return rc
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream: torch.cuda.Stream | None = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("liblatchmoe_b200 kernels take CUDA tensors only")
+
+
+def route_topk(
+    logits: torch.Tensor,
+    top_k: int,
+    *,
+    scoring_func: str = "softmax",
+    renormalize: bool = True,
+    routed_scaling_factor: float = 1.0,
+    e_score_correction_bias: torch.Tensor | None = None,
+    num_expert_group: int | None = None,
+    topk_group: int | None = None,
+    weights_bf16: torch.Tensor,
+    ids: torch.Tensor,
+    weights_f32: torch.Tensor | None = None,
+) -> None:
+    _require_cuda(logits, weights_bf16, ids, weights_f32, e_score_correction_bias)
+    assert logits.dtype == torch.float32 and logits.is_contiguous()
+    T, E = logits.shape
+    scoring = {"softmax": LM_SCORING_SOFTMAX, "sigmoid": LM_SCORING_SIGMOID}.get(scoring_func)
+    if scoring is None:
+        raise ValueError(f"unsupported scoring_func {scoring_func!r}")
+    _check(
+        "lm_route_topk",
+        lib().lm_route_topk(
+            _ptr(logits), T, E, int(top_k), scoring, int(bool(renormalize)),
+            float(routed_scaling_factor), _ptr(e_score_correction_bias),
+            int(num_expert_group or 0), int(topk_group or 0),
+            _ptr(weights_bf16), _ptr(weights_f32), _ptr(ids), _stream(),
+        ),
+    )
+
+
+def expert_histogram(ids: torch.Tensor, num_experts: int, counts: torch.Tensor,
+                     err_word: torch.Tensor | None = None) -> None:
+    _require_cuda(ids, counts, err_word)
+    _check(
+        "lm_expert_histogram",
+        lib().lm_expert_histogram(_ptr(ids), ids.numel(), int(num_experts), _ptr(counts),
+                                  _ptr(err_word), _stream()),
+    )
+
+
+def build_groups_scratch_elems(num_pairs: int, num_groups: int) -> int:
+    return int(lib().lm_build_groups_scratch_elems(int(num_pairs), int(num_groups)))
+
+
+def build_groups(ids: torch.Tensor, num_experts: int, expert_to_group: torch.Tensor,
+                 num_groups: int, group_offsets: torch.Tensor, pair_to_row: torch.Tensor,
+                 row_to_pair: torch.Tensor, scratch: torch.Tensor,
+                 err_word: torch.Tensor | None = None) -> None:
+    _require_cuda(ids, expert_to_group, group_offsets, pair_to_row, row_to_pair, scratch)
+    _check(
+        "lm_build_groups",
+        lib().lm_build_groups(
+            _ptr(ids), ids.numel(), int(num_experts), _ptr(expert_to_group), int(num_groups),
+            _ptr(group_offsets), _ptr(pair_to_row), _ptr(row_to_pair), _ptr(scratch),
+            scratch.numel(), _ptr(err_word), _stream(),
+        ),
+    )
+
+
+def permute_rows(hidden: torch.Tensor, row_to_pair: torch.Tensor, top_k: int, num_rows: int,
+                 x_perm: torch.Tensor) -> None:
+    _require_cuda(hidden, row_to_pair, x_perm)
+    _check(
+        "lm_permute_rows",
+        lib().lm_permute_rows(_ptr(hidden), hidden.shape[-1], _ptr(row_to_pair), int(top_k),
+                              int(num_rows), _ptr(x_perm), _stream()),
+    )
+
+
+def moe_mlp_decode(hidden, top_k, row_to_pair, group_offsets, group_bank_row, group_begin,
+                   group_end, max_rows_per_group, w13_bank, w2_bank, act, y_perm,
+                   err_word=None) -> None:
+    _require_cuda(hidden, row_to_pair, group_offsets, group_bank_row, w13_bank, w2_bank, act,
+                  y_perm)
+    H = hidden.shape[-1]
+    I = w2_bank.shape[-1]
+    _check(
+        "lm_moe_mlp_decode",
+        lib().lm_moe_mlp_decode(
+            _ptr(hidden), int(top_k), _ptr(row_to_pair), _ptr(group_offsets),
+            _ptr(group_bank_row), int(group_begin), int(group_end), int(max_rows_per_group),
+            _ptr(w13_bank), _ptr(w2_bank), w13_bank.shape[0], H, I, _ptr(act), _ptr(y_perm),
+            _ptr(err_word), _stream(),
+        ),
+    )
+
+
+def moe_mlp_prefill(x_perm, total_rows, group_offsets, group_bank_row, group_begin, group_end,
+                    w13_bank, w2_bank, act, y_perm, err_word=None) -> None:
+    _require_cuda(x_perm, group_offsets, group_bank_row, w13_bank, w2_bank, act, y_perm)
+    H = x_perm.shape[-1]
+    I = w2_bank.shape[-1]
+    _check(
+        "lm_moe_mlp_prefill",
+        lib().lm_moe_mlp_prefill(
+            _ptr(x_perm), int(total_rows), _ptr(group_offsets), _ptr(group_bank_row),
+            int(group_begin), int(group_end), _ptr(w13_bank), _ptr(w2_bank),
+            w13_bank.shape[0], H, I, _ptr(act), _ptr(y_perm), _ptr(err_word), _stream(),
+        ),
+    )
+
+
+def moe_combine(y_perm, pair_to_row, topk_weights_bf16, out) -> None:
+    _require_cuda(y_perm, pair_to_row, topk_weights_bf16, out)
+    T, k = topk_weights_bf16.shape
+    _check(
+        "lm_moe_combine",
+        lib().lm_moe_combine(_ptr(y_perm), _ptr(pair_to_row), _ptr(topk_weights_bf16), T, k,
+                             out.shape[-1], _ptr(out), _stream()),
+    )
+
+
+def stage_copy(dst: torch.Tensor, src: torch.Tensor, src_rows: list[int], dst_rows: list[int],
+               stream: torch.cuda.Stream | None = None) -> int:
+    """Copy expert rows src[src_rows[i]] -> dst[dst_rows[i]] (first dim = expert/slot row)."""
+    if len(src_rows) != len(dst_rows):
+        raise ValueError("src_rows and dst_rows must have the same length")
+    n = len(src_rows)
+    if n == 0:
+        return 0
+    if not dst.is_cuda:
+        raise RuntimeError("stage_copy destination must be a CUDA tensor")
+    if src.is_cuda:
+        kind = LM_COPY_D2D
+    else:
+        if not src.is_pinned():
+            raise RuntimeError("stage_copy host source must be pinned (cudaHostAlloc) memory")
+        kind = LM_COPY_H2D
+    row_bytes = dst[0].numel() * dst.element_size()
+    if src[0].numel() * src.element_size() != row_bytes or src.dtype != dst.dtype:
+        raise ValueError("stage_copy: source and destination rows differ in size or dtype")
+    arr = ctypes.c_int32 * n
+    src_arr = arr(*[int(r) for r in src_rows])
+    dst_arr = arr(*[int(r) for r in dst_rows])
+    return _check(
+        "lm_stage_copy",
+        lib().lm_stage_copy(
+            _ptr(dst), dst.stride(0) * dst.element_size(), _ptr(src),
+            src.stride(0) * src.element_size(), src_arr, dst_arr, n, row_bytes, kind,
+            _stream(stream),
+        ),
+    )
+
+
+def read_err_word(err_word: torch.Tensor) -> int:
+    return int(err_word.item())
+
+
+def raise_on_device_error(err_word: torch.Tensor, where: str) -> None:
+    code = read_err_word(err_word)
+    if code != 0:
+        raise RuntimeError(f"{where}: device error {code} ({DEVERR_NAMES.get(code, '?')})")

@@ -1,0 +1,538 @@
+// Routing-side kernels of the slot-bank MoE layer:
+//   K1 router (scores -> grouped/plain top-k -> renorm -> scale -> bf16),
+//   K2 expert histogram,
+//   K4/K9 stable pair grouping (expert -> group/slot table, original pair order kept),
+//   row gather (permute) and K8 weighted combine in the original top-k order.
+// All kernels are deterministic: atomics only add integers.
+#include <cfloat>
+#include <cmath>
+
+#include "lm_common.cuh"
+
+namespace lm {
+namespace {
+
+constexpr int kRouteWarpsPerBlock = 8;
+constexpr int kGroupTile = 512;  // pairs per tile in the grouping kernels
+constexpr int kGroupTileWarps = kGroupTile / 32;
+constexpr int kMaxGroups = 1024;
+
+// Warp arg-max with ties broken toward the lower index. Returns the winner to all lanes.
+__device__ __forceinline__ void warp_argmax(float& v, int& idx) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One warp per token. Expert e lives on lane e % 32, register slot e / 32.
+template <int EPL>
+__global__ void __launch_bounds__(kRouteWarpsPerBlock * 32)
+    route_topk_kernel(const float* __restrict__ logits, int64_t num_tokens, int num_experts,
+                      int top_k, int scoring, int renorm, float scale,
+                      const float* __restrict__ bias, int n_group, int topk_group,
+                      uint16_t* __restrict__ w_bf16, float* __restrict__ w_f32,
+                      int32_t* __restrict__ ids) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kRouteWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= num_tokens) return;
+  const float* row = logits + t * num_experts;
+
+  float lg[EPL], sc[EPL], key[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    lg[i] = (e < num_experts) ? __ldg(row + e) : -INFINITY;
+  }
+
+  if (scoring == LM_SCORING_SOFTMAX) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) m = fmaxf(m, lg[i]);
+    m = warp_max(m);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      sc[i] = (e < num_experts) ? expf(lg[i] - m) : 0.f;
+      s += sc[i];
+    }
+    s = warp_sum(s);
+    const float inv = 1.0f / s;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) sc[i] *= inv;
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) sc[i] = 1.0f / (1.0f + expf(-lg[i]));
+  }
+
+  // Selection key: the logit itself when no correction bias is given (scores are monotone
+  // in the logit, so the chosen set and order are those of the scores, computed exactly);
+  // otherwise score + bias as in group-limited routing with a correction bias.
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    if (e >= num_experts) {
+      key[i] = -INFINITY;
+    } else if (bias != nullptr) {
+      key[i] = sc[i] + __ldg(bias + e);
+    } else {
+      key[i] = lg[i];
+    }
+  }
+
+  // Group-limited selection: keep the topk_group best groups (max key per group, or the sum
+  // of the two best keys when a correction bias is used), ties toward the lower group id.
+  if (n_group > 1 && topk_group < n_group) {  // n_group <= 32 (checked on the host)
+    const int gsize = num_experts / n_group;
+    unsigned keep_mask = 0;
+    float gscore_mine = -INFINITY;  // lane g holds the score of group g
+    for (int g = 0; g < n_group; ++g) {
+      float b1 = -INFINITY;
+      int i1 = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        if (e < num_experts && e / gsize == g && key[i] > b1) {
+          b1 = key[i];
+          i1 = e;
+        }
+      }
+      float v = b1;
+      int vi = i1;
+      warp_argmax(v, vi);
+      float score = v;
+      if (bias != nullptr) {
+        float b2 = -INFINITY;
+        int i2 = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+          const int e = lane + 32 * i;
+          if (e < num_experts && e / gsize == g && e != vi && key[i] > b2) {
+            b2 = key[i];
+            i2 = e;
+          }
+        }
+        warp_argmax(b2, i2);
+        score = v + (b2 == -INFINITY ? 0.f : b2);
+      }
+      if (lane == g) gscore_mine = score;
+    }
+    float gs = (lane < n_group) ? gscore_mine : -INFINITY;
+    unsigned taken_groups = 0;
+    for (int j = 0; j < topk_group; ++j) {
+      float v = (lane < n_group && !((taken_groups >> lane) & 1u)) ? gs : -INFINITY;
+      int vi = (lane < n_group && !((taken_groups >> lane) & 1u)) ? lane : 0x7fffffff;
+      warp_argmax(v, vi);
+      if (vi < 32) {
+        keep_mask |= 1u << vi;
+        taken_groups |= 1u << vi;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      if (e < num_experts && !((keep_mask >> (e / gsize)) & 1u)) key[i] = -INFINITY;
+    }
+  }
+
+  // Top-k: k rounds of warp arg-max over the unselected keys.
+  float my_w = 0.f;
+  int my_id = 0;
+  unsigned taken = 0;
+  for (int j = 0; j < top_k; ++j) {
+    float v = -INFINITY;
+    int vi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      if (!((taken >> i) & 1u) && e < num_experts && (key[i] > v || (key[i] == v && e < vi))) {
+        v = key[i];
+        vi = e;
+      }
+    }
+    warp_argmax(v, vi);
+    if (vi == 0x7fffffff) vi = 0;  // only reachable with NaN logits: fall back to expert 0
+    // Fetch the winner's score from its owner lane.
+    const int owner = vi & 31;
+    const int slot = vi >> 5;
+    float mine = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i)
+      if (i == slot) mine = sc[i];
+    const float w = __shfl_sync(0xffffffffu, mine, owner);
+    if (lane == owner) taken |= 1u << slot;
+    if (lane == j) {
+      my_w = w;
+      my_id = vi;
+    }
+  }
+
+  if (renorm) {
+    const float s = warp_sum(lane < top_k ? my_w : 0.f);
+    my_w = my_w / fmaxf(s, FLT_EPSILON);
+  }
+  my_w *= scale;
+  if (lane < top_k) {
+    const int64_t o = t * top_k + lane;
+    w_bf16[o] = f32_to_bf16_bits(my_w);
+    if (w_f32 != nullptr) w_f32[o] = my_w;
+    ids[o] = my_id;
+  }
+}
+
+__global__ void histogram_kernel(const int32_t* __restrict__ ids, int64_t num_pairs,
+                                 int num_experts, int32_t* __restrict__ counts,
+                                 int32_t* __restrict__ err_word) {
+  extern __shared__ int32_t s_hist[];
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x) s_hist[e] = 0;
+  __syncthreads();
+  for (int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; p < num_pairs;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[p];
+    if (e < 0 || e >= num_experts) {
+      record_error(err_word, LM_DEVERR_BAD_EXPERT_ID);
+      continue;
+    }
+    atomicAdd(&s_hist[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < num_experts; e += blockDim.x)
+    if (s_hist[e]) atomicAdd(&counts[e], s_hist[e]);
+}
+
+__device__ __forceinline__ int pair_group(const int32_t* ids, int64_t p, int64_t num_pairs,
+                                          int num_experts, const int32_t* e2g, int num_groups,
+                                          int32_t* err_word, bool report) {
+  if (p >= num_pairs) return -2;
+  const int e = ids[p];
+  if (e < 0 || e >= num_experts) {
+    if (report) record_error(err_word, LM_DEVERR_BAD_EXPERT_ID);
+    return -1;
+  }
+  const int g = e2g[e];
+  if (g < 0 || g >= num_groups) {
+    if (report) record_error(err_word, LM_DEVERR_UNMAPPED_EXPERT);
+    return -1;
+  }
+  return g;
+}
+
+// Pass 1: per-tile group counts.
+__global__ void __launch_bounds__(kGroupTile)
+    group_tile_count_kernel(const int32_t* __restrict__ ids, int64_t num_pairs, int num_experts,
+                            const int32_t* __restrict__ e2g, int num_groups,
+                            int32_t* __restrict__ tile_counts, int32_t* __restrict__ err_word) {
+  extern __shared__ int32_t s_cnt[];
+  for (int g = threadIdx.x; g < num_groups; g += blockDim.x) s_cnt[g] = 0;
+  __syncthreads();
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * kGroupTile + threadIdx.x;
+  const int g = pair_group(ids, p, num_pairs, num_experts, e2g, num_groups, err_word, true);
+  if (g >= 0) atomicAdd(&s_cnt[g], 1);
+  __syncthreads();
+  int32_t* out = tile_counts + static_cast<int64_t>(blockIdx.x) * num_groups;
+  for (int gg = threadIdx.x; gg < num_groups; gg += blockDim.x) out[gg] = s_cnt[gg];
+}
+
+// Pass 2 (one block): per-group exclusive scan over tiles, then exclusive scan over groups.
+__global__ void __launch_bounds__(1024)
+    group_scan_kernel(int32_t* __restrict__ tile_counts, int num_tiles, int num_groups,
+                      int32_t* __restrict__ tile_base, int32_t* __restrict__ group_offsets) {
+  __shared__ int32_t s_tot[kMaxGroups];
+  __shared__ int32_t s_warp[32];
+  for (int g = threadIdx.x; g < num_groups; g += blockDim.x) {
+    int run = 0;
+    for (int t = 0; t < num_tiles; ++t) {
+      const int64_t o = static_cast<int64_t>(t) * num_groups + g;
+      const int c = tile_counts[o];
+      tile_base[o] = run;
+      run += c;
+    }
+    s_tot[g] = run;
+  }
+  __syncthreads();
+  // Exclusive scan of s_tot[0..num_groups) with one pass of 1024 threads.
+  const int g = threadIdx.x;
+  const int lane = g & 31, w = g >> 5;
+  int v = (g < num_groups) ? s_tot[g] : 0;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int tt = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += tt;
+  }
+  if (lane == 31) s_warp[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int ws = s_warp[lane];
+    int wi = ws;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int tt = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += tt;
+    }
+    s_warp[lane] = wi - ws;  // exclusive warp prefix
+  }
+  __syncthreads();
+  const int excl = s_warp[w] + incl - v;
+  if (g < num_groups) group_offsets[g] = excl;
+  if (g == num_groups - 1) group_offsets[num_groups] = excl + v;
+}
+
+// Pass 3: stable scatter. Rank inside the tile = pairs of the same group in earlier warps
+// plus earlier lanes of this warp, so rows keep the original flat pair order.
+__global__ void __launch_bounds__(kGroupTile)
+    group_scatter_kernel(const int32_t* __restrict__ ids, int64_t num_pairs, int num_experts,
+                         const int32_t* __restrict__ e2g, int num_groups,
+                         const int32_t* __restrict__ tile_base,
+                         const int32_t* __restrict__ group_offsets,
+                         int32_t* __restrict__ pair_to_row, int32_t* __restrict__ row_to_pair) {
+  extern __shared__ int32_t s_wcnt[];  // [kGroupTileWarps][num_groups]
+  for (int i = threadIdx.x; i < kGroupTileWarps * num_groups; i += blockDim.x) s_wcnt[i] = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * kGroupTile + threadIdx.x;
+  const int g = pair_group(ids, p, num_pairs, num_experts, e2g, num_groups, nullptr, false);
+  const unsigned peers = __match_any_sync(0xffffffffu, g);
+  const unsigned lt = (1u << lane) - 1u;
+  const int rank = __popc(peers & lt);
+  if (g >= 0 && rank == 0) s_wcnt[w * num_groups + g] = __popc(peers);
+  __syncthreads();
+  if (g >= 0) {
+    int off = rank;
+    for (int ww = 0; ww < w; ++ww) off += s_wcnt[ww * num_groups + g];
+    const int row =
+        group_offsets[g] + tile_base[static_cast<int64_t>(blockIdx.x) * num_groups + g] + off;
+    pair_to_row[p] = row;
+    row_to_pair[row] = static_cast<int32_t>(p);
+  } else if (g == -1) {
+    pair_to_row[p] = -1;
+  }
+}
+
+__global__ void permute_rows_kernel(const uint16_t* __restrict__ hidden, int hidden_size,
+                                    const int32_t* __restrict__ row_to_pair, int top_k,
+                                    int64_t num_rows, uint16_t* __restrict__ x_perm) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= num_rows) return;
+  const int64_t tok = row_to_pair[r] / top_k;
+  const uint4* src = reinterpret_cast<const uint4*>(hidden + tok * hidden_size);
+  uint4* dst = reinterpret_cast<uint4*>(x_perm + r * hidden_size);
+  for (int c = lane; c < hidden_size / 8; c += 32) dst[c] = __ldg(src + c);
+}
+
+__global__ void combine_kernel(const uint16_t* __restrict__ y_perm,
+                               const int32_t* __restrict__ pair_to_row,
+                               const uint16_t* __restrict__ w_bf16, int top_k, int hidden_size,
+                               uint16_t* __restrict__ out) {
+  __shared__ int32_t s_row[32];
+  __shared__ float s_w[32];
+  const int64_t t = blockIdx.x;
+  if (threadIdx.x < top_k) {
+    s_row[threadIdx.x] = pair_to_row[t * top_k + threadIdx.x];
+    s_w[threadIdx.x] = bf16_bits_to_f32(w_bf16[t * top_k + threadIdx.x]);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < hidden_size / 8; c += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int j = 0; j < top_k; ++j) {
+      const int row = s_row[j];
+      if (row < 0) continue;
+      const float w = s_w[j];
+      const uint4 v =
+          __ldg(reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(row) * hidden_size) + c);
+      float a, b;
+      unpack_bf16x2(v.x, a, b);
+      acc[0] += w * a;
+      acc[1] += w * b;
+      unpack_bf16x2(v.y, a, b);
+      acc[2] += w * a;
+      acc[3] += w * b;
+      unpack_bf16x2(v.z, a, b);
+      acc[4] += w * a;
+      acc[5] += w * b;
+      unpack_bf16x2(v.w, a, b);
+      acc[6] += w * a;
+      acc[7] += w * b;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + t * hidden_size)[c] = o;
+  }
+}
+
+}  // namespace
+}  // namespace lm
+
+using namespace lm;
+
+extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts,
+                             int32_t top_k, int32_t scoring_func, int32_t renormalize,
+                             float routed_scaling_factor, const float* e_score_correction_bias,
+                             int32_t num_expert_group, int32_t topk_group,
+                             uint16_t* topk_weights_bf16, float* topk_weights_f32,
+                             int32_t* topk_ids, void* stream) {
+  if (num_tokens < 0 || num_experts <= 0 || num_experts > 256)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_route_topk: need 0 < num_experts <= 256");
+  if (top_k <= 0 || top_k > 32 || top_k > num_experts)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_route_topk: need 0 < top_k <= min(32, E)");
+  if (scoring_func != LM_SCORING_SOFTMAX && scoring_func != LM_SCORING_SIGMOID)
+    return fail(LM_ERR_UNSUPPORTED, "lm_route_topk: scoring_func must be softmax or sigmoid");
+  if (num_expert_group > 1) {
+    if (num_expert_group > 32 || num_experts % num_expert_group != 0 || topk_group <= 0 ||
+        topk_group > num_expert_group)
+      return fail(LM_ERR_INVALID_ARGUMENT,
+                  "lm_route_topk: grouped top-k needs n_group <= 32 dividing E and "
+                  "0 < topk_group <= n_group");
+    if (topk_group * (num_experts / num_expert_group) < top_k)
+      return fail(LM_ERR_INVALID_ARGUMENT,
+                  "lm_route_topk: topk_group groups hold fewer than top_k experts");
+  }
+  if (topk_weights_bf16 == nullptr || topk_ids == nullptr || (num_tokens > 0 && logits == nullptr))
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_route_topk: null output or input pointer");
+  if (num_tokens == 0) return LM_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned blocks =
+      static_cast<unsigned>((num_tokens + kRouteWarpsPerBlock - 1) / kRouteWarpsPerBlock);
+  const int epl = (num_experts + 31) / 32;
+#define LM_ROUTE_LAUNCH(N)                                                                   \
+  route_topk_kernel<N><<<blocks, kRouteWarpsPerBlock * 32, 0, s>>>(                          \
+      logits, num_tokens, num_experts, top_k, scoring_func, renormalize,                     \
+      routed_scaling_factor, e_score_correction_bias, num_expert_group, topk_group,          \
+      topk_weights_bf16, topk_weights_f32, topk_ids)
+  if (epl <= 1) {
+    LM_ROUTE_LAUNCH(1);
+  } else if (epl <= 2) {
+    LM_ROUTE_LAUNCH(2);
+  } else if (epl <= 4) {
+    LM_ROUTE_LAUNCH(4);
+  } else {
+    LM_ROUTE_LAUNCH(8);
+  }
+#undef LM_ROUTE_LAUNCH
+  return launch_status("lm_route_topk");
+}
+
+extern "C" int lm_expert_histogram(const int32_t* topk_ids, int64_t num_pairs,
+                                   int32_t num_experts, int32_t* counts, int32_t* err_word,
+                                   void* stream) {
+  if (num_pairs < 0 || num_experts <= 0 || num_experts > 16384 || counts == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_expert_histogram: bad arguments");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = check_cuda(cudaMemsetAsync(counts, 0, sizeof(int32_t) * num_experts, s),
+                      "lm_expert_histogram: memset");
+  if (rc) return rc;
+  if (num_pairs == 0) return LM_OK;
+  const int threads = 256;
+  int64_t blocks64 = (num_pairs + threads - 1) / threads;
+  const unsigned blocks = static_cast<unsigned>(blocks64 > 1184 ? 1184 : blocks64);
+  histogram_kernel<<<blocks, threads, sizeof(int32_t) * num_experts, s>>>(
+      topk_ids, num_pairs, num_experts, counts, err_word);
+  return launch_status("lm_expert_histogram");
+}
+
+extern "C" int64_t lm_build_groups_scratch_elems(int64_t num_pairs, int32_t num_groups) {
+  if (num_pairs < 0 || num_groups <= 0) return 0;
+  const int64_t tiles = (num_pairs + kGroupTile - 1) / kGroupTile;
+  return 2 * (tiles > 0 ? tiles : 1) * static_cast<int64_t>(num_groups);
+}
+
+extern "C" int lm_build_groups(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
+                               const int32_t* expert_to_group, int32_t num_groups,
+                               int32_t* group_offsets, int32_t* pair_to_row,
+                               int32_t* row_to_pair, int32_t* scratch, int64_t scratch_elems,
+                               int32_t* err_word, void* stream) {
+  if (num_pairs < 0 || num_experts <= 0 || num_groups <= 0 || num_groups > kMaxGroups)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_build_groups: need num_pairs >= 0 and 0 < num_groups <= 1024");
+  if (group_offsets == nullptr || expert_to_group == nullptr ||
+      (num_pairs > 0 && (topk_ids == nullptr || pair_to_row == nullptr || row_to_pair == nullptr)))
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_build_groups: null pointer");
+  const int64_t need = lm_build_groups_scratch_elems(num_pairs, num_groups);
+  if (scratch == nullptr || scratch_elems < need)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_build_groups: scratch too small (need " + std::to_string(need) + " int32)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t tiles64 = (num_pairs + kGroupTile - 1) / kGroupTile;
+  const int tiles = static_cast<int>(tiles64 > 0 ? tiles64 : 1);
+  int32_t* tile_counts = scratch;
+  int32_t* tile_base = scratch + static_cast<int64_t>(tiles) * num_groups;
+  if (num_pairs == 0) {
+    int rc = check_cuda(cudaMemsetAsync(tile_counts, 0, sizeof(int32_t) * num_groups, s),
+                        "lm_build_groups: memset");
+    if (rc) return rc;
+  } else {
+    group_tile_count_kernel<<<tiles, kGroupTile, sizeof(int32_t) * num_groups, s>>>(
+        topk_ids, num_pairs, num_experts, expert_to_group, num_groups, tile_counts, err_word);
+    int rc = launch_status("lm_build_groups: count");
+    if (rc) return rc;
+  }
+  group_scan_kernel<<<1, 1024, 0, s>>>(tile_counts, tiles, num_groups, tile_base, group_offsets);
+  int rc = launch_status("lm_build_groups: scan");
+  if (rc || num_pairs == 0) return rc;
+  const size_t smem = sizeof(int32_t) * kGroupTileWarps * num_groups;
+  if (smem > 48 * 1024) {
+    rc = check_cuda(cudaFuncSetAttribute(group_scatter_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)),
+                    "lm_build_groups: smem attribute");
+    if (rc) return rc;
+  }
+  group_scatter_kernel<<<tiles, kGroupTile, smem, s>>>(topk_ids, num_pairs, num_experts,
+                                                       expert_to_group, num_groups, tile_base,
+                                                       group_offsets, pair_to_row, row_to_pair);
+  return launch_status("lm_build_groups: scatter");
+}
+
+extern "C" int lm_permute_rows(const uint16_t* hidden, int32_t hidden_size,
+                               const int32_t* row_to_pair, int32_t top_k, int64_t num_rows,
+                               uint16_t* x_perm, void* stream) {
+  if (hidden_size <= 0 || hidden_size % 8 != 0 || top_k <= 0 || num_rows < 0)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_permute_rows: need hidden_size % 8 == 0");
+  if (num_rows == 0) return LM_OK;
+  const int warps = 8;
+  const unsigned blocks = static_cast<unsigned>((num_rows + warps - 1) / warps);
+  permute_rows_kernel<<<blocks, warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      hidden, hidden_size, row_to_pair, top_k, num_rows, x_perm);
+  return launch_status("lm_permute_rows");
+}
+
+extern "C" int lm_moe_combine(const uint16_t* y_perm, const int32_t* pair_to_row,
+                              const uint16_t* topk_weights_bf16, int64_t num_tokens,
+                              int32_t top_k, int32_t hidden_size, uint16_t* out, void* stream) {
+  if (num_tokens < 0 || top_k <= 0 || top_k > 32 || hidden_size <= 0 || hidden_size % 8 != 0)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_moe_combine: need 0 < top_k <= 32 and hidden_size % 8 == 0");
+  if (num_tokens == 0) return LM_OK;
+  if (num_tokens > 0x7fffffff) return fail(LM_ERR_INVALID_ARGUMENT, "lm_moe_combine: too many tokens");
+  int threads = hidden_size / 8;
+  if (threads > 512) threads = 512;
+  if (threads < 32) threads = 32;
+  combine_kernel<<<static_cast<unsigned>(num_tokens), threads, 0,
+                   static_cast<cudaStream_t>(stream)>>>(y_perm, pair_to_row, topk_weights_bf16,
+                                                        top_k, hidden_size, out);
+  return launch_status("lm_moe_combine");
+}

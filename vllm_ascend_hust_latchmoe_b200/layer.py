@@ -1,0 +1,292 @@
+"""The slot-bank MoE layer on B200: router -> stage -> slot-indexed grouped MLP -> combine.
+
+This is the executor behind the plugin's seam ops. It mirrors the reference's data path:
+
+* router piece      -- ``ops/fused_moe/moe_router_op.py:72-278`` (K1 ``lm_route_topk``);
+* stage seam        -- ``ops/fused_moe/moe_offload_stage_op.py:160-471``: eager; no-op while
+                       capturing and in Regime A; reads the active set (a device histogram and
+                       one 4*E-byte copy instead of copying every top-k id), defers to waves
+                       when the working set exceeds the slots, else stages the slots;
+* MLP piece         -- ``ops/fused_moe/moe_mlp_op.py:69-130`` + patched ``fused_experts``
+                       (``patches/patch_fused_moe.py:3946-4003``): log2phy remap + grouping
+                       (``lm_build_groups``), grouped MLP over the fixed slot bank
+                       (``lm_moe_mlp_decode`` / ``lm_moe_mlp_prefill``), one combine. It reads
+                       only fixed buffers, so it can be captured in a CUDA graph;
+* multi-wave path   -- ``patches/patch_fused_moe.py:2443-3470``: canonical waves, double-
+                       buffered stage banks on the copy stream, one GEMM pass per wave, and
+                       ONE combine in the original top-k pair order at the end.
+
+All buffers are allocated once for ``max_tokens`` and reused, so launches see stable
+addresses. There is no CPU or eager-torch fallback for any of the math.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .moe_offload.phase_split import (
+    WaveIssuer,
+    plan_b2_prefill_async_schedule,
+    plan_balanced_b2_waves,
+)
+from .moe_offload.runtime import MoeOffloadRuntime
+
+PHASE_UNKNOWN = -1
+PHASE_DECODE = 0
+PHASE_PREFILL = 1
+PHASE_MIXED = 2
+
+# Above this many tokens per call the grouped MLP runs on the tcgen05 GEMM; at or below it
+# on the bandwidth-bound GEMV (a group never holds more rows than the call has tokens).
+DECODE_MAX_TOKENS = 64
+
+
+@dataclass
+class StageDecision:
+    mode: str                 # "capturing" | "static" | "slots" | "waves" | "passthrough"
+    active_experts: tuple[int, ...] = ()
+    counts: tuple[int, ...] = ()
+    prepared: object | None = None
+
+
+@dataclass
+class WaveReport:
+    waves: tuple[tuple[int, ...], ...] = ()
+    staged_bytes: int = 0
+    zero_copy: bool = False
+    launches: int = 0
+
+
+class SlotBankMoE:
+    def __init__(
+        self,
+        runtime: MoeOffloadRuntime,
+        layer_id: int,
+        *,
+        hidden_size: int,
+        intermediate_size: int,
+        num_experts: int,
+        top_k: int,
+        max_tokens: int,
+        renormalize: bool = True,
+        routed_scaling_factor: float = 1.0,
+        scoring_func: str = "softmax",
+        num_expert_group: int = 0,
+        topk_group: int = 0,
+        e_score_correction_bias: torch.Tensor | None = None,
+        device: torch.device | str | None = None,
+    ) -> None:
+        self.runtime = runtime
+        self.layer_id = int(layer_id)
+        self.H = int(hidden_size)
+        self.I = int(intermediate_size)
+        self.E = int(num_experts)
+        self.k = int(top_k)
+        self.max_tokens = int(max_tokens)
+        self.renormalize = bool(renormalize)
+        self.routed_scaling_factor = float(routed_scaling_factor)
+        self.scoring_func = scoring_func
+        self.num_expert_group = int(num_expert_group or 0)
+        self.topk_group = int(topk_group or 0)
+        self.device = torch.device(device) if device is not None else torch.device("cuda")
+        self.e_bias = (None if e_score_correction_bias is None else
+                       e_score_correction_bias.to(self.device, torch.float32).contiguous())
+        bank = runtime.slot_bank(self.layer_id)
+        self.E_total = runtime.total_logical_expert_count_for_layer(layer_id=self.layer_id,
+                                                                    fallback=self.E)
+        self.num_bank_rows = bank.physical_expert_count
+        d, i32 = self.device, torch.int32
+        P = self.max_tokens * self.k
+        self.G_max = max(self.E_total, self.num_bank_rows)
+        self.topk_ids = torch.zeros(self.max_tokens, self.k, dtype=i32, device=d)
+        self.topk_w = torch.zeros(self.max_tokens, self.k, dtype=torch.bfloat16, device=d)
+        self.counts = torch.zeros(self.E, dtype=i32, device=d)
+        self.counts_host = torch.zeros(self.E, dtype=i32, pin_memory=True)
+        self.err = torch.zeros(1, dtype=i32, device=d)
+        self.tables_host = torch.zeros(self.E_total + self.G_max, dtype=i32, pin_memory=True)
+        self.tables = torch.zeros(self.E_total + self.G_max, dtype=i32, device=d)
+        self.expert_to_group = self.tables[: self.E_total]
+        self.group_bank_row = self.tables[self.E_total:]
+        self.slot_rows = torch.arange(self.num_bank_rows, dtype=i32, device=d)
+        self.group_offsets = torch.zeros(self.G_max + 1, dtype=i32, device=d)
+        self.pair_to_row = torch.zeros(P, dtype=i32, device=d)
+        self.row_to_pair = torch.zeros(P, dtype=i32, device=d)
+        self.scratch = torch.zeros(_lib.build_groups_scratch_elems(P, self.G_max), dtype=i32, device=d)
+        self.x_perm = torch.zeros(P, self.H, dtype=torch.bfloat16, device=d)
+        self.act = torch.zeros(P, self.I, dtype=torch.bfloat16, device=d)
+        self.y_perm = torch.zeros(P, self.H, dtype=torch.bfloat16, device=d)
+        self.out = torch.zeros(self.max_tokens, self.H, dtype=torch.bfloat16, device=d)
+        self.last_waves = WaveReport()
+        self.kernel_launches = 0
+
+    # ------------------------------------------------------------------ pieces
+    def route(self, hidden: torch.Tensor, router_logits: torch.Tensor):
+        """K1: fills the fixed ``topk_w`` / ``topk_ids`` buffers; returns [T, k] views."""
+        T = int(router_logits.shape[0])
+        self._check_tokens(T)
+        logits = router_logits if router_logits.dtype == torch.float32 else router_logits.float()
+        _lib.route_topk(logits.contiguous(), self.k, scoring_func=self.scoring_func,
+                        renormalize=self.renormalize,
+                        routed_scaling_factor=self.routed_scaling_factor,
+                        e_score_correction_bias=self.e_bias,
+                        num_expert_group=self.num_expert_group, topk_group=self.topk_group,
+                        weights_bf16=self.topk_w[:T], ids=self.topk_ids[:T])
+        self.kernel_launches += 1
+        return self.topk_w[:T], self.topk_ids[:T]
+
+    def active_counts(self, topk_ids: torch.Tensor) -> tuple[int, ...]:
+        """K2 histogram + one small D2H: per-expert pair counts of this call."""
+        _lib.expert_histogram(topk_ids, self.E, self.counts, self.err)
+        self.kernel_launches += 1
+        self.counts_host.copy_(self.counts, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return tuple(self.counts_host.tolist())
+
+    def stage(self, topk_ids: torch.Tensor, phase: int = PHASE_UNKNOWN,
+              capturing: bool = False) -> StageDecision:
+        """Eager staging seam between the captured router and MLP pieces."""
+        rt = self.runtime
+        if capturing or torch.cuda.is_current_stream_capturing():
+            if rt.should_use_fixed_slot_plan_for_layer(self.layer_id) and not rt.is_layer_registered(self.layer_id):
+                raise RuntimeError(f"graph capture reached an unregistered fixed-slot MoE layer {self.layer_id}")
+            return StageDecision("capturing")
+        if rt.is_static_residency_regime(self.E):
+            return StageDecision("static")
+        if not rt.should_use_fixed_slot_plan_for_layer(self.layer_id):
+            return StageDecision("passthrough")
+        counts = self.active_counts(topk_ids)
+        active = tuple(e for e, c in enumerate(counts) if c > 0)
+        if len(active) > rt.config.num_slots:
+            if not rt.config.b2_wave_prefill:
+                raise RuntimeError(
+                    f"active expert working set size {len(active)} exceeds "
+                    f"num_slots={rt.config.num_slots} and multi-wave execution is disabled")
+            return StageDecision("waves", active, counts)
+        prepared = rt.stage_fixed_slot_plan(layer_id=self.layer_id, active_experts=active,
+                                            num_logical_experts=self.E)
+        return StageDecision("slots", active, counts, prepared)
+
+    def mlp_slots(self, hidden: torch.Tensor, T: int) -> torch.Tensor:
+        """Captured MLP piece: log2phy remap + grouping, grouped MLP on the slot bank, combine.
+
+        Reads only fixed addresses (slot bank, log2phy, this layer's buffers)."""
+        rt = self.runtime
+        bank = rt.slot_bank(self.layer_id)
+        log2phy = rt.log2phy_buffer(self.layer_id)
+        ids = self.topk_ids[:T]
+        G = self.num_bank_rows
+        _lib.build_groups(ids, self.E_total, log2phy, G, self.group_offsets, self.pair_to_row,
+                          self.row_to_pair, self.scratch, self.err)
+        self._grouped_mlp(hidden, T, self.slot_rows, 0, G, bank.w13_slots, bank.w2_slots)
+        _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], self.out[:T])
+        self.kernel_launches += 4
+        return self.out[:T]
+
+    def _grouped_mlp(self, hidden, T, bank_rows_dev, g0, g1, w13_bank, w2_bank) -> None:
+        if T <= DECODE_MAX_TOKENS:
+            _lib.moe_mlp_decode(hidden, self.k, self.row_to_pair, self.group_offsets,
+                                bank_rows_dev, g0, g1, T, w13_bank, w2_bank, self.act,
+                                self.y_perm, self.err)
+        else:
+            _lib.moe_mlp_prefill(self.x_perm, T * self.k, self.group_offsets, bank_rows_dev,
+                                 g0, g1, w13_bank, w2_bank, self.act, self.y_perm, self.err)
+
+    def forward_waves(self, hidden: torch.Tensor, T: int, counts: tuple[int, ...]) -> torch.Tensor:
+        """Capacity-bounded waves with one combine at the end (eager)."""
+        rt = self.runtime
+        cfg = rt.config
+        S = int(cfg.num_slots)
+        plan = plan_balanced_b2_waves({e: c for e, c in enumerate(counts) if c > 0}, S)
+        waves = plan.waves
+        store = rt.host_layer(self.layer_id)
+        zero_copy = store.on_device
+        e2g = self.tables_host[: self.E_total]
+        e2g.fill_(-1)
+        rows = self.tables_host[self.E_total:]
+        wave_groups: list[tuple[int, int]] = []
+        g = 0
+        for wave in waves:
+            g0 = g
+            for pos, e in enumerate(wave):
+                e2g[e] = g
+                rows[g] = e if zero_copy else pos
+                g += 1
+            wave_groups.append((g0, g))
+        self.tables.copy_(self.tables_host, non_blocking=True)
+        ids = self.topk_ids[:T]
+        _lib.build_groups(ids, self.E_total, self.expert_to_group, g, self.group_offsets,
+                          self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+        launches = 1
+        if T > DECODE_MAX_TOKENS:
+            _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
+            launches += 1
+        report = WaveReport(waves=waves, zero_copy=zero_copy)
+        if zero_copy:
+            # Every expert already has an HBM copy: read it in place, all waves in one pass.
+            self._grouped_mlp(hidden, T, self.group_bank_row, 0, g, store.w13, store.w2)
+            launches += 2
+        else:
+            main = rt.slot_bank(self.layer_id)
+            ready = main.ready_slot_ids(self.layer_id, [e for w in waves for e in w])
+            h2d = {i: sum(store.expert_bytes for e in w if e not in ready) for i, w in enumerate(waves)}
+            cost = {i: float(plan.wave_tokens(w)) for i, w in enumerate(waves)}
+            schedule = plan_b2_prefill_async_schedule(
+                waves, slot_readiness={}, prefetch_depth=cfg.effective_prefill_prefetch_depth,
+                buffer_count=cfg.effective_prefill_buffer_count, h2d_bytes_by_wave=h2d,
+                compute_cost_by_wave=cost, transfer_aware=cfg.transfer_aware_wave_schedule)
+            pending = {}
+            compute_stream = torch.cuda.current_stream()
+            for kind, w, buf in WaveIssuer(schedule).events():
+                if kind == "issue_stage":
+                    pending[w] = rt.prepare_prefill_stage_plan(
+                        layer_id=self.layer_id, active_experts=waves[w], buffer_index=buf,
+                        wait_event=rt.prefill_stage_buffer_release_event(self.layer_id, buf))
+                    report.staged_bytes += pending[w][1].bytes
+                elif kind == "compute":
+                    stage_bank, ready_ev = pending.pop(w)
+                    rt.wait_prefill_stage_plan(ready_ev, compute_stream)
+                    g0, g1 = wave_groups[w]
+                    self._grouped_mlp(hidden, T, self.group_bank_row, g0, g1,
+                                      stage_bank.w13_slots, stage_bank.w2_slots)
+                    launches += 2
+                    release = torch.cuda.Event()
+                    release.record(compute_stream)
+                    rt.remember_prefill_stage_buffer_release(self.layer_id, buf, release)
+        _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], self.out[:T])
+        launches += 1
+        report.launches = launches
+        self.last_waves = report
+        self.kernel_launches += launches
+        return self.out[:T]
+
+    # ------------------------------------------------------------------ whole layer
+    def forward(self, hidden: torch.Tensor, router_logits: torch.Tensor,
+                phase: int = PHASE_UNKNOWN) -> torch.Tensor:
+        """Eager layer call: route -> stage -> slot MLP or multi-wave MLP -> combine."""
+        T = int(hidden.shape[0])
+        self._check_tokens(T)
+        if hidden.dtype != torch.bfloat16 or not hidden.is_contiguous():
+            raise ValueError("hidden_states must be a contiguous bf16 tensor")
+        _, ids = self.route(hidden, router_logits)
+        decision = self.stage(ids, phase)
+        if decision.mode == "waves":
+            return self.forward_waves(hidden, T, decision.counts)
+        if decision.mode not in ("slots", "static"):
+            raise RuntimeError(f"layer {self.layer_id} is not offloaded under fixed slots")
+        rt = self.runtime
+        rt.capture_safe_slot_weights(layer_id=self.layer_id)
+        handle = rt.begin_slot_compute(decision.prepared) if decision.prepared is not None else None
+        out = self.mlp_slots(hidden, T)
+        rt.end_slot_compute(handle)
+        return out
+
+    def check_device_errors(self, where: str = "SlotBankMoE") -> None:
+        _lib.raise_on_device_error(self.err, f"{where} layer {self.layer_id}")
+
+    def _check_tokens(self, T: int) -> None:
+        if T <= 0 or T > self.max_tokens:
+            raise ValueError(f"token count {T} outside (0, {self.max_tokens}]")
+
