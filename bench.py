@@ -1,0 +1,409 @@
+"""Benchmark of the B200 slot-bank MoE hot path (one JSON line on stdout, rank 0).
+
+Workload (N=1): the multi-wave prefill layer on synthetic Qwen3-30B-A3B-shaped data
+(4096 tokens x hidden 2048, 128 experts, top-8, moe_intermediate 768, bf16 weights, 32 slots:
+the routed working set exceeds the slots, so the layer runs >= 4 capacity-bounded waves and
+one final combine). One step = one full layer call.
+
+* ``value``: layer tokens/s with hidden states, router logits and the layer's experts already
+  in HBM (an HBM-resident expert tier: each wave's experts are read in place).
+* ``e2e``: the same layer through the public layer API from HOST buffers: pinned hidden
+  states and logits copied in, every expert staged from the pinned host store into the
+  double-buffered stage banks on the copy stream (the offload path), the output copied out.
+* ``roofline``: the grouped expert MLP (``lm_moe_mlp_prefill``: gate_up+SiLU*mul and down
+  launches of the tcgen05 kernel), algorithmic FLOPs = pairs * 6 * H * I per call, timed with
+  CUDA events on its stream inside the timed region, against the measured bf16 peak.
+* ``cpu_baseline``: the numpy oracle (a restatement of the reference path) on a bounded
+  token sample on the host cores.
+
+``--impl reference`` times that CPU implementation alone (the reference ships no native or
+GPU code for this path; its arithmetic runs in an absent Ascend stack), prints the same line
+with ``"impl": "reference"`` and exits. Under torchrun only rank 0 runs it.
+N > 1: one independent replica of the layer per GPU (weak scaling, no data-path collective);
+timing is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "moe_layer_tokens_per_s"
+UNIT = "tokens/s"
+CONFIG_NAME = "c2_prefill"
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples taken while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU arm
+def cpu_reference_step(cfg, tokens: int, w13_bits, w2_bits, hidden_bits, logits_np) -> float:
+    """One bounded oracle pass (router + grouped MLP + combine) on `tokens` tokens."""
+    from oracle import mlp as omlp
+    from oracle import router as orouter
+
+    t0 = time.perf_counter()
+    wb, _, ids = orouter.route(logits_np[:tokens], cfg.top_k, renormalize=cfg.renormalize,
+                               routed_scaling_factor=cfg.routed_scaling_factor)
+    omlp.moe_layer(hidden_bits[:tokens], ids, wb, w13_bits, w2_bits)
+    return time.perf_counter() - t0
+
+
+def cpu_inputs(cfg, tokens: int):
+    import numpy as np
+    import torch
+
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+    def b(t):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    w13, w2 = syn.make_expert_weights(cfg, 0)
+    hidden = syn.make_hidden(cfg, 0, tokens=tokens)
+    logits = syn.make_router_logits(cfg, 0, tokens=tokens)
+    # Expert weights are converted to fp32 once (parameter load), outside the timed steps.
+    return w13.float().numpy(), w2.float().numpy(), b(hidden), logits.numpy()
+
+
+def run_reference(args, cfg) -> dict:
+    """The CPU implementation of the path, timed on the host cores (bounded samples)."""
+    cores = os.cpu_count() or 1
+    sample = args.cpu_sample_tokens
+    w13, w2, hid, lg = cpu_inputs(cfg, sample)
+    for _ in range(max(0, args.warmup)):
+        cpu_reference_step(cfg, sample, w13, w2, hid, lg)
+    times = [cpu_reference_step(cfg, sample, w13, w2, hid, lg) for _ in range(args.steps)]
+    total = sum(times)
+    value = sample * len(times) / total
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) bf16 weights, Zipf-biased router)",
+        "config": {"workload": cfg.name, "tokens_per_step": sample, "full_tokens": cfg.tokens,
+                   "hidden": cfg.hidden, "experts": cfg.num_experts, "top_k": cfg.top_k,
+                   "moe_intermediate": cfg.intermediate, "num_slots": cfg.num_slots},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{sample} of {cfg.tokens} tokens per step, numpy fp32 BLAS"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+# --------------------------------------------------------------------------- GPU arm
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="profiling override of the layer's token count (default: the config's)")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+    cfg = syn.CONFIGS[CONFIG_NAME]
+    if args.tokens:
+        cfg = cfg.with_tokens(args.tokens)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, cfg)), flush=True)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from tests.helpers import ExpertLayer
+    from vllm_ascend_hust_latchmoe_b200 import _lib
+    from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
+    from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
+
+    _lib.load()
+    peaks = _peaks()
+    w13, w2 = syn.make_expert_weights(cfg, 0)
+    hidden_cpu = syn.make_hidden(cfg, seed=rank)
+    logits_cpu = syn.make_router_logits(cfg, seed=rank)
+
+    def make_layer(store_on_device: bool) -> SlotBankMoE:
+        rt = MoeOffloadRuntime(MoeOffloadConfig(
+            enabled=True, num_slots=cfg.num_slots, async_load=True, b2_wave_prefill=True,
+            graph_compatible_offload=True, pin_host_memory=True))
+        rt.register_layer_for_fixed_slots(ExpertLayer(0, w13, w2), slot_device=dev,
+                                          store_device=dev if store_on_device else None)
+        return SlotBankMoE(rt, 0, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
+                           num_experts=cfg.num_experts, top_k=cfg.top_k, max_tokens=cfg.tokens,
+                           renormalize=cfg.renormalize, device=dev)
+
+    # ----------------------------------------------------------------- value (HBM inputs)
+    layer = make_layer(True)
+    hidden = hidden_cpu.to(dev)
+    logits = logits_cpu.to(dev)
+    mlp_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+    orig = layer._grouped_mlp
+
+    def timed_mlp(*a, **kw):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        orig(*a, **kw)
+        e.record()
+        mlp_events.append((s, e))
+
+    layer._grouped_mlp = timed_mlp
+    for _ in range(args.warmup):
+        layer.forward(hidden, logits)
+    torch.cuda.synchronize()
+    layer.check_device_errors("bench warmup")
+    mlp_events.clear()
+    pairs = cfg.tokens * cfg.top_k
+    launches0 = layer.kernel_launches
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        t_start.record()
+        for _ in range(args.steps):
+            layer.forward(hidden, logits)
+        t_end.record()
+        barrier()
+    layer.check_device_errors("bench")
+    ms_total = t_start.elapsed_time(t_end)
+    launches = layer.kernel_launches - launches0
+    mlp_ms = statistics.mean(s.elapsed_time(e) for s, e in mlp_events)
+    waves = len(layer.last_waves.waves)
+
+    if dist is not None:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = world * cfg.tokens * args.steps / (ms_total / 1e3)
+
+    flops_call = pairs * cfg.flops_per_pair
+    achieved_tflops = flops_call / (mlp_ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved_tflops, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved_tflops / peaks["bf16_tflops"],
+                "frac_of_sustained": achieved_tflops / peaks["bf16_tflops_sustained"],
+                "peak_source": peaks["source"], "traffic": None,
+                "kernel": "umma_grouped_kernel x2 (gate_up+SiLU*mul, down) per lm_moe_mlp_prefill",
+                "ms_per_call": mlp_ms, "flops_per_call": flops_call}
+    prof = ROOT / "profiles" / "traffic_umma_c2.json"
+    if prof.exists():
+        roofline["traffic"] = json.loads(prof.read_text()).get("bytes_per_call")
+    del layer
+    torch.cuda.empty_cache()
+
+    # ----------------------------------------------------------------- decode layer (C1)
+    dcfg = syn.CONFIGS["c1_decode"]
+    drt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=dcfg.num_slots,
+                                             async_load=True, b2_wave_prefill=True))
+    drt.register_layer_for_fixed_slots(ExpertLayer(0, w13, w2), slot_device=dev, store_device=dev)
+    dl = SlotBankMoE(drt, 0, hidden_size=dcfg.hidden, intermediate_size=dcfg.intermediate,
+                     num_experts=dcfg.num_experts, top_k=dcfg.top_k, max_tokens=dcfg.tokens,
+                     device=dev)
+    dh = syn.make_hidden(dcfg, seed=rank).to(dev)
+    dlg = syn.make_router_logits(dcfg, seed=rank).to(dev)
+    d_events: list = []
+    d_orig = dl._grouped_mlp
+
+    def d_timed(*a, **kw):
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        d_orig(*a, **kw)
+        e0.record()
+        d_events.append((s0, e0))
+
+    dl._grouped_mlp = d_timed
+    for _ in range(args.warmup):
+        dl.forward(dh, dlg)
+    torch.cuda.synchronize()
+    d_events.clear()
+    d_steps = 50
+    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(d_steps):
+        dl.forward(dh, dlg)
+    e0.record()
+    torch.cuda.synchronize()
+    dl.check_device_errors("bench decode")
+    d_active = sum(1 for c in dl.counts_host.tolist() if c > 0)
+    d_mlp_ms = statistics.mean(a.elapsed_time(b) for a, b in d_events)
+    d_bytes = d_active * dcfg.expert_bytes
+    decode = {"workload": dcfg.name, "layer_ms": s0.elapsed_time(e0) / d_steps,
+              "mlp_ms": d_mlp_ms, "active_experts": d_active,
+              "waves": len(dl.last_waves.waves),
+              "mlp_hbm_gbs": d_bytes / (d_mlp_ms / 1e3) / 1e9,
+              "mlp_frac_hbm": d_bytes / (d_mlp_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+              "algorithmic_bytes_per_call": d_bytes,
+              "kernel": "gemv_gate_up_kernel + gemv_down_kernel (lm_moe_mlp_decode)"}
+    del dl, drt
+    torch.cuda.empty_cache()
+
+    # ----------------------------------------------------------------- e2e (host buffers)
+    off = make_layer(False)
+    h_host = hidden_cpu.pin_memory()
+    lg_host = logits_cpu.pin_memory()
+    out_host = torch.empty(cfg.tokens, cfg.hidden, dtype=torch.bfloat16, pin_memory=True)
+    h_dev = torch.empty_like(hidden)
+    lg_dev = torch.empty_like(logits)
+
+    def e2e_step():
+        h_dev.copy_(h_host, non_blocking=True)
+        lg_dev.copy_(lg_host, non_blocking=True)
+        out = off.forward(h_dev, lg_dev)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    staged0 = off.runtime.transfer_engine.stats.bytes_h2d
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e.record()
+    barrier()
+    off.check_device_errors("bench e2e")
+    e2e_ms = s.elapsed_time(e)
+    staged = (off.runtime.transfer_engine.stats.bytes_h2d - staged0) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * cfg.tokens * e2e_steps / (e2e_ms / 1e3)
+    io_in = h_host.numel() * 2 + lg_host.numel() * 4
+    e2e = {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(io_in + staged),
+           "d2h_bytes_per_step": int(out_host.numel() * 2),
+           "h2d_breakdown": {"activations_and_logits": int(io_in), "expert_staging": int(staged)},
+           "h2d_gbs": (io_in + staged) / (e2e_ms / e2e_steps / 1e3) / 1e9,
+           "pcie_gen5_x16_gbs": 64.0, "ms_per_step": e2e_ms / e2e_steps}
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        sample = args.cpu_sample_tokens
+        w13b, w2b, hid, lg = cpu_inputs(cfg, sample)
+        cpu_reference_step(cfg, sample, w13b, w2b, hid, lg)
+        tt = [cpu_reference_step(cfg, sample, w13b, w2b, hid, lg) for _ in range(2)]
+        cpu = {"value": sample * len(tt) / sum(tt), "unit": UNIT, "cores": os.cpu_count(),
+               "kind": "port", "sample": f"{sample} of {cfg.tokens} tokens, numpy fp32 BLAS"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) bf16 weights, Zipf-biased router)",
+        "config": {"workload": cfg.name, "global_batch": world * cfg.tokens, "tokens": cfg.tokens,
+                   "hidden": cfg.hidden, "experts": cfg.num_experts, "top_k": cfg.top_k,
+                   "moe_intermediate": cfg.intermediate, "num_slots": cfg.num_slots,
+                   "waves": waves, "parallelism": f"replica x{world}",
+                   "l2": "weights 1.2 GB per step > 126 MB L2 (no flush needed)"},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode,
+        "clocks": clocks.summary(), "gpu_launches": int(launches),
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -34,12 +34,18 @@ def expert_mlp(x: np.ndarray, w13: np.ndarray, w2: np.ndarray) -> np.ndarray:
     return round_bf16(act @ w2.T)
 
 
+def _as_f32(w: np.ndarray) -> np.ndarray:
+    """bf16 bit patterns (uint16) -> fp32 values; fp32 arrays (pre-converted) pass through."""
+    return bf16_bits_to_f32(w) if w.dtype == np.uint16 else w
+
+
 def pair_outputs(hidden_bits: np.ndarray, topk_ids: np.ndarray, w13_bits: np.ndarray,
                  w2_bits: np.ndarray, experts: np.ndarray | None = None) -> np.ndarray:
     """y2 for every routed pair, ``[T*k, H]`` fp32 (bf16 values), in flat pair order.
 
-    ``experts`` optionally restricts the computation to a subset (pairs of other experts
-    stay zero); the union over disjoint subsets equals the full result.
+    Weights are bf16 bit patterns or their fp32 values (converted once, like loaded
+    parameters). ``experts`` optionally restricts the computation to a subset (pairs of
+    other experts stay zero); the union over disjoint subsets equals the full result.
     """
     x_all = bf16_bits_to_f32(hidden_bits)
     T, k = topk_ids.shape
@@ -52,7 +58,7 @@ def pair_outputs(hidden_bits: np.ndarray, topk_ids: np.ndarray, w13_bits: np.nda
         if pairs.size == 0:
             continue
         x = x_all[pairs // k]
-        out[pairs] = expert_mlp(x, bf16_bits_to_f32(w13_bits[e]), bf16_bits_to_f32(w2_bits[e]))
+        out[pairs] = expert_mlp(x, _as_f32(w13_bits[e]), _as_f32(w2_bits[e]))
     return out
 
 
