@@ -88,6 +88,22 @@ int lm_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts,
 int lm_expert_histogram(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
                         int32_t* counts, int32_t* err_word, void* stream);
 
+/*
+ * K9a canonical wave plan on the device (one CTA) from the histogram `counts` [E]:
+ * active experts sorted by (-count, id), ceil(U/S) waves, each expert into the least-loaded
+ * wave with room (lowest index on ties), members ordered by id; groups numbered wave by wave.
+ * Outputs: expert_to_group [E] (-1 inactive), group_bank_row [E] (entries 0..U-1: the
+ * expert id when bank_row_mode == 0 -- experts read in place from an [E, ...] bank -- or
+ * the position inside its wave when bank_row_mode == 1 -- positional stage-bank slots),
+ * wave_offsets [E+1] (group range of wave w = [wave_offsets[w], wave_offsets[w+1])) and
+ * num_waves [1]. E <= 1024.
+ * Replaces: moe_offload/phase_split.py:495-555 (plan_balanced_b2_waves) run on the host
+ * after the D2H of every top-k id (patches/patch_fused_moe.py:2518-2546).
+ */
+int lm_plan_waves(const int32_t* counts, int32_t num_experts, int32_t num_slots,
+                  int32_t bank_row_mode, int32_t* expert_to_group, int32_t* group_bank_row,
+                  int32_t* wave_offsets, int32_t* num_waves, void* stream);
+
 /* Scratch (int32 elements) lm_build_groups needs for `num_pairs` pairs and `num_groups`. */
 int64_t lm_build_groups_scratch_elems(int64_t num_pairs, int32_t num_groups);
 

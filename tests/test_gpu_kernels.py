@@ -186,3 +186,35 @@ def test_stage_copy_coalesces_runs(cuda):
     torch.cuda.synchronize()
     assert n == 3  # one run of 3 + two singles
     assert torch.equal(dst[[0, 1, 2, 4, 5]].cpu(), src[[3, 4, 5, 9, 0]])
+
+
+def test_device_wave_planner_matches_reference_golden(cuda):
+    """lm_plan_waves reproduces the reference's canonical wave plans bit for bit."""
+    import json
+    from pathlib import Path
+
+    cases = json.loads((Path(__file__).parent / "golden" / "waves.json").read_text())
+    for case in cases:
+        counts_d = {int(k): int(v) for k, v in case["counts"].items()}
+        E = max(counts_d) + 1
+        counts = torch.zeros(E, dtype=torch.int32)
+        for e, c in counts_d.items():
+            counts[e] = c
+        e2g = torch.empty(E, dtype=torch.int32, device=cuda)
+        rows = torch.empty(E, dtype=torch.int32, device=cuda)
+        woff = torch.empty(E + 1, dtype=torch.int32, device=cuda)
+        nw = torch.empty(1, dtype=torch.int32, device=cuda)
+        _lib.plan_waves(counts.to(cuda), case["num_slots"], e2g, rows, woff, nw, in_place_rows=True)
+        n = int(nw.item())
+        off = woff[: n + 1].tolist()
+        r = rows.tolist()
+        got = [r[off[w]:off[w + 1]] for w in range(n)]
+        assert got == case["waves"], case["num_slots"]
+        # expert_to_group numbers groups wave by wave, members by id
+        g = e2g.tolist()
+        flat = [e for w in case["waves"] for e in w]
+        assert [g[e] for e in flat] == list(range(len(flat)))
+        # positional rows (stage-bank mode)
+        _lib.plan_waves(counts.to(cuda), case["num_slots"], e2g, rows, woff, nw, in_place_rows=False)
+        r = rows.tolist()
+        assert [r[off[w]:off[w + 1]] for w in range(n)] == [list(range(len(w))) for w in case["waves"]]

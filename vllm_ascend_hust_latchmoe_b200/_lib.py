@@ -43,6 +43,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _P, _P, _P, _P],
     ),
     "lm_expert_histogram": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _P]),
+    "lm_plan_waves": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P]),
     "lm_build_groups_scratch_elems": (ctypes.c_int64, [_I64, _I32]),
     "lm_build_groups": (
         ctypes.c_int,
@@ -156,6 +157,19 @@ def expert_histogram(ids: torch.Tensor, num_experts: int, counts: torch.Tensor,
         "lm_expert_histogram",
         lib().lm_expert_histogram(_ptr(ids), ids.numel(), int(num_experts), _ptr(counts),
                                   _ptr(err_word), _stream()),
+    )
+
+
+def plan_waves(counts: torch.Tensor, num_slots: int, expert_to_group: torch.Tensor,
+               group_bank_row: torch.Tensor, wave_offsets: torch.Tensor,
+               num_waves: torch.Tensor, *, in_place_rows: bool = True) -> None:
+    _require_cuda(counts, expert_to_group, group_bank_row, wave_offsets, num_waves)
+    _check(
+        "lm_plan_waves",
+        lib().lm_plan_waves(_ptr(counts), counts.numel(), int(num_slots),
+                            0 if in_place_rows else 1, _ptr(expert_to_group),
+                            _ptr(group_bank_row), _ptr(wave_offsets), _ptr(num_waves),
+                            _stream()),
     )
 
 

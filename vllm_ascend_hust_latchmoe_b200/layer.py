@@ -119,6 +119,9 @@ class SlotBankMoE:
         self.act = torch.zeros(P, self.I, dtype=torch.bfloat16, device=d)
         self.y_perm = torch.zeros(P, self.H, dtype=torch.bfloat16, device=d)
         self.out = torch.zeros(self.max_tokens, self.H, dtype=torch.bfloat16, device=d)
+        self.wave_offsets = torch.zeros(self.E + 1, dtype=i32, device=d)
+        self.num_waves = torch.zeros(1, dtype=i32, device=d)
+        self.resident_tier = runtime.host_layer(self.layer_id).on_device
         self.last_waves = WaveReport()
         self.kernel_launches = 0
 
@@ -155,6 +158,10 @@ class SlotBankMoE:
             return StageDecision("capturing")
         if rt.is_static_residency_regime(self.E):
             return StageDecision("static")
+        if self.resident_tier:
+            # Every expert already has an HBM copy: nothing to stage, and the wave plan is
+            # made on the device inside the MLP piece (no host round trip).
+            return StageDecision("resident")
         if not rt.should_use_fixed_slot_plan_for_layer(self.layer_id):
             return StageDecision("passthrough")
         counts = self.active_counts(topk_ids)
@@ -184,6 +191,34 @@ class SlotBankMoE:
         _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], self.out[:T])
         self.kernel_launches += 4
         return self.out[:T]
+
+    def mlp_resident(self, hidden: torch.Tensor, T: int) -> torch.Tensor:
+        """MLP piece for an HBM-resident expert tier: histogram -> device wave plan ->
+        grouping (rows wave by wave) -> grouped MLP reading each expert in place -> one
+        combine. No host synchronisation; fixed buffers only, so it can be captured."""
+        store = self.runtime.host_layer(self.layer_id)
+        ids = self.topk_ids[:T]
+        _lib.expert_histogram(ids, self.E, self.counts, self.err)
+        _lib.plan_waves(self.counts, self.runtime.config.num_slots, self.expert_to_group,
+                        self.group_bank_row, self.wave_offsets, self.num_waves,
+                        in_place_rows=True)
+        _lib.build_groups(ids, self.E_total, self.expert_to_group, self.E, self.group_offsets,
+                          self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+        launches = 3
+        if T > DECODE_MAX_TOKENS:
+            _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
+            launches += 1
+        self._grouped_mlp(hidden, T, self.group_bank_row, 0, self.E, store.w13, store.w2)
+        _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], self.out[:T])
+        self.kernel_launches += launches + 3
+        return self.out[:T]
+
+    def resident_wave_plan(self) -> tuple[tuple[int, ...], ...]:
+        """Read back the last device wave plan (synchronises; diagnostics and tests)."""
+        nw = int(self.num_waves.item())
+        off = self.wave_offsets[: nw + 1].tolist()
+        rows = self.group_bank_row.tolist()
+        return tuple(tuple(rows[off[w]:off[w + 1]]) for w in range(nw))
 
     def _grouped_mlp(self, hidden, T, bank_rows_dev, g0, g1, w13_bank, w2_bank) -> None:
         if T <= DECODE_MAX_TOKENS:
@@ -274,6 +309,8 @@ class SlotBankMoE:
         decision = self.stage(ids, phase)
         if decision.mode == "waves":
             return self.forward_waves(hidden, T, decision.counts)
+        if decision.mode == "resident":
+            return self.mlp_resident(hidden, T)
         if decision.mode not in ("slots", "static"):
             raise RuntimeError(f"layer {self.layer_id} is not offloaded under fixed slots")
         rt = self.runtime
