@@ -126,6 +126,29 @@ int lm_build_groups(const int32_t* topk_ids, int64_t num_pairs, int32_t num_expe
                     void* stream);
 
 /*
+ * lm_build_groups without caller-owned scratch, for callers that cannot allocate device
+ * memory themselves: a host that has already handed all free HBM to its own pool (a
+ * serving engine sizing its KV cache to fill the card), or a foreign-language binding
+ * that has no device allocator. Same inputs, outputs and results as lm_build_groups; the
+ * scratch lives in one static device array of LM_NOALLOC_GROUP_SCRATCH_ELEMS int32 (512 KiB)
+ * that every GPU loading this library keeps until the process exits. Calls needing more
+ * (lm_build_groups_scratch_elems(num_pairs, num_groups) > the limit, e.g. more than
+ * 262144 pairs at 128 groups) return LM_ERR_INVALID_ARGUMENT. The first call on a device
+ * looks up the array's device address with that device current; make that first call
+ * before any stream capture. All calls on a device share its array and the array keeps
+ * the last call's contents, so calls that overlap on the GPU (for example on two streams
+ * of one device) race and must be ordered by the caller. The passes write every scratch
+ * entry they later read, so nothing needs clearing between calls. No cudaMalloc, cudaFree
+ * or allocating library routine is used.
+ * Has no counterpart in the reference (its grouping runs inside the Ascend stack).
+ */
+#define LM_NOALLOC_GROUP_SCRATCH_ELEMS 131072
+int lm_build_groups_noalloc(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
+                            const int32_t* expert_to_group, int32_t num_groups,
+                            int32_t* group_offsets, int32_t* pair_to_row, int32_t* row_to_pair,
+                            int32_t* err_word, void* stream);
+
+/*
  * Row gather: x_perm[r, :] = hidden[row_to_pair[r] / top_k, :] for r < num_rows.
  * hidden [T, H] bf16, x_perm [num_rows, H] bf16; H % 8 == 0.
  * Replaces: the token-permute half of npu_moe_init_routing_v2

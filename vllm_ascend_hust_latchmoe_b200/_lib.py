@@ -49,6 +49,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _I32, _P, _I32, _P, _P, _P, _P, _I64, _P, _P],
     ),
+    "lm_build_groups_noalloc": (
+        ctypes.c_int,
+        [_P, _I64, _I32, _P, _I32, _P, _P, _P, _P, _P],
+    ),
     "lm_permute_rows": (ctypes.c_int, [_P, _I32, _P, _I32, _I64, _P, _P]),
     "lm_moe_mlp_decode": (
         ctypes.c_int,
@@ -188,6 +192,22 @@ def build_groups(ids: torch.Tensor, num_experts: int, expert_to_group: torch.Ten
             _ptr(ids), ids.numel(), int(num_experts), _ptr(expert_to_group), int(num_groups),
             _ptr(group_offsets), _ptr(pair_to_row), _ptr(row_to_pair), _ptr(scratch),
             scratch.numel(), _ptr(err_word), _stream(),
+        ),
+    )
+
+
+def build_groups_noalloc(ids: torch.Tensor, num_experts: int, expert_to_group: torch.Tensor,
+                         num_groups: int, group_offsets: torch.Tensor, pair_to_row: torch.Tensor,
+                         row_to_pair: torch.Tensor, err_word: torch.Tensor | None = None) -> None:
+    """lm_build_groups with the library's built-in static scratch (no device allocation by
+    the caller or the library); see include/latchmoe_b200.h for its size limit."""
+    _require_cuda(ids, expert_to_group, group_offsets, pair_to_row, row_to_pair)
+    _check(
+        "lm_build_groups_noalloc",
+        lib().lm_build_groups_noalloc(
+            _ptr(ids), ids.numel(), int(num_experts), _ptr(expert_to_group), int(num_groups),
+            _ptr(group_offsets), _ptr(pair_to_row), _ptr(row_to_pair), _ptr(err_word),
+            _stream(),
         ),
     )
 

@@ -6,6 +6,8 @@
 // All kernels are deterministic: atomics only add integers.
 #include <cfloat>
 #include <cmath>
+#include <mutex>
+#include <string>
 
 #include "lm_common.cuh"
 
@@ -460,22 +462,14 @@ extern "C" int64_t lm_build_groups_scratch_elems(int64_t num_pairs, int32_t num_
   return 2 * (tiles > 0 ? tiles : 1) * static_cast<int64_t>(num_groups);
 }
 
-extern "C" int lm_build_groups(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
-                               const int32_t* expert_to_group, int32_t num_groups,
-                               int32_t* group_offsets, int32_t* pair_to_row,
-                               int32_t* row_to_pair, int32_t* scratch, int64_t scratch_elems,
-                               int32_t* err_word, void* stream) {
-  if (num_pairs < 0 || num_experts <= 0 || num_groups <= 0 || num_groups > kMaxGroups)
-    return fail(LM_ERR_INVALID_ARGUMENT,
-                "lm_build_groups: need num_pairs >= 0 and 0 < num_groups <= 1024");
-  if (group_offsets == nullptr || expert_to_group == nullptr ||
-      (num_pairs > 0 && (topk_ids == nullptr || pair_to_row == nullptr || row_to_pair == nullptr)))
-    return fail(LM_ERR_INVALID_ARGUMENT, "lm_build_groups: null pointer");
-  const int64_t need = lm_build_groups_scratch_elems(num_pairs, num_groups);
-  if (scratch == nullptr || scratch_elems < need)
-    return fail(LM_ERR_INVALID_ARGUMENT,
-                "lm_build_groups: scratch too small (need " + std::to_string(need) + " int32)");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+namespace {
+
+// Grouping passes on caller-chosen scratch (2 * tiles * num_groups int32, fully written by
+// the passes themselves, so it needs no clearing between calls).
+int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
+                      const int32_t* expert_to_group, int32_t num_groups,
+                      int32_t* group_offsets, int32_t* pair_to_row, int32_t* row_to_pair,
+                      int32_t* scratch, int32_t* err_word, cudaStream_t s) {
   const int64_t tiles64 = (num_pairs + kGroupTile - 1) / kGroupTile;
   const int tiles = static_cast<int>(tiles64 > 0 ? tiles64 : 1);
   int32_t* tile_counts = scratch;
@@ -505,6 +499,87 @@ extern "C" int lm_build_groups(const int32_t* topk_ids, int64_t num_pairs, int32
                                                        expert_to_group, num_groups, tile_base,
                                                        group_offsets, pair_to_row, row_to_pair);
   return launch_status("lm_build_groups: scatter");
+}
+
+int check_group_args(const char* who, const int32_t* topk_ids, int64_t num_pairs,
+                     int32_t num_experts, const int32_t* expert_to_group, int32_t num_groups,
+                     const int32_t* group_offsets, const int32_t* pair_to_row,
+                     const int32_t* row_to_pair) {
+  if (num_pairs < 0 || num_experts <= 0 || num_groups <= 0 || num_groups > kMaxGroups)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                std::string(who) + ": need num_pairs >= 0 and 0 < num_groups <= 1024");
+  if (group_offsets == nullptr || expert_to_group == nullptr ||
+      (num_pairs > 0 && (topk_ids == nullptr || pair_to_row == nullptr || row_to_pair == nullptr)))
+    return fail(LM_ERR_INVALID_ARGUMENT, std::string(who) + ": null pointer");
+  return LM_OK;
+}
+
+// Scratch of lm_build_groups_noalloc: one array per device that loads this library, kept
+// until the process exits. Calls share it, so calls that overlap on the GPU race.
+static __device__ __align__(256) int32_t g_group_scratch[LM_NOALLOC_GROUP_SCRATCH_ELEMS];
+
+// Device address of g_group_scratch for the current device, resolved once per device with
+// that device current (host code only sees a host-side shadow under the symbol's name).
+int noalloc_scratch(int32_t** out) {
+  static std::mutex mu;
+  static int32_t* ptrs[64] = {nullptr};
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "lm_build_groups_noalloc: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return fail(LM_ERR_UNSUPPORTED, "lm_build_groups_noalloc: device index >= 64");
+  std::lock_guard<std::mutex> lk(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(&p, g_group_scratch),
+                    "lm_build_groups_noalloc: cudaGetSymbolAddress");
+    if (rc) return rc;
+    ptrs[dev] = static_cast<int32_t*>(p);
+  }
+  *out = ptrs[dev];
+  return LM_OK;
+}
+
+}  // namespace
+
+extern "C" int lm_build_groups(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
+                               const int32_t* expert_to_group, int32_t num_groups,
+                               int32_t* group_offsets, int32_t* pair_to_row,
+                               int32_t* row_to_pair, int32_t* scratch, int64_t scratch_elems,
+                               int32_t* err_word, void* stream) {
+  int rc = check_group_args("lm_build_groups", topk_ids, num_pairs, num_experts,
+                            expert_to_group, num_groups, group_offsets, pair_to_row, row_to_pair);
+  if (rc) return rc;
+  const int64_t need = lm_build_groups_scratch_elems(num_pairs, num_groups);
+  if (scratch == nullptr || scratch_elems < need)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_build_groups: scratch too small (need " + std::to_string(need) + " int32)");
+  return build_groups_impl(topk_ids, num_pairs, num_experts, expert_to_group, num_groups,
+                           group_offsets, pair_to_row, row_to_pair, scratch, err_word,
+                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lm_build_groups_noalloc(const int32_t* topk_ids, int64_t num_pairs,
+                                       int32_t num_experts, const int32_t* expert_to_group,
+                                       int32_t num_groups, int32_t* group_offsets,
+                                       int32_t* pair_to_row, int32_t* row_to_pair,
+                                       int32_t* err_word, void* stream) {
+  int rc = check_group_args("lm_build_groups_noalloc", topk_ids, num_pairs, num_experts,
+                            expert_to_group, num_groups, group_offsets, pair_to_row, row_to_pair);
+  if (rc) return rc;
+  const int64_t need = lm_build_groups_scratch_elems(num_pairs, num_groups);
+  if (need > LM_NOALLOC_GROUP_SCRATCH_ELEMS)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_build_groups_noalloc: num_pairs=" + std::to_string(num_pairs) +
+                    " with num_groups=" + std::to_string(num_groups) + " needs " +
+                    std::to_string(need) + " int32 of scratch; the built-in array holds " +
+                    std::to_string(LM_NOALLOC_GROUP_SCRATCH_ELEMS) +
+                    " (use lm_build_groups with caller-owned scratch)");
+  int32_t* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return build_groups_impl(topk_ids, num_pairs, num_experts, expert_to_group, num_groups,
+                           group_offsets, pair_to_row, row_to_pair, scratch, err_word,
+                           static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int lm_permute_rows(const uint16_t* hidden, int32_t hidden_size,
