@@ -55,56 +55,75 @@ def _peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples taken while the timed region runs."""
+    """SM clock and throttle reasons sampled through NVML every few ms while the timed
+    region runs (a background thread; the timed region is often only tens of ms long)."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
-    def __init__(self, index: int) -> None:
-        self.index = index
-        self.proc = None
+    def __init__(self, cuda_index: int, period_s: float = 0.002) -> None:
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._nvml = None
+        self._handle = None
+
+    def _open(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        self._nvml = pynvml
+        try:
+            p = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+
+    def _run(self):
+        nv, h = self._nvml, self._handle
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(mhz), int(reasons)))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._open()
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
         except Exception:
-            self.proc = None
+            self._thread = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": "nvml"}
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(n for n, bit in self.REASONS.items() if seen & bit),
+                "samples": len(self.samples), "source": "nvml"}
 
 
 # --------------------------------------------------------------------------- CPU arm
@@ -264,7 +283,7 @@ def main() -> None:
     ms_total = t_start.elapsed_time(t_end)
     launches = layer.kernel_launches - launches0
     mlp_ms = statistics.mean(s.elapsed_time(e) for s, e in mlp_events)
-    waves = len(layer.last_waves.waves)
+    waves = len(layer.resident_wave_plan())
 
     if dist is not None:
         t = torch.tensor([ms_total], device=dev)
@@ -320,12 +339,13 @@ def main() -> None:
     e0.record()
     torch.cuda.synchronize()
     dl.check_device_errors("bench decode")
-    d_active = sum(1 for c in dl.counts_host.tolist() if c > 0)
+    d_plan = dl.resident_wave_plan()
+    d_active = sum(len(w) for w in d_plan)
     d_mlp_ms = statistics.mean(a.elapsed_time(b) for a, b in d_events)
     d_bytes = d_active * dcfg.expert_bytes
     decode = {"workload": dcfg.name, "layer_ms": s0.elapsed_time(e0) / d_steps,
               "mlp_ms": d_mlp_ms, "active_experts": d_active,
-              "waves": len(dl.last_waves.waves),
+              "waves": len(d_plan),
               "mlp_hbm_gbs": d_bytes / (d_mlp_ms / 1e3) / 1e9,
               "mlp_frac_hbm": d_bytes / (d_mlp_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
               "algorithmic_bytes_per_call": d_bytes,

@@ -15,6 +15,7 @@ from oracle.bf16 import bf16_bits_to_f32
 from tests.helpers import MAX_REL_ERR, MIN_COSINE, bits
 from vllm_ascend_hust_latchmoe_b200 import _lib
 from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+from vllm_ascend_hust_latchmoe_b200.weight_layout import to_tiled
 
 pytestmark = pytest.mark.gpu
 
@@ -121,13 +122,16 @@ def test_histogram(cuda):
     assert err.item() == 1
 
 
-def _mlp_case(cuda, T, k, E, H, I, G, use_prefill, seed=0):
+def _mlp_case(cuda, T, k, E, H, I, G, use_prefill, seed=0, skewed=False):
     rng = np.random.default_rng(seed)
     cfg = syn.LayerConfig("t", hidden=H, num_experts=E, top_k=k, intermediate=I, num_slots=G,
-                          tokens=T)
+                          tokens=T, zipf_s=2.0)
     w13, w2 = syn.make_expert_weights(cfg, seed=seed, experts=E)
     hidden = syn.make_hidden(cfg, seed=seed)
-    ids_np = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    if skewed:  # Zipf-biased routing: a few groups span many m-tiles, most span one
+        ids_np = orouter.route(syn.make_router_logits(cfg, seed=seed).numpy(), k)[2]
+    else:
+        ids_np = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
     wts = torch.from_numpy(rng.random((T, k)).astype(np.float32)).to(torch.bfloat16)
     active = np.unique(ids_np)
     e2g = np.full(E, -1, dtype=np.int64)
@@ -144,7 +148,7 @@ def _mlp_case(cuda, T, k, E, H, I, G, use_prefill, seed=0):
     _lib.build_groups(d_ids, E, torch.from_numpy(e2g.astype(np.int32)).to(cuda), Gn, off, p2r,
                       r2p, scratch, err)
     h = hidden.to(cuda)
-    W13, W2 = w13.to(cuda), w2.to(cuda)
+    W13, W2 = to_tiled(w13).to(cuda), to_tiled(w2).to(cuda)
     act = torch.zeros(P, I, dtype=torch.bfloat16, device=cuda)
     y = torch.zeros(P, H, dtype=torch.bfloat16, device=cuda)
     if use_prefill:
@@ -177,6 +181,13 @@ def test_decode_mlp_matches_oracle(cuda, T, k, E, H, I):
                                        (129, 2, 4, 256, 128), (512, 6, 64, 2048, 1408)])
 def test_prefill_tcgen05_mlp_matches_oracle(cuda, T, k, E, H, I):
     _mlp_case(cuda, T, k, E, H, I, 32, use_prefill=True)
+
+
+@pytest.mark.parametrize("T,k,E", [(2048, 4, 32), (1500, 8, 128), (700, 2, 8)])
+def test_prefill_tcgen05_skewed_groups(cuda, T, k, E):
+    """Heavy (multi-m-tile) and light (single-m-tile) groups in one launch: exercises the
+    merged heavy/light tile order of the persistent scheduler."""
+    _mlp_case(cuda, T, k, E, 2048, 768, 32, use_prefill=True, skewed=True)
 
 
 def test_stage_copy_coalesces_runs(cuda):
@@ -218,3 +229,20 @@ def test_device_wave_planner_matches_reference_golden(cuda):
         _lib.plan_waves(counts.to(cuda), case["num_slots"], e2g, rows, woff, nw, in_place_rows=False)
         r = rows.tolist()
         assert [r[off[w]:off[w + 1]] for w in range(n)] == [list(range(len(w))) for w in case["waves"]]
+
+
+def test_prefill_two_sm_tiles_match_oracle_in_subprocess(cuda):
+    """The cta_group::2 (256-row, 2-SM) tiles, selected per process by LM_UMMA_CTA_PAIR=2,
+    pass the same tcgen05 parity cases."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, LM_UMMA_CTA_PAIR="2")
+    proc = subprocess.run(
+        [sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", "-m", "gpu",
+         str(root / "tests" / "test_gpu_kernels.py"), "-k", "prefill_tcgen05"],
+        cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]

@@ -129,3 +129,15 @@ def test_should_use_b2_pair_waves_gate():
                                        slot_device=torch.device("cpu"))
     assert rt2.should_use_b2_pair_waves(layer_id=3, active_expert_count=3)
     assert not rt2.should_use_b2_pair_waves(layer_id=3, active_expert_count=2)
+
+
+def test_tiled_layout_round_trip_and_tile_contiguity():
+    from vllm_ascend_hust_latchmoe_b200.weight_layout import from_tiled, to_tiled
+
+    w = torch.arange(2 * 256 * 128, dtype=torch.float32).reshape(2, 256, 128)
+    t = to_tiled(w)
+    assert t.shape == w.shape and torch.equal(from_tiled(t), w)
+    flat = t.reshape(2, -1)
+    # tile (n-tile 1, k-block 1) of expert 1 is one contiguous 128 x 64 block
+    tile = flat[1, (1 * 2 + 1) * 8192:(1 * 2 + 2) * 8192].reshape(128, 64)
+    assert torch.equal(tile, w[1, 128:256, 64:128])

@@ -11,6 +11,8 @@
 // gate_up: warp rows = 8 gate rows (j0..j0+7) + the 8 matching up rows, so each lane ends up
 // holding gate and up for the same (token, j) and applies SiLU(gate) * up in registers.
 // down: warp rows = 16 consecutive output columns of the hidden dimension.
+// Weights are in the tile-contiguous bank layout [N/128][K/64][128][64]: a row's 64-element
+// K chunk is 128 contiguous bytes and the 8 rows a load instruction touches share a tile.
 #include "lm_common.cuh"
 
 namespace lm {
@@ -35,8 +37,16 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Element offset of (row, 0) of a [N, K] matrix in the tile-contiguous layout.
+__device__ __forceinline__ int64_t tiled_row_base(int row, int K) {
+  return (static_cast<int64_t>(row >> 7) * (K >> 6)) * 8192 + (row & 127) * 64;
+}
+
+// Offset of the 32-element K block `kb` from a row base in the tile-contiguous layout.
+__device__ __forceinline__ int tiled_kblock(int kb) { return (kb >> 1) * 8192 + (kb & 1) * 32; }
+
 // acc[n] += W[16 rows, klen] x X[8 tokens of chunk n, klen]^T for one warp.
-// w_lo: this lane's row for fragment rows 0..7 (row = lane/4), w_hi: rows 8..15.
+// w_lo: tiled row base of this lane's fragment row 0..7 (row = lane/4), w_hi: rows 8..15.
 // xrow[n]: this lane's token row for chunk n (token = chunk*8 + lane/4), or nullptr.
 template <int NC>
 __device__ __forceinline__ void warp_tile(const uint16_t* __restrict__ w_lo,
@@ -51,8 +61,8 @@ __device__ __forceinline__ void warp_tile(const uint16_t* __restrict__ w_lo,
     uint4 wl[U], wh[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      wl[u] = ld_stream_16(w_lo + (kb + u) * 32 + c8);
-      wh[u] = ld_stream_16(w_hi + (kb + u) * 32 + c8);
+      wl[u] = ld_stream_16(w_lo + tiled_kblock(kb + u) + c8);
+      wh[u] = ld_stream_16(w_hi + tiled_kblock(kb + u) + c8);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -66,8 +76,8 @@ __device__ __forceinline__ void warp_tile(const uint16_t* __restrict__ w_lo,
     }
   }
   for (; kb < nblk; ++kb) {
-    const uint4 wl = ld_stream_16(w_lo + kb * 32 + c8);
-    const uint4 wh = ld_stream_16(w_hi + kb * 32 + c8);
+    const uint4 wl = ld_stream_16(w_lo + tiled_kblock(kb) + c8);
+    const uint4 wh = ld_stream_16(w_hi + tiled_kblock(kb) + c8);
 #pragma unroll
     for (int n = 0; n < NC; ++n) {
       uint4 x = make_uint4(0, 0, 0, 0);
@@ -109,8 +119,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   const int j0 = (blockIdx.y * kGemvWarps + warp) * 8;
   if (j0 >= I) return;
   const uint16_t* wbase = w13_bank + static_cast<int64_t>(bank) * 2 * I * H;
-  const uint16_t* w_lo = wbase + static_cast<int64_t>(j0 + gq) * H;      // gate row
-  const uint16_t* w_hi = wbase + static_cast<int64_t>(I + j0 + gq) * H;  // up row
+  const uint16_t* w_lo = wbase + tiled_row_base(j0 + gq, H);      // gate row
+  const uint16_t* w_hi = wbase + tiled_row_base(I + j0 + gq, H);  // up row
   for (int t0 = 0; t0 < n; t0 += 8 * NC) {
     const uint16_t* xrow[NC];
 #pragma unroll
@@ -151,8 +161,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   const int n0 = (blockIdx.y * kGemvWarps + warp) * 16;
   if (n0 >= H) return;
   const uint16_t* wbase = w2_bank + static_cast<int64_t>(bank) * H * I;
-  const uint16_t* w_lo = wbase + static_cast<int64_t>(n0 + gq) * I;
-  const uint16_t* w_hi = wbase + static_cast<int64_t>(n0 + 8 + gq) * I;
+  const uint16_t* w_lo = wbase + tiled_row_base(n0 + gq, I);
+  const uint16_t* w_hi = wbase + tiled_row_base(n0 + 8 + gq, I);
   for (int t0 = 0; t0 < n; t0 += 8 * NC) {
     const uint16_t* xrow[NC];
 #pragma unroll
@@ -214,9 +224,10 @@ extern "C" int lm_moe_mlp_decode(const uint16_t* hidden, int32_t top_k,
                                  int32_t intermediate_size, uint16_t* act, uint16_t* y_perm,
                                  int32_t* err_word, void* stream) {
   const int H = hidden_size, I = intermediate_size;
-  if (H <= 0 || I <= 0 || H % 32 != 0 || I % 32 != 0)
+  if (H <= 0 || I <= 0 || H % 128 != 0 || I % 64 != 0)
     return fail(LM_ERR_INVALID_ARGUMENT,
-                "lm_moe_mlp_decode: hidden and intermediate sizes must be multiples of 32");
+                "lm_moe_mlp_decode: need hidden_size % 128 == 0 and intermediate_size % 64 == 0 "
+                "(tile-contiguous weight layout)");
   if (top_k <= 0 || group_begin < 0 || group_end < group_begin || bank_rows <= 0)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_moe_mlp_decode: bad group range or top_k");
   if (group_end == group_begin) return LM_OK;

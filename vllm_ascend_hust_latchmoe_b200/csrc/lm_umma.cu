@@ -10,13 +10,18 @@
 // tcgen05.mma into one of two TMEM accumulators (2 x 256 fp32 columns = all 512 columns),
 // warps 2-5 drain the other accumulator (tcgen05.ld -> epilogue -> global stores), so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
-// Tiles are enumerated (group, m-tile, n-tile) with n fastest, so CTAs running at the same
-// time share the A rows and the expert's weight tiles in L2. The tile list is derived on
-// the device from group_offsets, so the launch itself is independent of the routing.
+// Tile order: groups with several m-tiles ("heavy": their weight tiles are reused from L2,
+// so their tiles are tensor-bound) and single-m-tile groups ("light": every weight tile is
+// read from DRAM once, so their tiles are HBM-bound) form two lists, each enumerated
+// (group, m-tile, n-tile) with n fastest, and the two lists are merged in proportion. CTAs
+// running at the same time then mix both kinds, overlapping weight streaming with MMAs.
+// The tile lists are derived on the device from group_offsets, so the launch itself is
+// independent of the routing.
 // No TMA load uses cluster multicast; every operand is this GPU's own memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -25,35 +30,47 @@
 namespace lm {
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 64;
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int BM = 128;   // rows per CTA (TMEM lanes)
+constexpr int BN = 256;   // MMA N (mode 0: 128 gate + 128 up rows; mode 1: 256 outputs)
+constexpr int BK = 64;    // one 128-byte swizzle row of bf16
+constexpr int A_BYTES = BM * BK * 2;      // 16 KiB
+constexpr int B_TILE_BYTES = 128 * BK * 2;  // one 128-row weight tile, 16 KiB
 constexpr int TMEM_COLS = 512;
 constexpr int MAX_G = 256;
 constexpr int NUM_THREADS = 192;
 
+// PAIR = 1: one CTA owns a 128-row tile and loads the whole 256-row B tile.
+// PAIR = 2: a cluster of two CTAs owns a 256-row tile (M = 256, cta_group::2); each CTA
+// loads its own 128 A rows and one 128-row half of B, the leader issues the MMAs.
+template <int PAIR>
+struct Cfg {
+  static constexpr int STAGE_BYTES = A_BYTES + (PAIR == 1 ? 2 : 1) * B_TILE_BYTES;
+  static constexpr int STAGES = PAIR == 1 ? 4 : 6;
+  static constexpr int UNIT_ROWS = BM * PAIR;
+};
+
 struct SmemCtl {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[6];
+  uint64_t empty[6];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint32_t tmem_base;
   int abort_flag;
-  int mprefix[MAX_G + 1];
+  int hprefix[MAX_G + 1];  // unit-tiles of heavy groups before group i
+  int lprefix[MAX_G + 1];  // light groups (exactly one unit-tile) before group i
   int row0[MAX_G];
   int nrows[MAX_G];
   int bank[MAX_G];
 };
 
-constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + static_cast<int>(sizeof(SmemCtl));
+template <int PAIR>
+constexpr int smem_bytes() {
+  return 1024 + Cfg<PAIR>::STAGES * Cfg<PAIR>::STAGE_BYTES + static_cast<int>(sizeof(SmemCtl));
+}
 
 struct UmmaParams {
   CUtensorMap tmap_a;  // A rows [R, K] bf16, box {64, 128}
-  CUtensorMap tmap_b;  // weight bank [bank_rows, N_total, K], box {64, 128|256, 1}
+  CUtensorMap tmap_b;  // weight tiles [bank_rows * N/128 * K/64][128][64], box {64, 128, 1}
   const int32_t* group_offsets;
   const int32_t* group_bank_row;
   uint16_t* out;
@@ -63,35 +80,57 @@ struct UmmaParams {
   int32_t k_blocks;
   int32_t n_tiles;
   int32_t mode;
-  int32_t inter;   // I: row offset of the up half inside W13 (mode 0)
-  int32_t out_ld;  // output row stride (elements)
+  int32_t up_tile;   // mode 0: 128-row tile index of the first up row (I / 128)
+  int32_t out_ld;    // output row stride (elements)
   int32_t bank_rows;
+  int32_t w_ntiles;  // 128-row tiles per expert matrix (N / 128)
 };
 
 struct TileCoord {
   int g;      // local group index
-  int row0;   // first A row of the tile
-  int valid;  // rows of the tile that belong to the group
+  int row0;   // first A row of the unit tile
+  int valid;  // rows of the unit tile that belong to the group
   int nt;     // n-tile index
 };
 
-__device__ __forceinline__ TileCoord decode_tile(const SmemCtl& c, int t, int n_tiles, int G) {
-  const int mg = t / n_tiles;
-  TileCoord tc;
-  tc.nt = t - mg * n_tiles;
+// Largest i in [0, G) with prefix[i] <= v (prefix is non-decreasing, prefix[G] > v).
+__device__ __forceinline__ int find_group(const int* prefix, int v, int G) {
   int lo = 0, hi = G - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (c.mprefix[mid] <= mg)
+    if (prefix[mid] <= v)
       lo = mid;
     else
       hi = mid - 1;
   }
-  tc.g = lo;
-  const int ml = mg - c.mprefix[lo];
-  tc.row0 = c.row0[lo] + ml * BM;
-  const int rem = c.nrows[lo] - ml * BM;
-  tc.valid = rem < BM ? rem : BM;
+  return lo;
+}
+
+// Position t of the merged order -> (group, unit-tile, n-tile). Heavy tiles before position
+// t: floor(t * Th / T); t is heavy iff that count grows at t + 1.
+__device__ __forceinline__ TileCoord decode_tile(const SmemCtl& c, int t, int n_tiles, int G,
+                                                 int heavy_tiles, int total_tiles, int unit) {
+  const long long th = heavy_tiles, tt = total_tiles;
+  const int hb = static_cast<int>((static_cast<long long>(t) * th) / tt);
+  const int hb1 = static_cast<int>((static_cast<long long>(t + 1) * th) / tt);
+  TileCoord tc;
+  int g, ml;
+  if (hb1 > hb) {
+    const int mg = hb / n_tiles;
+    tc.nt = hb - mg * n_tiles;
+    g = find_group(c.hprefix, mg, G);
+    ml = mg - c.hprefix[g];
+  } else {
+    const int li = t - hb;
+    const int mg = li / n_tiles;
+    tc.nt = li - mg * n_tiles;
+    g = find_group(c.lprefix, mg, G);
+    ml = 0;
+  }
+  tc.g = g;
+  tc.row0 = c.row0[g] + ml * unit;
+  const int rem = c.nrows[g] - ml * unit;
+  tc.valid = rem < unit ? rem : unit;
   return tc;
 }
 
@@ -103,24 +142,29 @@ __device__ __forceinline__ void store_row_chunk(uint16_t* dst, const uint32_t (&
   d[3] = make_uint4(packed[12], packed[13], packed[14], packed[15]);
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    umma_grouped_kernel(const __grid_constant__ UmmaParams p) {
+template <int PAIR>
+__device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
+  using C = Cfg<PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  SmemCtl& c = *reinterpret_cast<SmemCtl*>(smem + STAGES * STAGE_BYTES);
+  SmemCtl& c = *reinterpret_cast<SmemCtl*>(smem + C::STAGES * C::STAGE_BYTES);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int G = p.num_groups;
+  const uint32_t rank = PAIR == 2 ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x / PAIR;
+  const int num_clusters = gridDim.x / PAIR;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&c.full[s], 1);
       mbar_init(&c.empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&c.tfull[a], 1);
-      mbar_init(&c.tempty[a], 4);
+      mbar_init(&c.tempty[a], 4 * PAIR);
     }
     c.abort_flag = 0;
     fence_mbarrier_init();
@@ -130,8 +174,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&p.tmap_b);
   }
   if (warp == 1) {
-    tmem_alloc(&c.tmem_base, TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR == 2) {
+      tmem_alloc_pair(&c.tmem_base, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&c.tmem_base, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   for (int i = threadIdx.x; i < G; i += NUM_THREADS) {
     const int g = p.group_begin + i;
@@ -148,27 +197,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     c.bank[i] = bank;
   }
   __syncthreads();
-  if (warp == 0) {
+  if (warp < 2) {
+    // warp 0: prefix of heavy unit-tiles; warp 1: prefix of light groups.
+    int* prefix = warp == 0 ? c.hprefix : c.lprefix;
     int carry = 0;
     for (int base = 0; base < G; base += 32) {
       const int i = base + lane;
-      int v = (i < G) ? (c.nrows[i] + BM - 1) / BM : 0;
+      const int mt = (i < G) ? (c.nrows[i] + C::UNIT_ROWS - 1) / C::UNIT_ROWS : 0;
+      int v = warp == 0 ? (mt >= 2 ? mt : 0) : (mt == 1 ? 1 : 0);
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int t = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += t;
       }
-      if (i < G) c.mprefix[i + 1] = carry + v;
+      if (i < G) prefix[i + 1] = carry + v;
       carry += __shfl_sync(0xffffffffu, v, 31);
     }
-    if (lane == 0) c.mprefix[0] = 0;
+    if (lane == 0) prefix[0] = 0;
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR == 2) cluster_sync_all();  // peer barriers initialised, both TMEM halves allocated
   tc_fence_after();
 
   const uint32_t tmem_base = c.tmem_base;
-  const int total_tiles = c.mprefix[G] * p.n_tiles;
+  const int heavy_tiles = c.hprefix[G] * p.n_tiles;
+  const int total_tiles = heavy_tiles + c.lprefix[G] * p.n_tiles;
   volatile int* abort_flag = &c.abort_flag;
 
   if (warp == 0) {
@@ -176,56 +230,66 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // ------------------------------------------------------------ TMA producer
       int stage = 0;
       uint32_t phase = 0;
-      int issued_parity[STAGES];
-      for (int s = 0; s < STAGES; ++s) issued_parity[s] = -1;
+      int issued_parity[6];
+      for (int s = 0; s < 6; ++s) issued_parity[s] = -1;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = decode_tile(c, t, p.n_tiles, G);
-        const int bank = c.bank[tc.g];
+      for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+        const TileCoord tc = decode_tile(c, t, p.n_tiles, G, heavy_tiles, total_tiles,
+                                         C::UNIT_ROWS);
+        // Tile index of (expert row, 128-row tile, k block) in the tile-contiguous bank.
+        const int ebase = c.bank[tc.g] * p.w_ntiles;
+        const int nt0 = p.mode == 0 ? tc.nt : 2 * tc.nt;
+        const int nt1 = p.mode == 0 ? p.up_tile + tc.nt : 2 * tc.nt + 1;
+        const int a_row = tc.row0 + static_cast<int>(rank) * BM;
+        const int my_nt = rank == 0 ? nt0 : nt1;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait_bounded(&c.empty[stage], phase ^ 1u, p.err_word, abort_flag)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + A_BYTES;
-          mbar_arrive_expect_tx(&c.full[stage], STAGE_BYTES);
-          tma_load_2d(sa, &p.tmap_a, &c.full[stage], kb * BK, tc.row0);
-          if (p.mode == 0) {
-            tma_load_3d(sb, &p.tmap_b, &c.full[stage], kb * BK, tc.nt * 128, bank);
-            tma_load_3d(sb + B_BYTES / 2, &p.tmap_b, &c.full[stage], kb * BK,
-                        p.inter + tc.nt * 128, bank);
+          if (PAIR == 1) {
+            mbar_arrive_expect_tx(&c.full[stage], C::STAGE_BYTES);
+            tma_load_2d(sa, &p.tmap_a, &c.full[stage], kb * BK, a_row);
+            tma_load_3d(sb, &p.tmap_b, &c.full[stage], 0, 0, (ebase + nt0) * p.k_blocks + kb);
+            tma_load_3d(sb + B_TILE_BYTES, &p.tmap_b, &c.full[stage], 0, 0,
+                        (ebase + nt1) * p.k_blocks + kb);
           } else {
-            tma_load_3d(sb, &p.tmap_b, &c.full[stage], kb * BK, tc.nt * BN, bank);
+            // Both CTAs' bytes complete on the leader's barrier; only the leader arrives.
+            const uint32_t full_leader = mapa_shared(smem_u32(&c.full[stage]), 0);
+            if (leader) mbar_arrive_expect_tx(&c.full[stage], 2 * C::STAGE_BYTES);
+            tma_load_2d_pair(sa, &p.tmap_a, full_leader, kb * BK, a_row);
+            tma_load_3d_pair(sb, &p.tmap_b, full_leader, 0, 0, (ebase + my_nt) * p.k_blocks + kb);
           }
           issued_parity[stage] = static_cast<int>(phase);
-          if (++stage == STAGES) {
+          if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      if (!ok) {
-        // Let copies already in flight land before the CTA can exit.
-        for (int s = 0; s < STAGES; ++s) {
-          if (issued_parity[s] < 0) continue;
-          const long long t0 = clock64();
-          while (!mbar_try_wait(&c.full[s], static_cast<uint32_t>(issued_parity[s])) &&
-                 clock64() - t0 < LM_SPIN_LIMIT_CYCLES) {
-          }
+      // Wait until the MMAs released every stage this CTA filled, so no TMA write or
+      // commit arrival into this CTA's shared memory is still in flight at exit.
+      for (int s = 0; s < C::STAGES; ++s) {
+        if (issued_parity[s] < 0) continue;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&c.empty[s], static_cast<uint32_t>(issued_parity[s])) &&
+               clock64() - t0 < LM_SPIN_LIMIT_CYCLES) {
+          if (*abort_flag && clock64() - t0 > 200000) break;
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       // ------------------------------------------------------------ MMA issuer
-      const uint32_t idesc = idesc_bf16_f32(BM, BN);
+      const uint32_t idesc = idesc_bf16_f32(BM * PAIR, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
         if (!mbar_wait_bounded(&c.tempty[acc], acc_phase ^ 1u, p.err_word, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -235,21 +299,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            umma_bf16(d_tmem, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32),
-                      idesc, (kb | kk) != 0 ? 1u : 0u);
+            const uint64_t ad = sdesc_k_sw128(a_addr + kk * 32);
+            const uint64_t bd = sdesc_k_sw128(b_addr + kk * 32);
+            const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
+            if (PAIR == 2)
+              umma_bf16_pair(d_tmem, ad, bd, idesc, accum);
+            else
+              umma_bf16(d_tmem, ad, bd, idesc, accum);
           }
-          umma_commit(&c.empty[stage]);
-          if (++stage == STAGES) {
+          if (PAIR == 2)
+            umma_commit_pair(&c.empty[stage], 0x3);
+          else
+            umma_commit(&c.empty[stage]);
+          if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&c.tfull[acc]);
+        if (PAIR == 2)
+          umma_commit_pair(&c.tfull[acc], 0x3);
+        else
+          umma_commit(&c.tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
@@ -258,14 +333,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // -------------------------------------------------------------- epilogue warps 2..5
     const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32) are visible to this warp
     const int r = quad * 32 + lane;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&c.tempty[0]), 0);
+    const uint32_t tempty_leader1 = mapa_shared(smem_u32(&c.tempty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileCoord tc = decode_tile(c, t, p.n_tiles, G);
+    for (int t = cluster_id; t < total_tiles; t += num_clusters) {
+      const TileCoord tc = decode_tile(c, t, p.n_tiles, G, heavy_tiles, total_tiles,
+                                       C::UNIT_ROWS);
       if (!mbar_wait_bounded(&c.tfull[acc], acc_phase, p.err_word, abort_flag)) break;
       tc_fence_after();
-      const bool valid = r < tc.valid;
-      uint16_t* out_row = p.out + static_cast<int64_t>(tc.row0 + r) * p.out_ld;
+      const int my_valid = tc.valid - static_cast<int>(rank) * BM;
+      const bool valid = r < my_valid;
+      uint16_t* out_row =
+          p.out + static_cast<int64_t>(tc.row0 + static_cast<int>(rank) * BM + r) * p.out_ld;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       if (p.mode == 0) {
@@ -300,7 +380,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&c.tempty[acc]);
+      if (lane == 0) {
+        if (PAIR == 2)
+          mbar_arrive_remote(acc == 0 ? tempty_leader0 : tempty_leader1);
+        else
+          mbar_arrive(&c.tempty[acc]);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -308,10 +393,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR == 2) cluster_sync_all();  // both CTAs done with TMEM and with remote barriers
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR == 2)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    umma_grouped_kernel(const __grid_constant__ UmmaParams p) {
+  umma_grouped_body<1>(p);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    umma_grouped_kernel_2sm(const __grid_constant__ UmmaParams p) {
+  umma_grouped_body<2>(p);
 }
 
 // ----------------------------------------------------------------------------- host side
@@ -332,11 +431,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 struct MapKey {
   const void* ptr;
   uint64_t d[3];
-  uint32_t box1;
   int rank;
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && d[0] == o.d[0] && d[1] == o.d[1] && d[2] == o.d[2] &&
-           box1 == o.box1 && rank == o.rank;
+    return ptr == o.ptr && d[0] == o.d[0] && d[1] == o.d[1] && d[2] == o.d[2] && rank == o.rank;
   }
 };
 
@@ -350,10 +447,11 @@ MapCache& map_cache() {
   return c;
 }
 
-// rank 2: dims {K, rows}; rank 3: dims {K, N, bank_rows}. Box {64, box1(, 1)}, 128B swizzle.
-int make_map(CUtensorMap* out, const void* ptr, int rank, uint64_t d0, uint64_t d1, uint64_t d2,
-             uint32_t box1) {
-  const MapKey key{ptr, {d0, d1, d2}, box1, rank};
+// rank 2: activation rows, dims {K, rows}, box {64, 128}.
+// rank 3: weight tiles, dims {64, 128, n_tiles} with strides {128 B, 16 KiB}, box {64, 128, 1}.
+// Both with 128-byte swizzle (the K-major SW128 layout the UMMA descriptors expect).
+int make_map(CUtensorMap* out, const void* ptr, int rank, uint64_t d0, uint64_t d1) {
+  const MapKey key{ptr, {d0, d1, 0}, rank};
   MapCache& cache = map_cache();
   {
     std::lock_guard<std::mutex> lk(cache.mu);
@@ -365,9 +463,20 @@ int make_map(CUtensorMap* out, const void* ptr, int rank, uint64_t d0, uint64_t 
   }
   auto fn = encode_fn();
   if (fn == nullptr) return fail(LM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[3] = {d0, d1, d2};
-  cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(BK), box1, 1};
+  cuuint64_t dims[3];
+  cuuint64_t strides[2];
+  if (rank == 2) {
+    dims[0] = d0;
+    dims[1] = d1;
+    strides[0] = d0 * 2;
+  } else {
+    dims[0] = BK;
+    dims[1] = 128;
+    dims[2] = d0;  // number of 128 x 64 tiles
+    strides[0] = BK * 2;
+    strides[1] = BK * 128 * 2;
+  }
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(BK), 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUtensorMap m;
   const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
@@ -403,10 +512,36 @@ int ensure_smem_attr() {
   if (dev >= 0 && dev < 64 && done[dev]) return LM_OK;
   int rc = check_cuda(cudaFuncSetAttribute(umma_grouped_kernel,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           SMEM_BYTES),
+                                           smem_bytes<1>()),
                       "lm_moe_mlp_prefill: smem attribute");
+  if (rc) return rc;
+  rc = check_cuda(cudaFuncSetAttribute(umma_grouped_kernel_2sm,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       smem_bytes<2>()),
+                  "lm_moe_mlp_prefill: smem attribute (2-SM)");
   if (rc == LM_OK && dev >= 0 && dev < 64) done[dev] = 1;
   return rc;
+}
+
+// Single-CTA tiles by default: on Zipf-skewed expert loads most groups fit one 128-row
+// tile, and a 256-row 2-SM tile would leave the second CTA's half empty for them (measured
+// 409 us vs 453 us on the 4096-token Qwen3-30B-A3B layer). LM_UMMA_CTA_PAIR=2 selects the
+// cta_group::2 tiles, which win on dense groups (1233 vs 1155 TFLOP/s on one 32768-row group).
+int cta_pair() {
+  static int v = [] {
+    const char* e = getenv("LM_UMMA_CTA_PAIR");
+    return (e != nullptr && e[0] == '2') ? 2 : 1;
+  }();
+  return v;
+}
+
+int launch_umma(const UmmaParams& p, int grid, cudaStream_t s, const char* what) {
+  if (cta_pair() == 2) {
+    umma_grouped_kernel_2sm<<<grid & ~1, NUM_THREADS, smem_bytes<2>(), s>>>(p);
+  } else {
+    umma_grouped_kernel<<<grid, NUM_THREADS, smem_bytes<1>(), s>>>(p);
+  }
+  return launch_status(what);
 }
 
 }  // namespace
@@ -444,9 +579,9 @@ extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
   const int grid = sm_count();
 
   UmmaParams p1{};
-  rc = make_map(&p1.tmap_a, x_perm, 2, H, total_rows, 1, BM);
+  rc = make_map(&p1.tmap_a, x_perm, 2, H, total_rows);
   if (rc) return rc;
-  rc = make_map(&p1.tmap_b, w13_bank, 3, H, 2 * static_cast<uint64_t>(I), bank_rows, 128);
+  rc = make_map(&p1.tmap_b, w13_bank, 3, static_cast<uint64_t>(bank_rows) * (2 * I / 128) * (H / BK), 0);
   if (rc) return rc;
   p1.group_offsets = group_offsets;
   p1.group_bank_row = group_bank_row;
@@ -457,23 +592,23 @@ extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
   p1.k_blocks = H / BK;
   p1.n_tiles = I / 128;
   p1.mode = 0;
-  p1.inter = I;
+  p1.up_tile = I / 128;
   p1.out_ld = I;
   p1.bank_rows = static_cast<int32_t>(bank_rows);
-  umma_grouped_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(p1);
-  rc = launch_status("lm_moe_mlp_prefill: gate_up");
+  p1.w_ntiles = 2 * I / 128;
+  rc = launch_umma(p1, grid, s, "lm_moe_mlp_prefill: gate_up");
   if (rc) return rc;
 
   UmmaParams p2 = p1;
-  rc = make_map(&p2.tmap_a, act, 2, I, total_rows, 1, BM);
+  rc = make_map(&p2.tmap_a, act, 2, I, total_rows);
   if (rc) return rc;
-  rc = make_map(&p2.tmap_b, w2_bank, 3, I, H, bank_rows, BN);
+  rc = make_map(&p2.tmap_b, w2_bank, 3, static_cast<uint64_t>(bank_rows) * (H / 128) * (I / BK), 0);
   if (rc) return rc;
   p2.out = y_perm;
   p2.k_blocks = I / BK;
   p2.n_tiles = H / BN;
   p2.mode = 1;
   p2.out_ld = H;
-  umma_grouped_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(p2);
-  return launch_status("lm_moe_mlp_prefill: down");
+  p2.w_ntiles = H / 128;
+  return launch_umma(p2, grid, s, "lm_moe_mlp_prefill: down");
 }

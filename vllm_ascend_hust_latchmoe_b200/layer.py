@@ -189,7 +189,7 @@ class SlotBankMoE:
                           self.row_to_pair, self.scratch, self.err)
         self._grouped_mlp(hidden, T, self.slot_rows, 0, G, bank.w13_slots, bank.w2_slots)
         _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], self.out[:T])
-        self.kernel_launches += 4
+        self.kernel_launches += 6  # grouping (3), gate_up, down, combine
         return self.out[:T]
 
     def mlp_resident(self, hidden: torch.Tensor, T: int) -> torch.Tensor:
@@ -204,7 +204,7 @@ class SlotBankMoE:
                         in_place_rows=True)
         _lib.build_groups(ids, self.E_total, self.expert_to_group, self.E, self.group_offsets,
                           self.pair_to_row, self.row_to_pair, self.scratch, self.err)
-        launches = 3
+        launches = 5  # histogram, plan, grouping (count, scan, scatter)
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
@@ -254,7 +254,7 @@ class SlotBankMoE:
         ids = self.topk_ids[:T]
         _lib.build_groups(ids, self.E_total, self.expert_to_group, g, self.group_offsets,
                           self.pair_to_row, self.row_to_pair, self.scratch, self.err)
-        launches = 1
+        launches = 3  # grouping: count, scan, scatter
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1

@@ -18,10 +18,12 @@ from __future__ import annotations
 import itertools
 import threading
 from dataclasses import dataclass
+from types import SimpleNamespace
 
 import torch
 
 from ..config import MoeOffloadConfig
+from ..weight_layout import maybe_tiled
 from .expert_key import ExpertKey
 from .host_store import HostExpertStore
 from .slot_bank import ExpertSlot, ExpertSlotBank, SlotLease, SlotState
@@ -108,6 +110,7 @@ class MoeOffloadRuntime:
         self._graph_slot_address_fingerprints: dict[int, SlotAddressFingerprint] = {}
         self._active_slot_ids_by_layer: dict[int, tuple[int, ...]] = {}
         self._stage_pools: dict[tuple, StagePool] = {}
+        self._tiled_layout: dict[int, bool] = {}
         self._step_counter = itertools.count()
         self._capturing = False
         self.stage_stats = {"calls": 0, "hits": 0, "misses": 0, "h2d_bytes": 0, "log2phy_updates": 0}
@@ -158,10 +161,22 @@ class MoeOffloadRuntime:
         routed = total - shared
         if routed <= 0:
             raise ValueError(f"fused shared layout needs a routed expert; total={total}, shared={shared}")
-        self._host_store.register_layer(layer, pin_memory=self.config.should_pin_host_memory or
-                                        torch.cuda.is_available(), routed_expert_count=routed,
-                                        device=store_device)
         device = torch.device(slot_device) if slot_device is not None else w13.device
+        # Store and banks hold the tile-contiguous layout the kernels stream from.
+        w13t, tiled13 = maybe_tiled(w13.detach())
+        w2t, tiled2 = maybe_tiled(w2.detach())
+        if not (tiled13 and tiled2):
+            if device.type == "cuda":
+                raise ValueError(
+                    "CUDA slot banks need w13 [E, 2I, H] and w2 [E, H, I] with 2I and H multiples "
+                    f"of 128 and H and I multiples of 64; got {tuple(w13.shape)}, {tuple(w2.shape)}")
+            w13t, w2t = w13.detach(), w2.detach()
+        self._tiled_layout[layer_id] = bool(tiled13 and tiled2)
+        self._host_store.register_layer(
+            SimpleNamespace(layer_id=layer_id, w13_weight=w13t, w2_weight=w2t),
+            pin_memory=self.config.should_pin_host_memory or torch.cuda.is_available(),
+            routed_expert_count=routed, device=store_device)
+        w13, w2 = w13t, w2t
         pinned = tuple(range(routed, total))
         bank = ExpertSlotBank(self.config.num_slots, tuple(w13.shape[1:]), tuple(w2.shape[1:]),
                               dtype=w13.dtype, device=device, pinned_logical_ids=pinned)
