@@ -199,6 +199,44 @@ def _combine_index(ps):
     return out
 
 
+def _autoconfig_cases():
+    import os
+    from types import SimpleNamespace
+
+    from vllm_moe_offload_ascend.moe_offload import autoconfig as ac
+
+    out = []
+    cfg = dict(ac._DEFAULT_QWEN3_30B_A3B_CONFIG)
+    keys = ("VLLM_ASCEND_MOE_OFFLOAD_SLOT_HBM_BUDGET_GB", "VLLM_ASCEND_MOE_OFFLOAD_MIN_NET_SAVING_RATIO")
+    saved = {k: os.environ.get(k) for k in keys}
+    try:
+        for gb in (7.0, 14.0, 21.0, 28.0, 48.0):
+            for budget in ("80", "20"):
+                for ratio in (None, "0.75"):
+                    for seqs in (1, 8):
+                        os.environ[keys[0]] = budget
+                        if ratio is None:
+                            os.environ.pop(keys[1], None)
+                        else:
+                            os.environ[keys[1]] = ratio
+                        pre = ac.derive_prefetch_defaults(gb, cfg)
+                        slots = ac.derive_num_slots_defaults(
+                            gb, cfg, pre, SimpleNamespace(max_num_seqs=seqs, max_model_len=None))
+                        out.append({"offload_gb": gb, "slot_hbm_budget_gb": budget,
+                                    "min_net_saving_ratio": ratio, "max_num_seqs": seqs,
+                                    "offloaded_layer_ids": list(pre["offloaded_layer_ids"]),
+                                    "num_slots": slots["num_slots"],
+                                    "target_b2_waves": slots["target_b2_waves"],
+                                    "estimated_b2_waves": slots["estimated_b2_waves"]})
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    return out
+
+
 def main() -> None:
     root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     _install_reference(root)
@@ -211,6 +249,7 @@ def main() -> None:
         "slot_traces.json": _slot_traces(),
         "pair_plans.json": _pair_plans(ps),
         "combine_index.json": _combine_index(ps),
+        "autoconfig.json": _autoconfig_cases(),
     }
     for name, data in blobs.items():
         (HERE / name).write_text(json.dumps(data, separators=(",", ":")) + "\n")

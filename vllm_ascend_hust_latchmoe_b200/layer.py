@@ -124,6 +124,9 @@ class SlotBankMoE:
         self.resident_tier = runtime.host_layer(self.layer_id).on_device
         self.last_waves = WaveReport()
         self.kernel_launches = 0
+        self.pending: StageDecision | None = None
+        self.shared_w13 = None
+        self.shared_w2 = None
 
     # ------------------------------------------------------------------ pieces
     def route(self, hidden: torch.Tensor, router_logits: torch.Tensor):
@@ -176,7 +179,12 @@ class SlotBankMoE:
                                             num_logical_experts=self.E)
         return StageDecision("slots", active, counts, prepared)
 
-    def mlp_slots(self, hidden: torch.Tensor, T: int) -> torch.Tensor:
+    def _combine(self, T: int, out: torch.Tensor | None) -> torch.Tensor:
+        dst = self.out[:T] if out is None else out
+        _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], dst)
+        return dst
+
+    def mlp_slots(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """Captured MLP piece: log2phy remap + grouping, grouped MLP on the slot bank, combine.
 
         Reads only fixed addresses (slot bank, log2phy, this layer's buffers)."""
@@ -188,11 +196,10 @@ class SlotBankMoE:
         _lib.build_groups(ids, self.E_total, log2phy, G, self.group_offsets, self.pair_to_row,
                           self.row_to_pair, self.scratch, self.err)
         self._grouped_mlp(hidden, T, self.slot_rows, 0, G, bank.w13_slots, bank.w2_slots)
-        _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], self.out[:T])
         self.kernel_launches += 6  # grouping (3), gate_up, down, combine
-        return self.out[:T]
+        return self._combine(T, out)
 
-    def mlp_resident(self, hidden: torch.Tensor, T: int) -> torch.Tensor:
+    def mlp_resident(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """MLP piece for an HBM-resident expert tier: histogram -> device wave plan ->
         grouping (rows wave by wave) -> grouped MLP reading each expert in place -> one
         combine. No host synchronisation; fixed buffers only, so it can be captured."""
@@ -209,9 +216,8 @@ class SlotBankMoE:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
         self._grouped_mlp(hidden, T, self.group_bank_row, 0, self.E, store.w13, store.w2)
-        _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], self.out[:T])
         self.kernel_launches += launches + 3
-        return self.out[:T]
+        return self._combine(T, out)
 
     def resident_wave_plan(self) -> tuple[tuple[int, ...], ...]:
         """Read back the last device wave plan (synchronises; diagnostics and tests)."""
@@ -229,7 +235,8 @@ class SlotBankMoE:
             _lib.moe_mlp_prefill(self.x_perm, T * self.k, self.group_offsets, bank_rows_dev,
                                  g0, g1, w13_bank, w2_bank, self.act, self.y_perm, self.err)
 
-    def forward_waves(self, hidden: torch.Tensor, T: int, counts: tuple[int, ...]) -> torch.Tensor:
+    def forward_waves(self, hidden: torch.Tensor, T: int, counts: tuple[int, ...],
+                      out: torch.Tensor | None = None) -> torch.Tensor:
         """Capacity-bounded waves with one combine at the end (eager)."""
         rt = self.runtime
         cfg = rt.config
@@ -290,12 +297,63 @@ class SlotBankMoE:
                     release = torch.cuda.Event()
                     release.record(compute_stream)
                     rt.remember_prefill_stage_buffer_release(self.layer_id, buf, release)
-        _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], self.out[:T])
+        dst = self._combine(T, out)
         launches += 1
         report.launches = launches
         self.last_waves = report
         self.kernel_launches += launches
-        return self.out[:T]
+        return dst
+
+    # ------------------------------------------------------------------ shared experts
+    def set_shared_experts(self, w13: torch.Tensor, w2: torch.Tensor) -> None:
+        """Always-resident shared expert(s) fused into one MLP: ``w13 [2*Is, H]`` (gate rows
+        then up rows) and ``w2 [H, Is]``; applied to every token by :meth:`shared_mlp`."""
+        from .weight_layout import to_tiled
+
+        Is = int(w2.shape[-1])
+        if tuple(w13.shape) != (2 * Is, self.H) or tuple(w2.shape) != (self.H, Is):
+            raise ValueError(f"shared expert shapes {tuple(w13.shape)}, {tuple(w2.shape)} do not "
+                             f"match hidden {self.H}")
+        self.shared_w13 = to_tiled(w13.to(self.device, torch.bfloat16))[None].contiguous()
+        self.shared_w2 = to_tiled(w2.to(self.device, torch.bfloat16))[None].contiguous()
+        d, i32 = self.device, torch.int32
+        self.shared_rows = torch.arange(self.max_tokens, dtype=i32, device=d)
+        self.shared_bank_row = torch.zeros(1, dtype=i32, device=d)
+        self.shared_offsets = torch.zeros(2, dtype=i32, device=d)
+        self.shared_act = torch.zeros(self.max_tokens, Is, dtype=torch.bfloat16, device=d)
+
+    def shared_mlp(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Resident shared-expert MLP over all T tokens (one group of T rows)."""
+        if self.shared_w13 is None:
+            raise RuntimeError(f"layer {self.layer_id} has no shared experts")
+        out = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device) if out is None else out
+        self.shared_offsets[1:].fill_(T)
+        if T <= DECODE_MAX_TOKENS:
+            _lib.moe_mlp_decode(hidden, 1, self.shared_rows, self.shared_offsets,
+                                self.shared_bank_row, 0, 1, T, self.shared_w13, self.shared_w2,
+                                self.shared_act, out, self.err)
+        else:
+            _lib.moe_mlp_prefill(hidden, T, self.shared_offsets, self.shared_bank_row, 0, 1,
+                                 self.shared_w13, self.shared_w2, self.shared_act, out, self.err)
+        self.kernel_launches += 2
+        return out
+
+    def run_mlp(self, hidden: torch.Tensor, decision: StageDecision,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        """MLP piece for a stage decision (the seam's second captured piece, or eager)."""
+        T = int(hidden.shape[0])
+        if decision.mode == "waves":
+            return self.forward_waves(hidden, T, decision.counts, out)
+        if decision.mode == "resident":
+            return self.mlp_resident(hidden, T, out)
+        if decision.mode not in ("slots", "static", "capturing"):
+            raise RuntimeError(f"layer {self.layer_id} is not offloaded under fixed slots")
+        rt = self.runtime
+        rt.capture_safe_slot_weights(layer_id=self.layer_id)
+        handle = rt.begin_slot_compute(decision.prepared) if decision.prepared is not None else None
+        result = self.mlp_slots(hidden, T, out)
+        rt.end_slot_compute(handle)
+        return result
 
     # ------------------------------------------------------------------ whole layer
     def forward(self, hidden: torch.Tensor, router_logits: torch.Tensor,
@@ -306,19 +364,7 @@ class SlotBankMoE:
         if hidden.dtype != torch.bfloat16 or not hidden.is_contiguous():
             raise ValueError("hidden_states must be a contiguous bf16 tensor")
         _, ids = self.route(hidden, router_logits)
-        decision = self.stage(ids, phase)
-        if decision.mode == "waves":
-            return self.forward_waves(hidden, T, decision.counts)
-        if decision.mode == "resident":
-            return self.mlp_resident(hidden, T)
-        if decision.mode not in ("slots", "static"):
-            raise RuntimeError(f"layer {self.layer_id} is not offloaded under fixed slots")
-        rt = self.runtime
-        rt.capture_safe_slot_weights(layer_id=self.layer_id)
-        handle = rt.begin_slot_compute(decision.prepared) if decision.prepared is not None else None
-        out = self.mlp_slots(hidden, T)
-        rt.end_slot_compute(handle)
-        return out
+        return self.run_mlp(hidden, self.stage(ids, phase))
 
     def check_device_errors(self, where: str = "SlotBankMoE") -> None:
         _lib.raise_on_device_error(self.err, f"{where} layer {self.layer_id}")
