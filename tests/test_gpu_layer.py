@@ -65,8 +65,11 @@ def test_c1_decode_overflow_runs_waves(cuda, store_on_device):
     assert np.array_equal(layer.topk_ids[:16].cpu().numpy(), ids_ref)
     counts = np.bincount(ids_ref.reshape(-1), minlength=cfg.num_experts)
     waves = ocontrol.plan_balanced_waves({e: int(c) for e, c in enumerate(counts)}, cfg.num_slots)
-    got = layer.resident_wave_plan() if store_on_device else layer.last_waves.waves
-    assert got == waves and len(waves) >= 2
+    if store_on_device:
+        # HBM-resident tier: nothing is staged, a decode call groups by expert id
+        assert layer.resident_wave_plan() == ()
+    else:
+        assert layer.last_waves.waves == waves and len(waves) >= 2
     _check(out, ref)
 
 

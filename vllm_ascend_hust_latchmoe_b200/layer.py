@@ -119,6 +119,9 @@ class SlotBankMoE:
         self.act = torch.zeros(P, self.I, dtype=torch.bfloat16, device=d)
         self.y_perm = torch.zeros(P, self.H, dtype=torch.bfloat16, device=d)
         self.out = torch.zeros(self.max_tokens, self.H, dtype=torch.bfloat16, device=d)
+        # Identity expert -> group table: for decode-sized calls on an HBM-resident tier the
+        # wave order is irrelevant (no staging), so grouping by expert id needs no plan.
+        self.identity_groups = torch.arange(self.E_total, dtype=i32, device=d)
         self.wave_offsets = torch.zeros(self.E + 1, dtype=i32, device=d)
         self.num_waves = torch.zeros(1, dtype=i32, device=d)
         self.resident_tier = runtime.host_layer(self.layer_id).on_device
@@ -205,6 +208,15 @@ class SlotBankMoE:
         combine. No host synchronisation; fixed buffers only, so it can be captured."""
         store = self.runtime.host_layer(self.layer_id)
         ids = self.topk_ids[:T]
+        if T <= DECODE_MAX_TOKENS:
+            # group = expert id, bank row = expert id: no histogram or wave plan needed
+            self.resident_planned = False
+            _lib.build_groups(ids, self.E_total, self.identity_groups, self.E, self.group_offsets,
+                              self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+            self._grouped_mlp(hidden, T, self.identity_groups, 0, self.E, store.w13, store.w2)
+            self.kernel_launches += 6
+            return self._combine(T, out)
+        self.resident_planned = True
         _lib.expert_histogram(ids, self.E, self.counts, self.err)
         _lib.plan_waves(self.counts, self.runtime.config.num_slots, self.expert_to_group,
                         self.group_bank_row, self.wave_offsets, self.num_waves,
@@ -220,7 +232,10 @@ class SlotBankMoE:
         return self._combine(T, out)
 
     def resident_wave_plan(self) -> tuple[tuple[int, ...], ...]:
-        """Read back the last device wave plan (synchronises; diagnostics and tests)."""
+        """Read back the last device wave plan (synchronises; diagnostics and tests). Empty
+        after a decode-sized resident call, which groups by expert id without waves."""
+        if not getattr(self, "resident_planned", False):
+            return ()
         nw = int(self.num_waves.item())
         off = self.wave_offsets[: nw + 1].tolist()
         rows = self.group_bank_row.tolist()

@@ -111,6 +111,19 @@ class HostExpertStore:
         return HostStoreRegisterReport(layer_id, n, bool(pin_memory), pinned,
                                        buf.expert_bytes * n)
 
+    def adopt_layer(self, layer_id: int, w13: torch.Tensor, w2: torch.Tensor) -> HostStoreRegisterReport:
+        """Use existing store tensors ``[E, 2I, H]`` / ``[E, H, I]`` (already in the bank
+        layout; pinned host memory or device memory) without copying them. Several layers
+        may adopt the same tensors."""
+        if w13.shape[0] != w2.shape[0]:
+            raise ValueError("w13 and w2 stores must have the same number of experts")
+        if not w13.is_cuda and torch.cuda.is_available() and not w13.is_pinned():
+            raise ValueError("a host store must be pinned memory")
+        buf = HostLayerBuffer(int(layer_id), w13, w2)
+        self._layers[int(layer_id)] = buf
+        return HostStoreRegisterReport(int(layer_id), buf.num_experts, not w13.is_cuda,
+                                       0 if w13.is_cuda else 2, buf.expert_bytes * buf.num_experts)
+
     def layer(self, layer_id: int) -> HostLayerBuffer:
         try:
             return self._layers[int(layer_id)]

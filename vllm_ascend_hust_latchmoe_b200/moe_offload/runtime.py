@@ -193,6 +193,33 @@ class MoeOffloadRuntime:
             self._log2phy_rings[layer_id] = _PinnedRing(total)
         self._log2phy_slot_by_expert[layer_id] = {}
 
+    def register_layer_with_store(self, layer_id: int, w13_store: torch.Tensor,
+                                  w2_store: torch.Tensor, *, slot_device: torch.device,
+                                  num_slots: int | None = None) -> None:
+        """Register a routed-only layer whose expert store tensors already exist in the bank
+        layout (tile-contiguous), pinned on the host or resident in HBM; no copy is made.
+        ``num_slots`` overrides the configured slot count for this layer's bank (an
+        HBM-resident layer reads its store in place and needs no real bank)."""
+        layer_id = int(layer_id)
+        if layer_id in self._graph_slot_address_fingerprints:
+            raise RuntimeError(f"layer {layer_id} fixed-slot addresses are already captured; "
+                               "re-registering would invalidate a CUDA graph replay")
+        self._host_store.adopt_layer(layer_id, w13_store, w2_store)
+        E = int(w13_store.shape[0])
+        device = torch.device(slot_device)
+        self._tiled_layout[layer_id] = True
+        self._slot_banks[layer_id] = ExpertSlotBank(
+            int(num_slots or self.config.num_slots), tuple(w13_store.shape[1:]),
+            tuple(w2_store.shape[1:]), dtype=w13_store.dtype, device=device)
+        self._routed_counts[layer_id] = E
+        self._total_counts[layer_id] = E
+        log2phy = torch.full((E,), -1, dtype=torch.int32, device=device)
+        self._log2phy_buffers[layer_id] = log2phy
+        self._log2phy_host[layer_id] = torch.full((E,), -1, dtype=torch.int32)
+        if device.type == "cuda":
+            self._log2phy_rings[layer_id] = _PinnedRing(E)
+        self._log2phy_slot_by_expert[layer_id] = {}
+
     def slot_bank(self, layer_id: int) -> ExpertSlotBank:
         bank = self._slot_banks.get(int(layer_id))
         if bank is None:
