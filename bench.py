@@ -180,6 +180,66 @@ def run_reference(args, cfg) -> dict:
     return line
 
 
+# --------------------------------------------------------------------------- C5 (N > 1)
+def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
+    """Qwen3-235B-A22B-shaped layer with the expert bank partitioned over the ranks: 256
+    decode tokens per step in total (256 / N per rank), NCCL all-to-all dispatch/combine.
+    Two stores per rank: HBM-resident, and pinned host memory staged into half as many
+    slots as the rank owns experts. Times are the max over ranks."""
+    import torch
+
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+    from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE,
+                                                                build_rank_layer, cuda_ops)
+
+    cfg = syn.CONFIGS["c5_ep"]
+    T = cfg.tokens // world
+    per = cfg.num_experts // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    I, H = cfg.intermediate, cfg.hidden
+    w13 = (torch.randn(per, 2 * I, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(per, H, I, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    hidden = syn.make_hidden(cfg, seed=rank, tokens=T).to(dev)
+    logits = syn.make_router_logits(cfg, seed=0, tokens=cfg.tokens)[rank * T:(rank + 1) * T].to(dev)
+    out = {"workload": cfg.name, "tokens_per_step": cfg.tokens, "tokens_per_rank": T,
+           "experts_per_rank": per}
+    for name, on_dev, slots in (("resident", True, per), ("offloaded", False, max(1, per // 2))):
+        local = build_rank_layer(w13_owned=w13 if on_dev else w13.cpu(),
+                                 w2_owned=w2 if on_dev else w2.cpu(), rank=rank, device=dev,
+                                 max_rows=cfg.tokens * cfg.top_k, num_slots=slots,
+                                 store_on_device=on_dev)
+        ep = ExpertParallelMoE(num_experts=cfg.num_experts, top_k=cfg.top_k, hidden_size=H,
+                               rank=rank, world_size=world, device=dev,
+                               ops=cuda_ops(local, num_experts=cfg.num_experts, top_k=cfg.top_k,
+                                            max_tokens=T))
+        for _ in range(3):
+            ep.forward(hidden, logits)
+        torch.cuda.synchronize()
+        dist.barrier()
+        sent0 = ep.stats.bytes_sent
+        steps = 10
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            ep.forward(hidden, logits)
+        e.record()
+        torch.cuda.synchronize()
+        local.check_device_errors("bench ep")
+        ms = torch.tensor([s.elapsed_time(e) / steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        nv = (ep.stats.bytes_sent - sent0) / steps
+        h2d = local.runtime.transfer_engine.stats.bytes_h2d
+        out[name] = {"ms_per_step": float(ms.item()),
+                     "tokens_per_s": cfg.tokens / (float(ms.item()) / 1e3),
+                     "nvlink_bytes_sent_per_rank_step": nv,
+                     "slots_per_rank": slots if not on_dev else None,
+                     "h2d_bytes_rank0_total": int(h2d)}
+        del ep, local
+        torch.cuda.empty_cache()
+    return out
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -429,7 +489,10 @@ def main() -> None:
            "h2d_gbs": (io_in + staged) / (e2e_ms / e2e_steps / 1e3) / 1e9,
            "pcie_gen5_x16_gbs": 64.0, "ms_per_step": e2e_ms / e2e_steps}
 
+    # ----------------------------------------------------------------- expert parallel (C5)
+    ep_report = None
     if dist is not None:
+        ep_report = run_expert_parallel(dist, rank, world, dev, args)
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -455,6 +518,7 @@ def main() -> None:
                    "waves": waves, "parallelism": f"replica x{world}",
                    "l2": "weights 1.2 GB per step > 126 MB L2 (no flush needed)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode, "tpot": tpot,
+        "expert_parallel": ep_report,
         "clocks": clocks.summary(), "gpu_launches": int(launches),
     }
     print(json.dumps(line), flush=True)

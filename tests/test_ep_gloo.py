@@ -1,0 +1,107 @@
+"""Expert-parallel exchange logic on CPU ranks (gloo, world size 2): routing -> group by owner
+-> count/row/id all-to-all -> owner MLP -> reverse all-to-all -> combine in top-k order,
+with the oracle supplying each compute step. Every rank's output must equal the
+single-process oracle layer on that rank's tokens."""
+
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import control as oc
+from oracle import mlp as omlp
+from oracle import router as orouter
+from oracle.bf16 import bf16_bits_to_f32, f32_to_bf16_bits
+from vllm_ascend_hust_latchmoe_b200.expert_parallel import EPOps, ExpertParallelMoE
+
+E, K, H, I, T = 16, 4, 64, 32, 24
+
+
+def _data(rank):
+    rng = np.random.default_rng(100 + rank)
+    logits = (rng.standard_normal((T, E)) + np.linspace(2, -2, E)[None, :]).astype(np.float32)
+    hidden = f32_to_bf16_bits(rng.standard_normal((T, H)).astype(np.float32))
+    wr = np.random.default_rng(7)
+    w13 = f32_to_bf16_bits((wr.standard_normal((E, 2 * I, H)) * 0.1).astype(np.float32))
+    w2 = f32_to_bf16_bits((wr.standard_normal((E, H, I)) * 0.1).astype(np.float32))
+    return logits, hidden, w13, w2
+
+
+def _bf16(bits):
+    return torch.from_numpy(bf16_bits_to_f32(bits)).to(torch.bfloat16)
+
+
+def _bits(t):
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _oracle_ops(w13, w2, rank, per_rank):
+    def route(logits):
+        wb, _, ids = orouter.route(logits.numpy(), K)
+        return _bf16(wb), torch.from_numpy(ids)
+
+    def group_by_owner(ids, owner, G):
+        off, p2r, r2p = oc.group_pairs(ids.numpy(), owner.numpy(), G)
+        return torch.from_numpy(off), torch.from_numpy(p2r), torch.from_numpy(r2p)
+
+    def gather_rows(hidden, rows, k):
+        return hidden.index_select(0, (rows.long() // k))
+
+    def expert_mlp(rows, local_ids):
+        x = bf16_bits_to_f32(_bits(rows))
+        out = np.zeros_like(x)
+        for le in np.unique(local_ids.numpy()):
+            sel = np.nonzero(local_ids.numpy() == le)[0]
+            e = rank * per_rank + int(le)
+            out[sel] = omlp.expert_mlp(x[sel], bf16_bits_to_f32(w13[e]), bf16_bits_to_f32(w2[e]))
+        return torch.from_numpy(out).to(torch.bfloat16)
+
+    def combine(back, p2r, w):
+        y = bf16_bits_to_f32(_bits(back))[p2r.numpy()]
+        return torch.from_numpy(omlp.combine(y, _bits(w))).to(torch.bfloat16)
+
+    return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine)
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        logits, hidden, w13, w2 = _data(rank)
+        ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank, world_size=world,
+                               ops=_oracle_ops(w13, w2, rank, E // world), device="cpu")
+        out = ep.forward(_bf16(hidden), torch.from_numpy(logits))
+        wb, _, ids = orouter.route(logits, K)
+        ref = omlp.moe_layer(hidden, ids, wb, w13, w2)
+        m = omlp.compare(bf16_bits_to_f32(_bits(out)), ref)
+        q.put((rank, m, ep.stats.send_rows, ep.stats.recv_rows, list(ep.owned_experts())))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_ep_exchange_matches_single_process_oracle():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    results.sort()
+    assert [r[4] for r in results] == [list(range(0, 8)), list(range(8, 16))]
+    assert sum(r[2] for r in results) == sum(r[3] for r in results) == 2 * T * K
+    for rank, m, *_ in results:
+        assert m["max_rel_err"] <= 1e-2 and m["cosine"] >= 0.9999, (rank, m)

@@ -1,0 +1,92 @@
+"""Expert-parallel layer on 2 GPUs with NCCL: each rank owns half of the experts in its own
+slot bank (pinned host store, staged) and the gathered outputs match the single-GPU oracle.
+Skipped with fewer than 2 GPUs."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+E, K, H, I, T, S = 32, 4, 2048, 768, 48, 8
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, store_on_device, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from oracle import mlp as omlp
+    from oracle import router as orouter
+    from oracle.bf16 import bf16_bits_to_f32
+    from tests.helpers import bits
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+    from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE,
+                                                                build_rank_layer, cuda_ops)
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        cfg = syn.LayerConfig("ep", hidden=H, num_experts=E, top_k=K, intermediate=I,
+                              num_slots=S, tokens=T)
+        w13, w2 = syn.make_expert_weights(cfg, seed=1)
+        per = E // world
+        local = build_rank_layer(w13_owned=w13[rank * per:(rank + 1) * per],
+                                 w2_owned=w2[rank * per:(rank + 1) * per], rank=rank,
+                                 device=dev, max_rows=world * T * K, num_slots=S,
+                                 store_on_device=store_on_device)
+        ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
+                               world_size=world, device=dev,
+                               ops=cuda_ops(local, num_experts=E, top_k=K, max_tokens=T))
+        hidden = syn.make_hidden(cfg, seed=10 + rank)
+        logits = syn.make_router_logits(cfg, seed=10 + rank)
+        for _ in range(2):  # second call reuses every buffer
+            out = ep.forward(hidden.to(dev), logits.to(dev))
+        torch.cuda.synchronize()
+        local.check_device_errors("ep")
+        wb, _, ids = orouter.route(logits.numpy(), K)
+        ref = omlp.moe_layer(bits(hidden), ids, wb, bits(w13), bits(w2))
+        m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)
+        dist.barrier()
+        q.put((rank, m, ep.stats.bytes_sent))
+    except Exception as exc:  # report instead of hanging the peer
+        q.put((rank, {"error": repr(exc)}, 0))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("store_on_device", [False, True])
+def test_ep_two_gpus_matches_oracle(store_on_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, store_on_device, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for rank, m, sent in results:
+        assert "error" not in m, m
+        assert m["max_rel_err"] <= 1e-2 and m["cosine"] >= 0.9999, (rank, m)
+        assert sent > 0
+    assert all(p.exitcode == 0 for p in procs)

@@ -1,0 +1,182 @@
+"""Expert-partitioned slot-bank MoE layer across the GPUs of one node (NCCL over NVLink).
+
+The reference runs on one NPU and rejects every parallel mode
+(``patches/patch_fused_moe.py:4898-4914``); this module is the B200 extension its scope
+asks for. Experts are owned in contiguous blocks (``owner(e) = e // (E / G)``); each rank
+keeps its own slot bank and pinned host store for the experts it owns. One layer call:
+
+1. route the rank's tokens (``lm_route_topk``);
+2. group the routed pairs by owner rank with the same stable grouping kernel the slot
+   remap uses (``lm_build_groups`` with expert -> owner), gather the rows
+   (``lm_permute_rows``) and the owner-local expert ids;
+3. exchange per-destination counts (``all_to_all_single`` of G int64), then rows and ids
+   (``all_to_all_single`` with those splits) -- the dispatch;
+4. run the owner's slot-bank MLP on the received rows (top-1, unit weight: staging, waves
+   and kernels exactly as a single-GPU layer);
+5. send the rows back with the reverse splits -- the combine exchange -- and reduce them in
+   the original top-k order with the router weights (``lm_moe_combine``, fp32).
+
+Remote rows always land in this GPU's buffers before any kernel reads them (NCCL copies);
+no kernel reads peer memory and no TMA multicast is used.
+
+The compute steps are injectable (``ops``) so the exchange bookkeeping can be exercised on
+CPU ranks with gloo against the oracle; the default ``ops`` are the CUDA kernels.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+
+@dataclass
+class EPStats:
+    send_rows: int = 0
+    recv_rows: int = 0
+    bytes_sent: int = 0
+    bytes_received: int = 0
+
+
+@dataclass
+class EPOps:
+    """Compute steps of one EP layer call (CUDA kernels by default)."""
+
+    route: Callable            # (logits [T,E]) -> (weights_bf16 [T,k], ids int32 [T,k])
+    group_by_owner: Callable   # (ids [T,k], owner [E], G) -> (offsets [G+1], p2r [P], r2p [P])
+    gather_rows: Callable      # (hidden [T,H], r2p [P], k) -> rows [P,H]
+    expert_mlp: Callable       # (rows [R,H], local_ids int32 [R]) -> out [R,H]
+    combine: Callable          # (rows_back [P,H], p2r [P], weights [T,k]) -> out [T,H]
+
+
+class ExpertParallelMoE:
+    def __init__(self, *, num_experts: int, top_k: int, hidden_size: int, rank: int,
+                 world_size: int, ops: EPOps, group: dist.ProcessGroup | None = None,
+                 device: torch.device | str = "cuda") -> None:
+        if num_experts % world_size != 0:
+            raise ValueError(f"{num_experts} experts do not split evenly over {world_size} ranks")
+        self.E = int(num_experts)
+        self.k = int(top_k)
+        self.H = int(hidden_size)
+        self.rank = int(rank)
+        self.G = int(world_size)
+        self.per_rank = self.E // self.G
+        self.base = self.rank * self.per_rank
+        self.ops = ops
+        self.group = group
+        self.device = torch.device(device)
+        self.owner = (torch.arange(self.E, dtype=torch.int32) // self.per_rank).to(self.device)
+        self.stats = EPStats()
+
+    def owned_experts(self) -> range:
+        return range(self.base, self.base + self.per_rank)
+
+    def forward(self, hidden: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        T = int(hidden.shape[0])
+        w, ids = self.ops.route(router_logits)
+        offsets, p2r, r2p = self.ops.group_by_owner(ids, self.owner, self.G)
+        P = T * self.k
+        send_rows = self.ops.gather_rows(hidden, r2p[:P], self.k)
+        send_ids = (ids.reshape(-1).long().index_select(0, r2p[:P].long()) % self.per_rank).to(torch.int32)
+        send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        s_split = send_counts.tolist()
+        r_split = recv_counts.tolist()
+        R = int(sum(r_split))
+        recv_rows = torch.empty(R, self.H, dtype=hidden.dtype, device=hidden.device)
+        recv_ids = torch.empty(R, dtype=torch.int32, device=hidden.device)
+        dist.all_to_all_single(recv_rows, send_rows, r_split, s_split, group=self.group)
+        dist.all_to_all_single(recv_ids, send_ids, r_split, s_split, group=self.group)
+        out_rows = self.ops.expert_mlp(recv_rows, recv_ids)
+        back = torch.empty(P, self.H, dtype=hidden.dtype, device=hidden.device)
+        dist.all_to_all_single(back, out_rows.contiguous(), s_split, r_split, group=self.group)
+        st = self.stats
+        elt = hidden.element_size()
+        st.send_rows += P
+        st.recv_rows += R
+        st.bytes_sent += (P - s_split[self.rank]) * self.H * elt * 2
+        st.bytes_received += (R - r_split[self.rank]) * self.H * elt * 2
+        return self.ops.combine(back, p2r[:P], w)
+
+
+def cuda_ops(local_moe, *, num_experts: int, top_k: int, renormalize: bool = True,
+             routed_scaling_factor: float = 1.0, max_tokens: int) -> EPOps:
+    """The CUDA kernels for one rank; ``local_moe`` is a top-1 SlotBankMoE over the rank's
+    owned experts (its own slot bank and host store)."""
+    dev = local_moe.device
+    P = max_tokens * top_k
+    wb = torch.empty(max_tokens, top_k, dtype=torch.bfloat16, device=dev)
+    ids = torch.empty(max_tokens, top_k, dtype=torch.int32, device=dev)
+    G_MAX = 64
+    off = torch.empty(G_MAX + 1, dtype=torch.int32, device=dev)
+    p2r = torch.empty(P, dtype=torch.int32, device=dev)
+    r2p = torch.empty(P, dtype=torch.int32, device=dev)
+    scratch = torch.empty(_lib.build_groups_scratch_elems(P, G_MAX), dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def route(logits):
+        T = logits.shape[0]
+        _lib.route_topk(logits.float().contiguous(), top_k, renormalize=renormalize,
+                        routed_scaling_factor=routed_scaling_factor, weights_bf16=wb[:T],
+                        ids=ids[:T])
+        return wb[:T], ids[:T]
+
+    def group_by_owner(i, owner, G):
+        _lib.build_groups(i, num_experts, owner, G, off[: G + 1], p2r, r2p, scratch, err)
+        return off[: G + 1], p2r, r2p
+
+    def gather_rows(hidden, rows, k):
+        out = torch.empty(rows.numel(), hidden.shape[1], dtype=hidden.dtype, device=hidden.device)
+        _lib.permute_rows(hidden, rows, k, rows.numel(), out)
+        return out
+
+    def expert_mlp(rows, local_ids):
+        R = rows.shape[0]
+        if R == 0:
+            return rows.new_empty((0, rows.shape[1]))
+        local_moe.topk_ids[:R, 0].copy_(local_ids)
+        local_moe.topk_w[:R].fill_(1.0)
+        decision = local_moe.stage(local_moe.topk_ids[:R])
+        return local_moe.run_mlp(rows, decision)
+
+    def combine(back, p2r_, w):
+        T = w.shape[0]
+        out = torch.empty(T, back.shape[1], dtype=back.dtype, device=back.device)
+        _lib.moe_combine(back, p2r_, w, out)
+        return out
+
+    return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine)
+
+
+def build_rank_layer(*, w13_owned: torch.Tensor, w2_owned: torch.Tensor, rank: int,
+                     device: torch.device, max_rows: int, num_slots: int,
+                     store_on_device: bool):
+    """A top-1 SlotBankMoE over one rank's owned experts (``w13_owned [E_r, 2I, H]``,
+    ``w2_owned [E_r, H, I]``, row-major). The store is pinned host memory (staged into
+    ``num_slots`` slots) or HBM (read in place)."""
+    from .config import MoeOffloadConfig
+    from .layer import SlotBankMoE
+    from .moe_offload.runtime import MoeOffloadRuntime
+    from .weight_layout import to_tiled
+
+    E_r, two_i, H = w13_owned.shape
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=int(num_slots),
+                                            async_load=True, b2_wave_prefill=True,
+                                            pin_host_memory=True))
+    w13t, w2t = to_tiled(w13_owned), to_tiled(w2_owned)
+    if store_on_device:
+        w13s, w2s = w13t.to(device), w2t.to(device)
+    else:
+        w13s = torch.empty(w13t.shape, dtype=w13t.dtype, pin_memory=True)
+        w2s = torch.empty(w2t.shape, dtype=w2t.dtype, pin_memory=True)
+        w13s.copy_(w13t)
+        w2s.copy_(w2t)
+    rt.register_layer_with_store(rank, w13s, w2s, slot_device=device,
+                                 num_slots=1 if store_on_device else int(num_slots))
+    return SlotBankMoE(rt, rank, hidden_size=H, intermediate_size=two_i // 2, num_experts=E_r,
+                       top_k=1, max_tokens=int(max_rows), device=device)

@@ -162,12 +162,16 @@ class SlotBankMoE:
             if rt.should_use_fixed_slot_plan_for_layer(self.layer_id) and not rt.is_layer_registered(self.layer_id):
                 raise RuntimeError(f"graph capture reached an unregistered fixed-slot MoE layer {self.layer_id}")
             return StageDecision("capturing")
-        if rt.is_static_residency_regime(self.E):
-            return StageDecision("static")
         if self.resident_tier:
             # Every expert already has an HBM copy: nothing to stage, and the wave plan is
             # made on the device inside the MLP piece (no host round trip).
             return StageDecision("resident")
+        if rt.is_static_residency_regime(self.E):
+            # Regime A: every expert owns a slot; stage them all once, log2phy stays static.
+            if not getattr(self, "_static_staged", False):
+                rt.stage_full_residency_slot_plan(layer_id=self.layer_id)
+                self._static_staged = True
+            return StageDecision("static")
         if not rt.should_use_fixed_slot_plan_for_layer(self.layer_id):
             return StageDecision("passthrough")
         counts = self.active_counts(topk_ids)
