@@ -54,64 +54,89 @@ def _peaks() -> dict:
             "source": "fallback"}
 
 
+def _clock_process(conn, bus: str, index: int, period: float) -> None:
+    """Child process body: polls NVML between "start" and "stop" messages (its own
+    interpreter, so the launch loop's GIL cannot starve it)."""
+    import time
+
+    import pynvml
+
+    pynvml.nvmlInit()
+    try:
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+    except Exception:
+        h = pynvml.nvmlDeviceGetHandleByIndex(index)
+    conn.send(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+    while conn.recv() == "start":
+        samples = []
+        while True:
+            try:
+                samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))))
+            except Exception:
+                pass
+            if conn.poll():
+                break
+            time.sleep(period)
+        conn.recv()
+        conn.send(samples)
+    pynvml.nvmlShutdown()
+
+
 class ClockSampler:
-    """SM clock and throttle reasons sampled through NVML every few ms while the timed
-    region runs (a background thread; the timed region is often only tens of ms long)."""
+    """SM clock and throttle reasons sampled through NVML every millisecond while the timed
+    region runs, from a spawned child process (the timed region is often only tens of ms)."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}
 
-    def __init__(self, cuda_index: int, period_s: float = 0.002) -> None:
+    def __init__(self, cuda_index: int, period_s: float = 0.001) -> None:
         self.cuda_index = cuda_index
         self.period = period_s
         self.samples: list[tuple[float, int]] = []
         self.max_mhz = None
-        self._stop = None
-        self._thread = None
-        self._nvml = None
-        self._handle = None
+        self._proc = None
+        self._conn = None
 
-    def _open(self):
-        import pynvml
+    def __enter__(self):
+        import multiprocessing as mp
+
         import torch
 
-        pynvml.nvmlInit()
-        self._nvml = pynvml
         try:
             p = torch.cuda.get_device_properties(self.cuda_index)
             bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
-            self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            ctx = mp.get_context("spawn")
+            self._conn, child = ctx.Pipe()
+            self._proc = ctx.Process(target=_clock_process,
+                                     args=(child, bus, self.cuda_index, self.period), daemon=True)
+            self._proc.start()
+            if not self._conn.poll(60):
+                raise TimeoutError("clock sampler did not start")
+            self.max_mhz = self._conn.recv()
+            self._conn.send("start")
         except Exception:
-            self._handle = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
-        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
-
-    def _run(self):
-        nv, h = self._nvml, self._handle
-        while not self._stop.is_set():
-            try:
-                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.samples.append((float(mhz), int(reasons)))
-            except Exception:
-                pass
-            self._stop.wait(self.period)
-
-    def __enter__(self):
-        import threading
-
-        try:
-            self._open()
-            self._stop = threading.Event()
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
-        except Exception:
-            self._thread = None
+            self._stop_proc()
         return self
 
+    def _stop_proc(self):
+        if self._proc is not None:
+            self._proc.join(timeout=5)
+            if self._proc.is_alive():
+                self._proc.kill()
+        self._proc = None
+
     def __exit__(self, *exc):
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join(timeout=2)
+        if self._proc is None:
+            return
+        try:
+            self._conn.send("stop")
+            if self._conn.poll(10):
+                self.samples = self._conn.recv()
+            self._conn.send("quit")
+        except Exception:
+            pass
+        self._stop_proc()
 
     def summary(self) -> dict:
         if not self.samples:
@@ -123,7 +148,19 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(m for m, _ in self.samples),
                 "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(n for n, bit in self.REASONS.items() if seen & bit),
-                "samples": len(self.samples), "source": "nvml"}
+                "samples": len(self.samples), "source": "nvml (1 ms, separate process)"}
+
+
+def _profiled_traffic(name: str) -> int | None:
+    """DRAM bytes (read + write) per call from a committed ncu summary under profiles/: the
+    value of its ``traffic_bytes_per_call:`` line."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_call:"):
+            return int(line.split(":", 1)[1].strip().split()[0])
+    return None
 
 
 # --------------------------------------------------------------------------- CPU arm
@@ -240,6 +277,73 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
     return out
 
 
+def run_value(args, cfg, make_layer, hidden, logits, dist, dev, world, local_rank, peaks,
+              barrier):
+    """``value``: the C2 layer with hidden states, logits and the expert store in HBM; the
+    grouped MLP calls are bracketed with CUDA events on the launching stream."""
+    import torch
+
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+    layer = make_layer(True)
+    mlp_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
+    orig = layer._grouped_mlp
+
+    def timed_mlp(*a, **kw):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        orig(*a, **kw)
+        e.record()
+        mlp_events.append((s, e))
+
+    layer._grouped_mlp = timed_mlp
+    for _ in range(args.warmup):
+        layer.forward(hidden, logits)
+    torch.cuda.synchronize()
+    layer.check_device_errors("bench warmup")
+    mlp_events.clear()
+    pairs = cfg.tokens * cfg.top_k
+    launches0 = layer.kernel_launches
+
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        t_start.record()
+        for _ in range(args.steps):
+            layer.forward(hidden, logits)
+        t_end.record()
+        barrier()
+    layer.check_device_errors("bench")
+    ms_total = t_start.elapsed_time(t_end)
+    launches = layer.kernel_launches - launches0
+    mlp_ms = statistics.mean(s.elapsed_time(e) for s, e in mlp_events)
+    waves = len(layer.resident_wave_plan())
+
+    if dist is not None:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = world * cfg.tokens * args.steps / (ms_total / 1e3)
+
+    flops_call = pairs * cfg.flops_per_pair
+    achieved_tflops = flops_call / (mlp_ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved_tflops, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved_tflops / peaks["bf16_tflops"],
+                "frac_of_sustained": achieved_tflops / peaks["bf16_tflops_sustained"],
+                "peak_source": peaks["source"], "traffic": None,
+                "kernel": "umma_grouped_kernel x2 (gate_up+SiLU*mul, down) per lm_moe_mlp_prefill",
+                "ms_per_call": mlp_ms, "flops_per_call": flops_call}
+    if cfg.tokens == syn.CONFIGS[CONFIG_NAME].tokens:
+        roofline["traffic"] = _profiled_traffic("umma_grouped_kernel_c2_t4096.md")
+        roofline["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum, " \
+                                     "both launches of one call"
+    del layer
+    torch.cuda.empty_cache()
+    return value, ms_step, roofline, int(launches), waves, clocks
+
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -252,8 +356,18 @@ def main() -> None:
     ap.add_argument("--no-tpot", action="store_true", help="skip the 48-layer decode TPOT section")
     ap.add_argument("--tokens", type=int, default=0,
                     help="profiling override of the layer's token count (default: the config's)")
+    ap.add_argument("--sections", default="all",
+                    help="comma list of value,decode,tpot,e2e,ep,cpu (profiling runs use one)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    every = {"value", "decode", "tpot", "e2e", "ep", "cpu"}
+    sec = every if args.sections == "all" else set(args.sections.split(","))
+    if not sec <= every:
+        ap.error(f"unknown sections {sorted(sec - every)}")
+    if args.no_tpot:
+        sec.discard("tpot")
+    if args.no_cpu_baseline:
+        sec.discard("cpu")
 
     from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
 
@@ -304,124 +418,77 @@ def main() -> None:
                            num_experts=cfg.num_experts, top_k=cfg.top_k, max_tokens=cfg.tokens,
                            renormalize=cfg.renormalize, device=dev)
 
-    # ----------------------------------------------------------------- value (HBM inputs)
-    layer = make_layer(True)
-    hidden = hidden_cpu.to(dev)
-    logits = logits_cpu.to(dev)
-    mlp_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
-    orig = layer._grouped_mlp
-
-    def timed_mlp(*a, **kw):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        orig(*a, **kw)
-        e.record()
-        mlp_events.append((s, e))
-
-    layer._grouped_mlp = timed_mlp
-    for _ in range(args.warmup):
-        layer.forward(hidden, logits)
-    torch.cuda.synchronize()
-    layer.check_device_errors("bench warmup")
-    mlp_events.clear()
-    pairs = cfg.tokens * cfg.top_k
-    launches0 = layer.kernel_launches
-
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        barrier()
-        t_start.record()
-        for _ in range(args.steps):
-            layer.forward(hidden, logits)
-        t_end.record()
-        barrier()
-    layer.check_device_errors("bench")
-    ms_total = t_start.elapsed_time(t_end)
-    launches = layer.kernel_launches - launches0
-    mlp_ms = statistics.mean(s.elapsed_time(e) for s, e in mlp_events)
-    waves = len(layer.resident_wave_plan())
-
-    if dist is not None:
-        t = torch.tensor([ms_total], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
-    ms_step = ms_total / args.steps
-    value = world * cfg.tokens * args.steps / (ms_total / 1e3)
-
-    flops_call = pairs * cfg.flops_per_pair
-    achieved_tflops = flops_call / (mlp_ms / 1e3) / 1e12
-    roofline = {"bound": "tensor", "achieved": achieved_tflops, "peak": peaks["bf16_tflops"],
-                "unit": "TFLOP/s", "frac": achieved_tflops / peaks["bf16_tflops"],
-                "frac_of_sustained": achieved_tflops / peaks["bf16_tflops_sustained"],
-                "peak_source": peaks["source"], "traffic": None,
-                "kernel": "umma_grouped_kernel x2 (gate_up+SiLU*mul, down) per lm_moe_mlp_prefill",
-                "ms_per_call": mlp_ms, "flops_per_call": flops_call}
-    prof = ROOT / "profiles" / "traffic_umma_c2.json"
-    if prof.exists():
-        roofline["traffic"] = json.loads(prof.read_text()).get("bytes_per_call")
-    del layer
-    torch.cuda.empty_cache()
-
+    # ----------------------------------------------------------------- value (HBM inputs)
+    hidden = hidden_cpu.to(dev)
+    logits = logits_cpu.to(dev)
+    value = ms_step = roofline = None
+    launches = waves = 0
+    clocks = ClockSampler(local_rank)
+    if "value" in sec:
+        value, ms_step, roofline, launches, waves, clocks = run_value(
+            args, cfg, make_layer, hidden, logits, dist, dev, world, local_rank, peaks, barrier)
     # ----------------------------------------------------------------- decode layer (C1)
-    dcfg = syn.CONFIGS["c1_decode"]
-    drt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=dcfg.num_slots,
-                                             async_load=True, b2_wave_prefill=True))
-    drt.register_layer_for_fixed_slots(ExpertLayer(0, w13, w2), slot_device=dev, store_device=dev)
-    dl = SlotBankMoE(drt, 0, hidden_size=dcfg.hidden, intermediate_size=dcfg.intermediate,
-                     num_experts=dcfg.num_experts, top_k=dcfg.top_k, max_tokens=dcfg.tokens,
-                     device=dev)
-    dh = syn.make_hidden(dcfg, seed=rank).to(dev)
-    dlg = syn.make_router_logits(dcfg, seed=rank).to(dev)
-    d_events: list = []
-    d_orig = dl._grouped_mlp
+    decode = None
+    if "decode" in sec:
+        dcfg = syn.CONFIGS["c1_decode"]
+        drt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=dcfg.num_slots,
+                                                 async_load=True, b2_wave_prefill=True))
+        drt.register_layer_for_fixed_slots(ExpertLayer(0, w13, w2), slot_device=dev, store_device=dev)
+        dl = SlotBankMoE(drt, 0, hidden_size=dcfg.hidden, intermediate_size=dcfg.intermediate,
+                         num_experts=dcfg.num_experts, top_k=dcfg.top_k, max_tokens=dcfg.tokens,
+                         device=dev)
+        dh = syn.make_hidden(dcfg, seed=rank).to(dev)
+        dlg = syn.make_router_logits(dcfg, seed=rank).to(dev)
+        d_events: list = []
+        d_orig = dl._grouped_mlp
 
-    def d_timed(*a, **kw):
+        def d_timed(*a, **kw):
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            d_orig(*a, **kw)
+            e0.record()
+            d_events.append((s0, e0))
+
+        dl._grouped_mlp = d_timed
+        for _ in range(args.warmup):
+            dl.forward(dh, dlg)
+        torch.cuda.synchronize()
+        d_events.clear()
+        d_steps = 50
         s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s0.record()
-        d_orig(*a, **kw)
+        for _ in range(d_steps):
+            dl.forward(dh, dlg)
         e0.record()
-        d_events.append((s0, e0))
+        torch.cuda.synchronize()
+        dl.check_device_errors("bench decode")
+        from vllm_ascend_hust_latchmoe_b200.moe_offload.phase_split import plan_balanced_b2_waves
 
-    dl._grouped_mlp = d_timed
-    for _ in range(args.warmup):
-        dl.forward(dh, dlg)
-    torch.cuda.synchronize()
-    d_events.clear()
-    d_steps = 50
-    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record()
-    for _ in range(d_steps):
-        dl.forward(dh, dlg)
-    e0.record()
-    torch.cuda.synchronize()
-    dl.check_device_errors("bench decode")
-    from vllm_ascend_hust_latchmoe_b200.moe_offload.phase_split import plan_balanced_b2_waves
-
-    d_counts = torch.bincount(dl.topk_ids[: dcfg.tokens].reshape(-1).long().cpu(),
-                              minlength=dcfg.num_experts).tolist()
-    d_active = sum(1 for c in d_counts if c > 0)
-    d_plan = plan_balanced_b2_waves({e: c for e, c in enumerate(d_counts) if c}, dcfg.num_slots).waves
-    d_mlp_ms = statistics.mean(a.elapsed_time(b) for a, b in d_events)
-    d_bytes = d_active * dcfg.expert_bytes
-    decode = {"workload": dcfg.name, "layer_ms": s0.elapsed_time(e0) / d_steps,
-              "mlp_ms": d_mlp_ms, "active_experts": d_active,
-              "waves_if_staged": len(d_plan),
-              "tier": "HBM-resident experts read in place (grouped by expert id)",
-              "mlp_hbm_gbs": d_bytes / (d_mlp_ms / 1e3) / 1e9,
-              "mlp_frac_hbm": d_bytes / (d_mlp_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
-              "algorithmic_bytes_per_call": d_bytes,
-              "kernel": "gemv_gate_up_kernel + gemv_down_kernel (lm_moe_mlp_decode)"}
-    del dl, drt
-    torch.cuda.empty_cache()
+        d_counts = torch.bincount(dl.topk_ids[: dcfg.tokens].reshape(-1).long().cpu(),
+                                  minlength=dcfg.num_experts).tolist()
+        d_active = sum(1 for c in d_counts if c > 0)
+        d_plan = plan_balanced_b2_waves({e: c for e, c in enumerate(d_counts) if c}, dcfg.num_slots).waves
+        d_mlp_ms = statistics.mean(a.elapsed_time(b) for a, b in d_events)
+        d_bytes = d_active * dcfg.expert_bytes
+        decode = {"workload": dcfg.name, "layer_ms": s0.elapsed_time(e0) / d_steps,
+                  "mlp_ms": d_mlp_ms, "active_experts": d_active,
+                  "waves_if_staged": len(d_plan),
+                  "tier": "HBM-resident experts read in place (grouped by expert id)",
+                  "mlp_hbm_gbs": d_bytes / (d_mlp_ms / 1e3) / 1e9,
+                  "mlp_frac_hbm": d_bytes / (d_mlp_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                  "algorithmic_bytes_per_call": d_bytes,
+                  "kernel": "gemv_gate_up_kernel + gemv_down_kernel (lm_moe_mlp_decode)"}
+        del dl, drt
+        torch.cuda.empty_cache()
 
     # ----------------------------------------------------------------- decode TPOT (C3)
     tpot = None
-    if not args.no_tpot:
+    if "tpot" in sec:
         from vllm_ascend_hust_latchmoe_b200.decode_harness import DecoderShape, SyntheticMoEDecoder
 
         shape = DecoderShape()
@@ -449,57 +516,60 @@ def main() -> None:
                 "data": "random-init weights and KV; synthetic routing"}
 
     # ----------------------------------------------------------------- e2e (host buffers)
-    off = make_layer(False)
-    h_host = hidden_cpu.pin_memory()
-    lg_host = logits_cpu.pin_memory()
-    out_host = torch.empty(cfg.tokens, cfg.hidden, dtype=torch.bfloat16, pin_memory=True)
-    h_dev = torch.empty_like(hidden)
-    lg_dev = torch.empty_like(logits)
+    e2e = None
+    if "e2e" in sec:
+        off = make_layer(False)
+        h_host = hidden_cpu.pin_memory()
+        lg_host = logits_cpu.pin_memory()
+        out_host = torch.empty(cfg.tokens, cfg.hidden, dtype=torch.bfloat16, pin_memory=True)
+        h_dev = torch.empty_like(hidden)
+        lg_dev = torch.empty_like(logits)
 
-    def e2e_step():
-        h_dev.copy_(h_host, non_blocking=True)
-        lg_dev.copy_(lg_host, non_blocking=True)
-        out = off.forward(h_dev, lg_dev)
-        out_host.copy_(out, non_blocking=True)
+        def e2e_step():
+            h_dev.copy_(h_host, non_blocking=True)
+            lg_dev.copy_(lg_host, non_blocking=True)
+            out = off.forward(h_dev, lg_dev)
+            out_host.copy_(out, non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    staged0 = off.runtime.transfer_engine.stats.bytes_h2d
-    e2e_steps = max(3, min(args.steps, 10))
-    barrier()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e.record()
-    barrier()
-    off.check_device_errors("bench e2e")
-    e2e_ms = s.elapsed_time(e)
-    staged = (off.runtime.transfer_engine.stats.bytes_h2d - staged0) / e2e_steps
-    if dist is not None:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * cfg.tokens * e2e_steps / (e2e_ms / 1e3)
-    io_in = h_host.numel() * 2 + lg_host.numel() * 4
-    e2e = {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(io_in + staged),
-           "d2h_bytes_per_step": int(out_host.numel() * 2),
-           "h2d_breakdown": {"activations_and_logits": int(io_in), "expert_staging": int(staged)},
-           "h2d_gbs": (io_in + staged) / (e2e_ms / e2e_steps / 1e3) / 1e9,
-           "pcie_gen5_x16_gbs": 64.0, "ms_per_step": e2e_ms / e2e_steps}
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        staged0 = off.runtime.transfer_engine.stats.bytes_h2d
+        e2e_steps = max(3, min(args.steps, 10))
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e.record()
+        barrier()
+        off.check_device_errors("bench e2e")
+        e2e_ms = s.elapsed_time(e)
+        staged = (off.runtime.transfer_engine.stats.bytes_h2d - staged0) / e2e_steps
+        if dist is not None:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e_value = world * cfg.tokens * e2e_steps / (e2e_ms / 1e3)
+        io_in = h_host.numel() * 2 + lg_host.numel() * 4
+        e2e = {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(io_in + staged),
+               "d2h_bytes_per_step": int(out_host.numel() * 2),
+               "h2d_breakdown": {"activations_and_logits": int(io_in), "expert_staging": int(staged)},
+               "h2d_gbs": (io_in + staged) / (e2e_ms / e2e_steps / 1e3) / 1e9,
+               "pcie_gen5_x16_gbs": 64.0, "ms_per_step": e2e_ms / e2e_steps}
 
     # ----------------------------------------------------------------- expert parallel (C5)
     ep_report = None
-    if dist is not None:
+    if dist is not None and "ep" in sec:
         ep_report = run_expert_parallel(dist, rank, world, dev, args)
+    if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
 
     cpu = None
-    if not args.no_cpu_baseline:
+    if "cpu" in sec:
         sample = args.cpu_sample_tokens
         w13b, w2b, hid, lg = cpu_inputs(cfg, sample)
         cpu_reference_step(cfg, sample, w13b, w2b, hid, lg)

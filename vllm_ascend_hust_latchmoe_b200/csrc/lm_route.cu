@@ -254,20 +254,47 @@ __global__ void __launch_bounds__(kGroupTile)
 }
 
 // Pass 2 (one block): per-group exclusive scan over tiles, then exclusive scan over groups.
+// The tiles of each group are split into chunks, one thread per (group, chunk), so that a
+// thread has a short, independent run of loads: chunk sums, a scan over each group's
+// chunks, then each thread rewrites its chunk as exclusive tile bases.
 __global__ void __launch_bounds__(1024)
     group_scan_kernel(int32_t* __restrict__ tile_counts, int num_tiles, int num_groups,
                       int32_t* __restrict__ tile_base, int32_t* __restrict__ group_offsets) {
   __shared__ int32_t s_tot[kMaxGroups];
   __shared__ int32_t s_warp[32];
+  __shared__ int32_t s_part[1024];
+  const int chunks = max(1, static_cast<int>(blockDim.x) / num_groups);
+  const int chunk_len = (num_tiles + chunks - 1) / chunks;
+  for (int i = threadIdx.x; i < chunks * num_groups; i += blockDim.x) {
+    const int g = i % num_groups, c = i / num_groups;
+    const int t0 = c * chunk_len, t1 = min(num_tiles, t0 + chunk_len);
+    int sum = 0;
+#pragma unroll 8
+    for (int t = t0; t < t1; ++t) sum += tile_counts[static_cast<int64_t>(t) * num_groups + g];
+    s_part[i] = sum;
+  }
+  __syncthreads();
   for (int g = threadIdx.x; g < num_groups; g += blockDim.x) {
     int run = 0;
-    for (int t = 0; t < num_tiles; ++t) {
-      const int64_t o = static_cast<int64_t>(t) * num_groups + g;
-      const int c = tile_counts[o];
-      tile_base[o] = run;
-      run += c;
+    for (int c = 0; c < chunks; ++c) {
+      const int v = s_part[c * num_groups + g];
+      s_part[c * num_groups + g] = run;
+      run += v;
     }
     s_tot[g] = run;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < chunks * num_groups; i += blockDim.x) {
+    const int g = i % num_groups, c = i / num_groups;
+    const int t0 = c * chunk_len, t1 = min(num_tiles, t0 + chunk_len);
+    int run = s_part[i];
+#pragma unroll 8
+    for (int t = t0; t < t1; ++t) {
+      const int64_t o = static_cast<int64_t>(t) * num_groups + g;
+      const int v = tile_counts[o];
+      tile_base[o] = run;
+      run += v;
+    }
   }
   __syncthreads();
   // Exclusive scan of s_tot[0..num_groups) with one pass of 1024 threads.
