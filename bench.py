@@ -332,7 +332,9 @@ def run_value(args, cfg, make_layer, hidden, logits, dist, dev, world, local_ran
                 "unit": "TFLOP/s", "frac": achieved_tflops / peaks["bf16_tflops"],
                 "frac_of_sustained": achieved_tflops / peaks["bf16_tflops_sustained"],
                 "peak_source": peaks["source"], "traffic": None,
-                "kernel": "umma_grouped_kernel x2 (gate_up+SiLU*mul, down) per lm_moe_mlp_prefill",
+                "kernel": "lm_moe_mlp_prefill: per GEMM (gate_up+SiLU*mul, down) a 2-SM "
+                          "umma_grouped_kernel_2sm launch (groups > 128 rows) beside a "
+                          "single-SM umma_grouped_kernel launch (groups <= 128 rows)",
                 "ms_per_call": mlp_ms, "flops_per_call": flops_call}
     if cfg.tokens == syn.CONFIGS[CONFIG_NAME].tokens:
         roofline["traffic"] = _profiled_traffic("umma_grouped_kernel_c2_t4096.md")

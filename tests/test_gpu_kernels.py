@@ -122,13 +122,15 @@ def test_histogram(cuda):
     assert err.item() == 1
 
 
-def _mlp_case(cuda, T, k, E, H, I, G, use_prefill, seed=0, skewed=False):
+def _mlp_case(cuda, T, k, E, H, I, G, use_prefill, seed=0, skewed=False, ids=None):
     rng = np.random.default_rng(seed)
     cfg = syn.LayerConfig("t", hidden=H, num_experts=E, top_k=k, intermediate=I, num_slots=G,
                           tokens=T, zipf_s=2.0)
     w13, w2 = syn.make_expert_weights(cfg, seed=seed, experts=E)
     hidden = syn.make_hidden(cfg, seed=seed)
-    if skewed:  # Zipf-biased routing: a few groups span many m-tiles, most span one
+    if ids is not None:
+        ids_np = ids
+    elif skewed:  # Zipf-biased routing: a few groups span many m-tiles, most span one
         ids_np = orouter.route(syn.make_router_logits(cfg, seed=seed).numpy(), k)[2]
     else:
         ids_np = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
@@ -190,6 +192,17 @@ def test_prefill_tcgen05_skewed_groups(cuda, T, k, E):
     _mlp_case(cuda, T, k, E, 2048, 768, 32, use_prefill=True, skewed=True)
 
 
+@pytest.mark.parametrize("H,I", [(512, 256), (2048, 768)])
+def test_prefill_group_size_boundaries(cuda, H, I):
+    """Group sizes on every boundary of the two tile kinds: groups of at most 128 rows run on
+    single-SM tiles (row loads trimmed to 16 / 32 / 64 / 128), larger ones on 256-row 2-SM
+    tiles; 1-row, exact-multiple and one-past groups."""
+    sizes = [1, 15, 16, 17, 31, 32, 33, 63, 64, 65, 100, 127, 128, 129, 255, 256, 257, 300, 513]
+    ids = np.concatenate([np.full(n, e, dtype=np.int32) for e, n in enumerate(sizes)])
+    ids = np.random.default_rng(5).permutation(ids).reshape(-1, 1)
+    _mlp_case(cuda, ids.shape[0], 1, len(sizes), H, I, 32, use_prefill=True, ids=ids)
+
+
 def test_stage_copy_coalesces_runs(cuda):
     src = torch.arange(10 * 64, dtype=torch.float32).reshape(10, 64).pin_memory()
     dst = torch.zeros(6, 64, dtype=torch.float32, device=cuda)
@@ -231,18 +244,19 @@ def test_device_wave_planner_matches_reference_golden(cuda):
         assert [r[off[w]:off[w + 1]] for w in range(n)] == [list(range(len(w))) for w in case["waves"]]
 
 
-def test_prefill_two_sm_tiles_match_oracle_in_subprocess(cuda):
-    """The cta_group::2 (256-row, 2-SM) tiles, selected per process by LM_UMMA_CTA_PAIR=2,
-    pass the same tcgen05 parity cases."""
+def test_prefill_single_sm_tiles_match_oracle_in_subprocess(cuda):
+    """Every group on single-SM tiles over all SMs (LM_UMMA_CTA_PAIR=1, set per process; the
+    default splits the groups between 2-SM and single-SM tiles) passes the same parity
+    cases."""
     import os
     import subprocess
     import sys
     from pathlib import Path
 
     root = Path(__file__).resolve().parents[1]
-    env = dict(os.environ, LM_UMMA_CTA_PAIR="2")
+    env = dict(os.environ, LM_UMMA_CTA_PAIR="1")
     proc = subprocess.run(
         [sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", "-m", "gpu",
-         str(root / "tests" / "test_gpu_kernels.py"), "-k", "prefill_tcgen05"],
+         str(root / "tests" / "test_gpu_kernels.py"), "-k", "prefill_tcgen05 or boundaries"],
         cwd=root, env=env, capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]

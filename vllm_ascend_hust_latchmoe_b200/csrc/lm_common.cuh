@@ -114,6 +114,14 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(desc) : "memory");
 }
 
+// Prefetch a 3D box of a tensor map into L2 (no shared memory, no completion signal).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* desc, int32_t x, int32_t y,
+                                                   int32_t z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(desc),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* desc, uint64_t* bar,
                                             int32_t x, int32_t y) {
   asm volatile(

@@ -1,26 +1,39 @@
 // Prefill path of the grouped expert MLP on the 5th-generation tensor cores (tcgen05).
 //
-// One persistent kernel runs both GEMMs of the expert MLP (selected by `mode`):
+// Persistent kernels run both GEMMs of the expert MLP (selected by `mode`):
 //   mode 0 (gate_up): act[r, n0:n0+128] = silu(X_r . W13[n0:n0+128]) * (X_r . W13[I+n0:...])
 //                     MMA N = 256 = 128 gate rows + the 128 matching up rows, so the fused
 //                     SiLU*mul epilogue has both halves of every output column in TMEM.
 //   mode 1 (down):    y[r, n0:n0+256] = act_r . W2[n0:n0+256]
-// Tiles: 128 rows x 256 MMA columns x 64-wide K steps (one 128-byte swizzle row of bf16).
-// Warp roles (192 threads): warp 0 issues TMA loads into a 4-stage smem ring, warp 1 issues
-// tcgen05.mma into one of two TMEM accumulators (2 x 256 fp32 columns = all 512 columns),
-// warps 2-5 drain the other accumulator (tcgen05.ld -> epilogue -> global stores), so the
-// epilogue of tile i overlaps the MMAs of tile i+1.
-// Tile order: groups with several m-tiles ("heavy": their weight tiles are reused from L2,
-// so their tiles are tensor-bound) and single-m-tile groups ("light": every weight tile is
-// read from DRAM once, so their tiles are HBM-bound) form two lists, each enumerated
-// (group, m-tile, n-tile) with n fastest, and the two lists are merged in proportion. CTAs
-// running at the same time then mix both kinds, overlapping weight streaming with MMAs.
-// The tile lists are derived on the device from group_offsets, so the launch itself is
-// independent of the routing.
+//
+// Measured on B200, these facts shape the kernels:
+//  * a tcgen05.mma of K = 16 costs about the same time for any N up to 256, and with
+//    cta_group::2 each SM supplies only half of the instruction's N rows;
+//  * one thread issues TMA loads at a limited rate, and each pipeline stage hand-off has a
+//    fixed cost, whatever the bytes moved.
+// So the groups of a call are split by size. Groups of more than LIGHT_MAX_ROWS rows
+// ("heavy": each weight tile serves many rows; tensor-bound) run on 2-SM tiles of
+// 256 x 256 (umma_grouped_kernel_2sm, cta_group::2; per K block each SM loads 32 KiB for
+// 128 x 256 MMA work). The other groups ("light": bound by streaming their weights) run on
+// single-SM tiles of 128 x 256 (umma_grouped_kernel), where one instruction consumes 256
+// weight rows per SM and only the group's rows of A are loaded. The two kinds are launched
+// on two streams, both with one CTA per SM; each launch derives the same split of the SMs
+// from group_offsets (in proportion to the estimated SM time of each kind), and CTAs beyond
+// their launch's share leave at once, handing their SMs to the other launch. With
+// LM_UMMA_CTA_PAIR=1 every group runs on the single-SM kernel over all SMs.
+//
+// Loads of a stage are issued by several lanes at once (one TMA load each), and two producer
+// warps take the stages in turn. Warp roles (224 threads): warps 0 and 6 issue TMA loads into
+// the smem ring, warp 1 issues tcgen05.mma into one of two TMEM accumulators (2 x 256 fp32
+// columns = all 512 columns), warps 2-5 drain the other accumulator (tcgen05.ld -> epilogue
+// -> global stores), so the epilogue of tile i overlaps the MMAs of tile i+1. The tile list
+// (group, m-tile, n-tile; n fastest) is derived on the device from group_offsets, so the
+// launches are independent of the routing.
 // No TMA load uses cluster multicast; every operand is this GPU's own memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
 #include <vector>
@@ -33,31 +46,44 @@ namespace {
 constexpr int BM = 128;   // rows per CTA (TMEM lanes)
 constexpr int BN = 256;   // MMA N (mode 0: 128 gate + 128 up rows; mode 1: 256 outputs)
 constexpr int BK = 64;    // one 128-byte swizzle row of bf16
-constexpr int A_BYTES = BM * BK * 2;      // 16 KiB
-constexpr int B_TILE_BYTES = 128 * BK * 2;  // one 128-row weight tile, 16 KiB
+constexpr int KB_BYTES = BM * BK * 2;  // one 128-row x 64 K block, 16 KiB
 constexpr int TMEM_COLS = 512;
 constexpr int MAX_G = 256;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 224;  // warps 0, 6: TMA; 1: MMA; 2-5: epilogue
+constexpr int NUM_PRODUCERS = 2;
+constexpr int MAX_STAGES = 4;
+constexpr int LIGHT_MAX_ROWS = 128;  // larger groups run on 2-SM tiles
+// Single-SM tiles prefetch their weight tiles into L2 this many K blocks ahead of the loads
+// (even): light tiles stream weights from DRAM, and the prefetches keep more bytes in
+// flight than the shared-memory ring can hold.
+constexpr int PREFETCH_KB = 8;
 
-// PAIR = 1: one CTA owns a 128-row tile and loads the whole 256-row B tile.
-// PAIR = 2: a cluster of two CTAs owns a 256-row tile (M = 256, cta_group::2); each CTA
-// loads its own 128 A rows and one 128-row half of B, the leader issues the MMAs.
+enum : int32_t { ROLE_HEAVY = 0, ROLE_LIGHT = 1, ROLE_ALL = 2 };
+
+// PAIR = 1: one CTA owns a 128-row tile; a stage is one K block: its rows (16 KiB at most)
+// and the 256 weight rows (both 128-row tiles, 32 KiB).
+// PAIR = 2: a cluster of two CTAs owns a 256-row tile (M = 256, cta_group::2); a stage is two
+// K blocks: each CTA's 128 rows (32 KiB) and its one weight tile (32 KiB); the leader issues
+// the MMAs.
 template <int PAIR>
 struct Cfg {
-  static constexpr int STAGE_BYTES = A_BYTES + (PAIR == 1 ? 2 : 1) * B_TILE_BYTES;
-  static constexpr int STAGES = PAIR == 1 ? 4 : 6;
+  static constexpr int KB_STAGE = PAIR == 1 ? 1 : 2;
+  static constexpr int A_BYTES = KB_STAGE * KB_BYTES;
+  static constexpr int B_BYTES = KB_STAGE * KB_BYTES * (PAIR == 1 ? 2 : 1);
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = PAIR == 1 ? 4 : 3;
   static constexpr int UNIT_ROWS = BM * PAIR;
 };
 
 struct SmemCtl {
-  uint64_t full[6];
-  uint64_t empty[6];
+  uint64_t full[MAX_STAGES];
+  uint64_t empty[MAX_STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint32_t tmem_base;
   int abort_flag;
-  int hprefix[MAX_G + 1];  // unit-tiles of heavy groups before group i
-  int lprefix[MAX_G + 1];  // light groups (exactly one unit-tile) before group i
+  int units_other;         // unit-tiles of the other kind (heavy / light split)
+  int prefix[MAX_G + 1];   // unit-tiles of this launch's groups before group i
   int row0[MAX_G];
   int nrows[MAX_G];
   int bank[MAX_G];
@@ -69,8 +95,9 @@ constexpr int smem_bytes() {
 }
 
 struct UmmaParams {
-  CUtensorMap tmap_a;  // A rows [R, K] bf16, box {64, 128}
-  CUtensorMap tmap_b;  // weight tiles [bank_rows * N/128 * K/64][128][64], box {64, 128, 1}
+  CUtensorMap tmap_a[4];  // A rows [R, K] bf16, boxes {64, 16 / 32 / 64 / 128}
+  CUtensorMap tmap_w2;    // weight tiles [tiles][128][64], box {64, 128, 2}: K blocks kb, kb+1
+  CUtensorMap tmap_w1;    // the same tiles, box {64, 128, 1}
   const int32_t* group_offsets;
   const int32_t* group_bank_row;
   uint16_t* out;
@@ -84,6 +111,10 @@ struct UmmaParams {
   int32_t out_ld;    // output row stride (elements)
   int32_t bank_rows;
   int32_t w_ntiles;  // 128-row tiles per expert matrix (N / 128)
+  int32_t role;      // ROLE_HEAVY (2-SM kernel), ROLE_LIGHT or ROLE_ALL (1-SM kernel)
+  int32_t split_sms;         // SMs shared by the heavy and the light launch
+  int32_t heavy_tile_cost;   // estimated SM time of a heavy tile, per SM of the pair
+  int32_t light_tile_cost;   // estimated SM time of a light tile
 };
 
 struct TileCoord {
@@ -106,32 +137,25 @@ __device__ __forceinline__ int find_group(const int* prefix, int v, int G) {
   return lo;
 }
 
-// Position t of the merged order -> (group, unit-tile, n-tile). Heavy tiles before position
-// t: floor(t * Th / T); t is heavy iff that count grows at t + 1.
+// Position t of the tile list -> (group, unit-tile, n-tile).
 __device__ __forceinline__ TileCoord decode_tile(const SmemCtl& c, int t, int n_tiles, int G,
-                                                 int heavy_tiles, int total_tiles, int unit) {
-  const long long th = heavy_tiles, tt = total_tiles;
-  const int hb = static_cast<int>((static_cast<long long>(t) * th) / tt);
-  const int hb1 = static_cast<int>((static_cast<long long>(t + 1) * th) / tt);
+                                                 int unit) {
   TileCoord tc;
-  int g, ml;
-  if (hb1 > hb) {
-    const int mg = hb / n_tiles;
-    tc.nt = hb - mg * n_tiles;
-    g = find_group(c.hprefix, mg, G);
-    ml = mg - c.hprefix[g];
-  } else {
-    const int li = t - hb;
-    const int mg = li / n_tiles;
-    tc.nt = li - mg * n_tiles;
-    g = find_group(c.lprefix, mg, G);
-    ml = 0;
-  }
+  const int mg = t / n_tiles;
+  tc.nt = t - mg * n_tiles;
+  const int g = find_group(c.prefix, mg, G);
+  const int ml = mg - c.prefix[g];
   tc.g = g;
   tc.row0 = c.row0[g] + ml * unit;
   const int rem = c.nrows[g] - ml * unit;
   tc.valid = rem < unit ? rem : unit;
   return tc;
+}
+
+// Rows of A loaded for a single-SM tile: the tile's rows rounded up to 16 / 32 / 64 / 128
+// (the rest of the 128-row operand is left as it is; those accumulator rows are not stored).
+__device__ __forceinline__ int a_box_index(int valid) {
+  return valid <= 16 ? 0 : valid <= 32 ? 1 : valid <= 64 ? 2 : 3;
 }
 
 __device__ __forceinline__ void store_row_chunk(uint16_t* dst, const uint32_t (&packed)[16]) {
@@ -140,6 +164,29 @@ __device__ __forceinline__ void store_row_chunk(uint16_t* dst, const uint32_t (&
   d[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
   d[2] = make_uint4(packed[8], packed[9], packed[10], packed[11]);
   d[3] = make_uint4(packed[12], packed[13], packed[14], packed[15]);
+}
+
+// Clusters of a launch that take tiles. For the heavy / light pair of launches both compute
+// the same split of split_sms SMs from the same inputs.
+__device__ __forceinline__ int active_clusters(const UmmaParams& p, int own_units,
+                                               int other_units, int num_clusters) {
+  if (p.role == ROLE_ALL) return num_clusters;
+  const long long ht =
+      static_cast<long long>(p.role == ROLE_HEAVY ? own_units : other_units) * p.n_tiles;
+  const long long lt =
+      static_cast<long long>(p.role == ROLE_LIGHT ? own_units : other_units) * p.n_tiles;
+  const int sms = p.split_sms;
+  const long long wh = ht * 2 * p.heavy_tile_cost, wl = lt * p.light_tile_cost;
+  long long heavy_sms = wh + wl > 0 ? (sms * wh + (wh + wl) / 2) / (wh + wl) : 0;
+  heavy_sms &= ~1ll;
+  if (heavy_sms > 2 * ht) heavy_sms = 2 * ht;                       // no more pairs than tiles
+  if (sms - heavy_sms > lt) heavy_sms = (sms - lt + 1) & ~1ll;      // no more SMs than tiles
+  if (heavy_sms > 2 * ht) heavy_sms = 2 * ht;
+  if (ht > 0 && heavy_sms < 2) heavy_sms = 2;
+  if (lt > 0 && heavy_sms > ((sms - 1) & ~1)) heavy_sms = (sms - 1) & ~1;
+  long long active = p.role == ROLE_HEAVY ? heavy_sms / 2 : sms - heavy_sms;
+  if (active > num_clusters) active = num_clusters;
+  return static_cast<int>(active);
 }
 
 template <int PAIR>
@@ -156,6 +203,7 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
   const bool leader = rank == 0;
   const int cluster_id = blockIdx.x / PAIR;
   const int num_clusters = gridDim.x / PAIR;
+  const int ksteps = p.k_blocks / C::KB_STAGE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -169,9 +217,59 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
     c.abort_flag = 0;
     fence_mbarrier_init();
   }
+  for (int i = threadIdx.x; i < G; i += NUM_THREADS) {
+    const int g = p.group_begin + i;
+    const int r0 = p.group_offsets[g];
+    int n = p.group_offsets[g + 1] - r0;
+    int bank = p.group_bank_row[g];
+    if (n > 0 && (bank < 0 || bank >= p.bank_rows)) {
+      if (p.role != ROLE_LIGHT) record_error(p.err_word, LM_DEVERR_BAD_GROUP);
+      n = 0;
+      bank = 0;
+    }
+    c.row0[i] = r0;
+    c.nrows[i] = n > 0 ? n : 0;
+    c.bank[i] = bank;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // prefix of unit-tiles over this launch's groups; unit-tiles of the other kind
+    int carry = 0, other = 0;
+    for (int base = 0; base < G; base += 32) {
+      const int i = base + lane;
+      const int n = (i < G) ? c.nrows[i] : 0;
+      const bool heavy = n > LIGHT_MAX_ROWS;
+      const bool mine =
+          n > 0 && (p.role == ROLE_ALL || (p.role == ROLE_HEAVY) == heavy);
+      int v = mine ? (n + C::UNIT_ROWS - 1) / C::UNIT_ROWS : 0;
+      if (!mine && n > 0 && p.role != ROLE_ALL) other += heavy ? (n + 2 * BM - 1) / (2 * BM) : 1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (i < G) c.prefix[i + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) other += __shfl_xor_sync(0xffffffffu, other, o);
+    if (lane == 0) {
+      c.prefix[0] = 0;
+      c.units_other = other;
+    }
+  }
+  __syncthreads();
+
+  const int total_tiles = c.prefix[G] * p.n_tiles;
+  const int active = active_clusters(p, c.prefix[G], c.units_other, num_clusters);
+  // Both CTAs of a cluster reach the same decision; an idle CTA leaves before taking TMEM,
+  // so its SM goes to the other launch right away.
+  if (cluster_id >= active || total_tiles == 0) return;
+
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&p.tmap_a);
-    tma_prefetch_desc(&p.tmap_b);
+    for (int i = 0; i < 4; ++i) tma_prefetch_desc(&p.tmap_a[i]);
+    tma_prefetch_desc(&p.tmap_w2);
+    tma_prefetch_desc(&p.tmap_w1);
   }
   if (warp == 1) {
     if (PAIR == 2) {
@@ -182,100 +280,89 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
       tmem_relinquish();
     }
   }
-  for (int i = threadIdx.x; i < G; i += NUM_THREADS) {
-    const int g = p.group_begin + i;
-    const int r0 = p.group_offsets[g];
-    int n = p.group_offsets[g + 1] - r0;
-    int bank = p.group_bank_row[g];
-    if (n > 0 && (bank < 0 || bank >= p.bank_rows)) {
-      record_error(p.err_word, LM_DEVERR_BAD_GROUP);
-      n = 0;
-      bank = 0;
-    }
-    c.row0[i] = r0;
-    c.nrows[i] = n > 0 ? n : 0;
-    c.bank[i] = bank;
-  }
-  __syncthreads();
-  if (warp < 2) {
-    // warp 0: prefix of heavy unit-tiles; warp 1: prefix of light groups.
-    int* prefix = warp == 0 ? c.hprefix : c.lprefix;
-    int carry = 0;
-    for (int base = 0; base < G; base += 32) {
-      const int i = base + lane;
-      const int mt = (i < G) ? (c.nrows[i] + C::UNIT_ROWS - 1) / C::UNIT_ROWS : 0;
-      int v = warp == 0 ? (mt >= 2 ? mt : 0) : (mt == 1 ? 1 : 0);
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += t;
-      }
-      if (i < G) prefix[i + 1] = carry + v;
-      carry += __shfl_sync(0xffffffffu, v, 31);
-    }
-    if (lane == 0) prefix[0] = 0;
-  }
   tc_fence_before();
   __syncthreads();
   if (PAIR == 2) cluster_sync_all();  // peer barriers initialised, both TMEM halves allocated
   tc_fence_after();
-
   const uint32_t tmem_base = c.tmem_base;
-  const int heavy_tiles = c.hprefix[G] * p.n_tiles;
-  const int total_tiles = heavy_tiles + c.lprefix[G] * p.n_tiles;
   volatile int* abort_flag = &c.abort_flag;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued_parity[6];
-      for (int s = 0; s < 6; ++s) issued_parity[s] = -1;
-      bool ok = true;
-      for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
-        const TileCoord tc = decode_tile(c, t, p.n_tiles, G, heavy_tiles, total_tiles,
-                                         C::UNIT_ROWS);
-        // Tile index of (expert row, 128-row tile, k block) in the tile-contiguous bank.
-        const int ebase = c.bank[tc.g] * p.w_ntiles;
-        const int nt0 = p.mode == 0 ? tc.nt : 2 * tc.nt;
-        const int nt1 = p.mode == 0 ? p.up_tile + tc.nt : 2 * tc.nt + 1;
-        const int a_row = tc.row0 + static_cast<int>(rank) * BM;
-        const int my_nt = rank == 0 ? nt0 : nt1;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait_bounded(&c.empty[stage], phase ^ 1u, p.err_word, abort_flag)) {
-            ok = false;
-            break;
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------------------ TMA producers
+    // Producer pw issues the pipeline steps seq with seq % 2 == pw (a step = one stage of one
+    // tile); lane i of the warp issues the i-th load of the step.
+    const int pw = warp == 0 ? 0 : 1;
+    int seq = 0;
+    bool ok = true;
+    for (int t = cluster_id; t < total_tiles && ok; t += active) {
+      const TileCoord tc = decode_tile(c, t, p.n_tiles, G, C::UNIT_ROWS);
+      const int ebase = c.bank[tc.g] * p.w_ntiles;
+      // weight tiles of the n-tile: gate / up (mode 0) or two consecutive W2 tiles (mode 1)
+      const int wt0 = ebase + (p.mode == 0 ? tc.nt : 2 * tc.nt);
+      const int wt1 = ebase + (p.mode == 0 ? p.up_tile + tc.nt : 2 * tc.nt + 1);
+      const int abox = PAIR == 1 ? a_box_index(tc.valid) : 3;
+      const uint32_t bytes = PAIR == 2 ? C::STAGE_BYTES : (16u << abox) * BK * 2 + C::B_BYTES;
+      for (int ks = 0; ks < ksteps; ++ks, ++seq) {
+        if (seq % NUM_PRODUCERS != pw) continue;
+        const int stage = seq % C::STAGES;
+        const uint32_t phase = static_cast<uint32_t>(seq / C::STAGES) & 1u;
+        bool got = true;
+        if (lane == 0) got = mbar_wait_bounded(&c.empty[stage], phase ^ 1u, p.err_word, abort_flag);
+        got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+        if (!got) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + stage * C::STAGE_BYTES;
+        uint8_t* sb = sa + C::A_BYTES;
+        const int kb = ks * C::KB_STAGE;
+        if (PAIR == 2) {
+          // Both CTAs' bytes complete on the leader's barrier; only the leader arrives.
+          const uint32_t full_leader = mapa_shared(smem_u32(&c.full[stage]), 0);
+          if (lane == 0 && leader) mbar_arrive_expect_tx(&c.full[stage], 2 * bytes);
+          __syncwarp();
+          if (lane < 2) {
+            tma_load_2d_pair(sa + lane * KB_BYTES, &p.tmap_a[3], full_leader, (kb + lane) * BK,
+                             tc.row0 + static_cast<int>(rank) * BM);
+          } else if (lane == 2) {
+            const int wt = rank == 0 ? wt0 : wt1;
+            tma_load_3d_pair(sb, &p.tmap_w2, full_leader, 0, 0, wt * p.k_blocks + kb);
           }
-          uint8_t* sa = smem + stage * C::STAGE_BYTES;
-          uint8_t* sb = sa + A_BYTES;
-          if (PAIR == 1) {
-            mbar_arrive_expect_tx(&c.full[stage], C::STAGE_BYTES);
-            tma_load_2d(sa, &p.tmap_a, &c.full[stage], kb * BK, a_row);
-            tma_load_3d(sb, &p.tmap_b, &c.full[stage], 0, 0, (ebase + nt0) * p.k_blocks + kb);
-            tma_load_3d(sb + B_TILE_BYTES, &p.tmap_b, &c.full[stage], 0, 0,
-                        (ebase + nt1) * p.k_blocks + kb);
-          } else {
-            // Both CTAs' bytes complete on the leader's barrier; only the leader arrives.
-            const uint32_t full_leader = mapa_shared(smem_u32(&c.full[stage]), 0);
-            if (leader) mbar_arrive_expect_tx(&c.full[stage], 2 * C::STAGE_BYTES);
-            tma_load_2d_pair(sa, &p.tmap_a, full_leader, kb * BK, a_row);
-            tma_load_3d_pair(sb, &p.tmap_b, full_leader, 0, 0, (ebase + my_nt) * p.k_blocks + kb);
-          }
-          issued_parity[stage] = static_cast<int>(phase);
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1u;
+        } else {
+          if (lane == 0) mbar_arrive_expect_tx(&c.full[stage], bytes);
+          __syncwarp();
+          if (lane == 0) {
+            tma_load_2d(sa, &p.tmap_a[abox], &c.full[stage], kb * BK, tc.row0);
+          } else if (lane <= 2) {
+            const int wt = lane == 1 ? wt0 : wt1;
+            tma_load_3d(sb + (lane - 1) * KB_BYTES, &p.tmap_w1, &c.full[stage], 0, 0,
+                        wt * p.k_blocks + kb);
+          } else if (lane <= 4 && p.role == ROLE_LIGHT) {
+            // weight tiles of K blocks (kb + PREFETCH_KB, +1), two per prefetch; at the
+            // tile's first step also the K blocks before that
+            const int wt = lane == 3 ? wt0 : wt1;
+            const int kp = kb + PREFETCH_KB;
+            if ((kp & 1) == 0 && kp < p.k_blocks)
+              tma_prefetch_l2_3d(&p.tmap_w2, 0, 0, wt * p.k_blocks + kp);
+            if (ks == 0)
+              for (int k2 = 2; k2 < PREFETCH_KB && k2 < p.k_blocks; k2 += 2)
+                tma_prefetch_l2_3d(&p.tmap_w2, 0, 0, wt * p.k_blocks + k2);
           }
         }
+        __syncwarp();
       }
-      // Wait until the MMAs released every stage this CTA filled, so no TMA write or
-      // commit arrival into this CTA's shared memory is still in flight at exit.
-      for (int s = 0; s < C::STAGES; ++s) {
-        if (issued_parity[s] < 0) continue;
+    }
+    // Producer 0 waits until the MMAs released every stage of every step this CTA issued
+    // (by either producer), so no TMA write or commit arrival into this CTA's shared memory
+    // is still in flight at exit.
+    if (warp == 0 && lane == 0) {
+      int total = 0;
+      for (int t = cluster_id; t < total_tiles; t += active) total += ksteps;
+      for (int s = 0; s < C::STAGES && s < total; ++s) {
+        const int last = s + ((total - 1 - s) / C::STAGES) * C::STAGES;
+        const uint32_t par = static_cast<uint32_t>(last / C::STAGES) & 1u;
         const long long t0 = clock64();
-        while (!mbar_try_wait(&c.empty[s], static_cast<uint32_t>(issued_parity[s])) &&
-               clock64() - t0 < LM_SPIN_LIMIT_CYCLES) {
+        while (!mbar_try_wait(&c.empty[s], par) && clock64() - t0 < LM_SPIN_LIMIT_CYCLES) {
           if (*abort_flag && clock64() - t0 > 200000) break;
         }
       }
@@ -284,41 +371,41 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
     if (lane == 0 && leader) {
       // ------------------------------------------------------------ MMA issuer
       const uint32_t idesc = idesc_bf16_f32(BM * PAIR, BN);
-      int stage = 0;
-      uint32_t phase = 0;
+      int seq = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+      for (int t = cluster_id; t < total_tiles && ok; t += active) {
         if (!mbar_wait_bounded(&c.tempty[acc], acc_phase ^ 1u, p.err_word, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int ks = 0; ks < ksteps; ++ks, ++seq) {
+          const int stage = seq % C::STAGES;
+          const uint32_t phase = static_cast<uint32_t>(seq / C::STAGES) & 1u;
           if (!mbar_wait_bounded(&c.full[stage], phase, p.err_word, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + A_BYTES;
+          const uint32_t b_addr = a_addr + C::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = sdesc_k_sw128(a_addr + kk * 32);
-            const uint64_t bd = sdesc_k_sw128(b_addr + kk * 32);
-            const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
-            if (PAIR == 2)
-              umma_bf16_pair(d_tmem, ad, bd, idesc, accum);
-            else
-              umma_bf16(d_tmem, ad, bd, idesc, accum);
+          for (int j = 0; j < C::KB_STAGE; ++j) {
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t ad = sdesc_k_sw128(a_addr + j * KB_BYTES + kk * 32);
+              const uint64_t bd = sdesc_k_sw128(b_addr + j * KB_BYTES + kk * 32);
+              const uint32_t accum = (ks | j | kk) != 0 ? 1u : 0u;
+              if (PAIR == 2)
+                umma_bf16_pair(d_tmem, ad, bd, idesc, accum);
+              else
+                umma_bf16(d_tmem, ad, bd, idesc, accum);
+            }
           }
           if (PAIR == 2)
             umma_commit_pair(&c.empty[stage], 0x3);
           else
             umma_commit(&c.empty[stage]);
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
         }
         if (!ok) break;
         if (PAIR == 2)
@@ -337,9 +424,8 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&c.tempty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = cluster_id; t < total_tiles; t += num_clusters) {
-      const TileCoord tc = decode_tile(c, t, p.n_tiles, G, heavy_tiles, total_tiles,
-                                       C::UNIT_ROWS);
+    for (int t = cluster_id; t < total_tiles; t += active) {
+      const TileCoord tc = decode_tile(c, t, p.n_tiles, G, C::UNIT_ROWS);
       if (!mbar_wait_bounded(&c.tfull[acc], acc_phase, p.err_word, abort_flag)) break;
       tc_fence_after();
       const int my_valid = tc.valid - static_cast<int>(rank) * BM;
@@ -348,34 +434,37 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
           p.out + static_cast<int64_t>(tc.row0 + static_cast<int>(rank) * BM + r) * p.out_ld;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      if (p.mode == 0) {
+      // Warps whose 32 lanes are all past the tile's rows only release the accumulator.
+      if (quad * 32 < my_valid) {
+        if (p.mode == 0) {
 #pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t gv[32], uv[32];
-          tmem_ld_32x32b_x32(tbase + ch * 32, gv);
-          tmem_ld_32x32b_x32(tbase + 128 + ch * 32, uv);
-          tmem_ld_wait();
-          uint32_t packed[16];
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t gv[32], uv[32];
+            tmem_ld_32x32b_x32(tbase + ch * 32, gv);
+            tmem_ld_32x32b_x32(tbase + 128 + ch * 32, uv);
+            tmem_ld_wait();
+            uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float a0 = silu_f32(__uint_as_float(gv[2 * i])) * __uint_as_float(uv[2 * i]);
-            const float a1 =
-                silu_f32(__uint_as_float(gv[2 * i + 1])) * __uint_as_float(uv[2 * i + 1]);
-            packed[i] = pack_bf16x2(a0, a1);
+            for (int i = 0; i < 16; ++i) {
+              const float a0 = silu_f32(__uint_as_float(gv[2 * i])) * __uint_as_float(uv[2 * i]);
+              const float a1 =
+                  silu_f32(__uint_as_float(gv[2 * i + 1])) * __uint_as_float(uv[2 * i + 1]);
+              packed[i] = pack_bf16x2(a0, a1);
+            }
+            if (valid) store_row_chunk(out_row + tc.nt * 128 + ch * 32, packed);
           }
-          if (valid) store_row_chunk(out_row + tc.nt * 128 + ch * 32, packed);
-        }
-      } else {
+        } else {
 #pragma unroll 1
-        for (int ch = 0; ch < 8; ++ch) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tbase + ch * 32, v);
-          tmem_ld_wait();
-          uint32_t packed[16];
+          for (int ch = 0; ch < 8; ++ch) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tbase + ch * 32, v);
+            tmem_ld_wait();
+            uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-          if (valid) store_row_chunk(out_row + tc.nt * BN + ch * 32, packed);
+            for (int i = 0; i < 16; ++i)
+              packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            if (valid) store_row_chunk(out_row + tc.nt * BN + ch * 32, packed);
+          }
         }
       }
       tc_fence_before();
@@ -430,10 +519,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct MapKey {
   const void* ptr;
-  uint64_t d[3];
+  uint64_t d[2];
   int rank;
+  int box_rows;
+  int box_depth;
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && d[0] == o.d[0] && d[1] == o.d[1] && d[2] == o.d[2] && rank == o.rank;
+    return ptr == o.ptr && d[0] == o.d[0] && d[1] == o.d[1] && rank == o.rank &&
+           box_rows == o.box_rows && box_depth == o.box_depth;
   }
 };
 
@@ -447,11 +539,13 @@ MapCache& map_cache() {
   return c;
 }
 
-// rank 2: activation rows, dims {K, rows}, box {64, 128}.
-// rank 3: weight tiles, dims {64, 128, n_tiles} with strides {128 B, 16 KiB}, box {64, 128, 1}.
+// rank 2: activation rows, dims {K, rows}, box {64, box_rows}.
+// rank 3: weight tiles, dims {64, 128, n_tiles} with strides {128 B, 16 KiB},
+//         box {64, 128, box_depth} (box_depth consecutive tiles: K blocks kb, kb+1, ...).
 // Both with 128-byte swizzle (the K-major SW128 layout the UMMA descriptors expect).
-int make_map(CUtensorMap* out, const void* ptr, int rank, uint64_t d0, uint64_t d1) {
-  const MapKey key{ptr, {d0, d1, 0}, rank};
+int make_map(CUtensorMap* out, const void* ptr, int rank, uint64_t d0, uint64_t d1,
+             int box_rows = 128, int box_depth = 1) {
+  const MapKey key{ptr, {d0, d1}, rank, box_rows, box_depth};
   MapCache& cache = map_cache();
   {
     std::lock_guard<std::mutex> lk(cache.mu);
@@ -476,7 +570,8 @@ int make_map(CUtensorMap* out, const void* ptr, int rank, uint64_t d0, uint64_t 
     strides[0] = BK * 2;
     strides[1] = BK * 128 * 2;
   }
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(BK), 128, 1};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows),
+                       static_cast<cuuint32_t>(box_depth)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUtensorMap m;
   const CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
@@ -523,25 +618,84 @@ int ensure_smem_attr() {
   return rc;
 }
 
-// Single-CTA tiles by default: on Zipf-skewed expert loads most groups fit one 128-row
-// tile, and a 256-row 2-SM tile would leave the second CTA's half empty for them (measured
-// 409 us vs 453 us on the 4096-token Qwen3-30B-A3B layer). LM_UMMA_CTA_PAIR=2 selects the
-// cta_group::2 tiles, which win on dense groups (1233 vs 1155 TFLOP/s on one 32768-row group).
+// Heavy groups on 2-SM tiles beside light groups on single-SM tiles by default;
+// LM_UMMA_CTA_PAIR=1 runs every group on the single-SM kernel.
 int cta_pair() {
   static int v = [] {
     const char* e = getenv("LM_UMMA_CTA_PAIR");
-    return (e != nullptr && e[0] == '2') ? 2 : 1;
+    return (e != nullptr && e[0] == '1') ? 1 : 2;
   }();
   return v;
 }
 
-int launch_umma(const UmmaParams& p, int grid, cudaStream_t s, const char* what) {
-  if (cta_pair() == 2) {
+// Relative SM time of a heavy tile (per SM of its pair) and of a light tile, per GEMM (mode),
+// for the split of the SMs between the two launches; measured on the 4096-token
+// Qwen3-30B-A3B layer. LM_UMMA_SPLIT_COST="h0:l0:h1:l1" overrides.
+void split_costs(int mode, int* heavy, int* light) {
+  static int c[4] = {4, 5, 4, 5};
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* e = getenv("LM_UMMA_SPLIT_COST");
+    int v[4] = {0, 0, 0, 0};
+    if (e != nullptr && sscanf(e, "%d:%d:%d:%d", &v[0], &v[1], &v[2], &v[3]) == 4 &&
+        v[0] > 0 && v[1] > 0 && v[2] > 0 && v[3] > 0)
+      for (int i = 0; i < 4; ++i) c[i] = v[i];
+  });
+  *heavy = c[2 * mode];
+  *light = c[2 * mode + 1];
+}
+
+// Per-device side stream for the light launches, with the fork / join events. Calls hold the
+// mutex from the fork to the join, so the shared events are never re-recorded before the
+// waits on them are enqueued.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join = nullptr;
+};
+
+std::mutex& side_mutex() {
+  static std::mutex mu;
+  return mu;
+}
+
+int side_stream(SideStream** out) {
+  static SideStream per_dev[64];
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "lm_moe_mlp_prefill: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return fail(LM_ERR_UNSUPPORTED, "lm_moe_mlp_prefill: device index >= 64");
+  SideStream& ss = per_dev[dev];
+  if (ss.stream == nullptr) {
+    rc = check_cuda(cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking),
+                    "lm_moe_mlp_prefill: side stream");
+    if (!rc) rc = check_cuda(cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming),
+                             "lm_moe_mlp_prefill: fork event");
+    if (!rc) rc = check_cuda(cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming),
+                             "lm_moe_mlp_prefill: join event");
+    if (rc) return rc;
+  }
+  *out = &ss;
+  return LM_OK;
+}
+
+int launch_umma(UmmaParams p, int role, int grid, cudaStream_t s, const char* what) {
+  p.role = role;
+  if (role == ROLE_HEAVY) {
     umma_grouped_kernel_2sm<<<grid & ~1, NUM_THREADS, smem_bytes<2>(), s>>>(p);
   } else {
     umma_grouped_kernel<<<grid, NUM_THREADS, smem_bytes<1>(), s>>>(p);
   }
   return launch_status(what);
+}
+
+// Activation-row maps: boxes of 16 / 32 / 64 / 128 rows over the same rows.
+int make_row_maps(CUtensorMap* maps, const void* ptr, uint64_t k, uint64_t rows) {
+  for (int i = 0; i < 4; ++i) {
+    int rc = make_map(&maps[i], ptr, 2, k, rows, 16 << i);
+    if (rc) return rc;
+  }
+  return LM_OK;
 }
 
 }  // namespace
@@ -579,9 +733,10 @@ extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
   const int grid = sm_count();
 
   UmmaParams p1{};
-  rc = make_map(&p1.tmap_a, x_perm, 2, H, total_rows);
-  if (rc) return rc;
-  rc = make_map(&p1.tmap_b, w13_bank, 3, static_cast<uint64_t>(bank_rows) * (2 * I / 128) * (H / BK), 0);
+  const uint64_t w13_tiles = static_cast<uint64_t>(bank_rows) * (2 * I / 128) * (H / BK);
+  rc = make_row_maps(p1.tmap_a, x_perm, H, total_rows);
+  if (!rc) rc = make_map(&p1.tmap_w2, w13_bank, 3, w13_tiles, 0, 128, 2);
+  if (!rc) rc = make_map(&p1.tmap_w1, w13_bank, 3, w13_tiles, 0, 128, 1);
   if (rc) return rc;
   p1.group_offsets = group_offsets;
   p1.group_bank_row = group_bank_row;
@@ -596,13 +751,14 @@ extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
   p1.out_ld = I;
   p1.bank_rows = static_cast<int32_t>(bank_rows);
   p1.w_ntiles = 2 * I / 128;
-  rc = launch_umma(p1, grid, s, "lm_moe_mlp_prefill: gate_up");
-  if (rc) return rc;
+  p1.split_sms = grid;
+  split_costs(0, &p1.heavy_tile_cost, &p1.light_tile_cost);
 
   UmmaParams p2 = p1;
-  rc = make_map(&p2.tmap_a, act, 2, I, total_rows);
-  if (rc) return rc;
-  rc = make_map(&p2.tmap_b, w2_bank, 3, static_cast<uint64_t>(bank_rows) * (H / 128) * (I / BK), 0);
+  const uint64_t w2_tiles = static_cast<uint64_t>(bank_rows) * (H / 128) * (I / BK);
+  rc = make_row_maps(p2.tmap_a, act, I, total_rows);
+  if (!rc) rc = make_map(&p2.tmap_w2, w2_bank, 3, w2_tiles, 0, 128, 2);
+  if (!rc) rc = make_map(&p2.tmap_w1, w2_bank, 3, w2_tiles, 0, 128, 1);
   if (rc) return rc;
   p2.out = y_perm;
   p2.k_blocks = I / BK;
@@ -610,5 +766,30 @@ extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
   p2.mode = 1;
   p2.out_ld = H;
   p2.w_ntiles = H / 128;
-  return launch_umma(p2, grid, s, "lm_moe_mlp_prefill: down");
+  split_costs(1, &p2.heavy_tile_cost, &p2.light_tile_cost);
+
+  if (cta_pair() == 1) {
+    rc = launch_umma(p1, ROLE_ALL, grid, s, "lm_moe_mlp_prefill: gate_up");
+    if (!rc) rc = launch_umma(p2, ROLE_ALL, grid, s, "lm_moe_mlp_prefill: down");
+    return rc;
+  }
+  // Heavy groups: the 2-SM launches on the caller's stream. Light groups: the single-SM
+  // launches on the side stream, forked after the caller's prior work and joined back before
+  // anything the caller enqueues next; the light down GEMM starts as soon as the light
+  // gate_up is done, while the heavy gate_up may still run. Each GEMM's pair of launches
+  // splits the SMs between them; the CTAs a launch does not need leave at once.
+  std::lock_guard<std::mutex> lk(side_mutex());
+  SideStream* ss = nullptr;
+  rc = side_stream(&ss);
+  if (!rc) rc = check_cuda(cudaEventRecord(ss->fork, s), "lm_moe_mlp_prefill: fork");
+  if (!rc) rc = check_cuda(cudaStreamWaitEvent(ss->stream, ss->fork, 0), "lm_moe_mlp_prefill: fork wait");
+  if (rc) return rc;
+  rc = launch_umma(p1, ROLE_HEAVY, grid, s, "lm_moe_mlp_prefill: gate_up (2-SM)");
+  if (!rc) rc = launch_umma(p1, ROLE_LIGHT, grid, ss->stream, "lm_moe_mlp_prefill: gate_up (1-SM)");
+  if (!rc) rc = launch_umma(p2, ROLE_HEAVY, grid, s, "lm_moe_mlp_prefill: down (2-SM)");
+  if (!rc) rc = launch_umma(p2, ROLE_LIGHT, grid, ss->stream, "lm_moe_mlp_prefill: down (1-SM)");
+  // Join even after a failed launch, so the caller's stream never runs ahead of the side.
+  const int rj = check_cuda(cudaEventRecord(ss->join, ss->stream), "lm_moe_mlp_prefill: join");
+  const int rw = rj ? rj : check_cuda(cudaStreamWaitEvent(s, ss->join, 0), "lm_moe_mlp_prefill: join wait");
+  return rc ? rc : rw;
 }

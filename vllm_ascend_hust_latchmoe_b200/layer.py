@@ -22,6 +22,7 @@ addresses. There is no CPU or eager-torch fallback for any of the math.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -42,6 +43,15 @@ PHASE_MIXED = 2
 # Above this many tokens per call the grouped MLP runs on the tcgen05 GEMM; at or below it
 # on the bandwidth-bound GEMV (a group never holds more rows than the call has tokens).
 DECODE_MAX_TOKENS = 64
+
+
+def mlp_launches(T: int) -> int:
+    """Kernel launches of one grouped-MLP call: the decode path runs two (gate_up, down); the
+    prefill path runs a 2-SM and a single-SM launch per GEMM (one launch per GEMM with
+    LM_UMMA_CTA_PAIR=1)."""
+    if T <= DECODE_MAX_TOKENS:
+        return 2
+    return 2 if os.environ.get("LM_UMMA_CTA_PAIR", "") == "1" else 4
 
 
 @dataclass
@@ -203,7 +213,7 @@ class SlotBankMoE:
         _lib.build_groups(ids, self.E_total, log2phy, G, self.group_offsets, self.pair_to_row,
                           self.row_to_pair, self.scratch, self.err)
         self._grouped_mlp(hidden, T, self.slot_rows, 0, G, bank.w13_slots, bank.w2_slots)
-        self.kernel_launches += 6  # grouping (3), gate_up, down, combine
+        self.kernel_launches += 3 + mlp_launches(T) + 1  # grouping (3), MLP, combine
         return self._combine(T, out)
 
     def mlp_resident(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -232,7 +242,7 @@ class SlotBankMoE:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
         self._grouped_mlp(hidden, T, self.group_bank_row, 0, self.E, store.w13, store.w2)
-        self.kernel_launches += launches + 3
+        self.kernel_launches += launches + mlp_launches(T) + 1
         return self._combine(T, out)
 
     def resident_wave_plan(self) -> tuple[tuple[int, ...], ...]:
@@ -312,7 +322,7 @@ class SlotBankMoE:
                     g0, g1 = wave_groups[w]
                     self._grouped_mlp(hidden, T, self.group_bank_row, g0, g1,
                                       stage_bank.w13_slots, stage_bank.w2_slots)
-                    launches += 2
+                    launches += mlp_launches(T)
                     release = torch.cuda.Event()
                     release.record(compute_stream)
                     rt.remember_prefill_stage_buffer_release(self.layer_id, buf, release)
@@ -354,7 +364,7 @@ class SlotBankMoE:
         else:
             _lib.moe_mlp_prefill(hidden, T, self.shared_offsets, self.shared_bank_row, 0, 1,
                                  self.shared_w13, self.shared_w2, self.shared_act, out, self.err)
-        self.kernel_launches += 2
+        self.kernel_launches += mlp_launches(T)
         return out
 
     def run_mlp(self, hidden: torch.Tensor, decision: StageDecision,
