@@ -104,3 +104,55 @@ def test_c4_deepseek_shaped_layer(cuda):
     layer.check_device_errors()
     assert np.array_equal(layer.topk_ids[:64].cpu().numpy(), ids_ref)
     _check(out, ref)
+
+
+@pytest.mark.parametrize("tokens", [16, 1024])
+def test_full_layer_reference_path(cuda, tokens):
+    """VLLM_ASCEND_MOE_OFFLOAD_B2_REFERENCE_FULL_LAYER: every routed expert staged into the
+    layout's full-layer bank, one MLP pass in the native top-k shape (decode and prefill)."""
+    cfg = syn.CONFIGS["c2_prefill"].with_tokens(tokens)
+    layer, rt, (w13, w2) = build_layer(cfg, reference_full_layer=True)
+    hidden = syn.make_hidden(cfg)
+    logits = syn.make_router_logits(cfg)
+    _, _, ref = _oracle_layer(cfg, hidden, logits, w13, w2)
+    out = layer.forward(hidden.to(cuda), logits.to(cuda))
+    torch.cuda.synchronize()
+    layer.check_device_errors()
+    assert layer.last_full_layer["execution_mode"] == "reference_full_layer"
+    assert layer.last_full_layer["routed_expert_count"] == cfg.num_experts
+    _check(out, ref)
+    out2 = layer.forward(hidden.to(cuda), logits.to(cuda))
+    torch.cuda.synchronize()
+    assert layer.last_full_layer["pool_reused"] and torch.equal(out, out2)
+
+
+def test_wave_fallback_reruns_full_layer(cuda, monkeypatch):
+    """A wave plan that fails qualification (B2WaveFallback before any wave runs) reruns the
+    layer on the full-layer path with the same result."""
+    from vllm_ascend_hust_latchmoe_b200.moe_offload import phase_split
+
+    cfg = syn.CONFIGS["c2_prefill"].with_tokens(512)
+    layer, rt, (w13, w2) = build_layer(cfg)
+    hidden = syn.make_hidden(cfg)
+    logits = syn.make_router_logits(cfg)
+    _, _, ref = _oracle_layer(cfg, hidden, logits, w13, w2)
+    good = layer.forward(hidden.to(cuda), logits.to(cuda))
+    torch.cuda.synchronize()
+    assert layer.last_fallback_reason is None
+    real = phase_split.plan_balanced_b2_waves
+
+    def drop_last_expert(counts, num_slots):  # a plan that misses an active expert
+        plan = real(counts, num_slots)
+        return phase_split.B2WavePlan(plan.waves[:-1] + (plan.waves[-1][:-1],),
+                                      plan.token_counts_by_expert)
+
+    monkeypatch.setattr("vllm_ascend_hust_latchmoe_b200.layer.plan_balanced_b2_waves",
+                        drop_last_expert)
+    out = layer.forward(hidden.to(cuda), logits.to(cuda))
+    torch.cuda.synchronize()
+    layer.check_device_errors()
+    assert layer.last_fallback_reason is not None and "exactly once" in layer.last_fallback_reason
+    assert layer.last_full_layer is not None
+    _check(out, ref)
+    m = omlp.compare(bf16_bits_to_f32(bits(out)), bf16_bits_to_f32(bits(good)))
+    assert m["max_rel_err"] <= MAX_REL_ERR, m

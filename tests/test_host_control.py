@@ -141,3 +141,59 @@ def test_tiled_layout_round_trip_and_tile_contiguity():
     # tile (n-tile 1, k-block 1) of expert 1 is one contiguous 128 x 64 block
     tile = flat[1, (1 * 2 + 1) * 8192:(1 * 2 + 2) * 8192].reshape(128, 64)
     assert torch.equal(tile, w[1, 128:256, 64:128])
+
+
+def test_full_layer_prefill_plan_on_cpu_bank():
+    """Full-layer fallback bank: row e holds expert e, one bank per layout reused across
+    layers, payload fields, memory ledger accounting."""
+    from tests.helpers import ExpertLayer
+    from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
+
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=2, b2_wave_prefill=True))
+    layers = []
+    for lid in (0, 1):
+        w13 = torch.arange(5 * 4 * 3, dtype=torch.float32).reshape(5, 4, 3) + 100 * lid
+        w2 = torch.arange(5 * 3 * 2, dtype=torch.float32).reshape(5, 3, 2) - 100 * lid
+        rt.register_layer_for_fixed_slots(ExpertLayer(lid, w13, w2), slot_device=torch.device("cpu"))
+        layers.append((w13, w2))
+    bank0, ready0, pay0 = rt.prepare_full_layer_prefill_plan(layer_id=0)
+    assert pay0["execution_mode"] == "reference_full_layer" and not pay0["pool_reused"]
+    assert pay0["routed_expert_count"] == 5 and ready0.event is None
+    assert torch.equal(bank0.w13_slots[:5], layers[0][0]) and torch.equal(bank0.w2_slots[:5], layers[0][1])
+    rt.wait_prefill_stage_plan(ready0)  # the consumer's wait publishes the rows READY
+    ledger_before = rt.memory_ledger().stage_bank_bytes
+    bank1, _, pay1 = rt.prepare_full_layer_prefill_plan(layer_id=1)
+    assert bank1 is bank0 and pay1["pool_reused"]
+    assert torch.equal(bank1.w13_slots[:5], layers[1][0])
+    assert rt.memory_ledger().stage_bank_bytes == ledger_before > 0
+
+
+def test_wave_plan_qualification_raises_fallback(monkeypatch):
+    from types import SimpleNamespace
+
+    from vllm_ascend_hust_latchmoe_b200 import layer as L
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.phase_split import B2WaveFallback, B2WavePlan
+
+    stub = SimpleNamespace(runtime=SimpleNamespace(config=SimpleNamespace(num_slots=2)))
+    plan = L.SlotBankMoE.plan_waves_checked(stub, (3, 0, 1, 2, 5))
+    assert sorted(e for w in plan.waves for e in w) == [0, 2, 3, 4]
+    monkeypatch.setattr(L, "plan_balanced_b2_waves",
+                        lambda counts, s: B2WavePlan(((0, 2, 3),), dict(counts)))
+    try:
+        L.SlotBankMoE.plan_waves_checked(stub, (3, 0, 1, 2, 5))
+    except B2WaveFallback as exc:
+        assert "exactly once" in str(exc)
+    else:
+        raise AssertionError("expected B2WaveFallback")
+
+    def bad(counts, s):
+        raise ValueError("no plan")
+
+    monkeypatch.setattr(L, "plan_balanced_b2_waves", bad)
+    try:
+        L.SlotBankMoE.plan_waves_checked(stub, (1, 1))
+    except B2WaveFallback as exc:
+        assert "wave planning failed" in str(exc)
+    else:
+        raise AssertionError("expected B2WaveFallback")

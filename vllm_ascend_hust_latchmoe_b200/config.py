@@ -25,6 +25,7 @@ class MoeOffloadConfig:
     graph_compatible_offload: bool = False
     offload_stage_seam: bool = False
     b2_wave_prefill: bool = False
+    b2_reference_full_layer: bool = False
     pin_host_memory: bool | None = None
     transfer_aware_wave_schedule: bool = True
     prefill_prefetch_depth: int = 1
@@ -58,6 +59,7 @@ class MoeOffloadConfig:
             graph_compatible_offload=env.get("VLLM_ASCEND_MOE_OFFLOAD_GRAPH_COMPATIBLE"),
             offload_stage_seam=env.get("VLLM_ASCEND_MOE_OFFLOAD_STAGE_SEAM"),
             b2_wave_prefill=env.get("VLLM_ASCEND_MOE_OFFLOAD_B2_WAVE_PREFILL"),
+            b2_reference_full_layer=bool(env.get("VLLM_ASCEND_MOE_OFFLOAD_B2_REFERENCE_FULL_LAYER")),
             pin_host_memory=env.get("VLLM_ASCEND_MOE_OFFLOAD_PIN_HOST_MEMORY"),
             transfer_aware_wave_schedule=env.get("VLLM_ASCEND_MOE_OFFLOAD_TRANSFER_AWARE_SCHEDULE"),
             prefill_prefetch_depth=env.get("VLLM_ASCEND_MOE_OFFLOAD_PREFILL_PREFETCH_DEPTH"),

@@ -29,6 +29,7 @@ import torch
 
 from . import _lib
 from .moe_offload.phase_split import (
+    B2WaveFallback,
     WaveIssuer,
     plan_b2_prefill_async_schedule,
     plan_balanced_b2_waves,
@@ -136,6 +137,8 @@ class SlotBankMoE:
         self.num_waves = torch.zeros(1, dtype=i32, device=d)
         self.resident_tier = runtime.host_layer(self.layer_id).on_device
         self.last_waves = WaveReport()
+        self.last_fallback_reason: str | None = None
+        self.last_full_layer: dict | None = None
         self.kernel_launches = 0
         self.pending: StageDecision | None = None
         self.shared_w13 = None
@@ -266,11 +269,65 @@ class SlotBankMoE:
 
     def forward_waves(self, hidden: torch.Tensor, T: int, counts: tuple[int, ...],
                       out: torch.Tensor | None = None) -> torch.Tensor:
-        """Capacity-bounded waves with one combine at the end (eager)."""
+        """Capacity-bounded waves with one combine at the end (eager). A wave plan that does
+        not qualify (``B2WaveFallback``, raised before any wave runs) reruns the layer on the
+        full-layer path, as does ``b2_reference_full_layer``."""
         rt = self.runtime
         cfg = rt.config
-        S = int(cfg.num_slots)
-        plan = plan_balanced_b2_waves({e: c for e, c in enumerate(counts) if c > 0}, S)
+        self.last_fallback_reason = None
+        if cfg.b2_reference_full_layer and not rt.host_layer(self.layer_id).on_device:
+            return self.forward_full_layer(hidden, T, out)
+        try:
+            plan = self.plan_waves_checked(counts)
+        except B2WaveFallback as exc:
+            self.last_fallback_reason = f"{type(exc).__name__}: {exc}"
+            return self.forward_full_layer(hidden, T, out)
+        return self._run_waves(hidden, T, plan, out)
+
+    def plan_waves_checked(self, counts: tuple[int, ...]):
+        """Canonical wave plan, qualified before anything runs: every active expert in
+        exactly one wave, no wave above the slot count (reference: ``patch_fused_moe.py``
+        :2540-2548, ``phase_split.py:1790-1856``). Failures raise ``B2WaveFallback``."""
+        S = int(self.runtime.config.num_slots)
+        active = {e: int(c) for e, c in enumerate(counts) if c > 0}
+        try:
+            plan = plan_balanced_b2_waves(active, S)
+        except ValueError as exc:
+            raise B2WaveFallback(f"wave planning failed: {exc}") from exc
+        members = [e for w in plan.waves for e in w]
+        if sorted(members) != sorted(active) or any(len(w) > S for w in plan.waves):
+            raise B2WaveFallback(
+                f"B2 waves must cover every active expert exactly once within {S} slots: "
+                f"covered={len(members)} active={len(active)}")
+        return plan
+
+    def forward_full_layer(self, hidden: torch.Tensor, T: int,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+        """Recoverable fallback: all routed experts staged into the full-layer bank (row e =
+        expert e), then one grouped MLP pass in the native top-k shape and the combine
+        (reference ``_run_b2_full_layer_reference``, ``patch_fused_moe.py:3472-3650``)."""
+        rt = self.runtime
+        bank, ready, payload = rt.prepare_full_layer_prefill_plan(layer_id=self.layer_id)
+        rt.wait_prefill_stage_plan(ready, torch.cuda.current_stream())
+        ids = self.topk_ids[:T]
+        _lib.build_groups(ids, self.E_total, self.identity_groups, self.E, self.group_offsets,
+                          self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+        launches = 3
+        if T > DECODE_MAX_TOKENS:
+            _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
+            launches += 1
+        self._grouped_mlp(hidden, T, self.identity_groups, 0, self.E, bank.w13_slots,
+                          bank.w2_slots)
+        launches += mlp_launches(T) + 1
+        self.kernel_launches += launches
+        self.last_full_layer = payload
+        self.last_waves = WaveReport(waves=(tuple(range(self.E)),),
+                                     staged_bytes=int(payload["h2d_bytes"]), launches=launches)
+        return self._combine(T, out)
+
+    def _run_waves(self, hidden: torch.Tensor, T: int, plan, out: torch.Tensor | None):
+        rt = self.runtime
+        cfg = rt.config
         waves = plan.waves
         store = rt.host_layer(self.layer_id)
         zero_copy = store.on_device
@@ -298,7 +355,7 @@ class SlotBankMoE:
         if zero_copy:
             # Every expert already has an HBM copy: read it in place, all waves in one pass.
             self._grouped_mlp(hidden, T, self.group_bank_row, 0, g, store.w13, store.w2)
-            launches += 2
+            launches += mlp_launches(T)
         else:
             main = rt.slot_bank(self.layer_id)
             ready = main.ready_slot_ids(self.layer_id, [e for w in waves for e in w])

@@ -18,6 +18,7 @@ from __future__ import annotations
 import itertools
 import threading
 from dataclasses import dataclass
+from time import perf_counter
 from types import SimpleNamespace
 
 import torch
@@ -110,6 +111,7 @@ class MoeOffloadRuntime:
         self._graph_slot_address_fingerprints: dict[int, SlotAddressFingerprint] = {}
         self._active_slot_ids_by_layer: dict[int, tuple[int, ...]] = {}
         self._stage_pools: dict[tuple, StagePool] = {}
+        self._full_layer_pool: dict[tuple, ExpertSlotBank] = {}
         self._tiled_layout: dict[int, bool] = {}
         self._step_counter = itertools.count()
         self._capturing = False
@@ -555,6 +557,51 @@ class MoeOffloadRuntime:
         nbytes = stage.slot_bytes * len(wave)
         return stage, TransferReadyEvent(event, tuple((s, s.lease()) for s in slots), bytes=nbytes)
 
+    def prepare_full_layer_prefill_plan(self, *, layer_id: int, step_id: int | None = None
+                                        ) -> tuple[ExpertSlotBank, TransferReadyEvent, dict]:
+        """Stage every routed expert of a layer into a full-layer bank (row e = expert e).
+
+        Recoverable fallback of the multi-wave executor (reference
+        ``runtime.py:2260-2370``, ``patch_fused_moe.py:3472-3650``): one bank per weight
+        layout and expert count, reused by every layer of that layout, so only one complete
+        layer is resident at a time. The copies are ordered on the copy stream (the consumer
+        waits on the returned event) instead of blocking the host.
+        """
+        layer_id = int(layer_id)
+        if self.is_resident_layer(layer_id):
+            raise RuntimeError(f"full-layer prefill plan must not run on resident layer {layer_id}")
+        template = self._slot_banks.get(layer_id)
+        if template is None:
+            raise RuntimeError(f"layer {layer_id} is not registered for fixed-slot execution")
+        store = self._host_store.layer(layer_id)
+        E = int(self._routed_counts.get(layer_id, store.w13.shape[0]))
+        key = (tuple(template.w13_slots.shape[1:]), tuple(template.w2_slots.shape[1:]),
+               template.w13_slots.dtype, str(template.w13_slots.device), E)
+        reused = key in self._full_layer_pool
+        if not reused:
+            self._full_layer_pool[key] = ExpertSlotBank(
+                E, tuple(template.w13_slots.shape[1:]), tuple(template.w2_slots.shape[1:]),
+                dtype=template.w13_slots.dtype, device=template.w13_slots.device)
+        bank = self._full_layer_pool[key]
+        step = int(step_id) if step_id is not None and int(step_id) >= 0 else self.next_step_id()
+        slots = [bank.assign_transient_slot(e, ExpertKey(layer_id, e), step_id=step)
+                 for e in range(E)]
+        t0 = perf_counter()
+        eng = self._transfer_engine
+        eng.copy_rows(store.w13, store.w2, list(range(E)), bank.w13_slots, bank.w2_slots,
+                      list(range(E)))
+        event = eng.record_event() if bank.w13_slots.is_cuda else None
+        payload = {
+            "execution_mode": "reference_full_layer",
+            "routed_expert_count": E,
+            "physical_expert_count": int(bank.physical_expert_count),
+            "h2d_bytes": int(bank.slot_bytes * E),
+            "stage_issue_ms": round((perf_counter() - t0) * 1000.0, 3),
+            "pool_reused": bool(reused),
+        }
+        return bank, TransferReadyEvent(event, tuple((sl, sl.lease()) for sl in slots),
+                                        bytes=bank.slot_bytes * E), payload
+
     def wait_prefill_stage_plan(self, ready: TransferReadyEvent,
                                 consumer_stream: torch.cuda.Stream | None = None) -> None:
         if consumer_stream is None and ready.event is not None:
@@ -567,7 +614,7 @@ class MoeOffloadRuntime:
         return MoeOffloadMemoryLedger(
             host_store_bytes=self._host_store.total_bytes,
             slot_bank_bytes=sum(b.total_bytes for b in self._slot_banks.values()),
-            stage_bank_bytes=stage,
+            stage_bank_bytes=stage + sum(b.total_bytes for b in self._full_layer_pool.values()),
             log2phy_bytes=sum(t.numel() * 4 for t in self._log2phy_buffers.values()),
         )
 
