@@ -54,6 +54,10 @@ extern "C" {
 #define LM_COPY_H2D 1
 #define LM_COPY_D2D 3
 
+/* Weight sources in lm_slot_plan's per-group table (see lm_slot_plan). */
+#define LM_SRC_MISS 0x40000000 /* flag: host store row, written through into the slot */
+#define LM_SRC_HOST (-2)       /* host store row, not cached (working set > slots) */
+
 /* ABI version (LM_ABI_VERSION of the built library). */
 int lm_abi_version(void);
 
@@ -209,6 +213,52 @@ int lm_moe_combine(const uint16_t* y_perm, const int32_t* pair_to_row,
 int lm_stage_copy(void* dst, int64_t dst_row_stride, const void* src, int64_t src_row_stride,
                   const int32_t* src_rows_host, const int32_t* dst_rows_host, int32_t n,
                   int64_t bytes_per_expert, int32_t kind, void* stream);
+
+/*
+ * Device-side staging decision of one decode stage call (no device->host round trip).
+ * State in device memory, persistent across calls, initialised by the caller once:
+ * slot_owner [num_slots] int32 = -1, slot_last_used [num_slots] int64 = -1,
+ * expert_slot [num_experts] int32 = -1, step_counter [1] int64 = 0.
+ * From topk_ids [num_pairs] it marks the active experts and, when their count is at most
+ * num_slots, assigns slots in ascending expert order: a resident expert's last-used step is
+ * bumped; a missing one takes the first empty slot, else the slot with the least
+ * (last_used, slot id) among those not assigned in this call; log2phy[e] = slot of every
+ * active expert. It writes group_src [num_experts] (group = expert id): slot s for a hit,
+ * s | LM_SRC_MISS for a miss (the MLP reads the host store and fills slot s), LM_SRC_HOST
+ * when the working set exceeds the slots (the bank is then left untouched, as the reference's
+ * multi-wave path leaves it), -1 for inactive experts. hit_miss_counts (int64 [2], may be
+ * NULL) accumulates the hits and misses of the calls that assigned slots.
+ * num_experts <= 8192, num_slots <= 1024.
+ * Replaces: the stage seam's blocking D2H and Python allocation loop
+ * (ops/fused_moe/moe_offload_stage_op.py:297-302, moe_offload/runtime.py:1636-1902,
+ * moe_offload/slot_bank.py:211-232).
+ */
+int lm_slot_plan(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
+                 int32_t num_slots, int32_t* slot_owner, int64_t* slot_last_used,
+                 int32_t* expert_slot, int64_t* step_counter, int32_t* log2phy,
+                 int32_t* group_src, int64_t* hit_miss_counts, int32_t* err_word,
+                 void* stream);
+
+/*
+ * Decode grouped MLP with the weight source per group taken from lm_slot_plan's table:
+ * slot rows of w13_slots [num_slots, 2I, H] / w2_slots [num_slots, H, I], or rows
+ * group_expert[g] of the pinned host store w13_host [num_experts, 2I, H] / w2_host
+ * [num_experts, H, I] (read by the kernel over PCIe; for LM_SRC_MISS every loaded chunk is
+ * also written into the slot). Same math and outputs as lm_moe_mlp_decode; at most 64 rows
+ * per group (one weight pass). Requires H % 128 == 0, I % 64 == 0, 16-byte aligned bases,
+ * host stores allocated as pinned memory.
+ * Replaces: the H2D staging of missed experts (moe_offload/transfer_engine.py:139-187)
+ * together with the grouped MLP (patches/patch_fused_moe.py:4249-4302).
+ */
+int lm_moe_mlp_decode_offload(const uint16_t* hidden, int32_t top_k,
+                              const int32_t* row_to_pair, const int32_t* group_offsets,
+                              const int32_t* group_src, const int32_t* group_expert,
+                              int32_t group_begin, int32_t group_end, int32_t max_rows_per_group,
+                              uint16_t* w13_slots, uint16_t* w2_slots, int32_t num_slots,
+                              const uint16_t* w13_host, const uint16_t* w2_host,
+                              int32_t num_experts, int32_t hidden_size,
+                              int32_t intermediate_size, uint16_t* act, uint16_t* y_perm,
+                              int32_t* err_word, void* stream);
 
 #ifdef __cplusplus
 }

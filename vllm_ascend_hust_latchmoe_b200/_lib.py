@@ -43,6 +43,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _P, _P, _P, _P],
     ),
     "lm_expert_histogram": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _P]),
+    "lm_slot_plan": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "lm_moe_mlp_decode_offload": (
+        ctypes.c_int,
+        [_P, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _P, _P, _I32, _P, _P, _I32, _I32, _I32,
+         _P, _P, _P, _P],
+    ),
     "lm_plan_waves": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P, _P]),
     "lm_build_groups_scratch_elems": (ctypes.c_int64, [_I64, _I32]),
     "lm_build_groups": (
@@ -251,6 +257,44 @@ def moe_mlp_prefill(x_perm, total_rows, group_offsets, group_bank_row, group_beg
             _ptr(x_perm), int(total_rows), _ptr(group_offsets), _ptr(group_bank_row),
             int(group_begin), int(group_end), _ptr(w13_bank), _ptr(w2_bank),
             w13_bank.shape[0], H, I, _ptr(act), _ptr(y_perm), _ptr(err_word), _stream(),
+        ),
+    )
+
+
+LM_SRC_MISS = 0x40000000
+LM_SRC_HOST = -2
+
+
+def slot_plan(topk_ids, num_experts, slot_owner, slot_last_used, expert_slot, step_counter,
+              log2phy, group_src, hit_miss=None, err_word=None) -> None:
+    """Device-side stage decision (see ``lm_slot_plan``); all state tensors on the device."""
+    _require_cuda(topk_ids, slot_owner, slot_last_used, expert_slot, step_counter, log2phy,
+                  group_src)
+    _check(
+        "lm_slot_plan",
+        lib().lm_slot_plan(
+            _ptr(topk_ids), topk_ids.numel(), int(num_experts), slot_owner.numel(),
+            _ptr(slot_owner), _ptr(slot_last_used), _ptr(expert_slot), _ptr(step_counter),
+            _ptr(log2phy), _ptr(group_src), _ptr(hit_miss), _ptr(err_word), _stream(),
+        ),
+    )
+
+
+def moe_mlp_decode_offload(hidden, top_k, row_to_pair, group_offsets, group_src, group_expert,
+                           group_begin, group_end, max_rows_per_group, w13_slots, w2_slots,
+                           w13_host, w2_host, act, y_perm, err_word=None) -> None:
+    """Decode MLP reading each group's weights from a slot or the pinned host store."""
+    _require_cuda(hidden, row_to_pair, group_offsets, group_src, group_expert, w13_slots,
+                  w2_slots, act, y_perm)
+    H = hidden.shape[-1]
+    I = w2_slots.shape[-1]
+    _check(
+        "lm_moe_mlp_decode_offload",
+        lib().lm_moe_mlp_decode_offload(
+            _ptr(hidden), int(top_k), _ptr(row_to_pair), _ptr(group_offsets), _ptr(group_src),
+            _ptr(group_expert), int(group_begin), int(group_end), int(max_rows_per_group),
+            _ptr(w13_slots), _ptr(w2_slots), w13_slots.shape[0], _ptr(w13_host), _ptr(w2_host),
+            w13_host.shape[0], H, I, _ptr(act), _ptr(y_perm), _ptr(err_word), _stream(),
         ),
     )
 

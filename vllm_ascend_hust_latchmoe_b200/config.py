@@ -26,6 +26,9 @@ class MoeOffloadConfig:
     offload_stage_seam: bool = False
     b2_wave_prefill: bool = False
     b2_reference_full_layer: bool = False
+    # B200 addition: decode staging decided on the device (lm_slot_plan) and missed experts
+    # read over PCIe by the MLP itself; no host round trip per layer.
+    device_staging: bool = False
     pin_host_memory: bool | None = None
     transfer_aware_wave_schedule: bool = True
     prefill_prefetch_depth: int = 1
@@ -60,6 +63,7 @@ class MoeOffloadConfig:
             offload_stage_seam=env.get("VLLM_ASCEND_MOE_OFFLOAD_STAGE_SEAM"),
             b2_wave_prefill=env.get("VLLM_ASCEND_MOE_OFFLOAD_B2_WAVE_PREFILL"),
             b2_reference_full_layer=bool(env.get("VLLM_ASCEND_MOE_OFFLOAD_B2_REFERENCE_FULL_LAYER")),
+            device_staging=bool(env.get("VLLM_ASCEND_MOE_OFFLOAD_DEVICE_STAGING")),
             pin_host_memory=env.get("VLLM_ASCEND_MOE_OFFLOAD_PIN_HOST_MEMORY"),
             transfer_aware_wave_schedule=env.get("VLLM_ASCEND_MOE_OFFLOAD_TRANSFER_AWARE_SCHEDULE"),
             prefill_prefetch_depth=env.get("VLLM_ASCEND_MOE_OFFLOAD_PREFILL_PREFETCH_DEPTH"),

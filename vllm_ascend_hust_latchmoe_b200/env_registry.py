@@ -98,6 +98,16 @@ ENVIRONMENT_VARIABLES: dict[str, Callable[[], Any]] = {
     name: (lambda n=name, k=kind, d=default: _parse(k, n, d)) for name, kind, default in _SPEC
 }
 
+# Settings of the B200 build that the reference does not have (kept apart from the
+# reference's inventory above).
+_B200_SPEC: tuple[tuple[str, str, str | None], ...] = (
+    ("VLLM_ASCEND_MOE_OFFLOAD_DEVICE_STAGING", "bool", None),
+)
+
+B200_ENVIRONMENT_VARIABLES: dict[str, Callable[[], Any]] = {
+    name: (lambda n=name, k=kind, d=default: _parse(k, n, d)) for name, kind, default in _B200_SPEC
+}
+
 _registered = False
 
 
@@ -111,7 +121,8 @@ def register_environment_variables() -> dict[str, Callable[[], Any]]:
 
         table = getattr(vllm_envs, "environment_variables", None)
         if isinstance(table, dict):
-            for name, loader in ENVIRONMENT_VARIABLES.items():
+            for name, loader in (*ENVIRONMENT_VARIABLES.items(),
+                                 *B200_ENVIRONMENT_VARIABLES.items()):
                 table.setdefault(name, loader)
     except Exception:
         pass
@@ -120,4 +131,5 @@ def register_environment_variables() -> dict[str, Callable[[], Any]]:
 
 
 def get(name: str) -> Any:
-    return ENVIRONMENT_VARIABLES[name]()
+    loader = ENVIRONMENT_VARIABLES.get(name) or B200_ENVIRONMENT_VARIABLES[name]
+    return loader()

@@ -57,7 +57,7 @@ def mlp_launches(T: int) -> int:
 
 @dataclass
 class StageDecision:
-    mode: str                 # "capturing" | "static" | "slots" | "waves" | "passthrough"
+    mode: str  # "capturing" | "static" | "slots" | "waves" | "resident" | "device" | "passthrough"
     active_experts: tuple[int, ...] = ()
     counts: tuple[int, ...] = ()
     prepared: object | None = None
@@ -138,6 +138,18 @@ class SlotBankMoE:
         self.resident_tier = runtime.host_layer(self.layer_id).on_device
         self.last_waves = WaveReport()
         self.last_fallback_reason: str | None = None
+        # Device staging (decode): slot state kept on the GPU, see lm_slot_plan.
+        self.device_staging = bool(runtime.config.device_staging) and not self.resident_tier
+        if self.device_staging:
+            if self.E_total != self.E:
+                raise ValueError("device staging serves routed experts only (no fused shared rows)")
+            S = int(runtime.config.num_slots)
+            self.slot_owner = torch.full((S,), -1, dtype=i32, device=d)
+            self.slot_last_used = torch.full((S,), -1, dtype=torch.int64, device=d)
+            self.expert_slot = torch.full((self.E_total,), -1, dtype=i32, device=d)
+            self.stage_step = torch.zeros(1, dtype=torch.int64, device=d)
+            self.group_src = torch.full((self.E_total,), -1, dtype=i32, device=d)
+            self.hit_miss = torch.zeros(2, dtype=torch.int64, device=d)
         self.last_full_layer: dict | None = None
         self.kernel_launches = 0
         self.pending: StageDecision | None = None
@@ -171,6 +183,17 @@ class SlotBankMoE:
               capturing: bool = False) -> StageDecision:
         """Eager staging seam between the captured router and MLP pieces."""
         rt = self.runtime
+        T = int(topk_ids.shape[0])
+        if self.device_staging:
+            # Decode: the slot decision runs on the device inside the MLP piece (capturable).
+            # Prefill: capacity-bounded waves, which never write the main bank, so the slot
+            # state held on the device stays the bank's only owner.
+            if T <= DECODE_MAX_TOKENS:
+                return StageDecision("device")
+            if capturing or torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("prefill-sized calls are not captured under device staging")
+            counts = self.active_counts(topk_ids)
+            return StageDecision("waves", tuple(e for e, c in enumerate(counts) if c > 0), counts)
         if capturing or torch.cuda.is_current_stream_capturing():
             if rt.should_use_fixed_slot_plan_for_layer(self.layer_id) and not rt.is_layer_registered(self.layer_id):
                 raise RuntimeError(f"graph capture reached an unregistered fixed-slot MoE layer {self.layer_id}")
@@ -217,6 +240,29 @@ class SlotBankMoE:
                           self.row_to_pair, self.scratch, self.err)
         self._grouped_mlp(hidden, T, self.slot_rows, 0, G, bank.w13_slots, bank.w2_slots)
         self.kernel_launches += 3 + mlp_launches(T) + 1  # grouping (3), MLP, combine
+        return self._combine(T, out)
+
+    def mlp_device(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Decode MLP piece with the staging decision on the device: slot allocation
+        (``lm_slot_plan``), grouping by expert id, the MLP reading hits from their slots and
+        misses from the pinned host store (written through into their slots), combine. No
+        host synchronisation; fixed buffers only, so it can be captured."""
+        if not self.device_staging or T > DECODE_MAX_TOKENS:
+            raise RuntimeError(f"layer {self.layer_id}: device staging serves decode-sized calls")
+        rt = self.runtime
+        bank = rt.slot_bank(self.layer_id)
+        store = rt.host_layer(self.layer_id)
+        ids = self.topk_ids[:T]
+        _lib.slot_plan(ids, self.E, self.slot_owner, self.slot_last_used, self.expert_slot,
+                       self.stage_step, rt.log2phy_buffer(self.layer_id), self.group_src,
+                       self.hit_miss, self.err)
+        _lib.build_groups(ids, self.E_total, self.identity_groups, self.E, self.group_offsets,
+                          self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+        _lib.moe_mlp_decode_offload(hidden, self.k, self.row_to_pair, self.group_offsets,
+                                    self.group_src, self.identity_groups, 0, self.E, T,
+                                    bank.w13_slots, bank.w2_slots, store.w13, store.w2,
+                                    self.act, self.y_perm, self.err)
+        self.kernel_launches += 1 + 3 + 2 + 1  # plan, grouping (3), MLP, combine
         return self._combine(T, out)
 
     def mlp_resident(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -428,6 +474,8 @@ class SlotBankMoE:
                 out: torch.Tensor | None = None) -> torch.Tensor:
         """MLP piece for a stage decision (the seam's second captured piece, or eager)."""
         T = int(hidden.shape[0])
+        if decision.mode == "device":
+            return self.mlp_device(hidden, T, out)
         if decision.mode == "waves":
             return self.forward_waves(hidden, T, decision.counts, out)
         if decision.mode == "resident":
