@@ -501,6 +501,13 @@ def main() -> None:
             lay.check_device_errors("bench tpot")
         del dec
         torch.cuda.empty_cache()
+        dec = SyntheticMoEDecoder(shape, offloaded_layers=offl, device=dev, seed=rank,
+                                  device_staging=True)
+        rep_dev = dec.run(shape.max_new, warmup=8)
+        for lay in dec.moe:
+            lay.check_device_errors("bench tpot (device staging)")
+        del dec
+        torch.cuda.empty_cache()
         dec = SyntheticMoEDecoder(shape, offloaded_layers=[], device=dev, seed=rank)
         rep_res = dec.run(shape.max_new, warmup=8)
         del dec
@@ -513,6 +520,14 @@ def main() -> None:
                 "h2d_gbs_per_token_time": rep.h2d_bytes_per_step / (rep.tpot_ms_p50 / 1e3) / 1e9,
                 "slot_hit_rate": rep.slot_hit_rate, "graphs_per_token": rep.graphs,
                 "stage_host_ms_per_token": rep.stage_ms_per_step,
+                "device_staging": {
+                    "tpot_ms_p50": rep_dev.tpot_ms_p50, "tpot_ms_p95": rep_dev.tpot_ms_p95,
+                    "h2d_bytes_per_token": rep_dev.h2d_bytes_per_step,
+                    "h2d_gbs_per_token_time":
+                        rep_dev.h2d_bytes_per_step / (rep_dev.tpot_ms_p50 / 1e3) / 1e9,
+                    "slot_hit_rate": rep_dev.slot_hit_rate, "graphs_per_token": rep_dev.graphs,
+                    "staging": "slot decision on the GPU (lm_slot_plan); misses read over "
+                               "PCIe by the MLP and written through into their slots"},
                 "all_resident_tpot_ms_p50": rep_res.tpot_ms_p50,
                 "all_resident_tpot_ms_p95": rep_res.tpot_ms_p95,
                 "data": "random-init weights and KV; synthetic routing"}

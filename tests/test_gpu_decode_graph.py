@@ -43,3 +43,29 @@ def test_tpot_report_tiny(cuda):
     assert rep.graphs == 3 and rep.tpot_ms_p50 > 0 and rep.slot_hit_rate is not None
     with pytest.raises(ValueError):
         d.run(steps=TINY.max_new + 1)
+
+
+def test_device_staged_decoder_is_one_graph_and_matches_host_staging(cuda):
+    """Device staging: no stage seam, a token is one captured graph; it takes the same slot
+    decisions as the host-staged decoder (log2phy equal every step) and the same hidden
+    state."""
+    a = SyntheticMoEDecoder(TINY, offloaded_layers=(1, 3), device=cuda, seed=7,
+                            teacher_forcing=True, device_staging=True)
+    b = SyntheticMoEDecoder(TINY, offloaded_layers=(1, 3), device=cuda, seed=7,
+                            teacher_forcing=True)
+    assert a.capture() == 1
+    a.reset_position()
+    b.reset_position()
+    for t in range(12):
+        a.step(t)
+        b.step_eager(t)
+        torch.cuda.synchronize()
+        for la, lb in zip(a.moe, b.moe):
+            assert torch.equal(la.topk_ids[:1], lb.topk_ids[:1]), t
+        for i in (1, 3):
+            assert torch.equal(a.runtime.log2phy_buffer(i), b.runtime.log2phy_buffer(i)), t
+        torch.testing.assert_close(a.h2.float(), b.h2.float(), rtol=2e-2, atol=2e-2)
+    for layer in a.moe + b.moe:
+        layer.check_device_errors()
+    rep = a.run(steps=8, warmup=2)
+    assert rep.graphs == 1 and rep.tpot_ms_p50 > 0 and rep.slot_hit_rate is not None

@@ -76,7 +76,8 @@ def _rand(shape, device, std=0.02, gen=None):
 
 class SyntheticMoEDecoder:
     def __init__(self, shape: DecoderShape, offloaded_layers, device, seed: int = 0,
-                 keep_prob: float = 0.7, host_store=None, teacher_forcing: bool = False):
+                 keep_prob: float = 0.7, host_store=None, teacher_forcing: bool = False,
+                 device_staging: bool = False):
         self.s = s = shape
         self.device = d = torch.device(device)
         self.offloaded = sorted(set(int(i) for i in offloaded_layers))
@@ -103,9 +104,13 @@ class SyntheticMoEDecoder:
 
         # experts: resident layers own an HBM store; offloaded layers share one pinned store
         I = s.intermediate
+        # device_staging: offloaded layers decide their staging on the GPU and read missed
+        # experts over PCIe inside the MLP piece, so a whole token is one graph.
+        self.device_staging = bool(device_staging)
         self.runtime = MoeOffloadRuntime(MoeOffloadConfig(
             enabled=True, num_slots=s.num_slots, async_load=True, b2_wave_prefill=True,
-            graph_compatible_offload=True, pin_host_memory=True))
+            graph_compatible_offload=True, pin_host_memory=True,
+            device_staging=self.device_staging))
         if self.offloaded:
             if host_store is None:
                 w13 = torch.empty(s.experts, 2 * I, H, dtype=torch.bfloat16, pin_memory=True)
@@ -184,7 +189,12 @@ class SyntheticMoEDecoder:
 
     def _moe(self, i):
         layer = self.moe[i]
-        out = layer.mlp_slots(self.h2, 1) if i in self.offloaded else layer.mlp_resident(self.h2, 1)
+        if i not in self.offloaded:
+            out = layer.mlp_resident(self.h2, 1)
+        elif self.device_staging:
+            out = layer.mlp_device(self.h2, 1)
+        else:
+            out = layer.mlp_slots(self.h2, 1)
         self.x.add_(out)
 
     def _head(self):
@@ -200,7 +210,7 @@ class SyntheticMoEDecoder:
         segs, cur = [], []
         for i in range(self.s.layers):
             cur.append(lambda i=i: self._attention(i))
-            if i in self.offloaded:
+            if i in self.offloaded and not self.device_staging:
                 segs.append((cur, i))
                 cur = []
             cur.append(lambda i=i: self._moe(i))
@@ -287,6 +297,17 @@ class SyntheticMoEDecoder:
         rt.end_slot_compute(pending)
         return stage_s
 
+    def _stage_counts(self) -> dict:
+        """Hits, misses and H2D bytes so far (device counters under device staging)."""
+        if not self.device_staging:
+            return dict(self.runtime.stage_stats)
+        hits = misses = 0
+        for i in self.offloaded:
+            h, m = self.moe[i].hit_miss.tolist()
+            hits, misses = hits + h, misses + m
+        per_expert = self.host_store[0][0].nbytes + self.host_store[1][0].nbytes
+        return {"hits": hits, "misses": misses, "h2d_bytes": misses * per_expert}
+
     def run(self, steps: int | None = None, warmup: int = 8) -> TpotReport:
         steps = int(steps or self.s.max_new)
         if steps > self.s.max_new or warmup > self.s.max_new:
@@ -297,7 +318,7 @@ class SyntheticMoEDecoder:
             self.step(t)
         torch.cuda.synchronize()
         self.reset_position()
-        st = self.runtime.stage_stats
+        st = self._stage_counts()
         h0, m0, c0 = st["h2d_bytes"], st["misses"], st["hits"]
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
         evs[0].record()
@@ -307,6 +328,7 @@ class SyntheticMoEDecoder:
             evs[t + 1].record()
         torch.cuda.synchronize()
         ms = [evs[t].elapsed_time(evs[t + 1]) for t in range(steps)]
+        st = self._stage_counts()
         h2d = (st["h2d_bytes"] - h0) / steps
         misses, hits = st["misses"] - m0, st["hits"] - c0
         srt = sorted(ms)
