@@ -260,6 +260,53 @@ int lm_moe_mlp_decode_offload(const uint16_t* hidden, int32_t top_k,
                               int32_t intermediate_size, uint16_t* act, uint16_t* y_perm,
                               int32_t* err_word, void* stream);
 
+/*
+ * Expert-parallel exchange over peer memory (one process per GPU; no NCCL on the data path).
+ * Each rank allocates one region (lm_ep_region_alloc, size lm_ep_region_bytes) and maps every
+ * other rank's region (lm_ipc_get_handle -> exchange the 64-byte handles -> lm_ipc_open_handle).
+ * peer_regions is a DEVICE array of `world` pointers (entry `rank` = the rank's own region).
+ * cap = most routed pairs one source sends to one owner. epoch = a call counter, the same on
+ * every rank and increasing by one per layer call (flags hold the last epoch seen).
+ * Per layer call, in stream order on every rank:
+ *   lm_ep_dispatch      pairs grouped by owner (pair_to_row / send_offsets from
+ *                       lm_build_groups with expert -> owner); each pair's hidden row and
+ *                       owner-local expert id go straight into the owner's region.
+ *   lm_ep_receive       waits for every source's dispatch (bounded), compacts the received rows
+ *                       and ids into rows_out / ids_out; *total_out = their number (device).
+ *   (local expert MLP, outputs written in received order at region + lm_ep_out_rows_offset)
+ *   lm_ep_signal_outputs  tells every source the outputs are there.
+ *   lm_ep_combine       waits for every owner (bounded), reads each pair's output row from its
+ *                       owner and reduces out[t] = sum_j w[t,j] * y[t,j] in fp32, j in order.
+ * done_counter: one device int32, zero before the first call. Waits that run out set
+ * LM_DEVERR_WAIT_TIMEOUT. Ranks must be on distinct GPUs.
+ * Replaces: nothing in the reference, which is single-device
+ * (patches/patch_fused_moe.py:4898-4914); the combine follows token_combine's order
+ * (moe_offload/phase_split.py:1765-1856).
+ */
+int64_t lm_ep_region_bytes(int32_t world, int32_t cap, int32_t hidden_size);
+int64_t lm_ep_out_rows_offset(int32_t world, int32_t cap, int32_t hidden_size);
+int lm_ep_region_alloc(int64_t bytes, void** region);
+int lm_ep_region_free(void* region);
+int lm_ipc_get_handle(const void* region, void* handle_out /* 64 bytes */);
+int lm_ipc_open_handle(const void* handle /* 64 bytes */, void** region_out);
+int lm_ipc_close_handle(void* region);
+int lm_ep_dispatch(const uint16_t* hidden, int64_t num_tokens, int32_t top_k,
+                   int32_t hidden_size, const int32_t* topk_ids, int32_t experts_per_rank,
+                   const int32_t* pair_to_row, const int32_t* send_offsets, int32_t rank,
+                   int32_t world, void* const* peer_regions, int32_t cap, int64_t epoch,
+                   int32_t* done_counter, int32_t* err_word, void* stream);
+int lm_ep_receive(void* region, int32_t world, int32_t cap, int32_t hidden_size, int64_t epoch,
+                  uint16_t* rows_out, int32_t* ids_out, int32_t* total_out, int32_t* err_word,
+                  void* stream);
+int lm_ep_signal_outputs(void* const* peer_regions, int32_t rank, int32_t world, int32_t cap,
+                         int32_t hidden_size, int64_t epoch, void* stream);
+int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,
+                  int64_t num_tokens, int32_t top_k, int32_t hidden_size,
+                  int32_t experts_per_rank, const int32_t* pair_to_row,
+                  const int32_t* send_offsets, int32_t rank, int32_t world,
+                  void* const* peer_regions, void* local_region, int32_t cap, int64_t epoch,
+                  uint16_t* out, int32_t* err_word, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,5 +1,6 @@
-"""Expert-parallel layer on 2 GPUs with NCCL: each rank owns half of the experts in its own
-slot bank (pinned host store, staged) and the gathered outputs match the single-GPU oracle.
+"""Expert-parallel layer on 2 GPUs: each rank owns half of the experts in its own slot bank
+(pinned host store, staged, or HBM-resident) and the outputs match the single-GPU oracle,
+with the exchange over NCCL or over peer memory (the library's dispatch / combine kernels).
 Skipped with fewer than 2 GPUs."""
 
 import os
@@ -20,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, store_on_device, q):
+def _worker(rank, world, port, store_on_device, transport, q):
     import datetime
 
     import torch.distributed as dist
@@ -30,7 +31,7 @@ def _worker(rank, world, port, store_on_device, q):
     from oracle.bf16 import bf16_bits_to_f32
     from tests.helpers import bits
     from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
-    from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE,
+    from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE, PeerExchange,
                                                                 build_rank_layer, cuda_ops)
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -49,15 +50,26 @@ def _worker(rank, world, port, store_on_device, q):
                                  w2_owned=w2[rank * per:(rank + 1) * per], rank=rank,
                                  device=dev, max_rows=world * T * K, num_slots=S,
                                  store_on_device=store_on_device)
+        exchange = None
+        if transport == "peer":
+            exchange = PeerExchange(world_size=world, rank=rank, max_tokens=T, top_k=K,
+                                    hidden_size=H, device=dev)
         ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
-                               world_size=world, device=dev,
+                               world_size=world, device=dev, exchange=exchange,
                                ops=cuda_ops(local, num_experts=E, top_k=K, max_tokens=T))
+        # a call with other routing first: the checked call reuses every area and flag
+        ep.forward(syn.make_hidden(cfg, seed=30 + rank).to(dev),
+                   syn.make_router_logits(cfg, seed=30 + rank).to(dev))
         hidden = syn.make_hidden(cfg, seed=10 + rank)
         logits = syn.make_router_logits(cfg, seed=10 + rank)
-        for _ in range(2):  # second call reuses every buffer
+        for _ in range(2):
             out = ep.forward(hidden.to(dev), logits.to(dev))
         torch.cuda.synchronize()
         local.check_device_errors("ep")
+        ep.check_exchange_errors()
+        if exchange is not None:
+            out = out.clone()
+            exchange.close()
         wb, _, ids = orouter.route(logits.numpy(), K)
         ref = omlp.moe_layer(bits(hidden), ids, wb, bits(w13), bits(w2))
         m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)
@@ -70,8 +82,9 @@ def _worker(rank, world, port, store_on_device, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("transport", ["nccl", "peer"])
 @pytest.mark.parametrize("store_on_device", [False, True])
-def test_ep_two_gpus_matches_oracle(store_on_device):
+def test_ep_two_gpus_matches_oracle(store_on_device, transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -79,7 +92,8 @@ def test_ep_two_gpus_matches_oracle(store_on_device):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, store_on_device, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, store_on_device, transport, q))
+             for r in range(2)]
     for p in procs:
         p.start()
     results = sorted(q.get(timeout=300) for _ in procs)

@@ -43,6 +43,23 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _P, _P, _P, _P],
     ),
     "lm_expert_histogram": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _P]),
+    "lm_ep_region_bytes": (ctypes.c_int64, [_I32, _I32, _I32]),
+    "lm_ep_out_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
+    "lm_ep_region_alloc": (ctypes.c_int, [_I64, ctypes.POINTER(ctypes.c_void_p)]),
+    "lm_ep_region_free": (ctypes.c_int, [_P]),
+    "lm_ipc_get_handle": (ctypes.c_int, [_P, _P]),
+    "lm_ipc_open_handle": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "lm_ipc_close_handle": (ctypes.c_int, [_P]),
+    "lm_ep_dispatch": (
+        ctypes.c_int,
+        [_P, _I64, _I32, _I32, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _I64, _P, _P, _P],
+    ),
+    "lm_ep_receive": (ctypes.c_int, [_P, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P]),
+    "lm_ep_signal_outputs": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _I64, _P]),
+    "lm_ep_combine": (
+        ctypes.c_int,
+        [_P, _P, _I64, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _P, _I32, _I64, _P, _P, _P],
+    ),
     "lm_slot_plan": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "lm_moe_mlp_decode_offload": (
         ctypes.c_int,
@@ -259,6 +276,72 @@ def moe_mlp_prefill(x_perm, total_rows, group_offsets, group_bank_row, group_beg
             w13_bank.shape[0], H, I, _ptr(act), _ptr(y_perm), _ptr(err_word), _stream(),
         ),
     )
+
+
+def ep_region_bytes(world: int, cap: int, hidden: int) -> int:
+    return int(lib().lm_ep_region_bytes(int(world), int(cap), int(hidden)))
+
+
+def ep_out_rows_offset(world: int, cap: int, hidden: int) -> int:
+    return int(lib().lm_ep_out_rows_offset(int(world), int(cap), int(hidden)))
+
+
+def ep_region_alloc(nbytes: int) -> int:
+    out = ctypes.c_void_p()
+    _check("lm_ep_region_alloc", lib().lm_ep_region_alloc(int(nbytes), ctypes.byref(out)))
+    return int(out.value)
+
+
+def ep_region_free(ptr: int) -> None:
+    _check("lm_ep_region_free", lib().lm_ep_region_free(ptr))
+
+
+def ipc_get_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(64)
+    _check("lm_ipc_get_handle", lib().lm_ipc_get_handle(ptr, buf))
+    return buf.raw
+
+
+def ipc_open_handle(handle: bytes) -> int:
+    buf = ctypes.create_string_buffer(bytes(handle), 64)
+    out = ctypes.c_void_p()
+    _check("lm_ipc_open_handle", lib().lm_ipc_open_handle(buf, ctypes.byref(out)))
+    return int(out.value)
+
+
+def ipc_close_handle(ptr: int) -> None:
+    _check("lm_ipc_close_handle", lib().lm_ipc_close_handle(ptr))
+
+
+def ep_dispatch(hidden, topk_ids, experts_per_rank, pair_to_row, send_offsets, rank, world,
+                peer_regions, cap, epoch, done_counter, err_word=None) -> None:
+    T, k = topk_ids.shape
+    _check("lm_ep_dispatch", lib().lm_ep_dispatch(
+        _ptr(hidden), T, k, hidden.shape[-1], _ptr(topk_ids), int(experts_per_rank),
+        _ptr(pair_to_row), _ptr(send_offsets), int(rank), int(world), _ptr(peer_regions),
+        int(cap), int(epoch), _ptr(done_counter), _ptr(err_word), _stream()))
+
+
+def ep_receive(region: int, world, cap, hidden_size, epoch, rows_out, ids_out, total_out,
+               err_word=None) -> None:
+    _check("lm_ep_receive", lib().lm_ep_receive(
+        region, int(world), int(cap), int(hidden_size), int(epoch), _ptr(rows_out),
+        _ptr(ids_out), _ptr(total_out), _ptr(err_word), _stream()))
+
+
+def ep_signal_outputs(peer_regions, rank, world, cap, hidden_size, epoch) -> None:
+    _check("lm_ep_signal_outputs", lib().lm_ep_signal_outputs(
+        _ptr(peer_regions), int(rank), int(world), int(cap), int(hidden_size), int(epoch),
+        _stream()))
+
+
+def ep_combine(topk_ids, topk_weights_bf16, experts_per_rank, pair_to_row, send_offsets, rank,
+               world, peer_regions, local_region: int, cap, epoch, out, err_word=None) -> None:
+    T, k = topk_ids.shape
+    _check("lm_ep_combine", lib().lm_ep_combine(
+        _ptr(topk_ids), _ptr(topk_weights_bf16), T, k, out.shape[-1], int(experts_per_rank),
+        _ptr(pair_to_row), _ptr(send_offsets), int(rank), int(world), _ptr(peer_regions),
+        local_region, int(cap), int(epoch), _ptr(out), _ptr(err_word), _stream()))
 
 
 LM_SRC_MISS = 0x40000000

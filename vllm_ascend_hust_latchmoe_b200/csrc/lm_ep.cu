@@ -1,0 +1,417 @@
+// Expert-parallel exchange over peer memory (NVLink / NVSwitch), one process per GPU.
+//
+// Every rank owns one "region" allocated with cudaMalloc and mapped into every other rank's
+// address space through CUDA IPC. Layout (lm_ep_layout): arrival flags of the dispatch and of
+// the outputs (one int64 per source rank), the per-source row counts, the owner's exclusive
+// prefix of those counts, and a capacity-strided receive area (source s writes its rows at
+// [s * cap, s * cap + count)), plus the owner's output rows in compacted order.
+//
+//   dispatch (source r):  gather each routed pair's hidden row and store it straight into the
+//                         owner's receive area (plus its owner-local expert id); the last
+//                         block stores the counts and raises r's flag in every owner.
+//   receive  (owner o):   wait for every source's flag (bounded), prefix the counts, compact
+//                         the rows for the local expert MLP.
+//   signal   (owner o):   raise o's output flag in every source once its outputs are written.
+//   combine  (source r):  wait for every owner's output flag (bounded), then per token read
+//                         its pairs' output rows from the owners' memory and reduce them in
+//                         fp32 in the original top-k order.
+// A source only re-dispatches after its combine read every owner's outputs (stream order),
+// and an owner only compacts / overwrites after every source's next dispatch flag, so the
+// areas need no other barrier. Flags carry the call's epoch (the same on every rank).
+// No kernel waits on a kernel of its own GPU; waits are bounded and report
+// LM_DEVERR_WAIT_TIMEOUT. No TMA and no multicast: plain peer loads and stores.
+#include <cstring>
+
+#include "lm_common.cuh"
+
+namespace lm {
+namespace {
+
+constexpr int kLayoutFields = 8;
+enum : int { F_FLAG_DISPATCH = 0, F_FLAG_OUT, F_COUNTS, F_PREFIX, F_RECV_IDS, F_RECV_ROWS,
+             F_OUT_ROWS, F_TOTAL };
+
+int64_t align256(int64_t v) { return (v + 255) & ~static_cast<int64_t>(255); }
+
+void layout(int G, int cap, int H, int64_t* off) {
+  int64_t o = 0;
+  off[F_FLAG_DISPATCH] = o;
+  o = align256(o + 8ll * G);
+  off[F_FLAG_OUT] = o;
+  o = align256(o + 8ll * G);
+  off[F_COUNTS] = o;
+  o = align256(o + 4ll * G);
+  off[F_PREFIX] = o;
+  o = align256(o + 4ll * (G + 1));
+  off[F_RECV_IDS] = o;
+  o = align256(o + 4ll * G * cap);
+  off[F_RECV_ROWS] = o;
+  o = align256(o + 2ll * G * cap * H);
+  off[F_OUT_ROWS] = o;
+  o = align256(o + 2ll * G * cap * H);
+  off[F_TOTAL] = o;
+}
+
+struct Layout {
+  int64_t off[kLayoutFields];
+};
+
+template <typename T>
+__device__ __forceinline__ T* field(void* region, const Layout& L, int f) {
+  return reinterpret_cast<T*>(static_cast<uint8_t*>(region) + L.off[f]);
+}
+
+__device__ __forceinline__ void st_release_sys(long long* p, long long v) {
+  asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until flags[s] >= epoch for every s < G, by one full warp; the result is the
+// same in every lane (false on time-out).
+__device__ bool wait_flags(const long long* flags, int G, long long epoch, int32_t* err_word) {
+  const long long t0 = clock64();
+  bool ok = true;
+  for (int s = threadIdx.x; s < G && ok; s += 32) {
+    while (ld_acquire_sys(flags + s) < epoch) {
+      if (clock64() - t0 > LM_SPIN_LIMIT_CYCLES) {
+        record_error(err_word, LM_DEVERR_WAIT_TIMEOUT);
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+__global__ void __launch_bounds__(256)
+    ep_dispatch_kernel(const uint16_t* __restrict__ hidden, int64_t num_pairs, int top_k, int H,
+                       const int32_t* __restrict__ ids, int per_rank,
+                       const int32_t* __restrict__ pair_to_row,
+                       const int32_t* __restrict__ send_offsets, int rank, int G,
+                       void* const* __restrict__ peers, Layout L, int cap, long long epoch,
+                       int32_t* __restrict__ done, int32_t* __restrict__ err_word) {
+  // one warp per pair
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t p = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       p < num_pairs; p += warps) {
+    const int e = ids[p];
+    const int o = e / per_rank;
+    if (e < 0 || o >= G) {
+      if (lane == 0) record_error(err_word, LM_DEVERR_BAD_EXPERT_ID);
+      continue;
+    }
+    const int pos = pair_to_row[p] - send_offsets[o];
+    if (pos < 0 || pos >= cap) {
+      if (lane == 0) record_error(err_word, LM_DEVERR_BAD_GROUP);
+      continue;
+    }
+    void* region = peers[o];
+    const int64_t slot = static_cast<int64_t>(rank) * cap + pos;
+    if (lane == 0) field<int32_t>(region, L, F_RECV_IDS)[slot] = e - o * per_rank;
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + (p / top_k) * static_cast<int64_t>(H));
+    uint4* dst = reinterpret_cast<uint4*>(field<uint16_t>(region, L, F_RECV_ROWS) + slot * H);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = __ldg(src + c);
+  }
+  __threadfence_system();
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) last = atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();
+  for (int o = threadIdx.x; o < G; o += blockDim.x)
+    field<int32_t>(peers[o], L, F_COUNTS)[rank] = send_offsets[o + 1] - send_offsets[o];
+  __threadfence_system();
+  __syncthreads();
+  for (int o = threadIdx.x; o < G; o += blockDim.x)
+    st_release_sys(field<long long>(peers[o], L, F_FLAG_DISPATCH) + rank, epoch);
+  if (threadIdx.x == 0) *done = 0;  // ready for the next call
+}
+
+__global__ void __launch_bounds__(32)
+    ep_receive_wait_kernel(void* region, Layout L, int G, int cap, long long epoch,
+                           int32_t* __restrict__ total_out, int32_t* __restrict__ err_word) {
+  int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
+  if (!wait_flags(field<long long>(region, L, F_FLAG_DISPATCH), G, epoch, err_word)) {
+    if (threadIdx.x == 0) {
+      for (int s = 0; s <= G; ++s) prefix[s] = 0;
+      *total_out = 0;
+    }
+    return;
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    const volatile int32_t* counts = field<int32_t>(region, L, F_COUNTS);
+    int run = 0;
+    for (int s = 0; s < G; ++s) {
+      int c = counts[s];
+      if (c < 0 || c > cap) {
+        record_error(err_word, LM_DEVERR_BAD_GROUP);
+        c = 0;
+      }
+      prefix[s] = run;
+      run += c;
+    }
+    prefix[G] = run;
+    *total_out = run;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    ep_compact_kernel(void* region, Layout L, int G, int cap, int H,
+                      uint16_t* __restrict__ rows_out, int32_t* __restrict__ ids_out) {
+  const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
+  const int32_t* recv_ids = field<int32_t>(region, L, F_RECV_IDS);
+  const uint16_t* recv_rows = field<uint16_t>(region, L, F_RECV_ROWS);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       q < static_cast<int64_t>(G) * cap; q += warps) {
+    const int s = static_cast<int>(q / cap), i = static_cast<int>(q - static_cast<int64_t>(s) * cap);
+    const int n = prefix[s + 1] - prefix[s];
+    if (i >= n) continue;
+    const int64_t d = prefix[s] + i;
+    if (lane == 0) ids_out[d] = __ldcg(recv_ids + q);
+    const uint4* src = reinterpret_cast<const uint4*>(recv_rows + q * H);
+    uint4* dst = reinterpret_cast<uint4*>(rows_out + d * H);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = __ldcg(src + c);
+  }
+}
+
+__global__ void ep_signal_kernel(void* const* __restrict__ peers, Layout L, int rank, int G,
+                                 long long epoch) {
+  __threadfence_system();
+  for (int o = threadIdx.x; o < G; o += blockDim.x)
+    st_release_sys(field<long long>(peers[o], L, F_FLAG_OUT) + rank, epoch);
+}
+
+__global__ void __launch_bounds__(32)
+    ep_wait_out_kernel(void* region, Layout L, int G, long long epoch, int32_t* err_word) {
+  wait_flags(field<long long>(region, L, F_FLAG_OUT), G, epoch, err_word);
+}
+
+// One block per token; the same accumulation order and arithmetic as combine_kernel.
+__global__ void ep_combine_kernel(const int32_t* __restrict__ ids,
+                                  const uint16_t* __restrict__ w_bf16, int top_k, int H,
+                                  int per_rank, const int32_t* __restrict__ pair_to_row,
+                                  const int32_t* __restrict__ send_offsets, int rank, int G,
+                                  void* const* __restrict__ peers, Layout L,
+                                  uint16_t* __restrict__ out) {
+  __shared__ const uint16_t* s_src[32];
+  __shared__ float s_w[32];
+  const int64_t t = blockIdx.x;
+  if (threadIdx.x < top_k) {
+    const int64_t p = t * top_k + threadIdx.x;
+    const int e = ids[p];
+    const int o = e / per_rank;
+    const uint16_t* src = nullptr;
+    if (e >= 0 && o < G) {
+      const int pos = pair_to_row[p] - send_offsets[o];
+      const int32_t* prefix = field<int32_t>(peers[o], L, F_PREFIX);
+      const int64_t row = __ldcg(prefix + rank) + pos;
+      src = field<uint16_t>(peers[o], L, F_OUT_ROWS) + row * H;
+    }
+    s_src[threadIdx.x] = src;
+    s_w[threadIdx.x] = bf16_bits_to_f32(w_bf16[p]);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int j = 0; j < top_k; ++j) {
+      const uint16_t* src = s_src[j];
+      if (src == nullptr) continue;
+      const float w = s_w[j];
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src) + c);
+      float a, b;
+      unpack_bf16x2(v.x, a, b);
+      acc[0] += w * a;
+      acc[1] += w * b;
+      unpack_bf16x2(v.y, a, b);
+      acc[2] += w * a;
+      acc[3] += w * b;
+      unpack_bf16x2(v.z, a, b);
+      acc[4] += w * a;
+      acc[5] += w * b;
+      unpack_bf16x2(v.w, a, b);
+      acc[6] += w * a;
+      acc[7] += w * b;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + t * H)[c] = o;
+  }
+}
+
+Layout make_layout(int G, int cap, int H) {
+  Layout L;
+  layout(G, cap, H, L.off);
+  return L;
+}
+
+int check_ep(const char* who, int G, int cap, int H) {
+  if (G <= 0 || G > 64 || cap <= 0 || H <= 0 || H % 8 != 0)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                std::string(who) + ": need 0 < world <= 64, cap > 0, hidden % 8 == 0");
+  return LM_OK;
+}
+
+}  // namespace
+}  // namespace lm
+
+using namespace lm;
+
+extern "C" int64_t lm_ep_region_bytes(int32_t world, int32_t cap, int32_t hidden_size) {
+  if (world <= 0 || cap <= 0 || hidden_size <= 0) return 0;
+  int64_t off[kLayoutFields];
+  layout(world, cap, hidden_size, off);
+  return off[F_TOTAL];
+}
+
+extern "C" int lm_ep_region_alloc(int64_t bytes, void** region) {
+  if (bytes <= 0 || region == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_region_alloc: bad size or null output");
+  void* p = nullptr;
+  int rc = check_cuda(cudaMalloc(&p, static_cast<size_t>(bytes)), "lm_ep_region_alloc: cudaMalloc");
+  if (rc) return rc;
+  rc = check_cuda(cudaMemset(p, 0, static_cast<size_t>(bytes)), "lm_ep_region_alloc: cudaMemset");
+  if (rc) {
+    cudaFree(p);
+    return rc;
+  }
+  *region = p;
+  return LM_OK;
+}
+
+extern "C" int lm_ep_region_free(void* region) {
+  if (region == nullptr) return LM_OK;
+  return check_cuda(cudaFree(region), "lm_ep_region_free");
+}
+
+extern "C" int lm_ipc_get_handle(const void* region, void* handle_out) {
+  if (region == nullptr || handle_out == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ipc_get_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  int rc = check_cuda(cudaIpcGetMemHandle(&h, const_cast<void*>(region)), "lm_ipc_get_handle");
+  if (rc) return rc;
+  std::memcpy(handle_out, &h, sizeof(h));
+  return LM_OK;
+}
+
+extern "C" int lm_ipc_open_handle(const void* handle, void** region_out) {
+  if (handle == nullptr || region_out == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ipc_open_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(region_out, h, cudaIpcMemLazyEnablePeerAccess),
+                    "lm_ipc_open_handle");
+}
+
+extern "C" int lm_ipc_close_handle(void* region) {
+  if (region == nullptr) return LM_OK;
+  return check_cuda(cudaIpcCloseMemHandle(region), "lm_ipc_close_handle");
+}
+
+extern "C" int lm_ep_dispatch(const uint16_t* hidden, int64_t num_tokens, int32_t top_k,
+                              int32_t hidden_size, const int32_t* topk_ids,
+                              int32_t experts_per_rank, const int32_t* pair_to_row,
+                              const int32_t* send_offsets, int32_t rank, int32_t world,
+                              void* const* peer_regions, int32_t cap, int64_t epoch,
+                              int32_t* done_counter, int32_t* err_word, void* stream) {
+  int rc = check_ep("lm_ep_dispatch", world, cap, hidden_size);
+  if (rc) return rc;
+  if (num_tokens < 0 || top_k <= 0 || experts_per_rank <= 0 || rank < 0 || rank >= world ||
+      epoch <= 0 || done_counter == nullptr || peer_regions == nullptr ||
+      send_offsets == nullptr || (num_tokens > 0 && (hidden == nullptr || topk_ids == nullptr ||
+                                                     pair_to_row == nullptr)))
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_dispatch: bad arguments");
+  if (reinterpret_cast<uintptr_t>(hidden) & 15)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_dispatch: hidden must be 16-byte aligned");
+  const int64_t pairs = num_tokens * top_k;
+  int64_t blocks = (pairs + 7) / 8;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 1184) blocks = 1184;
+  ep_dispatch_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      hidden, pairs, top_k, hidden_size, topk_ids, experts_per_rank, pair_to_row, send_offsets,
+      rank, world, peer_regions, make_layout(world, cap, hidden_size), cap, epoch, done_counter,
+      err_word);
+  return launch_status("lm_ep_dispatch");
+}
+
+extern "C" int lm_ep_receive(void* region, int32_t world, int32_t cap, int32_t hidden_size,
+                             int64_t epoch, uint16_t* rows_out, int32_t* ids_out,
+                             int32_t* total_out, int32_t* err_word, void* stream) {
+  int rc = check_ep("lm_ep_receive", world, cap, hidden_size);
+  if (rc) return rc;
+  if (region == nullptr || rows_out == nullptr || ids_out == nullptr || total_out == nullptr ||
+      epoch <= 0)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_receive: bad arguments");
+  const Layout L = make_layout(world, cap, hidden_size);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ep_receive_wait_kernel<<<1, 32, 0, s>>>(region, L, world, cap, epoch, total_out, err_word);
+  rc = launch_status("lm_ep_receive: wait");
+  if (rc) return rc;
+  int64_t blocks = (static_cast<int64_t>(world) * cap + 7) / 8;
+  if (blocks > 1184) blocks = 1184;
+  ep_compact_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(region, L, world, cap,
+                                                                 hidden_size, rows_out, ids_out);
+  return launch_status("lm_ep_receive: compact");
+}
+
+extern "C" int64_t lm_ep_out_rows_offset(int32_t world, int32_t cap, int32_t hidden_size) {
+  if (world <= 0 || cap <= 0 || hidden_size <= 0) return -1;
+  int64_t off[kLayoutFields];
+  layout(world, cap, hidden_size, off);
+  return off[F_OUT_ROWS];
+}
+
+extern "C" int lm_ep_signal_outputs(void* const* peer_regions, int32_t rank, int32_t world,
+                                    int32_t cap, int32_t hidden_size, int64_t epoch,
+                                    void* stream) {
+  int rc = check_ep("lm_ep_signal_outputs", world, cap, hidden_size);
+  if (rc) return rc;
+  if (peer_regions == nullptr || rank < 0 || rank >= world || epoch <= 0)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_signal_outputs: bad arguments");
+  ep_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      peer_regions, make_layout(world, cap, hidden_size), rank, world, epoch);
+  return launch_status("lm_ep_signal_outputs");
+}
+
+extern "C" int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,
+                             int64_t num_tokens, int32_t top_k, int32_t hidden_size,
+                             int32_t experts_per_rank, const int32_t* pair_to_row,
+                             const int32_t* send_offsets, int32_t rank, int32_t world,
+                             void* const* peer_regions, void* local_region, int32_t cap,
+                             int64_t epoch, uint16_t* out, int32_t* err_word, void* stream) {
+  int rc = check_ep("lm_ep_combine", world, cap, hidden_size);
+  if (rc) return rc;
+  if (top_k <= 0 || top_k > 32 || num_tokens < 0 || experts_per_rank <= 0 || rank < 0 ||
+      rank >= world || epoch <= 0 || peer_regions == nullptr || local_region == nullptr ||
+      (num_tokens > 0 && (topk_ids == nullptr || topk_weights_bf16 == nullptr ||
+                          pair_to_row == nullptr || send_offsets == nullptr || out == nullptr)))
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_combine: bad arguments");
+  if (reinterpret_cast<uintptr_t>(out) & 15)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_combine: out must be 16-byte aligned");
+  const Layout L = make_layout(world, cap, hidden_size);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ep_wait_out_kernel<<<1, 32, 0, s>>>(local_region, L, world, epoch, err_word);
+  rc = launch_status("lm_ep_combine: wait");
+  if (rc || num_tokens == 0) return rc;
+  int threads = hidden_size / 8;
+  if (threads > 256) threads = 256;
+  if (threads < 32) threads = 32;
+  ep_combine_kernel<<<static_cast<unsigned>(num_tokens), threads, 0, s>>>(
+      topk_ids, topk_weights_bf16, top_k, hidden_size, experts_per_rank, pair_to_row,
+      send_offsets, rank, world, peer_regions, L, out);
+  return launch_status("lm_ep_combine");
+}

@@ -21,6 +21,15 @@ no kernel reads peer memory and no TMA multicast is used.
 
 The compute steps are injectable (``ops``) so the exchange bookkeeping can be exercised on
 CPU ranks with gloo against the oracle; the default ``ops`` are the CUDA kernels.
+
+Two transports carry the exchange. ``"nccl"``: ``all_to_all_single`` of counts, rows and ids
+and back (the collective library; one host sync for the counts). ``"peer"`` (a
+:class:`PeerExchange`): the library's own kernels over peer memory mapped with CUDA IPC.
+``lm_ep_dispatch`` gathers each pair's row straight into the owner's receive area (no
+permute, no staging buffer), ``lm_ep_receive`` compacts on the owner, and ``lm_ep_combine``
+reads every pair's output row from its owner and reduces it in the original top-k order
+(no return collective). The owner's row count is read once on the host to size the local
+MLP.
 """
 
 from __future__ import annotations
@@ -53,10 +62,72 @@ class EPOps:
     combine: Callable          # (rows_back [P,H], p2r [P], weights [T,k]) -> out [T,H]
 
 
+class _DevicePtrArray:
+    """A raw device allocation seen as a tensor (``__cuda_array_interface__``)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3}
+
+
+class PeerExchange:
+    """One rank's peer-memory exchange area: its region (``lm_ep_region_alloc``) mapped into
+    every rank through CUDA IPC, the device array of all ranks' region pointers, and the
+    local buffers of the receive side. Ranks must be on distinct GPUs: the exchange's waits
+    spin on flags written by the other ranks' kernels."""
+
+    def __init__(self, *, world_size: int, rank: int, max_tokens: int, top_k: int,
+                 hidden_size: int, device: torch.device, group=None) -> None:
+        self.G, self.rank, self.H = int(world_size), int(rank), int(hidden_size)
+        self.cap = int(max_tokens) * int(top_k)
+        self.device = torch.device(device)
+        uuids = [None] * self.G
+        dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(self.device).uuid),
+                               group=group)
+        if len(set(uuids)) != self.G:
+            raise RuntimeError("peer exchange needs one rank per GPU (ranks share a device)")
+        nbytes = _lib.ep_region_bytes(self.G, self.cap, self.H)
+        self.region = _lib.ep_region_alloc(nbytes)
+        handles = [None] * self.G
+        dist.all_gather_object(handles, _lib.ipc_get_handle(self.region), group=group)
+        self.peer_ptrs = [self.region if r == self.rank else _lib.ipc_open_handle(handles[r])
+                          for r in range(self.G)]
+        self.peers = torch.tensor(self.peer_ptrs, dtype=torch.int64, device=self.device)
+        rows = self.G * self.cap
+        off = _lib.ep_out_rows_offset(self.G, self.cap, self.H)
+        self.out_rows = torch.as_tensor(
+            _DevicePtrArray(self.region + off, (rows, self.H), "<i2"),
+            device=self.device).view(torch.bfloat16)
+        self.rows = torch.empty(rows, self.H, dtype=torch.bfloat16, device=self.device)
+        self.ids = torch.empty(rows, dtype=torch.int32, device=self.device)
+        self.total = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        self.group = group
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Unmap the peers' regions and free this rank's (collective: every rank calls it)."""
+        if self.region is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for r, ptr in enumerate(self.peer_ptrs):
+            if r != self.rank:
+                _lib.ipc_close_handle(ptr)
+        dist.barrier(group=self.group)
+        self.out_rows = None
+        _lib.ep_region_free(self.region)
+        self.region = None
+
+
 class ExpertParallelMoE:
     def __init__(self, *, num_experts: int, top_k: int, hidden_size: int, rank: int,
                  world_size: int, ops: EPOps, group: dist.ProcessGroup | None = None,
-                 device: torch.device | str = "cuda") -> None:
+                 device: torch.device | str = "cuda",
+                 exchange: PeerExchange | None = None) -> None:
         if num_experts % world_size != 0:
             raise ValueError(f"{num_experts} experts do not split evenly over {world_size} ranks")
         self.E = int(num_experts)
@@ -71,11 +142,15 @@ class ExpertParallelMoE:
         self.device = torch.device(device)
         self.owner = (torch.arange(self.E, dtype=torch.int32) // self.per_rank).to(self.device)
         self.stats = EPStats()
+        self.exchange = exchange
+        self.transport = "peer" if exchange is not None else "nccl"
 
     def owned_experts(self) -> range:
         return range(self.base, self.base + self.per_rank)
 
     def forward(self, hidden: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        if self.exchange is not None:
+            return self._forward_peer(hidden, router_logits)
         T = int(hidden.shape[0])
         w, ids = self.ops.route(router_logits)
         offsets, p2r, r2p = self.ops.group_by_owner(ids, self.owner, self.G)
@@ -102,6 +177,37 @@ class ExpertParallelMoE:
         st.bytes_sent += (P - s_split[self.rank]) * self.H * elt * 2
         st.bytes_received += (R - r_split[self.rank]) * self.H * elt * 2
         return self.ops.combine(back, p2r[:P], w)
+
+    def _forward_peer(self, hidden: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        x = self.exchange
+        T = int(hidden.shape[0])
+        if T * self.k > x.cap:
+            raise ValueError(f"{T} tokens exceed the exchange capacity ({x.cap // self.k})")
+        w, ids = self.ops.route(router_logits)
+        offsets, p2r, _ = self.ops.group_by_owner(ids, self.owner, self.G)
+        x.epoch += 1
+        _lib.ep_dispatch(hidden, ids, self.per_rank, p2r, offsets, self.rank, self.G, x.peers,
+                         x.cap, x.epoch, x.done, x.err)
+        _lib.ep_receive(x.region, self.G, x.cap, self.H, x.epoch, x.rows, x.ids, x.total, x.err)
+        R = int(x.total.item())  # sizes the local expert MLP
+        if R:
+            self.ops.expert_mlp(x.rows[:R], x.ids[:R], out=x.out_rows[:R])
+        _lib.ep_signal_outputs(x.peers, self.rank, self.G, x.cap, self.H, x.epoch)
+        out = torch.empty(T, self.H, dtype=hidden.dtype, device=hidden.device)
+        _lib.ep_combine(ids, w, self.per_rank, p2r, offsets, self.rank, self.G, x.peers,
+                        x.region, x.cap, x.epoch, out, x.err)
+        counts = (offsets[1:] - offsets[:-1]).tolist()
+        st = self.stats
+        elt = hidden.element_size()
+        st.send_rows += T * self.k
+        st.recv_rows += R
+        st.bytes_sent += (T * self.k - counts[self.rank]) * self.H * elt
+        st.bytes_received += (T * self.k - counts[self.rank]) * self.H * elt
+        return out
+
+    def check_exchange_errors(self) -> None:
+        if self.exchange is not None:
+            _lib.raise_on_device_error(self.exchange.err, f"expert-parallel rank {self.rank}")
 
 
 def cuda_ops(local_moe, *, num_experts: int, top_k: int, renormalize: bool = True,
@@ -135,14 +241,14 @@ def cuda_ops(local_moe, *, num_experts: int, top_k: int, renormalize: bool = Tru
         _lib.permute_rows(hidden, rows, k, rows.numel(), out)
         return out
 
-    def expert_mlp(rows, local_ids):
+    def expert_mlp(rows, local_ids, out=None):
         R = rows.shape[0]
         if R == 0:
             return rows.new_empty((0, rows.shape[1]))
         local_moe.topk_ids[:R, 0].copy_(local_ids)
         local_moe.topk_w[:R].fill_(1.0)
         decision = local_moe.stage(local_moe.topk_ids[:R])
-        return local_moe.run_mlp(rows, decision)
+        return local_moe.run_mlp(rows, decision, out)
 
     def combine(back, p2r_, w):
         T = w.shape[0]
