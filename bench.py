@@ -220,13 +220,15 @@ def run_reference(args, cfg) -> dict:
 # --------------------------------------------------------------------------- C5 (N > 1)
 def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
     """Qwen3-235B-A22B-shaped layer with the expert bank partitioned over the ranks: 256
-    decode tokens per step in total (256 / N per rank), NCCL all-to-all dispatch/combine.
-    Two stores per rank: HBM-resident, and pinned host memory staged into half as many
-    slots as the rank owns experts. Times are the max over ranks."""
+    decode tokens per step in total (256 / N per rank). Cases: HBM-resident store with the
+    exchange over NCCL and over peer memory (the library's dispatch / combine kernels), and a
+    pinned-host store staged into half as many slots as the rank owns experts (peer
+    exchange). Times are the max over ranks; `hbm_gbs_per_rank` counts the weights of the
+    rank's active experts read once per step."""
     import torch
 
     from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
-    from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE,
+    from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE, PeerExchange,
                                                                 build_rank_layer, cuda_ops)
 
     cfg = syn.CONFIGS["c5_ep"]
@@ -238,16 +240,27 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
     w13 = (torch.randn(per, 2 * I, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
     w2 = (torch.randn(per, H, I, device=dev, generator=g) * 0.02).to(torch.bfloat16)
     hidden = syn.make_hidden(cfg, seed=rank, tokens=T).to(dev)
-    logits = syn.make_router_logits(cfg, seed=0, tokens=cfg.tokens)[rank * T:(rank + 1) * T].to(dev)
+    all_logits = syn.make_router_logits(cfg, seed=0, tokens=cfg.tokens)
+    logits = all_logits[rank * T:(rank + 1) * T].to(dev)
+    ids_all = torch.topk(all_logits, cfg.top_k, dim=1).indices
+    owned = ids_all[(ids_all // per) == rank]
+    active_owned = int(torch.unique(owned).numel())
+    expert_bytes = 6 * H * I
     out = {"workload": cfg.name, "tokens_per_step": cfg.tokens, "tokens_per_rank": T,
-           "experts_per_rank": per}
-    for name, on_dev, slots in (("resident", True, per), ("offloaded", False, max(1, per // 2))):
+           "experts_per_rank": per, "active_experts_rank": active_owned}
+    cases = (("resident_nccl", True, per, "nccl"), ("resident_peer", True, per, "peer"),
+             ("offloaded_peer", False, max(1, per // 2), "peer"))
+    for name, on_dev, slots, transport in cases:
         local = build_rank_layer(w13_owned=w13 if on_dev else w13.cpu(),
                                  w2_owned=w2 if on_dev else w2.cpu(), rank=rank, device=dev,
                                  max_rows=cfg.tokens * cfg.top_k, num_slots=slots,
                                  store_on_device=on_dev)
+        exchange = None
+        if transport == "peer":
+            exchange = PeerExchange(world_size=world, rank=rank, max_tokens=T,
+                                    top_k=cfg.top_k, hidden_size=H, device=dev)
         ep = ExpertParallelMoE(num_experts=cfg.num_experts, top_k=cfg.top_k, hidden_size=H,
-                               rank=rank, world_size=world, device=dev,
+                               rank=rank, world_size=world, device=dev, exchange=exchange,
                                ops=cuda_ops(local, num_experts=cfg.num_experts, top_k=cfg.top_k,
                                             max_tokens=T))
         for _ in range(3):
@@ -255,6 +268,7 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
         torch.cuda.synchronize()
         dist.barrier()
         sent0 = ep.stats.bytes_sent
+        h2d0 = local.runtime.transfer_engine.stats.bytes_h2d
         steps = 10
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
@@ -263,15 +277,20 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
         e.record()
         torch.cuda.synchronize()
         local.check_device_errors("bench ep")
+        ep.check_exchange_errors()
         ms = torch.tensor([s.elapsed_time(e) / steps], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        t_ms = float(ms.item())
         nv = (ep.stats.bytes_sent - sent0) / steps
-        h2d = local.runtime.transfer_engine.stats.bytes_h2d
-        out[name] = {"ms_per_step": float(ms.item()),
-                     "tokens_per_s": cfg.tokens / (float(ms.item()) / 1e3),
-                     "nvlink_bytes_sent_per_rank_step": nv,
+        h2d = (local.runtime.transfer_engine.stats.bytes_h2d - h2d0) / steps
+        out[name] = {"transport": transport, "ms_per_step": t_ms,
+                     "tokens_per_s": cfg.tokens / (t_ms / 1e3),
+                     "nvlink_bytes_per_rank_step": nv,
+                     "hbm_gbs_per_rank": active_owned * expert_bytes / (t_ms / 1e3) / 1e9,
                      "slots_per_rank": slots if not on_dev else None,
-                     "h2d_bytes_rank0_total": int(h2d)}
+                     "h2d_bytes_rank0_step": int(h2d)}
+        if exchange is not None:
+            exchange.close()
         del ep, local
         torch.cuda.empty_cache()
     return out

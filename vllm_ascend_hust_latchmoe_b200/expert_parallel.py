@@ -201,8 +201,9 @@ class ExpertParallelMoE:
         elt = hidden.element_size()
         st.send_rows += T * self.k
         st.recv_rows += R
-        st.bytes_sent += (T * self.k - counts[self.rank]) * self.H * elt
-        st.bytes_received += (T * self.k - counts[self.rank]) * self.H * elt
+        remote = (T * self.k - counts[self.rank]) * self.H * elt
+        st.bytes_sent += 2 * remote       # rows stored into owners + outputs read back
+        st.bytes_received += 2 * (R - int(counts[self.rank])) * self.H * elt
         return out
 
     def check_exchange_errors(self) -> None:
