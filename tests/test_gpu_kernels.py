@@ -174,7 +174,8 @@ def _mlp_case(cuda, T, k, E, H, I, G, use_prefill, seed=0, skewed=False, ids=Non
 
 
 @pytest.mark.parametrize("T,k,E,H,I", [(16, 8, 128, 2048, 768), (1, 8, 128, 2048, 768),
-                                       (64, 6, 64, 2048, 1408), (40, 8, 16, 256, 128)])
+                                       (64, 6, 64, 2048, 1408), (40, 8, 16, 256, 128),
+                                       (150, 2, 4, 512, 192)])
 def test_decode_mlp_matches_oracle(cuda, T, k, E, H, I):
     _mlp_case(cuda, T, k, E, H, I, 32, use_prefill=False)
 

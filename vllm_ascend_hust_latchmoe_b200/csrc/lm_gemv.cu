@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "lm_common.cuh"
+#include "lm_tmap.cuh"
 
 namespace lm {
 namespace {
@@ -319,6 +320,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   }
 }
 
+// Register-streaming launch pair: the fallback for calls whose (group, pass) count or group
+// count exceeds the persistent kernel's tables.
 template <int NC>
 int launch_decode(const uint16_t* hidden, int top_k, const int32_t* row_to_pair,
                   const int32_t* group_offsets, const int32_t* group_bank_row, int group_begin,
@@ -336,6 +339,567 @@ int launch_decode(const uint16_t* hidden, int top_k, const int32_t* row_to_pair,
   gemv_down_kernel<NC><<<grid2, block, 0, s>>>(act, group_offsets, group_bank_row, group_begin,
                                                 w2_bank, bank_rows, H, I, y_perm, err_word);
   return launch_status("lm_moe_mlp_decode: down");
+}
+
+// ------------------------------------------------------------ persistent decode MLP kernel
+// Both GEMMs of the decode MLP in one persistent launch (three CTAs per SM: more CTAs with
+// shallower rings stream faster than fewer with deeper ones, measured). The work is a queue
+// of small items, claimed one at a time with an atomic counter:
+//   gate_up item: 32 gate rows + the matching 32 up rows of one expert x one token pass
+//                 (8 * NC tokens of the group), over all of K = H;
+//   down item:    64 W2 rows of one expert x one token pass, over K = I.
+// All gate_up items come first in the queue, so a CTA that runs out of work early takes the
+// next item anywhere, and the tail of the launch is one small item, not a whole expert.
+// A down item reads the activations its expert's gate_up items wrote: each finished
+// gate_up warp adds one to the pass's counter (a release reduction) and the down
+// item's producer waits, bounded, until the count is complete. Items are claimed in queue
+// order and a CTA processes its items in claim order (it claims the next one only after
+// its current item's wait), so every awaited gate_up item belongs to a running CTA that
+// reaches it without waiting on anything later: the wait always ends.
+//
+// Per CTA: one producer warp and 4 consumer warps around a ring of stages. A stage covers
+// two 64-wide K tiles: the weight boxes, loaded by TMA from the bank's 3D tile map with box
+// depth two (gate_up: gate rows and, from a second lane, up rows, 8 KiB each; down: 16 KiB),
+// 128-byte swizzled, plus the matching K slices of the pass's 8 * NC token rows, copied by
+// all producer lanes with cp.async (zero-filled past the group's end or the last K tile) and
+// swizzled the same way. The stage's full barrier completes when the TMA bytes have landed
+// and all 32 lanes' copies have, so consumers read only shared memory. The producer also
+// writes each stage's item description next to the ring, published by the same barrier.
+//
+// The queue counter, the per-pass counters and an exit count live in a static per-device
+// pool of counter sets (one per stream, so launches on different streams never share
+// one); the last CTA to finish resets its set, so every launch starts from zeros.
+constexpr int kPdConsumers = 4;
+constexpr int kPdThreads = (kPdConsumers + 1) * 32;
+constexpr int kPdWeightBytes = 16384;  // per stage: 2 K tiles x 64 weight rows
+constexpr int kPdMaxGroups = 2048;
+constexpr int kPdMaxSlots = 2048;  // (group, pass) pairs per launch
+constexpr int kPdCounterSets = 16;
+constexpr int kPdFirst = 1, kPdLast = 2, kPdDown = 4, kPdExit = 8;
+
+struct PdCounters {
+  int32_t work;
+  int32_t exited;
+  int32_t done[kPdMaxSlots];
+};
+
+__device__ PdCounters g_pd_counters[kPdCounterSets];
+
+struct PdMeta {
+  int32_t r0;      // first row of the group
+  int32_t n;       // rows of the group
+  int32_t tok0;    // first row of the pass within the group
+  int32_t row0;    // first weight row of the item (gate / W2 row index)
+  int32_t kt;      // first K tile of the stage
+  int32_t ktiles;  // K tiles of the item
+  int32_t slot;    // (group, pass) index
+  int32_t flags;
+};
+
+struct PdParams {
+  CUtensorMap w13map;  // w13 bank tiles, box {64, 32, 2}
+  CUtensorMap w2map;   // w2 bank tiles, box {64, 64, 2}
+  const uint16_t* hidden;
+  const int32_t* row_to_pair;
+  const int32_t* group_offsets;
+  const int32_t* group_bank_row;
+  uint16_t* act;
+  uint16_t* y_perm;
+  int32_t* err_word;
+  int64_t bank_rows;
+  int32_t counter_set;
+  int32_t group_begin;
+  int32_t num_groups;
+  int32_t top_k;
+  int32_t H;
+  int32_t I;
+};
+
+template <int NC>
+__host__ __device__ constexpr int pd_stages() {
+  return NC == 8 ? 2 : 3;  // three CTAs per SM
+}
+
+template <int NC>
+__host__ __device__ constexpr int pd_stage_bytes() {
+  return kPdWeightBytes + 2 * NC * 8 * 128;  // multiple of 1024: bases stay swizzle-aligned
+}
+
+template <int NC>
+constexpr int pd_smem_bytes(int num_groups) {
+  return 1024 + pd_stages<NC>() * pd_stage_bytes<NC>() + ((num_groups + 1) * 4 + 15) / 16 * 16;
+}
+
+__device__ __forceinline__ uint4 lds_swz(const uint8_t* box, int row, int chunk) {
+  return *reinterpret_cast<const uint4*>(box + row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// 16-byte global -> shared copy through L2; src_bytes 0 writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+// Arrive on `bar` once this thread's earlier cp.async copies have completed (the barrier's
+// expected count includes this arrival).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+__device__ __forceinline__ void red_release_add_gpu(int32_t* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One queue item as the producer streams it. xrow[j]: the token row behind the lane's j-th
+// copied row (gate_up: the pair index, divided by top_k at use; down: the act row), or -1.
+template <int NC>
+struct PdItem {
+  int w;  // queue index; >= the item count: the queue is exhausted
+  int slot, row0, r0, n, bank, tok0;
+  bool down;
+  int xrow[2 * NC];
+};
+
+// Resolves queue index w (all producer lanes; lane l fills the rows it copies).
+template <int NC>
+__device__ __forceinline__ void pd_resolve(const PdParams& p, const int32_t* slot_prefix, int G,
+                                           int w, int items, int items_gu, int tiles_gu,
+                                           int tiles_dn, int lane, PdItem<NC>& it) {
+  it.w = w;
+  if (w >= items) return;
+  it.down = w >= items_gu;
+  const int wi = it.down ? w - items_gu : w;
+  const int tiles = it.down ? tiles_dn : tiles_gu;
+  it.slot = wi / tiles;
+  const int tile = wi - it.slot * tiles;
+  // group of the slot: the last g with slot_prefix[g] <= slot
+  int lo = 0, hi = G - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (slot_prefix[mid] <= it.slot) lo = mid; else hi = mid - 1;
+  }
+  it.r0 = p.group_offsets[p.group_begin + lo];
+  it.n = p.group_offsets[p.group_begin + lo + 1] - it.r0;
+  it.bank = p.group_bank_row[p.group_begin + lo];
+  it.tok0 = (it.slot - slot_prefix[lo]) * 8 * NC;
+  it.row0 = tile * (it.down ? 64 : 32);
+#pragma unroll
+  for (int j = 0; j < 2 * NC; ++j) {
+    const int tok = it.tok0 + j * 4 + (lane >> 3);
+    it.xrow[j] = tok >= it.n ? -1 : (it.down ? it.r0 + tok : p.row_to_pair[it.r0 + tok]);
+  }
+}
+
+template <int NC>
+__global__ void __launch_bounds__(kPdThreads)
+    gemv_persistent_kernel(const __grid_constant__ PdParams p) {
+  constexpr int S = pd_stages<NC>();
+  constexpr int kStage = pd_stage_bytes<NC>();
+  constexpr int kXSlice = NC * 8 * 128;  // one K tile of the pass's token rows
+  constexpr int kLaneRows = NC * 2;      // token rows one producer lane copies per K tile
+  constexpr int kPassRows = 8 * NC;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  int32_t* slot_prefix = reinterpret_cast<int32_t*>(ring + S * kStage);  // [num_groups + 1]
+  __shared__ uint64_t full[S], empty[S];
+  __shared__ PdMeta meta[S];
+  __shared__ int abort_flag;
+  PdCounters* ctr = &g_pd_counters[p.counter_set];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.num_groups;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1 + 32);  // lane 0's arrival + 32 lanes' copy arrivals
+      mbar_init(&empty[s], kPdConsumers);
+    }
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  volatile int* ab = &abort_flag;
+
+  if (warp == kPdConsumers) {
+    // ---------------------------------------------------------------- producer
+    // (group, pass) slots: slot_prefix[g] = slots of the groups before g. Empty groups and
+    // groups with an out-of-range bank row get none (the latter also set the error word).
+    int run = 0;
+    for (int base = 0; base < G; base += 128) {
+      // lane l: groups base + 4 l .. base + 4 l + 3, all table loads issued before any use
+      const int g0 = base + lane * 4;
+      int o[5], bk[4];
+#pragma unroll
+      for (int u = 0; u < 5; ++u)
+        o[u] = g0 + u <= G ? p.group_offsets[p.group_begin + g0 + u] : 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        bk[u] = g0 + u < G ? p.group_bank_row[p.group_begin + g0 + u] : 0;
+      int ps[4], tot = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int n = o[u + 1] - o[u];
+        ps[u] = 0;
+        if (g0 + u < G && n > 0) {
+          if (bk[u] < 0 || bk[u] >= p.bank_rows)
+            record_error(p.err_word, LM_DEVERR_BAD_GROUP);
+          else
+            ps[u] = (n + kPassRows - 1) / kPassRows;
+        }
+        tot += ps[u];
+      }
+      int incl = tot;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += v;
+      }
+      int excl = run + incl - tot;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (g0 + u < G) slot_prefix[g0 + u] = excl;
+        excl += ps[u];
+      }
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) slot_prefix[G] = run;
+    __syncwarp();
+    // more (group, pass) pairs than counters (max_rows_per_group understated the groups):
+    // nothing is computed and the error word says so
+    const bool fits = run <= kPdMaxSlots;
+    if (!fits) record_error(p.err_word, LM_DEVERR_BAD_GROUP);
+    const int slots = fits ? run : 0;
+    const int tiles_gu = p.I / 32, tiles_dn = p.H / 64;
+    const int items_gu = slots * tiles_gu;
+    const int items = items_gu + slots * tiles_dn;
+    const int kt_gu = p.H >> 6, kt_dn = p.I >> 6;
+    const int xchunk = lane & 7;
+    if (lane == 0) {
+      tma_prefetch_desc(&p.w13map);
+      tma_prefetch_desc(&p.w2map);
+    }
+    int i = 0;  // stages issued
+    bool ok = true;
+    // The next item is claimed halfway through the current one and resolved (group lookup,
+    // token rows) at its last stage, so neither the queue atomic nor the table loads stall
+    // the ring; a CTA holds at most one item beyond the one it streams.
+    PdItem<NC> cur;
+    {
+      int w = 0;
+      if (lane == 0) w = atomicAdd(&ctr->work, 1);
+      pd_resolve<NC>(p, slot_prefix, G, __shfl_sync(0xffffffffu, w, 0), items, items_gu,
+                     tiles_gu, tiles_dn, lane, cur);
+    }
+    while (ok && cur.w < items) {
+      const bool down = cur.down;
+      const int K = down ? p.I : p.H;
+      const int ktiles = down ? kt_dn : kt_gu;
+      if (down) {
+        // wait until the pass's gate_up items have all written their activations
+        const int need = tiles_gu * kPdConsumers;
+        bool ready = true;
+        if (lane == 0) {
+          const long long t0 = clock64();
+          while (ld_acquire_gpu(&ctr->done[cur.slot]) < need) {
+            if (*ab || clock64() - t0 > LM_SPIN_LIMIT_CYCLES) {
+              record_error(p.err_word, LM_DEVERR_WAIT_TIMEOUT);
+              *ab = 1;
+              ready = false;
+              break;
+            }
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ready, 0)) break;
+        (void)ld_acquire_gpu(&ctr->done[cur.slot]);  // every copying lane acquires
+      }
+      const uint16_t* xsrc[kLaneRows];
+#pragma unroll
+      for (int j = 0; j < kLaneRows; ++j) {
+        const int src = cur.xrow[j];
+        xsrc[j] = src < 0 ? nullptr
+                          : (down ? p.act : p.hidden) +
+                                static_cast<int64_t>(down ? src : src / p.top_k) * K;
+      }
+      const int64_t zbase = (static_cast<int64_t>(cur.bank) *
+                                 (down ? (p.H >> 7) : (2 * p.I) >> 7) +
+                             (cur.row0 >> 7)) * ktiles;
+      const int64_t zup = (static_cast<int64_t>(cur.bank) * ((2 * p.I) >> 7) +
+                           ((p.I + cur.row0) >> 7)) * ktiles;
+      const int kpairs = (ktiles + 1) >> 1;
+      int w_next = 0;
+      PdItem<NC> nxt;
+      for (int kp = 0; kp < kpairs; ++kp, ++i) {
+        const int st = i % S;
+        const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&empty[st], ph ^ 1u, p.err_word, ab))) {
+          ok = false;
+          break;
+        }
+        uint8_t* dst = ring + st * kStage;
+        const int kt = 2 * kp;
+        if (lane == 0) {
+          PdMeta m;
+          m.r0 = cur.r0;
+          m.n = cur.n;
+          m.tok0 = cur.tok0;
+          m.row0 = cur.row0;
+          m.kt = kt;
+          m.ktiles = ktiles;
+          m.slot = cur.slot;
+          m.flags = (kp == 0 ? kPdFirst : 0) | (kp == kpairs - 1 ? kPdLast : 0) |
+                    (down ? kPdDown : 0);
+          meta[st] = m;
+          mbar_arrive_expect_tx(&full[st], kPdWeightBytes);
+        }
+        __syncwarp();
+        const int la = (2 * i) & 31;
+        if (down) {
+          if (lane == la)
+            tma_load_3d(dst, &p.w2map, &full[st], 0, cur.row0 & 127,
+                        static_cast<int>(zbase + kt));
+        } else if (lane == la) {
+          tma_load_3d(dst, &p.w13map, &full[st], 0, cur.row0 & 127,
+                      static_cast<int>(zbase + kt));
+        } else if (lane == la + 1) {
+          tma_load_3d(dst + kPdWeightBytes / 2, &p.w13map, &full[st], 0,
+                      (p.I + cur.row0) & 127, static_cast<int>(zup + kt));
+        }
+        uint8_t* xs = dst + kPdWeightBytes;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const bool kin = kt + kk < ktiles;
+#pragma unroll
+          for (int j = 0; j < kLaneRows; ++j) {
+            const int row = j * 4 + (lane >> 3);
+            const bool v = kin && xsrc[j] != nullptr;
+            cp_async_16(xs + kk * kXSlice + row * 128 + ((xchunk ^ (row & 7)) << 4),
+                        v ? xsrc[j] + (kt + kk) * 64 + xchunk * 8 : p.hidden, v ? 16u : 0u);
+          }
+        }
+        cp_async_arrive_noinc(&full[st]);
+        if (kp == kpairs / 2 && lane == 0) w_next = atomicAdd(&ctr->work, 1);
+        if (kp == kpairs - 1)
+          pd_resolve<NC>(p, slot_prefix, G, __shfl_sync(0xffffffffu, w_next, 0), items,
+                         items_gu, tiles_gu, tiles_dn, lane, nxt);
+      }
+      if (!ok) break;
+      cur = nxt;
+    }
+    if (ok && !*ab) {
+      // exit stage: consumers stop when they reach it
+      const int st = i % S;
+      const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+      if (__all_sync(0xffffffffu, mbar_wait_bounded(&empty[st], ph ^ 1u, p.err_word, ab))) {
+        if (lane == 0) {
+          meta[st].flags = kPdExit;
+          mbar_arrive(&full[st]);
+        }
+        cp_async_arrive_noinc(&full[st]);
+      }
+    } else if (lane == 0) {
+      // gave up: let the loads already issued land before the CTA can exit
+      for (int j = i - S > 0 ? i - S : 0; j < i; ++j) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&full[j % S], static_cast<uint32_t>(j / S) & 1u) &&
+               clock64() - t0 < 2000000) {
+        }
+      }
+    }
+    cp_async_wait_all();
+  } else {
+    // ---------------------------------------------------------------- consumers
+    const int gq = lane >> 2, c = lane & 3;
+    // independent accumulator chains (one per K block while registers allow) so that the
+    // MMAs of a stage do not wait on one another
+    constexpr int CH = NC <= 2 ? 2 : 1;
+    float acc[CH][NC][4];
+    for (int i = 0;; ++i) {
+      const int st = i % S;
+      const uint32_t ph = static_cast<uint32_t>(i / S) & 1u;
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[st], ph, p.err_word, ab))) break;
+      const PdMeta m = meta[st];
+      if (m.flags & kPdExit) break;
+      const bool down = (m.flags & kPdDown) != 0;
+      if (m.flags & kPdFirst) {
+#pragma unroll
+        for (int h = 0; h < CH; ++h)
+#pragma unroll
+          for (int q = 0; q < NC; ++q) acc[h][q][0] = acc[h][q][1] = acc[h][q][2] = acc[h][q][3] = 0.f;
+      }
+      const uint8_t* stage = ring + st * kStage;
+      // gate_up: lo = gate row 8 warp + gq of the gate box, hi = the same row of the up box;
+      // down: lo / hi = rows 16 warp + gq and 16 warp + 8 + gq of the 64-row box.
+      const int lo_row = down ? 16 * warp + gq : 8 * warp + gq;
+      const int hi_row = down ? lo_row + 8 : lo_row;
+      const int ksub = down ? 8192 : 4096;
+      const int hi_off = down ? 0 : kPdWeightBytes / 2;
+      const int nk = m.kt + 1 < m.ktiles ? 2 : 1;
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        if (kk < nk) {
+          const uint8_t* box = stage + kk * ksub;
+          const uint8_t* xs = stage + kPdWeightBytes + kk * kXSlice;
+#pragma unroll
+          for (int kb = 0; kb < 2; ++kb) {
+            const int h = (kk * 2 + kb) % CH;
+            const uint4 wl = lds_swz(box, lo_row, kb * 4 + c);
+            const uint4 wh = lds_swz(box + hi_off, hi_row, kb * 4 + c);
+#pragma unroll
+            for (int q = 0; q < NC; ++q) {
+              const uint4 xv = lds_swz(xs, q * 8 + gq, kb * 4 + c);
+              mma_16816(acc[h][q], wl.x, wh.x, wl.y, wh.y, xv.x, xv.y);
+              mma_16816(acc[h][q], wl.z, wh.z, wl.w, wh.w, xv.z, xv.w);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (!(m.flags & kPdLast)) continue;
+#pragma unroll
+      for (int h = 1; h < CH; ++h)
+#pragma unroll
+        for (int q = 0; q < NC; ++q)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[0][q][e] += acc[h][q][e];
+#pragma unroll
+      for (int q = 0; q < NC; ++q) {
+        const int ta = m.tok0 + q * 8 + 2 * c;
+        if (!down) {
+          const int j = m.row0 + 8 * warp + gq;
+          if (ta < m.n)
+            p.act[static_cast<int64_t>(m.r0 + ta) * p.I + j] =
+                f32_to_bf16_bits(silu_f32(acc[0][q][0]) * acc[0][q][2]);
+          if (ta + 1 < m.n)
+            p.act[static_cast<int64_t>(m.r0 + ta + 1) * p.I + j] =
+                f32_to_bf16_bits(silu_f32(acc[0][q][1]) * acc[0][q][3]);
+        } else {
+          const int n0 = m.row0 + 16 * warp;
+          if (ta < m.n) {
+            uint16_t* yr = p.y_perm + static_cast<int64_t>(m.r0 + ta) * p.H;
+            yr[n0 + gq] = f32_to_bf16_bits(acc[0][q][0]);
+            yr[n0 + 8 + gq] = f32_to_bf16_bits(acc[0][q][2]);
+          }
+          if (ta + 1 < m.n) {
+            uint16_t* yr = p.y_perm + static_cast<int64_t>(m.r0 + ta + 1) * p.H;
+            yr[n0 + gq] = f32_to_bf16_bits(acc[0][q][1]);
+            yr[n0 + 8 + gq] = f32_to_bf16_bits(acc[0][q][3]);
+          }
+        }
+      }
+      if (!down) {
+        // the warp's activation stores, then one release increment of the pass's counter
+        __syncwarp();
+        if (lane == 0) red_release_add_gpu(&ctr->done[m.slot], 1);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&ctr->exited, 1) == static_cast<int>(gridDim.x) - 1) {
+      // last CTA: every other CTA has finished with the counters
+      const int slots = min(slot_prefix[G], kPdMaxSlots);
+      for (int s = 0; s < slots; ++s) atomicExch(&ctr->done[s], 0);
+      atomicExch(&ctr->work, 0);
+      __threadfence();
+      atomicExch(&ctr->exited, 0);
+    }
+  }
+}
+
+// Counter set of (device, stream): at most kPdCounterSets streams per device use the
+// persistent kernel; further streams take the register-streaming launch pair.
+int pd_counter_set(cudaStream_t s) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, cudaStream_t>, int>> reg;
+  static int used[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+  std::lock_guard<std::mutex> lk(mu);
+  for (const auto& e : reg)
+    if (e.first.first == dev && e.first.second == s) return e.second;
+  if (used[dev] >= kPdCounterSets) return -1;
+  reg.push_back({{dev, s}, used[dev]});
+  return used[dev]++;
+}
+
+template <int NC>
+int launch_decode_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_pair,
+                             const int32_t* group_offsets, const int32_t* group_bank_row,
+                             int group_begin, int num_groups, int max_rows,
+                             const uint16_t* w13_bank, const uint16_t* w2_bank,
+                             int64_t bank_rows, int H, int I, uint16_t* act, uint16_t* y_perm,
+                             int32_t* err_word, cudaStream_t s) {
+  const int max_passes = (max_rows + 8 * NC - 1) / (8 * NC);
+  const int set = pd_counter_set(s);
+  if (num_groups > kPdMaxGroups || static_cast<int64_t>(num_groups) * max_passes > kPdMaxSlots ||
+      set < 0)
+    return launch_decode<NC>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
+                             group_begin, num_groups, w13_bank, w2_bank, bank_rows, H, I, act,
+                             y_perm, err_word, s);
+  struct DevInfo {
+    bool attr = false;
+    int grid = 0;
+  };
+  static DevInfo info[64];
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "lm_moe_mlp_decode: device");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return fail(LM_ERR_CUDA, "lm_moe_mlp_decode: device index");
+  if (!info[dev].attr) {
+    rc = check_cuda(cudaFuncSetAttribute(gemv_persistent_kernel<NC>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         pd_smem_bytes<NC>(kPdMaxGroups)),
+                    "lm_moe_mlp_decode: smem attribute");
+    if (rc) return rc;
+    int sms = 0, per_sm = 0;
+    rc = check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
+                    "lm_moe_mlp_decode: SM count");
+    if (rc) return rc;
+    rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                        &per_sm, gemv_persistent_kernel<NC>, kPdThreads,
+                        pd_smem_bytes<NC>(kPdMaxGroups)),
+                    "lm_moe_mlp_decode: occupancy");
+    if (rc) return rc;
+    info[dev].grid = sms * (per_sm < 1 ? 1 : (per_sm > 3 ? 3 : per_sm));
+    info[dev].attr = true;
+  }
+  PdParams prm{};
+  rc = make_map(&prm.w13map, w13_bank, 3,
+                static_cast<uint64_t>(bank_rows) * (2 * I / 128) * (H / 64), 0, 32, 2);
+  if (rc) return rc;
+  rc = make_map(&prm.w2map, w2_bank, 3,
+                static_cast<uint64_t>(bank_rows) * (H / 128) * (I / 64), 0, 64, 2);
+  if (rc) return rc;
+  prm.hidden = hidden;
+  prm.row_to_pair = row_to_pair;
+  prm.group_offsets = group_offsets;
+  prm.group_bank_row = group_bank_row;
+  prm.act = act;
+  prm.y_perm = y_perm;
+  prm.err_word = err_word;
+  prm.bank_rows = bank_rows;
+  prm.counter_set = set;
+  prm.group_begin = group_begin;
+  prm.num_groups = num_groups;
+  prm.top_k = top_k;
+  prm.H = H;
+  prm.I = I;
+  gemv_persistent_kernel<NC><<<info[dev].grid, kPdThreads, pd_smem_bytes<NC>(num_groups), s>>>(
+      prm);
+  return launch_status("lm_moe_mlp_decode: persistent");
 }
 
 template <int NC>
@@ -466,17 +1030,18 @@ extern "C" int lm_moe_mlp_decode(const uint16_t* hidden, int32_t top_k,
   const int ng = group_end - group_begin;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (max_rows_per_group <= 8)
-    return launch_decode<1>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
-                            group_begin, ng, w13_bank, w2_bank, bank_rows, H, I, act, y_perm,
-                            err_word, s);
+    return launch_decode_persistent<1>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
+                                       group_begin, ng, max_rows_per_group, w13_bank, w2_bank,
+                                       bank_rows, H, I, act, y_perm, err_word, s);
   if (max_rows_per_group <= 16)
-    return launch_decode<2>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
-                            group_begin, ng, w13_bank, w2_bank, bank_rows, H, I, act, y_perm,
-                            err_word, s);
+    return launch_decode_persistent<2>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
+                                       group_begin, ng, max_rows_per_group, w13_bank, w2_bank,
+                                       bank_rows, H, I, act, y_perm, err_word, s);
   if (max_rows_per_group <= 32)
-    return launch_decode<4>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
-                            group_begin, ng, w13_bank, w2_bank, bank_rows, H, I, act, y_perm,
-                            err_word, s);
-  return launch_decode<8>(hidden, top_k, row_to_pair, group_offsets, group_bank_row, group_begin,
-                          ng, w13_bank, w2_bank, bank_rows, H, I, act, y_perm, err_word, s);
+    return launch_decode_persistent<4>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
+                                       group_begin, ng, max_rows_per_group, w13_bank, w2_bank,
+                                       bank_rows, H, I, act, y_perm, err_word, s);
+  return launch_decode_persistent<8>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
+                                     group_begin, ng, max_rows_per_group, w13_bank, w2_bank,
+                                     bank_rows, H, I, act, y_perm, err_word, s);
 }
