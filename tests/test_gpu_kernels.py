@@ -91,7 +91,8 @@ def _groups_case(cuda, ids_np, e2g_np, G, E):
 
 
 @pytest.mark.parametrize("T,k,E,G", [(16, 8, 128, 32), (4096, 8, 128, 122), (1, 8, 128, 8),
-                                     (1000, 6, 64, 64), (513, 8, 128, 128), (4096, 8, 128, 1)])
+                                     (1000, 6, 64, 64), (513, 8, 128, 128), (4096, 8, 128, 1),
+                                     (64, 8, 128, 1024), (64, 8, 128, 128), (65, 8, 128, 128)])
 def test_build_groups_bit_exact(cuda, T, k, E, G):
     rng = np.random.default_rng(T * 31 + G)
     ids = np.stack([rng.permutation(E)[:k] for _ in range(T)])

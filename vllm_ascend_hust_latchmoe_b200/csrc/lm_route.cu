@@ -356,6 +356,68 @@ __global__ void __launch_bounds__(kGroupTile)
   }
 }
 
+// All three passes for a call with at most kGroupTile pairs (decode), in one block: per-warp
+// group counts, the scan over groups, then the same stable scatter as the tiled passes, so
+// the tables are identical to theirs without the scratch round trips between launches.
+__global__ void __launch_bounds__(kGroupTile)
+    group_single_tile_kernel(const int32_t* __restrict__ ids, int64_t num_pairs,
+                             int num_experts, const int32_t* __restrict__ e2g, int num_groups,
+                             int32_t* __restrict__ group_offsets,
+                             int32_t* __restrict__ pair_to_row, int32_t* __restrict__ row_to_pair,
+                             int32_t* __restrict__ err_word) {
+  extern __shared__ int32_t sm[];
+  int32_t* s_base = sm;               // [num_groups]: first row of each group
+  int32_t* s_wcnt = sm + num_groups;  // [kGroupTileWarps][num_groups]
+  __shared__ int32_t s_warp[kGroupTileWarps];
+  for (int i = threadIdx.x; i < kGroupTileWarps * num_groups; i += blockDim.x) s_wcnt[i] = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int p = threadIdx.x;
+  const int g = pair_group(ids, p, num_pairs, num_experts, e2g, num_groups, err_word, true);
+  const unsigned peers = __match_any_sync(0xffffffffu, g);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  if (g >= 0 && rank == 0) s_wcnt[w * num_groups + g] = __popc(peers);
+  __syncthreads();
+  // thread t owns groups [t * gpt, t * gpt + gpt): totals, then a block exclusive scan
+  const int gpt = (num_groups + kGroupTile - 1) / kGroupTile;
+  const int ga = threadIdx.x * gpt;
+  int mine = 0;
+  for (int j = 0; j < gpt; ++j) {
+    const int gg = ga + j;
+    if (gg < num_groups)
+      for (int ww = 0; ww < kGroupTileWarps; ++ww) mine += s_wcnt[ww * num_groups + gg];
+  }
+  int incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp[w] = incl;
+  __syncthreads();
+  int before = 0;
+  for (int ww = 0; ww < w; ++ww) before += s_warp[ww];
+  int run = before + incl - mine;
+  for (int j = 0; j < gpt; ++j) {
+    const int gg = ga + j;
+    if (gg < num_groups) {
+      s_base[gg] = run;
+      group_offsets[gg] = run;
+      for (int ww = 0; ww < kGroupTileWarps; ++ww) run += s_wcnt[ww * num_groups + gg];
+    }
+  }
+  if (ga < num_groups && ga + gpt >= num_groups) group_offsets[num_groups] = run;
+  __syncthreads();
+  if (g >= 0) {
+    int row = s_base[g] + rank;
+    for (int ww = 0; ww < w; ++ww) row += s_wcnt[ww * num_groups + g];
+    pair_to_row[p] = row;
+    row_to_pair[row] = p;
+  } else if (g == -1) {
+    pair_to_row[p] = -1;
+  }
+}
+
 __global__ void permute_rows_kernel(const uint16_t* __restrict__ hidden, int hidden_size,
                                     const int32_t* __restrict__ row_to_pair, int top_k,
                                     int64_t num_rows, uint16_t* __restrict__ x_perm) {
@@ -497,6 +559,21 @@ int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_ex
                       const int32_t* expert_to_group, int32_t num_groups,
                       int32_t* group_offsets, int32_t* pair_to_row, int32_t* row_to_pair,
                       int32_t* scratch, int32_t* err_word, cudaStream_t s) {
+  if (num_pairs > 0 && num_pairs <= kGroupTile) {
+    const size_t smem = sizeof(int32_t) * (1 + kGroupTileWarps) * num_groups;
+    if (smem > 48 * 1024) {
+      int rc = check_cuda(cudaFuncSetAttribute(group_single_tile_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem)),
+                          "lm_build_groups: smem attribute");
+      if (rc) return rc;
+    }
+    group_single_tile_kernel<<<1, kGroupTile, smem, s>>>(topk_ids, num_pairs, num_experts,
+                                                          expert_to_group, num_groups,
+                                                          group_offsets, pair_to_row,
+                                                          row_to_pair, err_word);
+    return launch_status("lm_build_groups: single tile");
+  }
   const int64_t tiles64 = (num_pairs + kGroupTile - 1) / kGroupTile;
   const int tiles = static_cast<int>(tiles64 > 0 ? tiles64 : 1);
   int32_t* tile_counts = scratch;
