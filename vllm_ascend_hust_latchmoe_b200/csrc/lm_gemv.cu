@@ -434,24 +434,6 @@ __device__ __forceinline__ uint4 lds_swz(const uint8_t* box, int row, int chunk)
   return *reinterpret_cast<const uint4*>(box + row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// 16-byte global -> shared copy through L2; src_bytes 0 writes zeros and reads nothing.
-__device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(src_bytes)
-               : "memory");
-}
-
-// Arrive on `bar` once this thread's earlier cp.async copies have completed (the barrier's
-// expected count includes this arrival).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;" ::: "memory");
-}
-
 __device__ __forceinline__ void red_release_add_gpu(int32_t* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

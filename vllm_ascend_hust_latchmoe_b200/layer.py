@@ -47,12 +47,18 @@ DECODE_MAX_TOKENS = 64
 
 
 def mlp_launches(T: int) -> int:
-    """Kernel launches of one grouped-MLP call: the decode path runs two (gate_up, down); the
-    prefill path runs a 2-SM and a single-SM launch per GEMM (one launch per GEMM with
-    LM_UMMA_CTA_PAIR=1)."""
+    """Kernel launches of one grouped-MLP call: the decode path runs one persistent launch for
+    both GEMMs; the prefill path runs a 2-SM and a single-SM launch per GEMM (one launch per
+    GEMM with LM_UMMA_CTA_PAIR=1)."""
     if T <= DECODE_MAX_TOKENS:
-        return 2
+        return 1
     return 2 if os.environ.get("LM_UMMA_CTA_PAIR", "") == "1" else 4
+
+
+def group_launches(pairs: int) -> int:
+    """Kernel launches of one lm_build_groups call: one block up to 512 pairs, else three
+    passes (count, scan, scatter)."""
+    return 1 if 0 < pairs <= 512 else 3
 
 
 @dataclass
@@ -239,7 +245,7 @@ class SlotBankMoE:
         _lib.build_groups(ids, self.E_total, log2phy, G, self.group_offsets, self.pair_to_row,
                           self.row_to_pair, self.scratch, self.err)
         self._grouped_mlp(hidden, T, self.slot_rows, 0, G, bank.w13_slots, bank.w2_slots)
-        self.kernel_launches += 3 + mlp_launches(T) + 1  # grouping (3), MLP, combine
+        self.kernel_launches += group_launches(T * self.k) + mlp_launches(T) + 1  # + combine
         return self._combine(T, out)
 
     def mlp_device(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -262,7 +268,8 @@ class SlotBankMoE:
                                     self.group_src, self.identity_groups, 0, self.E, T,
                                     bank.w13_slots, bank.w2_slots, store.w13, store.w2,
                                     self.act, self.y_perm, self.err)
-        self.kernel_launches += 1 + 3 + 2 + 1  # plan, grouping (3), MLP, combine
+        # slot plan, grouping, the two offload GEMV launches, combine
+        self.kernel_launches += 1 + group_launches(T * self.k) + 2 + 1
         return self._combine(T, out)
 
     def mlp_resident(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -277,7 +284,7 @@ class SlotBankMoE:
             _lib.build_groups(ids, self.E_total, self.identity_groups, self.E, self.group_offsets,
                               self.pair_to_row, self.row_to_pair, self.scratch, self.err)
             self._grouped_mlp(hidden, T, self.identity_groups, 0, self.E, store.w13, store.w2)
-            self.kernel_launches += 6
+            self.kernel_launches += group_launches(T * self.k) + mlp_launches(T) + 1
             return self._combine(T, out)
         self.resident_planned = True
         _lib.expert_histogram(ids, self.E, self.counts, self.err)
@@ -286,7 +293,7 @@ class SlotBankMoE:
                         in_place_rows=True)
         _lib.build_groups(ids, self.E_total, self.expert_to_group, self.E, self.group_offsets,
                           self.pair_to_row, self.row_to_pair, self.scratch, self.err)
-        launches = 5  # histogram, plan, grouping (count, scan, scatter)
+        launches = 2 + group_launches(T * self.k)  # histogram, plan, grouping
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
@@ -358,7 +365,7 @@ class SlotBankMoE:
         ids = self.topk_ids[:T]
         _lib.build_groups(ids, self.E_total, self.identity_groups, self.E, self.group_offsets,
                           self.pair_to_row, self.row_to_pair, self.scratch, self.err)
-        launches = 3
+        launches = group_launches(T * self.k)
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
@@ -393,7 +400,7 @@ class SlotBankMoE:
         ids = self.topk_ids[:T]
         _lib.build_groups(ids, self.E_total, self.expert_to_group, g, self.group_offsets,
                           self.pair_to_row, self.row_to_pair, self.scratch, self.err)
-        launches = 3  # grouping: count, scan, scatter
+        launches = group_launches(T * self.k)
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
