@@ -77,6 +77,7 @@ struct Cfg {
 };
 
 struct SmemCtl {
+  uint4 xpose[4][128];     // per epilogue warp: 32 rows x 64 B, for coalesced output stores
   uint64_t full[MAX_STAGES];
   uint64_t empty[MAX_STAGES];
   uint64_t tfull[2];
@@ -159,12 +160,29 @@ __device__ __forceinline__ int a_box_index(int valid) {
   return valid <= 16 ? 0 : valid <= 32 ? 1 : valid <= 64 ? 2 : 3;
 }
 
-__device__ __forceinline__ void store_row_chunk(uint16_t* dst, const uint32_t (&packed)[16]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-  d[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-  d[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-  d[2] = make_uint4(packed[8], packed[9], packed[10], packed[11]);
-  d[3] = make_uint4(packed[12], packed[13], packed[14], packed[15]);
+// One epilogue warp's 32-row x 32-column bf16 chunk (lane = row, 64 B each in `packed`) to
+// global memory. A lane-per-row store would touch 32 rows per instruction; instead the rows
+// pass through a 2 KiB shared buffer (16-byte chunk c of row r at r * 64 + ((c ^ (r >> 1 & 3))
+// * 16), conflict-free both ways) and each store instruction writes 8 rows x 64 contiguous
+// bytes. Rows at or past `valid_rows` (of this warp's 32) are not written.
+__device__ __forceinline__ void store_chunk_coalesced(uint4* xbuf, uint16_t* out0, int64_t ld,
+                                                      int valid_rows,
+                                                      const uint32_t (&packed)[16]) {
+  const int lane = threadIdx.x & 31;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    xbuf[lane * 4 + (c ^ sw)] =
+        make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+  __syncwarp();
+  const int cc = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = 8 * i + (lane >> 2);
+    const uint4 v = xbuf[row * 4 + (cc ^ ((row >> 1) & 3))];
+    if (row < valid_rows) *reinterpret_cast<uint4*>(out0 + row * ld + cc * 8) = v;
+  }
+  __syncwarp();
 }
 
 // Clusters of a launch that take tiles. For the heavy / light pair of launches both compute
@@ -420,7 +438,6 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
   } else {
     // -------------------------------------------------------------- epilogue warps 2..5
     const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32) are visible to this warp
-    const int r = quad * 32 + lane;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&c.tempty[0]), 0);
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&c.tempty[1]), 0);
     int acc = 0;
@@ -430,9 +447,9 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
       if (!mbar_wait_bounded(&c.tfull[acc], acc_phase, p.err_word, abort_flag)) break;
       tc_fence_after();
       const int my_valid = tc.valid - static_cast<int>(rank) * BM;
-      const bool valid = r < my_valid;
-      uint16_t* out_row =
-          p.out + static_cast<int64_t>(tc.row0 + static_cast<int>(rank) * BM + r) * p.out_ld;
+      const int warp_rows = my_valid - quad * 32;  // rows of this warp's 32 in the tile
+      uint16_t* out_warp = p.out + static_cast<int64_t>(tc.row0 + static_cast<int>(rank) * BM +
+                                                        quad * 32) * p.out_ld;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       // Warps whose 32 lanes are all past the tile's rows only release the accumulator.
@@ -452,7 +469,8 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
                   silu_f32(__uint_as_float(gv[2 * i + 1])) * __uint_as_float(uv[2 * i + 1]);
               packed[i] = pack_bf16x2(a0, a1);
             }
-            if (valid) store_row_chunk(out_row + tc.nt * 128 + ch * 32, packed);
+            store_chunk_coalesced(c.xpose[quad], out_warp + tc.nt * 128 + ch * 32, p.out_ld,
+                                  warp_rows, packed);
           }
         } else {
 #pragma unroll 1
@@ -464,7 +482,8 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
 #pragma unroll
             for (int i = 0; i < 16; ++i)
               packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-            if (valid) store_row_chunk(out_row + tc.nt * BN + ch * 32, packed);
+            store_chunk_coalesced(c.xpose[quad], out_warp + tc.nt * BN + ch * 32, p.out_ld,
+                                  warp_rows, packed);
           }
         }
       }
