@@ -181,6 +181,53 @@ def test_decode_mlp_matches_oracle(cuda, T, k, E, H, I):
     _mlp_case(cuda, T, k, E, H, I, 32, use_prefill=False)
 
 
+def test_decode_mlp_concurrent_streams(cuda):
+    """The persistent decode kernel keeps its work queue and pass counters per stream: two
+    layers' decode calls running at the same time on two streams give exactly what each gives
+    alone, call after call (a shared counter set would mix their queues)."""
+    E, H, I, k = 64, 512, 256, 8
+    g = torch.Generator().manual_seed(11)
+    W13 = to_tiled((torch.randn(E, 2 * I, H, generator=g) * 0.05).to(torch.bfloat16)).to(cuda)
+    W2 = to_tiled((torch.randn(E, H, I, generator=g) * 0.05).to(torch.bfloat16)).to(cuda)
+    ident = torch.arange(E, dtype=torch.int32, device=cuda)
+    cases = []
+    for T, seed in ((16, 1), (40, 2)):
+        rng = np.random.default_rng(seed)
+        ids = torch.from_numpy(np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)).to(cuda)
+        h = (torch.randn(T, H, generator=g)).to(torch.bfloat16).to(cuda)
+        P = T * k
+        off = torch.empty(E + 1, dtype=torch.int32, device=cuda)
+        p2r = torch.empty(P, dtype=torch.int32, device=cuda)
+        r2p = torch.empty(P, dtype=torch.int32, device=cuda)
+        scratch = torch.empty(_lib.build_groups_scratch_elems(P, E), dtype=torch.int32, device=cuda)
+        err = torch.zeros(1, dtype=torch.int32, device=cuda)
+        _lib.build_groups(ids, E, ident, E, off, p2r, r2p, scratch, err)
+        act = torch.zeros(P, I, dtype=torch.bfloat16, device=cuda)
+        y = torch.zeros(P, H, dtype=torch.bfloat16, device=cuda)
+        cases.append(dict(T=T, h=h, off=off, r2p=r2p, act=act, y=y, err=err))
+
+    def run(c):
+        _lib.moe_mlp_decode(c["h"], k, c["r2p"], c["off"], ident, 0, E, c["T"], W13, W2, c["act"],
+                            c["y"], c["err"])
+
+    for c in cases:  # alone, on the default stream
+        run(c)
+    torch.cuda.synchronize()
+    refs = [c["y"].clone() for c in cases]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for _ in range(20):
+        for c, st in zip(cases, streams):
+            c["y"].zero_()
+        torch.cuda.synchronize()
+        for c, st in zip(cases, streams):
+            with torch.cuda.stream(st):
+                run(c)
+        torch.cuda.synchronize()
+        for c, ref in zip(cases, refs):
+            assert int(c["err"].item()) == 0
+            assert torch.equal(c["y"], ref)
+
+
 @pytest.mark.parametrize("T,k,E,H,I", [(256, 8, 32, 2048, 768), (300, 8, 128, 2048, 768),
                                        (129, 2, 4, 256, 128), (512, 6, 64, 2048, 1408)])
 def test_prefill_tcgen05_mlp_matches_oracle(cuda, T, k, E, H, I):

@@ -564,9 +564,9 @@ int cta_pair() {
 
 // Relative SM time of a heavy tile (per SM of its pair) and of a light tile, per GEMM (mode),
 // for the split of the SMs between the two launches; measured on the 4096-token
-// Qwen3-30B-A3B layer. LM_UMMA_SPLIT_COST="h0:l0:h1:l1" overrides.
+// Qwen3-30B-A3B layer (gate_up 4:5, down 5:5). LM_UMMA_SPLIT_COST="h0:l0:h1:l1" overrides.
 void split_costs(int mode, int* heavy, int* light) {
-  static int c[4] = {4, 5, 4, 5};
+  static int c[4] = {4, 5, 5, 5};
   static std::once_flag once;
   std::call_once(once, [] {
     const char* e = getenv("LM_UMMA_SPLIT_COST");
