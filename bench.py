@@ -378,10 +378,10 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=0,
                     help="profiling override of the layer's token count (default: the config's)")
     ap.add_argument("--sections", default="all",
-                    help="comma list of value,decode,tpot,e2e,ep,cpu (profiling runs use one)")
+                    help="comma list of value,decode,c4,tpot,e2e,ep,cpu (profiling runs use one)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    every = {"value", "decode", "tpot", "e2e", "ep", "cpu"}
+    every = {"value", "decode", "c4", "tpot", "e2e", "ep", "cpu"}
     sec = every if args.sections == "all" else set(args.sections.split(","))
     if not sec <= every:
         ap.error(f"unknown sections {sorted(sec - every)}")
@@ -525,6 +525,59 @@ def main() -> None:
         del dl, drt
         torch.cuda.empty_cache()
 
+    # ----------------------------------------------------------------- shared-expert layer (C4)
+    c4 = None
+    if "c4" in sec:
+        ccfg = syn.CONFIGS["c4_shared"]
+        cw13, cw2 = syn.make_expert_weights(ccfg, 0)
+        sw13, sw2 = syn.make_shared_weights(ccfg, 0)
+        crt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=ccfg.num_slots,
+                                                 async_load=True, b2_wave_prefill=True))
+        crt.register_layer_for_fixed_slots(ExpertLayer(0, cw13, cw2), slot_device=dev,
+                                           store_device=dev)
+        cl = SlotBankMoE(crt, 0, hidden_size=ccfg.hidden, intermediate_size=ccfg.intermediate,
+                         num_experts=ccfg.num_experts, top_k=ccfg.top_k, max_tokens=ccfg.tokens,
+                         renormalize=ccfg.renormalize,
+                         routed_scaling_factor=ccfg.routed_scaling_factor,
+                         scoring_func=ccfg.scoring_func, num_expert_group=ccfg.num_expert_group,
+                         topk_group=ccfg.topk_group, device=dev)
+        cl.set_shared_experts(sw13, sw2)
+        ch = syn.make_hidden(ccfg, seed=rank).to(dev)
+        clg = syn.make_router_logits(ccfg, seed=rank).to(dev)
+        Tc = ccfg.tokens
+        shared_out = torch.empty(Tc, ccfg.hidden, dtype=torch.bfloat16, device=dev)
+        for _ in range(args.warmup):
+            cl.forward(ch, clg)
+            cl.shared_mlp(ch, Tc, shared_out)
+        torch.cuda.synchronize()
+        g_c4 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_c4):
+            cl.route(ch, clg)
+            cl.mlp_resident(ch, Tc)
+            cl.shared_mlp(ch, Tc, shared_out)
+        for _ in range(3):
+            g_c4.replay()
+        a4, b4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a4.record()
+        for _ in range(50):
+            g_c4.replay()
+        b4.record()
+        torch.cuda.synchronize()
+        c4_ms = a4.elapsed_time(b4) / 50
+        del g_c4
+        cl.check_device_errors("bench c4")
+        c_active = int((torch.bincount(cl.topk_ids[:Tc].reshape(-1).long(),
+                                       minlength=ccfg.num_experts) > 0).sum())
+        c_bytes = c_active * ccfg.expert_bytes + ccfg.num_shared * ccfg.expert_bytes
+        c4 = {"workload": ccfg.name + " + 2 resident shared experts", "layer_ms": c4_ms,
+              "timing": "CUDA-graph replay x50: route, grouping, routed MLP (experts read in "
+                        "place), combine, shared-expert MLP",
+              "active_experts": c_active, "algorithmic_bytes_per_call": c_bytes,
+              "hbm_gbs": c_bytes / (c4_ms / 1e3) / 1e9,
+              "frac_hbm": c_bytes / (c4_ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+        del cl, crt, cw13, cw2
+        torch.cuda.empty_cache()
+
     # ----------------------------------------------------------------- decode TPOT (C3)
     tpot = None
     if "tpot" in sec:
@@ -641,7 +694,7 @@ def main() -> None:
                    "moe_intermediate": cfg.intermediate, "num_slots": cfg.num_slots,
                    "waves": waves, "parallelism": f"replica x{world}",
                    "l2": "weights 1.2 GB per step > 126 MB L2 (no flush needed)"},
-        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode, "tpot": tpot,
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode, "c4": c4, "tpot": tpot,
         "expert_parallel": ep_report,
         "clocks": clocks.summary(), "gpu_launches": int(launches),
     }
