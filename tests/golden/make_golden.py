@@ -15,6 +15,7 @@ oracle and the product host logic against these files.
 from __future__ import annotations
 
 import json
+import os
 import random
 import sys
 import types
@@ -238,7 +239,11 @@ def _autoconfig_cases():
 
 
 def main() -> None:
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    # the reference checkout: first argument, else LATCHMOE_REFERENCE_ROOT
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LATCHMOE_REFERENCE_ROOT", "")
+    if not root:
+        raise SystemExit("usage: make_golden.py <reference checkout> "
+                         "(or set LATCHMOE_REFERENCE_ROOT)")
     _install_reference(root)
     sys.path.insert(0, str(REPO))
     from vllm_moe_offload_ascend.moe_offload import phase_split as ps
