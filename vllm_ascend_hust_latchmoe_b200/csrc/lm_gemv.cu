@@ -375,6 +375,7 @@ constexpr int kPdWeightBytes = 16384;  // per stage: 2 K tiles x 64 weight rows
 constexpr int kPdMaxGroups = 2048;
 constexpr int kPdMaxSlots = 2048;  // (group, pass) pairs per launch
 constexpr int kPdCounterSets = 16;
+constexpr int kPdSmallPairs = 16;  // at most this many pairs: the deep-ring configuration
 constexpr int kPdFirst = 1, kPdLast = 2, kPdDown = 4, kPdExit = 8;
 
 struct PdCounters {
@@ -425,9 +426,9 @@ __host__ __device__ constexpr int pd_stage_bytes() {
   return kPdWeightBytes + 2 * NC * 8 * 128;  // multiple of 1024: bases stay swizzle-aligned
 }
 
-template <int NC>
+template <int NC, int S>
 constexpr int pd_smem_bytes(int num_groups) {
-  return 1024 + pd_stages<NC>() * pd_stage_bytes<NC>() + ((num_groups + 1) * 4 + 15) / 16 * 16;
+  return 1024 + S * pd_stage_bytes<NC>() + ((num_groups + 1) * 4 + 15) / 16 * 16;
 }
 
 __device__ __forceinline__ uint4 lds_swz(const uint8_t* box, int row, int chunk) {
@@ -484,10 +485,9 @@ __device__ __forceinline__ void pd_resolve(const PdParams& p, const int32_t* slo
   }
 }
 
-template <int NC>
+template <int NC, int S>
 __global__ void __launch_bounds__(kPdThreads)
     gemv_persistent_kernel(const __grid_constant__ PdParams p) {
-  constexpr int S = pd_stages<NC>();
   constexpr int kStage = pd_stage_bytes<NC>();
   constexpr int kXSlice = NC * 8 * 128;  // one K tile of the pass's token rows
   constexpr int kLaneRows = NC * 2;      // token rows one producer lane copies per K tile
@@ -515,6 +515,9 @@ __global__ void __launch_bounds__(kPdThreads)
 
   if (warp == kPdConsumers) {
     // ---------------------------------------------------------------- producer
+    // first item claimed at once, its latency hidden behind the table loads
+    int w_first = 0;
+    if (lane == 0) w_first = atomicAdd(&ctr->work, 1);
     // (group, pass) slots: slot_prefix[g] = slots of the groups before g. Empty groups and
     // groups with an out-of-range bank row get none (the latter also set the error word).
     int run = 0;
@@ -577,12 +580,8 @@ __global__ void __launch_bounds__(kPdThreads)
     // token rows) at its last stage, so neither the queue atomic nor the table loads stall
     // the ring; a CTA holds at most one item beyond the one it streams.
     PdItem<NC> cur;
-    {
-      int w = 0;
-      if (lane == 0) w = atomicAdd(&ctr->work, 1);
-      pd_resolve<NC>(p, slot_prefix, G, __shfl_sync(0xffffffffu, w, 0), items, items_gu,
-                     tiles_gu, tiles_dn, lane, cur);
-    }
+    pd_resolve<NC>(p, slot_prefix, G, __shfl_sync(0xffffffffu, w_first, 0), items, items_gu,
+                   tiles_gu, tiles_dn, lane, cur);
     while (ok && cur.w < items) {
       const bool down = cur.down;
       const int K = down ? p.I : p.H;
@@ -817,13 +816,13 @@ int pd_counter_set(cudaStream_t s) {
   return used[dev]++;
 }
 
-template <int NC>
-int launch_decode_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_pair,
+template <int NC, int S>
+int launch_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_pair,
                              const int32_t* group_offsets, const int32_t* group_bank_row,
                              int group_begin, int num_groups, int max_rows,
                              const uint16_t* w13_bank, const uint16_t* w2_bank,
                              int64_t bank_rows, int H, int I, uint16_t* act, uint16_t* y_perm,
-                             int32_t* err_word, cudaStream_t s) {
+                             int32_t* err_word, int per_sm_cap, cudaStream_t s) {
   const int max_passes = (max_rows + 8 * NC - 1) / (8 * NC);
   const int set = pd_counter_set(s);
   if (num_groups > kPdMaxGroups || static_cast<int64_t>(num_groups) * max_passes > kPdMaxSlots ||
@@ -841,9 +840,9 @@ int launch_decode_persistent(const uint16_t* hidden, int top_k, const int32_t* r
   if (rc) return rc;
   if (dev < 0 || dev >= 64) return fail(LM_ERR_CUDA, "lm_moe_mlp_decode: device index");
   if (!info[dev].attr) {
-    rc = check_cuda(cudaFuncSetAttribute(gemv_persistent_kernel<NC>,
+    rc = check_cuda(cudaFuncSetAttribute(gemv_persistent_kernel<NC, S>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         pd_smem_bytes<NC>(kPdMaxGroups)),
+                                         pd_smem_bytes<NC, S>(kPdMaxGroups)),
                     "lm_moe_mlp_decode: smem attribute");
     if (rc) return rc;
     int sms = 0, per_sm = 0;
@@ -851,11 +850,11 @@ int launch_decode_persistent(const uint16_t* hidden, int top_k, const int32_t* r
                     "lm_moe_mlp_decode: SM count");
     if (rc) return rc;
     rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                        &per_sm, gemv_persistent_kernel<NC>, kPdThreads,
-                        pd_smem_bytes<NC>(kPdMaxGroups)),
+                        &per_sm, gemv_persistent_kernel<NC, S>, kPdThreads,
+                        pd_smem_bytes<NC, S>(kPdMaxGroups)),
                     "lm_moe_mlp_decode: occupancy");
     if (rc) return rc;
-    info[dev].grid = sms * (per_sm < 1 ? 1 : (per_sm > 3 ? 3 : per_sm));
+    info[dev].grid = sms * (per_sm < 1 ? 1 : (per_sm > per_sm_cap ? per_sm_cap : per_sm));
     info[dev].attr = true;
   }
   PdParams prm{};
@@ -879,9 +878,29 @@ int launch_decode_persistent(const uint16_t* hidden, int top_k, const int32_t* r
   prm.top_k = top_k;
   prm.H = H;
   prm.I = I;
-  gemv_persistent_kernel<NC><<<info[dev].grid, kPdThreads, pd_smem_bytes<NC>(num_groups), s>>>(
+  gemv_persistent_kernel<NC, S><<<info[dev].grid, kPdThreads, pd_smem_bytes<NC, S>(num_groups), s>>>(
       prm);
   return launch_status("lm_moe_mlp_decode: persistent");
+}
+
+// Few pairs (batch 1 or 2): few items, each CTA streaming a long run, so deeper rings (5
+// stages, two CTAs per SM) instead of three CTAs with three stages (measured at one token:
+// 25 us vs 29.5 us for the 75 MB of its 8 experts).
+template <int NC>
+int launch_decode_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_pair,
+                             const int32_t* group_offsets, const int32_t* group_bank_row,
+                             int group_begin, int num_groups, int max_rows,
+                             const uint16_t* w13_bank, const uint16_t* w2_bank,
+                             int64_t bank_rows, int H, int I, uint16_t* act, uint16_t* y_perm,
+                             int32_t* err_word, cudaStream_t s) {
+  if (static_cast<int64_t>(max_rows) * top_k <= kPdSmallPairs)
+    return launch_persistent<NC, 5>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
+                                    group_begin, num_groups, max_rows, w13_bank, w2_bank,
+                                    bank_rows, H, I, act, y_perm, err_word, 2, s);
+  return launch_persistent<NC, pd_stages<NC>()>(hidden, top_k, row_to_pair, group_offsets,
+                                                group_bank_row, group_begin, num_groups,
+                                                max_rows, w13_bank, w2_bank, bank_rows, H, I,
+                                                act, y_perm, err_word, 3, s);
 }
 
 template <int NC>
