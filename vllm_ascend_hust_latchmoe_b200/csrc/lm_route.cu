@@ -446,25 +446,38 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y_perm,
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int j = 0; j < top_k; ++j) {
-      const int row = s_row[j];
-      if (row < 0) continue;
-      const float w = s_w[j];
-      const uint4 v =
-          __ldg(reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(row) * hidden_size) + c);
-      float a, b;
-      unpack_bf16x2(v.x, a, b);
-      acc[0] += w * a;
-      acc[1] += w * b;
-      unpack_bf16x2(v.y, a, b);
-      acc[2] += w * a;
-      acc[3] += w * b;
-      unpack_bf16x2(v.z, a, b);
-      acc[4] += w * a;
-      acc[5] += w * b;
-      unpack_bf16x2(v.w, a, b);
-      acc[6] += w * a;
-      acc[7] += w * b;
+    // up to 8 pairs' rows loaded at once, then accumulated in j order (the loads of a token's
+    // rows are independent; only the sums are ordered)
+    for (int j0 = 0; j0 < top_k; j0 += 8) {
+      uint4 v[8];
+      bool use[8];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int row = j0 + jj < top_k ? s_row[j0 + jj] : -1;
+        use[jj] = row >= 0;
+        if (use[jj])
+          v[jj] = __ldg(
+              reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(row) * hidden_size) +
+              c);
+      }
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        if (!use[jj]) continue;
+        const float w = s_w[j0 + jj];
+        float a, b;
+        unpack_bf16x2(v[jj].x, a, b);
+        acc[0] += w * a;
+        acc[1] += w * b;
+        unpack_bf16x2(v[jj].y, a, b);
+        acc[2] += w * a;
+        acc[3] += w * b;
+        unpack_bf16x2(v[jj].z, a, b);
+        acc[4] += w * a;
+        acc[5] += w * b;
+        unpack_bf16x2(v[jj].w, a, b);
+        acc[6] += w * a;
+        acc[7] += w * b;
+      }
     }
     uint4 o;
     o.x = pack_bf16x2(acc[0], acc[1]);
