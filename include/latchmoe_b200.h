@@ -202,6 +202,26 @@ int lm_moe_combine(const uint16_t* y_perm, const int32_t* pair_to_row,
                    int32_t hidden_size, uint16_t* out, void* stream);
 
 /*
+ * Device-count variants, for a caller whose count is only known on the device (e.g. rows an
+ * exchange has just received): each call covers min(max, *count_dev) pairs / rows / tokens,
+ * read by the kernels, with buffers sized for max. Same results as the plain calls on that
+ * many items; entries past the count are left as they are.
+ */
+int lm_build_groups_count(const int32_t* topk_ids, int64_t max_pairs,
+                          const int32_t* num_pairs_dev, int32_t num_experts,
+                          const int32_t* expert_to_group, int32_t num_groups,
+                          int32_t* group_offsets, int32_t* pair_to_row, int32_t* row_to_pair,
+                          int32_t* scratch, int64_t scratch_elems, int32_t* err_word,
+                          void* stream);
+int lm_permute_rows_count(const uint16_t* hidden, int32_t hidden_size,
+                          const int32_t* row_to_pair, int32_t top_k, int64_t max_rows,
+                          const int32_t* num_rows_dev, uint16_t* x_perm, void* stream);
+int lm_moe_combine_count(const uint16_t* y_perm, const int32_t* pair_to_row,
+                         const uint16_t* topk_weights_bf16, int64_t max_tokens,
+                         const int32_t* num_tokens_dev, int32_t top_k, int32_t hidden_size,
+                         uint16_t* out, void* stream);
+
+/*
  * K10 expert staging: for i < n, copy bytes_per_expert bytes from
  * src + src_rows_host[i]*src_row_stride to dst + dst_rows_host[i]*dst_row_stride with
  * cudaMemcpyAsync on `stream`, coalescing runs where both row sequences are consecutive

@@ -77,6 +77,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _I32, _P, _I32, _P, _P, _P, _P, _P],
     ),
     "lm_permute_rows": (ctypes.c_int, [_P, _I32, _P, _I32, _I64, _P, _P]),
+    "lm_permute_rows_count": (ctypes.c_int, [_P, _I32, _P, _I32, _I64, _P, _P, _P]),
+    "lm_build_groups_count": (
+        ctypes.c_int,
+        [_P, _I64, _P, _I32, _P, _I32, _P, _P, _P, _P, _I64, _P, _P],
+    ),
+    "lm_moe_combine_count": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I32, _I32, _P, _P]),
     "lm_moe_mlp_decode": (
         ctypes.c_int,
         [_P, _I32, _P, _P, _P, _I32, _I32, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
@@ -232,6 +238,49 @@ def build_groups_noalloc(ids: torch.Tensor, num_experts: int, expert_to_group: t
             _ptr(group_offsets), _ptr(pair_to_row), _ptr(row_to_pair), _ptr(err_word),
             _stream(),
         ),
+    )
+
+
+def build_groups_count(ids: torch.Tensor, num_pairs_dev: torch.Tensor, num_experts: int,
+                       expert_to_group: torch.Tensor, num_groups: int,
+                       group_offsets: torch.Tensor, pair_to_row: torch.Tensor,
+                       row_to_pair: torch.Tensor, scratch: torch.Tensor,
+                       err_word: torch.Tensor | None = None) -> None:
+    """lm_build_groups over the first ``num_pairs_dev`` (int32 on the device) of ``ids``."""
+    _require_cuda(ids, num_pairs_dev, expert_to_group, group_offsets, pair_to_row, row_to_pair,
+                  scratch)
+    _check(
+        "lm_build_groups_count",
+        lib().lm_build_groups_count(
+            _ptr(ids), ids.numel(), _ptr(num_pairs_dev), int(num_experts),
+            _ptr(expert_to_group), int(num_groups), _ptr(group_offsets), _ptr(pair_to_row),
+            _ptr(row_to_pair), _ptr(scratch), scratch.numel(), _ptr(err_word), _stream(),
+        ),
+    )
+
+
+def permute_rows_count(hidden: torch.Tensor, row_to_pair: torch.Tensor, top_k: int,
+                       max_rows: int, num_rows_dev: torch.Tensor, x_perm: torch.Tensor) -> None:
+    """lm_permute_rows over the first ``num_rows_dev`` (device int32) of ``max_rows`` rows."""
+    _require_cuda(hidden, row_to_pair, num_rows_dev, x_perm)
+    _check(
+        "lm_permute_rows_count",
+        lib().lm_permute_rows_count(_ptr(hidden), hidden.shape[-1], _ptr(row_to_pair),
+                                    int(top_k), int(max_rows), _ptr(num_rows_dev), _ptr(x_perm),
+                                    _stream()),
+    )
+
+
+def moe_combine_count(y_perm, pair_to_row, topk_weights_bf16, num_tokens_dev, out) -> None:
+    """lm_moe_combine over the first ``num_tokens_dev`` (device int32) tokens of
+    ``topk_weights_bf16`` / ``out``."""
+    _require_cuda(y_perm, pair_to_row, topk_weights_bf16, num_tokens_dev, out)
+    T, k = topk_weights_bf16.shape
+    _check(
+        "lm_moe_combine_count",
+        lib().lm_moe_combine_count(_ptr(y_perm), _ptr(pair_to_row), _ptr(topk_weights_bf16), T,
+                                   _ptr(num_tokens_dev), k, out.shape[-1], _ptr(out),
+                                   _stream()),
     )
 
 

@@ -220,6 +220,14 @@ __global__ void histogram_kernel(const int32_t* __restrict__ ids, int64_t num_pa
     if (s_hist[e]) atomicAdd(&counts[e], s_hist[e]);
 }
 
+// Pairs / rows / tokens a call covers: the host bound, or fewer when the caller passes the
+// count on the device (a count only known after earlier kernels, e.g. rows received).
+__device__ __forceinline__ int64_t live_count(int64_t bound, const int32_t* count) {
+  if (count == nullptr) return bound;
+  const int64_t c = *count;
+  return c < 0 ? 0 : (c < bound ? c : bound);
+}
+
 __device__ __forceinline__ int pair_group(const int32_t* ids, int64_t p, int64_t num_pairs,
                                           int num_experts, const int32_t* e2g, int num_groups,
                                           int32_t* err_word, bool report) {
@@ -241,7 +249,9 @@ __device__ __forceinline__ int pair_group(const int32_t* ids, int64_t p, int64_t
 __global__ void __launch_bounds__(kGroupTile)
     group_tile_count_kernel(const int32_t* __restrict__ ids, int64_t num_pairs, int num_experts,
                             const int32_t* __restrict__ e2g, int num_groups,
-                            int32_t* __restrict__ tile_counts, int32_t* __restrict__ err_word) {
+                            int32_t* __restrict__ tile_counts, int32_t* __restrict__ err_word,
+                            const int32_t* __restrict__ count) {
+  num_pairs = live_count(num_pairs, count);
   extern __shared__ int32_t s_cnt[];
   for (int g = threadIdx.x; g < num_groups; g += blockDim.x) s_cnt[g] = 0;
   __syncthreads();
@@ -332,7 +342,9 @@ __global__ void __launch_bounds__(kGroupTile)
                          const int32_t* __restrict__ e2g, int num_groups,
                          const int32_t* __restrict__ tile_base,
                          const int32_t* __restrict__ group_offsets,
-                         int32_t* __restrict__ pair_to_row, int32_t* __restrict__ row_to_pair) {
+                         int32_t* __restrict__ pair_to_row, int32_t* __restrict__ row_to_pair,
+                         const int32_t* __restrict__ count) {
+  num_pairs = live_count(num_pairs, count);
   extern __shared__ int32_t s_wcnt[];  // [kGroupTileWarps][num_groups]
   for (int i = threadIdx.x; i < kGroupTileWarps * num_groups; i += blockDim.x) s_wcnt[i] = 0;
   __syncthreads();
@@ -364,7 +376,8 @@ __global__ void __launch_bounds__(kGroupTile)
                              int num_experts, const int32_t* __restrict__ e2g, int num_groups,
                              int32_t* __restrict__ group_offsets,
                              int32_t* __restrict__ pair_to_row, int32_t* __restrict__ row_to_pair,
-                             int32_t* __restrict__ err_word) {
+                             int32_t* __restrict__ err_word, const int32_t* __restrict__ count) {
+  num_pairs = live_count(num_pairs, count);
   extern __shared__ int32_t sm[];
   int32_t* s_base = sm;               // [num_groups]: first row of each group
   int32_t* s_wcnt = sm + num_groups;  // [kGroupTileWarps][num_groups]
@@ -420,7 +433,9 @@ __global__ void __launch_bounds__(kGroupTile)
 
 __global__ void permute_rows_kernel(const uint16_t* __restrict__ hidden, int hidden_size,
                                     const int32_t* __restrict__ row_to_pair, int top_k,
-                                    int64_t num_rows, uint16_t* __restrict__ x_perm) {
+                                    int64_t num_rows, uint16_t* __restrict__ x_perm,
+                                    const int32_t* __restrict__ count) {
+  num_rows = live_count(num_rows, count);
   const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= num_rows) return;
@@ -433,10 +448,11 @@ __global__ void permute_rows_kernel(const uint16_t* __restrict__ hidden, int hid
 __global__ void combine_kernel(const uint16_t* __restrict__ y_perm,
                                const int32_t* __restrict__ pair_to_row,
                                const uint16_t* __restrict__ w_bf16, int top_k, int hidden_size,
-                               uint16_t* __restrict__ out) {
+                               uint16_t* __restrict__ out, const int32_t* __restrict__ count) {
   __shared__ int32_t s_row[32];
   __shared__ float s_w[32];
   const int64_t t = blockIdx.x;
+  if (t >= live_count(gridDim.x, count)) return;
   if (threadIdx.x < top_k) {
     s_row[threadIdx.x] = pair_to_row[t * top_k + threadIdx.x];
     s_w[threadIdx.x] = bf16_bits_to_f32(w_bf16[t * top_k + threadIdx.x]);
@@ -571,7 +587,8 @@ namespace {
 int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_experts,
                       const int32_t* expert_to_group, int32_t num_groups,
                       int32_t* group_offsets, int32_t* pair_to_row, int32_t* row_to_pair,
-                      int32_t* scratch, int32_t* err_word, cudaStream_t s) {
+                      int32_t* scratch, int32_t* err_word, cudaStream_t s,
+                      const int32_t* count = nullptr) {
   if (num_pairs > 0 && num_pairs <= kGroupTile) {
     const size_t smem = sizeof(int32_t) * (1 + kGroupTileWarps) * num_groups;
     if (smem > 48 * 1024) {
@@ -584,7 +601,7 @@ int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_ex
     group_single_tile_kernel<<<1, kGroupTile, smem, s>>>(topk_ids, num_pairs, num_experts,
                                                           expert_to_group, num_groups,
                                                           group_offsets, pair_to_row,
-                                                          row_to_pair, err_word);
+                                                          row_to_pair, err_word, count);
     return launch_status("lm_build_groups: single tile");
   }
   const int64_t tiles64 = (num_pairs + kGroupTile - 1) / kGroupTile;
@@ -597,7 +614,8 @@ int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_ex
     if (rc) return rc;
   } else {
     group_tile_count_kernel<<<tiles, kGroupTile, sizeof(int32_t) * num_groups, s>>>(
-        topk_ids, num_pairs, num_experts, expert_to_group, num_groups, tile_counts, err_word);
+        topk_ids, num_pairs, num_experts, expert_to_group, num_groups, tile_counts, err_word,
+        count);
     int rc = launch_status("lm_build_groups: count");
     if (rc) return rc;
   }
@@ -614,7 +632,8 @@ int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_ex
   }
   group_scatter_kernel<<<tiles, kGroupTile, smem, s>>>(topk_ids, num_pairs, num_experts,
                                                        expert_to_group, num_groups, tile_base,
-                                                       group_offsets, pair_to_row, row_to_pair);
+                                                       group_offsets, pair_to_row, row_to_pair,
+                                                       count);
   return launch_status("lm_build_groups: scatter");
 }
 
@@ -675,6 +694,27 @@ extern "C" int lm_build_groups(const int32_t* topk_ids, int64_t num_pairs, int32
                            static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int lm_build_groups_count(const int32_t* topk_ids, int64_t max_pairs,
+                                     const int32_t* num_pairs_dev, int32_t num_experts,
+                                     const int32_t* expert_to_group, int32_t num_groups,
+                                     int32_t* group_offsets, int32_t* pair_to_row,
+                                     int32_t* row_to_pair, int32_t* scratch,
+                                     int64_t scratch_elems, int32_t* err_word, void* stream) {
+  if (num_pairs_dev == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_build_groups_count: null pair count");
+  int rc = check_group_args("lm_build_groups_count", topk_ids, max_pairs, num_experts,
+                            expert_to_group, num_groups, group_offsets, pair_to_row, row_to_pair);
+  if (rc) return rc;
+  const int64_t need = lm_build_groups_scratch_elems(max_pairs, num_groups);
+  if (scratch == nullptr || scratch_elems < need)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_build_groups_count: scratch too small (need " + std::to_string(need) +
+                    " int32)");
+  return build_groups_impl(topk_ids, max_pairs, num_experts, expert_to_group, num_groups,
+                           group_offsets, pair_to_row, row_to_pair, scratch, err_word,
+                           static_cast<cudaStream_t>(stream), num_pairs_dev);
+}
+
 extern "C" int lm_build_groups_noalloc(const int32_t* topk_ids, int64_t num_pairs,
                                        int32_t num_experts, const int32_t* expert_to_group,
                                        int32_t num_groups, int32_t* group_offsets,
@@ -708,8 +748,24 @@ extern "C" int lm_permute_rows(const uint16_t* hidden, int32_t hidden_size,
   const int warps = 8;
   const unsigned blocks = static_cast<unsigned>((num_rows + warps - 1) / warps);
   permute_rows_kernel<<<blocks, warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      hidden, hidden_size, row_to_pair, top_k, num_rows, x_perm);
+      hidden, hidden_size, row_to_pair, top_k, num_rows, x_perm, nullptr);
   return launch_status("lm_permute_rows");
+}
+
+extern "C" int lm_permute_rows_count(const uint16_t* hidden, int32_t hidden_size,
+                                     const int32_t* row_to_pair, int32_t top_k,
+                                     int64_t max_rows, const int32_t* num_rows_dev,
+                                     uint16_t* x_perm, void* stream) {
+  if (hidden_size <= 0 || hidden_size % 8 != 0 || top_k <= 0 || max_rows < 0 ||
+      num_rows_dev == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_permute_rows_count: need hidden_size % 8 == 0 and a row count");
+  if (max_rows == 0) return LM_OK;
+  const int warps = 8;
+  const unsigned blocks = static_cast<unsigned>((max_rows + warps - 1) / warps);
+  permute_rows_kernel<<<blocks, warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      hidden, hidden_size, row_to_pair, top_k, max_rows, x_perm, num_rows_dev);
+  return launch_status("lm_permute_rows_count");
 }
 
 extern "C" int lm_moe_combine(const uint16_t* y_perm, const int32_t* pair_to_row,
@@ -725,6 +781,24 @@ extern "C" int lm_moe_combine(const uint16_t* y_perm, const int32_t* pair_to_row
   if (threads < 32) threads = 32;
   combine_kernel<<<static_cast<unsigned>(num_tokens), threads, 0,
                    static_cast<cudaStream_t>(stream)>>>(y_perm, pair_to_row, topk_weights_bf16,
-                                                        top_k, hidden_size, out);
+                                                        top_k, hidden_size, out, nullptr);
   return launch_status("lm_moe_combine");
+}
+
+extern "C" int lm_moe_combine_count(const uint16_t* y_perm, const int32_t* pair_to_row,
+                                    const uint16_t* topk_weights_bf16, int64_t max_tokens,
+                                    const int32_t* num_tokens_dev, int32_t top_k,
+                                    int32_t hidden_size, uint16_t* out, void* stream) {
+  if (max_tokens < 0 || max_tokens > 0x7fffffff || top_k <= 0 || top_k > 32 ||
+      hidden_size <= 0 || hidden_size % 8 != 0 || num_tokens_dev == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_moe_combine_count: need 0 < top_k <= 32, hidden_size % 8 == 0 and a count");
+  if (max_tokens == 0) return LM_OK;
+  int threads = hidden_size / 8;
+  if (threads > 512) threads = 512;
+  if (threads < 32) threads = 32;
+  combine_kernel<<<static_cast<unsigned>(max_tokens), threads, 0,
+                   static_cast<cudaStream_t>(stream)>>>(y_perm, pair_to_row, topk_weights_bf16,
+                                                        top_k, hidden_size, out, num_tokens_dev);
+  return launch_status("lm_moe_combine_count");
 }

@@ -28,8 +28,10 @@ and back (the collective library; one host sync for the counts). ``"peer"`` (a
 ``lm_ep_dispatch`` gathers each pair's row straight into the owner's receive area (no
 permute, no staging buffer), ``lm_ep_receive`` compacts on the owner, and ``lm_ep_combine``
 reads every pair's output row from its owner and reduces it in the original top-k order
-(no return collective). The owner's row count is read once on the host to size the local
-MLP.
+(no return collective). With an HBM-resident local store the owner's MLP takes the received
+row count on the device (grouping, gather and combine read it there), so a peer step has no
+host synchronisation; a staged local store reads the count once on the host to stage its
+experts.
 """
 
 from __future__ import annotations
@@ -60,6 +62,9 @@ class EPOps:
     gather_rows: Callable      # (hidden [T,H], r2p [P], k) -> rows [P,H]
     expert_mlp: Callable       # (rows [R,H], local_ids int32 [R]) -> out [R,H]
     combine: Callable          # (rows_back [P,H], p2r [P], weights [T,k]) -> out [T,H]
+    # (rows [Rmax,H], local_ids [Rmax], count int32 [1] on the device, out [Rmax,H]): the
+    # owner's MLP with the received row count kept on the device (None: not available)
+    expert_mlp_count: Callable | None = None
 
 
 class _DevicePtrArray:
@@ -141,9 +146,26 @@ class ExpertParallelMoE:
         self.group = group
         self.device = torch.device(device)
         self.owner = (torch.arange(self.E, dtype=torch.int32) // self.per_rank).to(self.device)
-        self.stats = EPStats()
+        self._stats = EPStats()
+        # peer steps without a host sync: per-step figures accumulate on the device
+        self._dev_rows = torch.zeros(2, dtype=torch.int64, device=self.device)  # recv, local
+        self._dev_steps = 0
+        self._dev_pairs = 0
         self.exchange = exchange
         self.transport = "peer" if exchange is not None else "nccl"
+
+    @property
+    def stats(self) -> EPStats:
+        """Exchange totals (reads the device-side part of peer steps: synchronises)."""
+        st = EPStats(**vars(self._stats))
+        if self._dev_steps:
+            recv, local_rows = (int(v) for v in self._dev_rows.tolist())
+            elt = 2  # bf16 rows
+            st.send_rows += self._dev_pairs
+            st.recv_rows += recv
+            st.bytes_sent += 2 * (self._dev_pairs - local_rows) * self.H * elt
+            st.bytes_received += 2 * (recv - local_rows) * self.H * elt
+        return st
 
     def owned_experts(self) -> range:
         return range(self.base, self.base + self.per_rank)
@@ -170,7 +192,7 @@ class ExpertParallelMoE:
         out_rows = self.ops.expert_mlp(recv_rows, recv_ids)
         back = torch.empty(P, self.H, dtype=hidden.dtype, device=hidden.device)
         dist.all_to_all_single(back, out_rows.contiguous(), s_split, r_split, group=self.group)
-        st = self.stats
+        st = self._stats
         elt = hidden.element_size()
         st.send_rows += P
         st.recv_rows += R
@@ -189,21 +211,33 @@ class ExpertParallelMoE:
         _lib.ep_dispatch(hidden, ids, self.per_rank, p2r, offsets, self.rank, self.G, x.peers,
                          x.cap, x.epoch, x.done, x.err)
         _lib.ep_receive(x.region, self.G, x.cap, self.H, x.epoch, x.rows, x.ids, x.total, x.err)
-        R = int(x.total.item())  # sizes the local expert MLP
-        if R:
-            self.ops.expert_mlp(x.rows[:R], x.ids[:R], out=x.out_rows[:R])
+        no_sync = self.ops.expert_mlp_count is not None
+        if no_sync:
+            # the received count stays on the device: no host round trip in the step
+            self.ops.expert_mlp_count(x.rows, x.ids, x.total, x.out_rows)
+        else:
+            R = int(x.total.item())  # sizes (and stages) the local expert MLP
+            if R:
+                self.ops.expert_mlp(x.rows[:R], x.ids[:R], out=x.out_rows[:R])
         _lib.ep_signal_outputs(x.peers, self.rank, self.G, x.cap, self.H, x.epoch)
         out = torch.empty(T, self.H, dtype=hidden.dtype, device=hidden.device)
         _lib.ep_combine(ids, w, self.per_rank, p2r, offsets, self.rank, self.G, x.peers,
                         x.region, x.cap, x.epoch, out, x.err)
-        counts = (offsets[1:] - offsets[:-1]).tolist()
-        st = self.stats
-        elt = hidden.element_size()
-        st.send_rows += T * self.k
-        st.recv_rows += R
-        remote = (T * self.k - counts[self.rank]) * self.H * elt
-        st.bytes_sent += 2 * remote       # rows stored into owners + outputs read back
-        st.bytes_received += 2 * (R - int(counts[self.rank])) * self.H * elt
+        if no_sync:
+            # rows received, and rows this rank kept for itself (its own experts' pairs)
+            self._dev_rows[0] += x.total[0]
+            self._dev_rows[1] += offsets[self.rank + 1] - offsets[self.rank]
+            self._dev_steps += 1
+            self._dev_pairs += T * self.k
+        else:
+            counts = (offsets[1:] - offsets[:-1]).tolist()
+            st = self._stats
+            elt = hidden.element_size()
+            st.send_rows += T * self.k
+            st.recv_rows += R
+            remote = (T * self.k - counts[self.rank]) * self.H * elt
+            st.bytes_sent += 2 * remote       # rows stored into owners + outputs read back
+            st.bytes_received += 2 * (R - int(counts[self.rank])) * self.H * elt
         return out
 
     def check_exchange_errors(self) -> None:
@@ -257,7 +291,12 @@ def cuda_ops(local_moe, *, num_experts: int, top_k: int, renormalize: bool = Tru
         _lib.moe_combine(back, p2r_, w, out)
         return out
 
-    return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine)
+    expert_mlp_count = None
+    if local_moe.runtime.host_layer(local_moe.layer_id).on_device:
+        def expert_mlp_count(rows, local_ids, count, out):
+            return local_moe.mlp_rows_count(rows, local_ids, count, out)
+
+    return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine, expert_mlp_count)
 
 
 def build_rank_layer(*, w13_owned: torch.Tensor, w2_owned: torch.Tensor, rank: int,

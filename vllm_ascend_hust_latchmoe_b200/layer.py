@@ -301,6 +301,35 @@ class SlotBankMoE:
         self.kernel_launches += launches + mlp_launches(T) + 1
         return self._combine(T, out)
 
+    def mlp_rows_count(self, rows: torch.Tensor, ids: torch.Tensor, count_dev: torch.Tensor,
+                       out: torch.Tensor) -> torch.Tensor:
+        """Top-1 MLP over the first ``count_dev`` (int32 on the device) of ``rows`` [R, H]
+        with their expert ids ``ids`` [R] (HBM-resident store, experts read in place); row r's
+        output (unit weight) goes to ``out[r]``. The count never reaches the host: grouping,
+        row gather and combine read it on the device, the MLP is sized by R."""
+        store = self.runtime.host_layer(self.layer_id)
+        if self.k != 1 or not store.on_device:
+            raise RuntimeError("mlp_rows_count needs a top-1 layer with an HBM-resident store")
+        R = int(rows.shape[0])
+        if R > self.max_tokens:
+            raise ValueError(f"{R} rows exceed the layer's {self.max_tokens}")
+        if getattr(self, "_unit_w", None) is None:
+            self._unit_w = torch.ones(self.max_tokens, 1, dtype=torch.bfloat16, device=self.device)
+        _lib.build_groups_count(ids.view(R, 1), count_dev, self.E_total, self.identity_groups,
+                                self.E, self.group_offsets, self.pair_to_row, self.row_to_pair,
+                                self.scratch, self.err)
+        if R <= DECODE_MAX_TOKENS:
+            _lib.moe_mlp_decode(rows, 1, self.row_to_pair, self.group_offsets,
+                                self.identity_groups, 0, self.E, R, store.w13, store.w2,
+                                self.act, self.y_perm, self.err)
+        else:
+            _lib.permute_rows_count(rows, self.row_to_pair, 1, R, count_dev, self.x_perm)
+            _lib.moe_mlp_prefill(self.x_perm, R, self.group_offsets, self.identity_groups, 0,
+                                 self.E, store.w13, store.w2, self.act, self.y_perm, self.err)
+        _lib.moe_combine_count(self.y_perm, self.pair_to_row, self._unit_w[:R], count_dev, out)
+        self.kernel_launches += group_launches(R) + mlp_launches(R) + 1 + (R > DECODE_MAX_TOKENS)
+        return out
+
     def resident_wave_plan(self) -> tuple[tuple[int, ...], ...]:
         """Read back the last device wave plan (synchronises; diagnostics and tests). Empty
         after a decode-sized resident call, which groups by expert id without waves."""
