@@ -206,6 +206,8 @@ int lm_moe_combine(const uint16_t* y_perm, const int32_t* pair_to_row,
  * exchange has just received): each call covers min(max, *count_dev) pairs / rows / tokens,
  * read by the kernels, with buffers sized for max. Same results as the plain calls on that
  * many items; entries past the count are left as they are.
+ * Replaces: nothing in the reference, which is single-device; these serve the owner side of
+ * the expert-partitioned exchange (lm_ep_* below), keeping its received count on the device.
  */
 int lm_build_groups_count(const int32_t* topk_ids, int64_t max_pairs,
                           const int32_t* num_pairs_dev, int32_t num_experts,
