@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "latchmoe_b200.h"
 
@@ -25,6 +26,35 @@ void set_last_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int check_cuda(cudaError_t e, const char* what);
 int launch_status(const char* what);
+
+// Programmatic dependent launch. A kernel launched with launch_dependent() may start (its
+// CTAs resident, their prologue running) while the previous kernel on the stream drains; in
+// every CTA it executes pdl_wait() before its first global access that another kernel
+// produced or may still read. pdl_wait() returns once the previous grid has completed and
+// its writes are visible; in a kernel launched the ordinary way it returns at once. Every
+// kernel launched this way waits in every CTA, so the ordering stays transitive along the
+// stream. pdl_trigger() lets the next kernel's launch begin once every CTA of this grid has
+// executed it (or exited).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ----------------------------------------------------------------------------------------
 // device helpers

@@ -512,6 +512,9 @@ __global__ void __launch_bounds__(kPdThreads)
   }
   __syncthreads();
   volatile int* ab = &abort_flag;
+  // launched while the grouping drains: the work queue, the tables, the tokens and the
+  // outputs are all touched only after this
+  pdl_wait();
 
   if (warp == kPdConsumers) {
     // ---------------------------------------------------------------- producer
@@ -677,6 +680,9 @@ __global__ void __launch_bounds__(kPdThreads)
       if (!ok) break;
       cur = nxt;
     }
+    // this CTA claims nothing more: the next kernel (the combine) may start launching once
+    // every CTA is here
+    pdl_trigger();
     if (ok && !*ab) {
       // exit stage: consumers stop when they reach it
       const int st = i % S;
@@ -878,8 +884,10 @@ int launch_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_p
   prm.top_k = top_k;
   prm.H = H;
   prm.I = I;
-  gemv_persistent_kernel<NC, S><<<info[dev].grid, kPdThreads, pd_smem_bytes<NC, S>(num_groups), s>>>(
-      prm);
+  const cudaError_t e =
+      launch_dependent(gemv_persistent_kernel<NC, S>, dim3(info[dev].grid), dim3(kPdThreads),
+                       pd_smem_bytes<NC, S>(num_groups), s, prm);
+  if (e != cudaSuccess) return check_cuda(e, "lm_moe_mlp_decode: persistent");
   return launch_status("lm_moe_mlp_decode: persistent");
 }
 

@@ -44,17 +44,16 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// One warp per token. Expert e lives on lane e % 32, register slot e / 32.
+// Routes token t with one warp (expert e lives on lane e % 32, register slot e / 32): writes
+// the token's top-k weights and ids and returns, on lane j < top_k, the j-th chosen expert.
 template <int EPL>
-__global__ void __launch_bounds__(kRouteWarpsPerBlock * 32)
-    route_topk_kernel(const float* __restrict__ logits, int64_t num_tokens, int num_experts,
-                      int top_k, int scoring, int renorm, float scale,
-                      const float* __restrict__ bias, int n_group, int topk_group,
-                      uint16_t* __restrict__ w_bf16, float* __restrict__ w_f32,
-                      int32_t* __restrict__ ids) {
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * kRouteWarpsPerBlock + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= num_tokens) return;
+__device__ __forceinline__ int route_one_token(const float* __restrict__ logits, int64_t t,
+                                               int num_experts, int top_k, int scoring,
+                                               int renorm, float scale,
+                                               const float* __restrict__ bias, int n_group,
+                                               int topk_group, uint16_t* __restrict__ w_bf16,
+                                               float* __restrict__ w_f32,
+                                               int32_t* __restrict__ ids, int lane) {
   const float* row = logits + t * num_experts;
 
   float lg[EPL], sc[EPL], key[EPL];
@@ -198,6 +197,24 @@ __global__ void __launch_bounds__(kRouteWarpsPerBlock * 32)
     if (w_f32 != nullptr) w_f32[o] = my_w;
     ids[o] = my_id;
   }
+  return my_id;
+}
+
+// One warp per token.
+template <int EPL>
+__global__ void __launch_bounds__(kRouteWarpsPerBlock * 32)
+    route_topk_kernel(const float* __restrict__ logits, int64_t num_tokens, int num_experts,
+                      int top_k, int scoring, int renorm, float scale,
+                      const float* __restrict__ bias, int n_group, int topk_group,
+                      uint16_t* __restrict__ w_bf16, float* __restrict__ w_f32,
+                      int32_t* __restrict__ ids) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kRouteWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= num_tokens) return;
+  route_one_token<EPL>(logits, t, num_experts, top_k, scoring, renorm, scale, bias, n_group,
+                       topk_group, w_bf16, w_f32, ids, lane);
 }
 
 __global__ void histogram_kernel(const int32_t* __restrict__ ids, int64_t num_pairs,
@@ -368,17 +385,17 @@ __global__ void __launch_bounds__(kGroupTile)
   }
 }
 
-// All three passes for a call with at most kGroupTile pairs (decode), in one block: per-warp
-// group counts, the scan over groups, then the same stable scatter as the tiled passes, so
-// the tables are identical to theirs without the scratch round trips between launches.
-__global__ void __launch_bounds__(kGroupTile)
-    group_single_tile_kernel(const int32_t* __restrict__ ids, int64_t num_pairs,
-                             int num_experts, const int32_t* __restrict__ e2g, int num_groups,
-                             int32_t* __restrict__ group_offsets,
-                             int32_t* __restrict__ pair_to_row, int32_t* __restrict__ row_to_pair,
-                             int32_t* __restrict__ err_word, const int32_t* __restrict__ count) {
-  num_pairs = live_count(num_pairs, count);
-  extern __shared__ int32_t sm[];
+// All three passes for a call with at most kGroupTile pairs (decode), in one block of
+// kGroupTile threads: per-warp group counts, the scan over groups, then the same stable
+// scatter as the tiled passes, so the tables are identical to theirs without the scratch
+// round trips between launches. sm: (1 + kGroupTileWarps) * num_groups int32 of shared
+// memory; ids may be in global or shared memory.
+__device__ __forceinline__ void group_one_tile(const int32_t* ids, int64_t num_pairs,
+                                               int num_experts, const int32_t* __restrict__ e2g,
+                                               int num_groups, int32_t* __restrict__ group_offsets,
+                                               int32_t* __restrict__ pair_to_row,
+                                               int32_t* __restrict__ row_to_pair,
+                                               int32_t* __restrict__ err_word, int32_t* sm) {
   int32_t* s_base = sm;               // [num_groups]: first row of each group
   int32_t* s_wcnt = sm + num_groups;  // [kGroupTileWarps][num_groups]
   __shared__ int32_t s_warp[kGroupTileWarps];
@@ -431,6 +448,19 @@ __global__ void __launch_bounds__(kGroupTile)
   }
 }
 
+__global__ void __launch_bounds__(kGroupTile)
+    group_single_tile_kernel(const int32_t* __restrict__ ids, int64_t num_pairs,
+                             int num_experts, const int32_t* __restrict__ e2g, int num_groups,
+                             int32_t* __restrict__ group_offsets,
+                             int32_t* __restrict__ pair_to_row, int32_t* __restrict__ row_to_pair,
+                             int32_t* __restrict__ err_word, const int32_t* __restrict__ count) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ int32_t sm[];
+  group_one_tile(ids, live_count(num_pairs, count), num_experts, e2g, num_groups, group_offsets,
+                 pair_to_row, row_to_pair, err_word, sm);
+}
+
 __global__ void permute_rows_kernel(const uint16_t* __restrict__ hidden, int hidden_size,
                                     const int32_t* __restrict__ row_to_pair, int top_k,
                                     int64_t num_rows, uint16_t* __restrict__ x_perm,
@@ -451,6 +481,8 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y_perm,
                                uint16_t* __restrict__ out, const int32_t* __restrict__ count) {
   __shared__ int32_t s_row[32];
   __shared__ float s_w[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t t = blockIdx.x;
   if (t >= live_count(gridDim.x, count)) return;
   if (threadIdx.x < top_k) {
@@ -509,12 +541,11 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y_perm,
 
 using namespace lm;
 
-extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts,
-                             int32_t top_k, int32_t scoring_func, int32_t renormalize,
-                             float routed_scaling_factor, const float* e_score_correction_bias,
-                             int32_t num_expert_group, int32_t topk_group,
-                             uint16_t* topk_weights_bf16, float* topk_weights_f32,
-                             int32_t* topk_ids, void* stream) {
+namespace {
+int check_route_args(int64_t num_tokens, int32_t num_experts, int32_t top_k,
+                     int32_t scoring_func, int32_t num_expert_group, int32_t topk_group,
+                     const float* logits, const uint16_t* topk_weights_bf16,
+                     const int32_t* topk_ids) {
   if (num_tokens < 0 || num_experts <= 0 || num_experts > 256)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_route_topk: need 0 < num_experts <= 256");
   if (top_k <= 0 || top_k > 32 || top_k > num_experts)
@@ -533,16 +564,30 @@ extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t nu
   }
   if (topk_weights_bf16 == nullptr || topk_ids == nullptr || (num_tokens > 0 && logits == nullptr))
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_route_topk: null output or input pointer");
+  return LM_OK;
+}
+}  // namespace
+
+extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts,
+                             int32_t top_k, int32_t scoring_func, int32_t renormalize,
+                             float routed_scaling_factor, const float* e_score_correction_bias,
+                             int32_t num_expert_group, int32_t topk_group,
+                             uint16_t* topk_weights_bf16, float* topk_weights_f32,
+                             int32_t* topk_ids, void* stream) {
+  int rc = check_route_args(num_tokens, num_experts, top_k, scoring_func, num_expert_group,
+                            topk_group, logits, topk_weights_bf16, topk_ids);
+  if (rc) return rc;
   if (num_tokens == 0) return LM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned blocks =
       static_cast<unsigned>((num_tokens + kRouteWarpsPerBlock - 1) / kRouteWarpsPerBlock);
   const int epl = (num_experts + 31) / 32;
+  cudaError_t e = cudaSuccess;
 #define LM_ROUTE_LAUNCH(N)                                                                   \
-  route_topk_kernel<N><<<blocks, kRouteWarpsPerBlock * 32, 0, s>>>(                          \
-      logits, num_tokens, num_experts, top_k, scoring_func, renormalize,                     \
-      routed_scaling_factor, e_score_correction_bias, num_expert_group, topk_group,          \
-      topk_weights_bf16, topk_weights_f32, topk_ids)
+  e = launch_dependent(route_topk_kernel<N>, dim3(blocks), dim3(kRouteWarpsPerBlock * 32), 0, s, \
+                       logits, num_tokens, num_experts, top_k, scoring_func, renormalize,    \
+                       routed_scaling_factor, e_score_correction_bias, num_expert_group,     \
+                       topk_group, topk_weights_bf16, topk_weights_f32, topk_ids)
   if (epl <= 1) {
     LM_ROUTE_LAUNCH(1);
   } else if (epl <= 2) {
@@ -553,6 +598,7 @@ extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t nu
     LM_ROUTE_LAUNCH(8);
   }
 #undef LM_ROUTE_LAUNCH
+  if (e != cudaSuccess) return check_cuda(e, "lm_route_topk");
   return launch_status("lm_route_topk");
 }
 
@@ -598,10 +644,11 @@ int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_ex
                           "lm_build_groups: smem attribute");
       if (rc) return rc;
     }
-    group_single_tile_kernel<<<1, kGroupTile, smem, s>>>(topk_ids, num_pairs, num_experts,
-                                                          expert_to_group, num_groups,
-                                                          group_offsets, pair_to_row,
-                                                          row_to_pair, err_word, count);
+    const cudaError_t e =
+        launch_dependent(group_single_tile_kernel, dim3(1), dim3(kGroupTile), smem, s, topk_ids,
+                         num_pairs, num_experts, expert_to_group, num_groups, group_offsets,
+                         pair_to_row, row_to_pair, err_word, count);
+    if (e != cudaSuccess) return check_cuda(e, "lm_build_groups: single tile");
     return launch_status("lm_build_groups: single tile");
   }
   const int64_t tiles64 = (num_pairs + kGroupTile - 1) / kGroupTile;
@@ -779,9 +826,11 @@ extern "C" int lm_moe_combine(const uint16_t* y_perm, const int32_t* pair_to_row
   int threads = hidden_size / 8;
   if (threads > 512) threads = 512;
   if (threads < 32) threads = 32;
-  combine_kernel<<<static_cast<unsigned>(num_tokens), threads, 0,
-                   static_cast<cudaStream_t>(stream)>>>(y_perm, pair_to_row, topk_weights_bf16,
-                                                        top_k, hidden_size, out, nullptr);
+  const cudaError_t e = launch_dependent(
+      combine_kernel, dim3(static_cast<unsigned>(num_tokens)), dim3(threads), 0,
+      static_cast<cudaStream_t>(stream), y_perm, pair_to_row, topk_weights_bf16, top_k,
+      hidden_size, out, static_cast<const int32_t*>(nullptr));
+  if (e != cudaSuccess) return check_cuda(e, "lm_moe_combine");
   return launch_status("lm_moe_combine");
 }
 
@@ -797,8 +846,10 @@ extern "C" int lm_moe_combine_count(const uint16_t* y_perm, const int32_t* pair_
   int threads = hidden_size / 8;
   if (threads > 512) threads = 512;
   if (threads < 32) threads = 32;
-  combine_kernel<<<static_cast<unsigned>(max_tokens), threads, 0,
-                   static_cast<cudaStream_t>(stream)>>>(y_perm, pair_to_row, topk_weights_bf16,
-                                                        top_k, hidden_size, out, num_tokens_dev);
+  const cudaError_t e = launch_dependent(
+      combine_kernel, dim3(static_cast<unsigned>(max_tokens)), dim3(threads), 0,
+      static_cast<cudaStream_t>(stream), y_perm, pair_to_row, topk_weights_bf16, top_k,
+      hidden_size, out, num_tokens_dev);
+  if (e != cudaSuccess) return check_cuda(e, "lm_moe_combine_count");
   return launch_status("lm_moe_combine_count");
 }
