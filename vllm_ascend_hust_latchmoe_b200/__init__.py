@@ -28,4 +28,10 @@ def register() -> None:
         from . import seam_ops
 
         seam_ops.register_ops()
+        if env_registry.get("VLLM_ASCEND_MOE_OFFLOAD_STAGE_SEAM"):
+            # vLLM CUDA integration: PIECEWISE split at the stage op, runner seam entry,
+            # attachment after weight loading (each patch best-effort and idempotent)
+            from . import vllm_integration
+
+            vllm_integration.install_vllm_patches()
         _registered = True
