@@ -32,6 +32,16 @@ __device__ __forceinline__ void warp_argmax(float& v, int& idx) {
   }
 }
 
+// Order-preserving image of a float key on uint32: a > b as floats <=> image(a) > image(b).
+// -0.0 and +0.0 share an image (they compare equal as floats, so ties fall to the lower id),
+// -inf maps above 0, and NaN maps to 0, below every key (a NaN key never wins a compare).
+__device__ __forceinline__ uint32_t ordered_key(float f) {
+  if (f != f) return 0u;
+  uint32_t b = __float_as_uint(f);
+  if (b == 0x80000000u) b = 0u;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -154,23 +164,31 @@ __device__ __forceinline__ int route_one_token(const float* __restrict__ logits,
     }
   }
 
-  // Top-k: k rounds of warp arg-max over the unselected keys.
+  // Top-k: k rounds of a warp arg-max over the unselected keys, on order-preserving integer
+  // images of the keys so that each round is two warp reductions (max key, then the lowest
+  // expert id holding it) instead of a shuffle tree.
+  uint32_t okey[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) okey[i] = (lane + 32 * i < num_experts) ? ordered_key(key[i]) : 0u;
   float my_w = 0.f;
   int my_id = 0;
   unsigned taken = 0;
   for (int j = 0; j < top_k; ++j) {
-    float v = -INFINITY;
-    int vi = 0x7fffffff;
+    uint32_t best = 0;  // 0: no candidate (NaN keys map there and never win)
+    int bi = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
-      const int e = lane + 32 * i;
-      if (!((taken >> i) & 1u) && e < num_experts && (key[i] > v || (key[i] == v && e < vi))) {
-        v = key[i];
-        vi = e;
+      // experts of a lane ascend with i, so a strict compare keeps the lowest id of a tie
+      if (!((taken >> i) & 1u) && okey[i] > best) {
+        best = okey[i];
+        bi = lane + 32 * i;
       }
     }
-    warp_argmax(v, vi);
-    if (vi == 0x7fffffff) vi = 0;  // only reachable with NaN logits: fall back to expert 0
+    const uint32_t top = __reduce_max_sync(0xffffffffu, best);
+    int vi = static_cast<int>(
+        __reduce_min_sync(0xffffffffu, (top != 0u && best == top) ? static_cast<uint32_t>(bi)
+                                                                   : 0xffffffffu));
+    if (top == 0u) vi = 0;  // only reachable with NaN logits: fall back to expert 0
     // Fetch the winner's score from its owner lane.
     const int owner = vi & 31;
     const int slot = vi >> 5;
