@@ -348,7 +348,11 @@ def attach_fused_moe_layer(fused_moe: Any, *, runtime=None, layer_id: int | None
     seam_ops.register_moe_layer(name, moe)
     if runner is not None:
         runner._latchmoe_seam = SeamBinding(name, lid, E, shared=False)
-    fused_moe.layer_id = lid
+    if getattr(fused_moe, "layer_id", None) != lid:
+        try:
+            fused_moe.layer_id = lid
+        except AttributeError:  # read-only (vLLM's FusedMoE derives it from its name)
+            pass
     return moe
 
 
