@@ -221,3 +221,32 @@ def test_weight_loading_hook_attaches_once_before_vllm_post_processing(seam_on):
     FakeMethod().process_weights_after_loading(layer)
     FakeMethod().process_weights_after_loading(layer)  # already attached: not again
     assert events == [("attach", "l0", 512), ("vllm", "l0"), ("vllm", "l0")]
+
+
+def test_traced_seam_entry_splits_into_router_stage_and_mlp_pieces():
+    """The runner's seam entry traced with fake tensors (what vLLM's compiler sees) splits
+    at the stage op into a router piece, the eager stage and the MLP piece."""
+    from torch.fx.experimental.proxy_tensor import make_fx
+    from vllm.compilation.backends import split_graph
+
+    plugin.register()
+    runner = SimpleNamespace(layer_name="model.layers.5.mlp.experts",
+                             _latchmoe_seam=vi.SeamBinding("model.layers.5.mlp.experts", 5, 128,
+                                                           shared=False))
+
+    def forward(h, lg):
+        return vi.seam_forward_entry(runner, h, lg, None, None, "from_forward_context", 0)
+
+    graph = make_fx(forward, tracing_mode="fake")(torch.empty(4, 256, dtype=torch.bfloat16),
+                                                  torch.empty(4, 128))
+    ops = [n.target for n in graph.graph.nodes if n.op == "call_function"
+           and "vllm" in str(n.target)]
+    assert [str(o) for o in ops] == ["vllm.moe_router_indirect.default",
+                                     "vllm.moe_offload_stage.default", "vllm.moe_mlp.default"]
+    _, items = split_graph(graph, [vi.SPLITTING_OP])
+    pieces = [[str(n.target) for n in it.graph.graph.nodes if n.op == "call_function"]
+              for it in items]
+    assert [it.is_splitting_graph for it in items] == [False, True, False]
+    assert any("moe_router_indirect" in t for t in pieces[0])
+    assert pieces[1] == ["vllm.moe_offload_stage.default"]
+    assert any("moe_mlp" in t for t in pieces[2])
