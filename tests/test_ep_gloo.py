@@ -1,4 +1,4 @@
-"""Expert-parallel exchange logic on CPU ranks (gloo, world size 2): routing -> group by owner
+"""Expert-parallel exchange logic on CPU ranks (gloo, world sizes 2 and 4): routing -> group by owner
 -> count/row/id all-to-all -> owner MLP -> reverse all-to-all -> combine in top-k order,
 with the oracle supplying each compute step. Every rank's output must equal the
 single-process oracle layer on that rank's tokens."""
@@ -7,6 +7,7 @@ import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -89,11 +90,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_ep_exchange_matches_single_process_oracle():
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_exchange_matches_single_process_oracle(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in procs]
@@ -101,7 +103,8 @@ def test_ep_exchange_matches_single_process_oracle():
         p.join(timeout=60)
         assert p.exitcode == 0
     results.sort()
-    assert [r[4] for r in results] == [list(range(0, 8)), list(range(8, 16))]
-    assert sum(r[2] for r in results) == sum(r[3] for r in results) == 2 * T * K
+    per = E // world
+    assert [r[4] for r in results] == [list(range(r * per, (r + 1) * per)) for r in range(world)]
+    assert sum(r[2] for r in results) == sum(r[3] for r in results) == world * T * K
     for rank, m, *_ in results:
         assert m["max_rel_err"] <= 1e-2 and m["cosine"] >= 0.9999, (rank, m)
