@@ -58,11 +58,15 @@ def test_stage_seam_fails_closed_for_any_full_graph(seam_on, mode):
 def test_platform_patch_appends_after_platform_defaults(seam_on):
     calls = []
 
-    class FakeCudaPlatform:
+    class FakePlatformBase:
         @classmethod
         def check_and_update_config(cls, vllm_config):
             calls.append(cls)
-            vllm_config.compilation_config.splitting_ops.append("vllm::unified_attention")
+            if vllm_config.compilation_config.splitting_ops is not None:
+                vllm_config.compilation_config.splitting_ops.append("vllm::unified_attention")
+
+    class FakeCudaPlatform(FakePlatformBase):  # inherits the hook, like vLLM's CUDA classes
+        pass
 
     assert vi.patch_platform_splitting_ops(FakeCudaPlatform)
     assert not vi.patch_platform_splitting_ops(FakeCudaPlatform)  # idempotent
@@ -70,6 +74,12 @@ def test_platform_patch_appends_after_platform_defaults(seam_on):
     FakeCudaPlatform.check_and_update_config(cfg)
     assert calls == [FakeCudaPlatform]
     assert cfg.compilation_config.splitting_ops == ["vllm::unified_attention", vi.SPLITTING_OP]
+    # an unset list stays unset: vLLM fills in its attention ops only while it is None
+    unset = _config(CUDAGraphMode.PIECEWISE, None)
+    FakeCudaPlatform.check_and_update_config(unset)
+    assert unset.compilation_config.splitting_ops is None
+    FakePlatformBase.check_and_update_config(cfg)  # the base class itself is not wrapped
+    assert calls[-1] is FakePlatformBase
 
 
 def test_engine_args_final_config_boundary(seam_on, monkeypatch, tmp_path, capsys):
@@ -204,7 +214,7 @@ def test_layer_ids_and_attachment_guards():
         vi.attach_fused_moe_layer(layer(global_num_experts=8), runtime=object())
 
 
-def test_weight_loading_hook_attaches_once_before_vllm_post_processing(seam_on):
+def test_weight_loading_hook_attaches_once_and_skips_native_setup(seam_on, monkeypatch):
     events = []
 
     class FakeMethod:
@@ -220,7 +230,31 @@ def test_weight_loading_hook_attaches_once_before_vllm_post_processing(seam_on):
     layer = SimpleNamespace(name="l0", runner=SimpleNamespace())
     FakeMethod().process_weights_after_loading(layer)
     FakeMethod().process_weights_after_loading(layer)  # already attached: not again
-    assert events == [("attach", "l0", 512), ("vllm", "l0"), ("vllm", "l0")]
+    assert events == [("attach", "l0", 512)]
+    monkeypatch.delenv("VLLM_ASCEND_MOE_OFFLOAD_STAGE_SEAM")
+    FakeMethod().process_weights_after_loading(SimpleNamespace(name="l1", runner=None))
+    assert events[-1] == ("vllm", "l1")  # seam off: vLLM's own post-processing
+
+
+def test_seam_entry_applies_the_runner_gate(seam_on, monkeypatch):
+    rec = _Recorder()
+    monkeypatch.setattr(vi, "_seam_ops", lambda: rec)
+    seen = []
+
+    def gate(h):
+        seen.append(h)
+        return "logits", None
+
+    orig_router = rec.moe_router_indirect
+
+    def router(h, lg, name):
+        seen.append(lg)
+        return orig_router(h, lg, name)
+
+    rec.moe_router_indirect = router
+    runner = SimpleNamespace(gate=gate, _latchmoe_seam=vi.SeamBinding("x.layers.0.e", 0, 8, False))
+    assert vi.seam_forward_entry(runner, "h", "h", None, None) == "routed"
+    assert seen == ["h", "logits"]
 
 
 def test_traced_seam_entry_splits_into_router_stage_and_mlp_pieces():

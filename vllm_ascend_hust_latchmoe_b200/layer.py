@@ -228,6 +228,19 @@ class SlotBankMoE:
                                             num_logical_experts=self.E)
         return StageDecision("slots", active, counts, prepared)
 
+    def capture_decision(self, T: int) -> StageDecision:
+        """Decision for an MLP piece being captured into a CUDA graph: the path that reads
+        only fixed buffers and makes no host decision for this layer's tier. An HBM-resident
+        store reads experts in place; device staging decides slots on the GPU; otherwise the
+        slot-bank path reads whatever the eager stage published in log2phy at replay."""
+        if self.resident_tier:
+            return StageDecision("resident")
+        if self.device_staging:
+            if T > DECODE_MAX_TOKENS:
+                raise RuntimeError("prefill-sized calls are not captured under device staging")
+            return StageDecision("device")
+        return StageDecision("capturing")
+
     def _combine(self, T: int, out: torch.Tensor | None) -> torch.Tensor:
         dst = self.out[:T] if out is None else out
         _lib.moe_combine(self.y_perm, self.pair_to_row[: T * self.k], self.topk_w[:T], dst)

@@ -132,9 +132,9 @@ def _moe_offload_stage_fake(topk_ids, layer_id, num_logical_experts, phase):
     return None
 
 
-def _take_decision(layer: SlotBankMoE) -> StageDecision:
+def _take_decision(layer: SlotBankMoE, T: int) -> StageDecision:
     if torch.cuda.is_current_stream_capturing():
-        return StageDecision("capturing")
+        return layer.capture_decision(T)
     decision = layer.pending
     layer.pending = None
     if decision is None:
@@ -157,7 +157,7 @@ def _moe_mlp(hidden_states, router_logits, topk_weights, topk_ids, shared_expert
     layer = get_layer(layer_name)
     _adopt_topk(layer, topk_weights, topk_ids)
     out = torch.empty_like(hidden_states)
-    return layer.run_mlp(hidden_states, _take_decision(layer), out)
+    return layer.run_mlp(hidden_states, _take_decision(layer, int(hidden_states.shape[0])), out)
 
 
 def _moe_mlp_fake(hidden_states, router_logits, topk_weights, topk_ids, shared_experts_input,
@@ -171,7 +171,8 @@ def _moe_mlp_shared(hidden_states, router_logits, topk_weights, topk_ids, shared
     _adopt_topk(layer, topk_weights, topk_ids)
     src = shared_experts_input if shared_experts_input is not None else hidden_states
     shared_out = layer.shared_mlp(src.contiguous(), int(src.shape[0]))
-    routed_out = layer.run_mlp(hidden_states, _take_decision(layer), torch.empty_like(hidden_states))
+    routed_out = layer.run_mlp(hidden_states, _take_decision(layer, int(hidden_states.shape[0])),
+                               torch.empty_like(hidden_states))
     return shared_out, routed_out
 
 

@@ -29,6 +29,7 @@ class leaves the rest working. The seam only takes effect while
 
 from __future__ import annotations
 
+import inspect
 import json
 import os
 import re
@@ -54,13 +55,16 @@ def stage_seam_enabled() -> bool:
 
 
 # ------------------------------------------------------------------ graph configuration
-def ensure_moe_offload_splitting_op(vllm_config: Any, *, fail_closed: bool = False) -> bool:
+def ensure_moe_offload_splitting_op(vllm_config: Any, *, fail_closed: bool = False,
+                                    create: bool = True) -> bool:
     """Put the eager staging seam into the final piecewise graph config.
 
     Returns True when ``vllm::moe_offload_stage`` is in ``splitting_ops``. With the seam off,
     or a graph mode that needs no piecewise split, nothing changes and the result is False.
     Any full-graph mode is refused when ``fail_closed`` (the staging would be captured and
-    replayed with stale routing), as is a config without a compilation config.
+    replayed with stale routing), as is a config without a compilation config. With
+    ``create=False`` an unset (None) ``splitting_ops`` is left unset: vLLM fills in its own
+    defaults (the attention ops) only while the list is None.
     """
     if not stage_seam_enabled():
         return False
@@ -87,6 +91,8 @@ def ensure_moe_offload_splitting_op(vllm_config: Any, *, fail_closed: bool = Fal
         return False
     ops = getattr(cc, "splitting_ops", None)
     if ops is None:
+        if not create:
+            return False
         cc.splitting_ops = []
         ops = cc.splitting_ops
     if SPLITTING_OP not in ops:
@@ -99,7 +105,9 @@ def ensure_moe_offload_splitting_op(vllm_config: Any, *, fail_closed: bool = Fal
 
 
 def _wrap_classmethod(cls: type, name: str, make: Callable[[Callable], Callable]) -> bool:
-    current = cls.__dict__.get(name)
+    """Wrap a classmethod of ``cls``, also when it is inherited (the wrapper is set on
+    ``cls`` itself and calls the inherited function)."""
+    current = inspect.getattr_static(cls, name, None)
     fn = getattr(current, "__func__", current)
     if fn is None or getattr(fn, _MARK, False):
         return False
@@ -111,8 +119,9 @@ def _wrap_classmethod(cls: type, name: str, make: Callable[[Callable], Callable]
 
 def patch_platform_splitting_ops(platform_cls: type | None = None) -> bool:
     """Wrap the platform's ``check_and_update_config`` so the splitting op is appended after
-    the platform's own defaults. Best-effort: False when the class cannot be imported or is
-    already wrapped."""
+    the platform's own defaults. vLLM runs this hook before it fills in its default splitting
+    ops, so an unset list is left to vLLM here and the EngineArgs boundary appends the op
+    afterwards. Best-effort: False when the class cannot be imported or is already wrapped."""
     if platform_cls is None:
         try:
             from vllm.platforms.cuda import CudaPlatform as platform_cls
@@ -122,7 +131,7 @@ def patch_platform_splitting_ops(platform_cls: type | None = None) -> bool:
     def make(original):
         def check_and_update_config(cls, vllm_config):
             original(cls, vllm_config)
-            ensure_moe_offload_splitting_op(vllm_config)
+            ensure_moe_offload_splitting_op(vllm_config, create=False)
         return check_and_update_config
 
     return _wrap_classmethod(platform_cls, "check_and_update_config", make)
@@ -230,6 +239,10 @@ def seam_forward_entry(runner: Any, hidden_states: torch.Tensor, router_logits: 
         raise RuntimeError(
             f"LatchMoE seam: MoE layer {getattr(runner, 'layer_name', '?')!r} was not attached "
             "to the slot bank; refusing native fallback")
+    gate = getattr(runner, "gate", None)
+    if gate is not None:
+        # the runner owns the router gate (vLLM passes hidden states in the logits slot)
+        router_logits, _ = gate(hidden_states)
     ops = _seam_ops()
     name = binding.layer_name
     topk_weights, topk_ids = ops.moe_router_indirect(hidden_states, router_logits, name)
@@ -318,6 +331,13 @@ def attach_fused_moe_layer(fused_moe: Any, *, runtime=None, layer_id: int | None
     if tuple(w2.shape) != (E, H, two_i // 2) or two_i % 2:
         raise ValueError(f"{name}: w13 {tuple(w13.shape)} and w2 {tuple(w2.shape)} do not form "
                          "an [E, 2I, H] / [E, H, I] expert pair")
+    for attr, what in (("custom_routing_function", "a custom routing function"),
+                       ("hash_indices_table", "hash routing"),
+                       ("zero_expert_type", "zero experts")):
+        if getattr(fused_moe, attr, None) is not None:
+            raise RuntimeError(f"{name}: {what} is not implemented by the slot-bank router")
+    if getattr(fused_moe, "apply_router_weight_on_input", False):
+        raise RuntimeError(f"{name}: router weights applied to the input are not implemented")
     global_e = int(getattr(fused_moe, "global_num_experts", E) or E)
     if global_e != E:
         raise RuntimeError(f"{name}: {E} local of {global_e} experts; expert-parallel vLLM "
@@ -359,8 +379,9 @@ def attach_fused_moe_layer(fused_moe: Any, *, runtime=None, layer_id: int | None
 def patch_weight_loading(method_cls: type | None = None, *, max_tokens: Callable[[], int] | None = None,
                          attach: Callable[..., Any] = attach_fused_moe_layer) -> bool:
     """Wrap ``UnquantizedFusedMoEMethod.process_weights_after_loading`` so that, with the seam
-    on, each layer is attached to the slot bank before vLLM post-processes its weights for its
-    own kernels (which the seam then never calls)."""
+    on, each layer is attached to the slot bank from its checkpoint-layout weights. vLLM's own
+    post-processing for its fused-MoE kernels (weight shuffles, kernel set-up) is then skipped:
+    the seam entry never calls those kernels and refuses to fall back to them."""
     if method_cls is None:
         try:
             from vllm.model_executor.layers.fused_moe.unquantized_fused_moe_method import (
@@ -374,10 +395,11 @@ def patch_weight_loading(method_cls: type | None = None, *, max_tokens: Callable
     original = current
 
     def process_weights_after_loading(self, layer):
-        if stage_seam_enabled() and getattr(getattr(layer, "runner", None), "_latchmoe_seam",
-                                            None) is None:
+        if not stage_seam_enabled():
+            return original(self, layer)
+        if getattr(getattr(layer, "runner", None), "_latchmoe_seam", None) is None:
             attach(layer, max_tokens=(max_tokens or _scheduler_max_tokens)())
-        return original(self, layer)
+        return None
 
     setattr(process_weights_after_loading, _MARK, True)
     method_cls.process_weights_after_loading = process_weights_after_loading
