@@ -19,6 +19,8 @@ __global__ void __launch_bounds__(kPlanThreads)
                       int bank_row_mode, int32_t* __restrict__ expert_to_group,
                       int32_t* __restrict__ group_bank_row, int32_t* __restrict__ wave_offsets,
                       int32_t* __restrict__ num_waves_out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ unsigned long long s_key[kPlanMaxExperts];
   __shared__ int32_t s_wave[kPlanMaxExperts];
   __shared__ long long s_load[kPlanMaxExperts];
@@ -173,8 +175,10 @@ extern "C" int lm_plan_waves(const int32_t* counts, int32_t num_experts, int32_t
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_plan_waves: null pointer");
   int threads = 32;  // one thread per sort key, at least one warp
   while (threads < num_experts) threads <<= 1;
-  plan_waves_kernel<<<1, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      counts, num_experts, num_slots, bank_row_mode, expert_to_group, group_bank_row,
-      wave_offsets, num_waves);
+  const cudaError_t e = launch_dependent(
+      plan_waves_kernel, dim3(1), dim3(threads), 0, static_cast<cudaStream_t>(stream), counts,
+      num_experts, num_slots, bank_row_mode, expert_to_group, group_bank_row, wave_offsets,
+      num_waves);
+  if (e != cudaSuccess) return check_cuda(e, "lm_plan_waves");
   return launch_status("lm_plan_waves");
 }

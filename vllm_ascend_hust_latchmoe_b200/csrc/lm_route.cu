@@ -238,6 +238,8 @@ __global__ void __launch_bounds__(kRouteWarpsPerBlock * 32)
 __global__ void histogram_kernel(const int32_t* __restrict__ ids, int64_t num_pairs,
                                  int num_experts, int32_t* __restrict__ counts,
                                  int32_t* __restrict__ err_word) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int32_t s_hist[];
   for (int e = threadIdx.x; e < num_experts; e += blockDim.x) s_hist[e] = 0;
   __syncthreads();
@@ -286,6 +288,8 @@ __global__ void __launch_bounds__(kGroupTile)
                             const int32_t* __restrict__ e2g, int num_groups,
                             int32_t* __restrict__ tile_counts, int32_t* __restrict__ err_word,
                             const int32_t* __restrict__ count) {
+  pdl_wait();
+  pdl_trigger();
   num_pairs = live_count(num_pairs, count);
   extern __shared__ int32_t s_cnt[];
   for (int g = threadIdx.x; g < num_groups; g += blockDim.x) s_cnt[g] = 0;
@@ -305,6 +309,8 @@ __global__ void __launch_bounds__(kGroupTile)
 __global__ void __launch_bounds__(1024)
     group_scan_kernel(int32_t* __restrict__ tile_counts, int num_tiles, int num_groups,
                       int32_t* __restrict__ tile_base, int32_t* __restrict__ group_offsets) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int32_t s_tot[kMaxGroups];
   __shared__ int32_t s_warp[32];
   __shared__ int32_t s_part[1024];
@@ -379,6 +385,8 @@ __global__ void __launch_bounds__(kGroupTile)
                          const int32_t* __restrict__ group_offsets,
                          int32_t* __restrict__ pair_to_row, int32_t* __restrict__ row_to_pair,
                          const int32_t* __restrict__ count) {
+  pdl_wait();
+  pdl_trigger();
   num_pairs = live_count(num_pairs, count);
   extern __shared__ int32_t s_wcnt[];  // [kGroupTileWarps][num_groups]
   for (int i = threadIdx.x; i < kGroupTileWarps * num_groups; i += blockDim.x) s_wcnt[i] = 0;
@@ -483,6 +491,8 @@ __global__ void permute_rows_kernel(const uint16_t* __restrict__ hidden, int hid
                                     const int32_t* __restrict__ row_to_pair, int top_k,
                                     int64_t num_rows, uint16_t* __restrict__ x_perm,
                                     const int32_t* __restrict__ count) {
+  pdl_wait();
+  pdl_trigger();
   num_rows = live_count(num_rows, count);
   const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -678,13 +688,18 @@ int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_ex
                         "lm_build_groups: memset");
     if (rc) return rc;
   } else {
-    group_tile_count_kernel<<<tiles, kGroupTile, sizeof(int32_t) * num_groups, s>>>(
+    const cudaError_t e = launch_dependent(
+        group_tile_count_kernel, dim3(tiles), dim3(kGroupTile), sizeof(int32_t) * num_groups, s,
         topk_ids, num_pairs, num_experts, expert_to_group, num_groups, tile_counts, err_word,
         count);
+    if (e != cudaSuccess) return check_cuda(e, "lm_build_groups: count");
     int rc = launch_status("lm_build_groups: count");
     if (rc) return rc;
   }
-  group_scan_kernel<<<1, 1024, 0, s>>>(tile_counts, tiles, num_groups, tile_base, group_offsets);
+  const cudaError_t es = launch_dependent(group_scan_kernel, dim3(1), dim3(1024), 0, s,
+                                          tile_counts, tiles, num_groups, tile_base,
+                                          group_offsets);
+  if (es != cudaSuccess) return check_cuda(es, "lm_build_groups: scan");
   int rc = launch_status("lm_build_groups: scan");
   if (rc || num_pairs == 0) return rc;
   const size_t smem = sizeof(int32_t) * kGroupTileWarps * num_groups;
@@ -695,10 +710,11 @@ int build_groups_impl(const int32_t* topk_ids, int64_t num_pairs, int32_t num_ex
                     "lm_build_groups: smem attribute");
     if (rc) return rc;
   }
-  group_scatter_kernel<<<tiles, kGroupTile, smem, s>>>(topk_ids, num_pairs, num_experts,
-                                                       expert_to_group, num_groups, tile_base,
-                                                       group_offsets, pair_to_row, row_to_pair,
-                                                       count);
+  const cudaError_t ec = launch_dependent(group_scatter_kernel, dim3(tiles), dim3(kGroupTile),
+                                          smem, s, topk_ids, num_pairs, num_experts,
+                                          expert_to_group, num_groups, tile_base, group_offsets,
+                                          pair_to_row, row_to_pair, count);
+  if (ec != cudaSuccess) return check_cuda(ec, "lm_build_groups: scatter");
   return launch_status("lm_build_groups: scatter");
 }
 
@@ -812,8 +828,11 @@ extern "C" int lm_permute_rows(const uint16_t* hidden, int32_t hidden_size,
   if (num_rows == 0) return LM_OK;
   const int warps = 8;
   const unsigned blocks = static_cast<unsigned>((num_rows + warps - 1) / warps);
-  permute_rows_kernel<<<blocks, warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      hidden, hidden_size, row_to_pair, top_k, num_rows, x_perm, nullptr);
+  const cudaError_t e = launch_dependent(
+      permute_rows_kernel, dim3(blocks), dim3(warps * 32), 0, static_cast<cudaStream_t>(stream),
+      hidden, hidden_size, row_to_pair, top_k, num_rows, x_perm,
+      static_cast<const int32_t*>(nullptr));
+  if (e != cudaSuccess) return check_cuda(e, "lm_permute_rows");
   return launch_status("lm_permute_rows");
 }
 
@@ -828,8 +847,10 @@ extern "C" int lm_permute_rows_count(const uint16_t* hidden, int32_t hidden_size
   if (max_rows == 0) return LM_OK;
   const int warps = 8;
   const unsigned blocks = static_cast<unsigned>((max_rows + warps - 1) / warps);
-  permute_rows_kernel<<<blocks, warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  const cudaError_t e = launch_dependent(
+      permute_rows_kernel, dim3(blocks), dim3(warps * 32), 0, static_cast<cudaStream_t>(stream),
       hidden, hidden_size, row_to_pair, top_k, max_rows, x_perm, num_rows_dev);
+  if (e != cudaSuccess) return check_cuda(e, "lm_permute_rows_count");
   return launch_status("lm_permute_rows_count");
 }
 
