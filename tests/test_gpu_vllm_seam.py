@@ -3,7 +3,8 @@
 its checkpoint-layout weights are attached to the host store and slot bank, and
 ``FusedMoE.forward`` then runs router -> stage -> grouped MLP -> combine through the seam ops.
 Top-k ids must equal the oracle's and outputs stay within the bf16 tolerance, on a decode call
-with more active experts than slots (waves) and on a prefill-sized call.
+with more active experts than slots (waves) and on a prefill-sized call, after vLLM's own
+copies of the expert tensors were released (the seam reads only the store and slot bank).
 
 The vLLM part runs in a child process: it initialises vLLM's distributed state and its global
 config, which must not leak into the other tests of this session.
@@ -37,6 +38,7 @@ def _child(port: int) -> None:
     os.environ["VLLM_ASCEND_MOE_OFFLOAD_ASYNC_LOAD"] = "1"
     os.environ["VLLM_ASCEND_MOE_OFFLOAD_B2_WAVE_PREFILL"] = "1"
     os.environ["VLLM_ASCEND_MOE_OFFLOAD_GRAPH_COMPATIBLE"] = "1"
+    os.environ["VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS"] = "1"
     import torch
 
     import vllm_ascend_hust_latchmoe_b200 as plugin
@@ -72,6 +74,8 @@ def _child(port: int) -> None:
         layer.w2_weight.data.copy_(w2.to(dev))
         moe = vi.attach_fused_moe_layer(layer, max_tokens=1024)
         result["layer_id"] = moe.layer_id
+        # offloaded layer: vLLM's own expert tensors were emptied, the seam reads the store
+        result["released_shapes"] = [list(layer.w13_weight.shape), list(layer.w2_weight.shape)]
         cases = []
         for tokens, seed in ((16, 0), (16, 1), (512, 2)):
             c = cfg.with_tokens(tokens)
@@ -101,6 +105,7 @@ def test_vllm_fused_moe_layer_runs_through_the_seam(cuda):
     from tests.helpers import MAX_REL_ERR, MIN_COSINE
 
     assert res["entry_is_seam"] and res["layer_id"] == 0
+    assert res["released_shapes"] == [[0, 1536, 2048], [0, 2048, 768]]
     for case in res["cases"]:
         assert case["ids_equal"], case
         assert case["max_rel_err"] <= MAX_REL_ERR and case["cosine"] >= MIN_COSINE, case

@@ -197,3 +197,37 @@ def test_wave_plan_qualification_raises_fallback(monkeypatch):
         assert "wave planning failed" in str(exc)
     else:
         raise AssertionError("expected B2WaveFallback")
+
+
+def test_release_original_expert_weights_after_the_store_holds_them():
+    """Opt-in release (the reference's ``release_original_expert_weights_if_ready``): only a
+    non-resident layer whose store holds the experts; staging still reads the store."""
+    E = 6
+    w13 = torch.arange(E * 2 * 3, dtype=torch.float32).reshape(E, 2, 3)
+    w2 = torch.arange(E * 3 * 2, dtype=torch.float32).reshape(E, 3, 2)
+
+    def layer(lid):
+        return ExpertLayer(lid, torch.nn.Parameter(w13.clone(), requires_grad=False),
+                           torch.nn.Parameter(w2.clone(), requires_grad=False))
+
+    off = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=2))
+    l0 = layer(0)
+    off.register_layer_for_fixed_slots(l0, slot_device=torch.device("cpu"))
+    assert off.release_original_expert_weights_if_ready(l0) == (
+        False, ("release_original_expert_weights_disabled",))
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=2,
+                                            release_original_expert_weights=True,
+                                            resident_layer_ids=frozenset({1})))
+    assert rt.release_original_expert_weights_if_ready(layer(4)) == (
+        False, ("host_store_missing:4",))
+    l0, l1 = layer(0), layer(1)
+    for lay in (l0, l1):
+        rt.register_layer_for_fixed_slots(lay, slot_device=torch.device("cpu"))
+    assert rt.release_original_expert_weights_if_ready(l1) == (False, ("resident_layer:1",))
+    assert rt.release_original_expert_weights_if_ready(l0) == (True, ())
+    assert rt.release_original_expert_weights_if_ready(l0) == (True, ())  # idempotent
+    assert tuple(l0.w13_weight.shape) == (0, 2, 3) and tuple(l0.w2_weight.shape) == (0, 3, 2)
+    assert tuple(l1.w13_weight.shape) == (E, 2, 3)
+    p = rt.stage_fixed_slot_plan(layer_id=0, active_experts=(4, 1), num_logical_experts=E)
+    for e, s in zip(p.mapping.active_experts, p.mapping.active_slot_ids):
+        assert torch.equal(p.w1[s], w13[e]) and torch.equal(p.w2[s], w2[e])

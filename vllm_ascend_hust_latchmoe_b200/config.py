@@ -26,6 +26,7 @@ class MoeOffloadConfig:
     offload_stage_seam: bool = False
     b2_wave_prefill: bool = False
     b2_reference_full_layer: bool = False
+    release_original_expert_weights: bool = False
     # B200 addition: decode staging decided on the device (lm_slot_plan) and missed experts
     # read over PCIe by the MLP itself; no host round trip per layer.
     device_staging: bool = False
@@ -63,6 +64,8 @@ class MoeOffloadConfig:
             offload_stage_seam=env.get("VLLM_ASCEND_MOE_OFFLOAD_STAGE_SEAM"),
             b2_wave_prefill=env.get("VLLM_ASCEND_MOE_OFFLOAD_B2_WAVE_PREFILL"),
             b2_reference_full_layer=bool(env.get("VLLM_ASCEND_MOE_OFFLOAD_B2_REFERENCE_FULL_LAYER")),
+            release_original_expert_weights=bool(
+                env.get("VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS")),
             device_staging=bool(env.get("VLLM_ASCEND_MOE_OFFLOAD_DEVICE_STAGING")),
             pin_host_memory=env.get("VLLM_ASCEND_MOE_OFFLOAD_PIN_HOST_MEMORY"),
             transfer_aware_wave_schedule=env.get("VLLM_ASCEND_MOE_OFFLOAD_TRANSFER_AWARE_SCHEDULE"),

@@ -115,6 +115,7 @@ class MoeOffloadRuntime:
         self._tiled_layout: dict[int, bool] = {}
         self._step_counter = itertools.count()
         self._capturing = False
+        self._released_original_weight_layers: set[int] = set()
         self.stage_stats = {"calls": 0, "hits": 0, "misses": 0, "h2d_bytes": 0, "log2phy_updates": 0}
 
     # ------------------------------------------------------------------ registration
@@ -609,6 +610,31 @@ class MoeOffloadRuntime:
         ready.install_consumer_dependency(consumer_stream)
 
     # ------------------------------------------------------------------ ledger
+    def release_original_expert_weights_if_ready(self, layer: torch.nn.Module
+                                                 ) -> tuple[bool, tuple[str, ...]]:
+        """Opt-in release of a non-resident layer's original expert tensors once its host
+        store holds a copy (``moe_offload/runtime.py:1400-1453``). ``w13_weight`` and
+        ``w2_weight`` keep their per-expert shape but hold zero experts, so their device memory
+        returns to the allocator while the module stays intact. Returns (released, blockers)."""
+        if not self.config.release_original_expert_weights:
+            return False, ("release_original_expert_weights_disabled",)
+        if not self.should_use_fixed_slots:
+            return False, ("fixed_slots_disabled",)
+        layer_id = int(getattr(layer, "layer_id", -1))
+        if layer_id < 0:
+            return False, ("invalid_layer_id",)
+        if self.is_resident_layer(layer_id):
+            return False, (f"resident_layer:{layer_id}",)
+        if layer_id in self._released_original_weight_layers:
+            return True, ()
+        if layer_id not in self._slot_banks or self._host_store.layer(layer_id).on_device:
+            return False, (f"host_store_missing:{layer_id}",)
+        for name in ("w13_weight", "w2_weight"):
+            param = getattr(layer, name)
+            param.data = param.data.new_empty((0, *param.shape[1:]))
+        self._released_original_weight_layers.add(layer_id)
+        return True, ()
+
     def memory_ledger(self) -> MoeOffloadMemoryLedger:
         stage = sum(b.total_bytes for p in self._stage_pools.values() for b in p.banks)
         return MoeOffloadMemoryLedger(

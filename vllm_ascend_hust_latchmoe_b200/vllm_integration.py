@@ -303,8 +303,10 @@ def attach_fused_moe_layer(fused_moe: Any, *, runtime=None, layer_id: int | None
     go into the runtime's host store (or an HBM-resident store when ``store_device`` is a GPU,
     and always for the runtime's resident layers) and a slot bank; a :class:`SlotBankMoE` built with the layer's router settings is
     registered with the seam ops under the layer's name, and the layer's runner gets the
-    binding its seam entry reads. Tensor/expert-parallel layers and layers whose capability
-    descriptor is not supported are refused.
+    binding its seam entry reads. With ``release_original_expert_weights`` the offloaded
+    layer's original expert tensors are emptied afterwards (the store holds the copy).
+    Tensor/expert-parallel layers and layers whose capability descriptor is not supported are
+    refused.
     """
     from . import seam_ops
     from .capabilities import describe_layer_capability, require_support
@@ -368,6 +370,9 @@ def attach_fused_moe_layer(fused_moe: Any, *, runtime=None, layer_id: int | None
     seam_ops.register_moe_layer(name, moe)
     if runner is not None:
         runner._latchmoe_seam = SeamBinding(name, lid, E, shared=False)
+    # the seam never reads the original tensors: an offloaded layer may give their HBM back
+    rt.release_original_expert_weights_if_ready(SimpleNamespace(
+        layer_id=lid, w13_weight=fused_moe.w13_weight, w2_weight=fused_moe.w2_weight))
     if getattr(fused_moe, "layer_id", None) != lid:
         try:
             fused_moe.layer_id = lid

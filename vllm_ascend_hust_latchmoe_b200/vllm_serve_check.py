@@ -8,7 +8,8 @@ What it exercises, end to end inside vLLM's own engine (in-process, one GPU):
   engine config must come out PIECEWISE with ``vllm::moe_offload_stage`` as a splitting op;
 * vLLM builds ``Qwen3MoeForCausalLM`` (random "dummy" weights, no checkpoint or tokenizer);
   every ``FusedMoE`` layer is attached to the slot bank while vLLM post-processes weights
-  (odd layers offloaded to the pinned host store, even layers on an HBM-resident store);
+  (odd layers offloaded to the pinned host store, their original expert tensors released;
+  even layers on an HBM-resident store);
 * vLLM compiles the model, captures PIECEWISE CUDA graphs for the decode batch sizes and
   generates greedily: router and MLP pieces replay from graphs, the stage op runs eagerly.
 
@@ -66,6 +67,7 @@ def main(argv=None) -> int:
         "VLLM_ASCEND_MOE_OFFLOAD_GRAPH_COMPATIBLE": "1",
         "VLLM_ASCEND_MOE_OFFLOAD_PIN_HOST_MEMORY": "1",
         "VLLM_ASCEND_MOE_OFFLOAD_RESIDENT_LAYER_IDS": resident,
+        "VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS": "1",
     })
     import vllm_ascend_hust_latchmoe_b200 as plugin
 
@@ -115,6 +117,7 @@ def main(argv=None) -> int:
         "model": f"qwen3-30b-a3b-shaped, {args.layers} layers, dummy weights",
         "attached_moe_layers": len(seam_ops._LAYERS_BY_NAME),
         "offloaded_layers": args.layers - len(resident.split(",")),
+        "released_original_expert_layers": sorted(rt._released_original_weight_layers),
         "num_slots": args.slots,
         "engine_build_s": round(build_s, 1),
         "prompt_tokens": args.prompt_tokens,
