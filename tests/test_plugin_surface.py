@@ -104,3 +104,27 @@ def test_autoconfig_b200_memory_model(monkeypatch):
     plan = ac.apply_moe_offload_defaults(14.0, env=env)
     assert env["VLLM_ASCEND_MOE_OFFLOAD_NUM_SLOTS"] == str(plan["slot_defaults"]["num_slots"])
     assert env["VLLM_ASCEND_MOE_OFFLOAD_RESIDENT_LAYER_IDS"].startswith("0,1,2,4")
+
+
+def test_autoconfig_seam_dataplane_defaults_and_release_conflict():
+    """Seam data plane: its settings become the defaults (layered runtime off, originals
+    released) and explicit user settings stay; the layered runtime cannot run with the
+    original expert tensors released (reference ``moe_offload/autoconfig.py:83-102,700-711``)."""
+    env = {"VLLM_ASCEND_MOE_OFFLOAD_SEW_DATAPLANE": "1",
+           "VLLM_ASCEND_MOE_OFFLOAD_RESIDENT_LAYER_IDS": "0,1",
+           "VLLM_ASCEND_MOE_OFFLOAD_PREFILL_BUFFER_COUNT": "3"}
+    plan = ac.apply_moe_offload_defaults(14.0, env=env)
+    assert plan["sew_dataplane"]
+    for name, value in ac.SEW_DATAPLANE_ENV_VARS.items():
+        if name != "VLLM_ASCEND_MOE_OFFLOAD_PREFILL_BUFFER_COUNT":
+            assert env[name] == value, name
+    assert env["VLLM_ASCEND_MOE_OFFLOAD_PREFILL_BUFFER_COUNT"] == "3"
+    assert env["VLLM_ASCEND_MOE_OFFLOAD_RESIDENT_LAYER_IDS"] == "0,1"
+    assert env["VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME"] == "0"
+    layered = {"VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS": "1"}
+    with pytest.raises(ValueError, match="LAYERED_RUNTIME=1"):
+        ac.apply_moe_offload_defaults(14.0, env=layered, sew_dataplane=False)
+    plain = {}
+    assert not ac.apply_moe_offload_defaults(14.0, env=plain)["sew_dataplane"]
+    assert plain["VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME"] == "1"
+    assert "VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS" not in plain

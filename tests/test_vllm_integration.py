@@ -10,6 +10,7 @@ import pytest
 import torch
 
 import vllm_ascend_hust_latchmoe_b200 as plugin
+from vllm_ascend_hust_latchmoe_b200 import autoconfig as ac
 from vllm_ascend_hust_latchmoe_b200 import vllm_integration as vi
 
 CUDAGraphMode = pytest.importorskip("vllm.config").CUDAGraphMode
@@ -106,8 +107,9 @@ def test_engine_args_final_config_boundary(seam_on, monkeypatch, tmp_path, capsy
                  "VLLM_ASCEND_MOE_OFFLOAD_RESIDENT_LAYER_IDS",
                  "VLLM_ASCEND_MOE_OFFLOAD_FANOUT_THRESHOLD",
                  "VLLM_ASCEND_MOE_OFFLOAD_B2_WAVE_PREFILL", "VLLM_ASCEND_MOE_OFFLOAD_ASYNC_LOAD",
-                 "VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME"):
-        monkeypatch.delenv(name, raising=False)
+                 "VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME", *ac.SEW_DATAPLANE_ENV_VARS):
+        if name != "VLLM_ASCEND_MOE_OFFLOAD_STAGE_SEAM":
+            monkeypatch.delenv(name, raising=False)
     assert vi.patch_engine_args(FakeEngineArgs)
     assert not vi.patch_engine_args(FakeEngineArgs)
     args = FakeEngineArgs()
@@ -120,6 +122,9 @@ def test_engine_args_final_config_boundary(seam_on, monkeypatch, tmp_path, capsy
 
     assert int(os.environ["VLLM_ASCEND_MOE_OFFLOAD_NUM_SLOTS"]) > 0  # AutoConfig applied
     assert os.environ["VLLM_ASCEND_MOE_OFFLOAD_ENABLED"] == "1"
+    # the seam selects the fixed-slot data plane defaults
+    assert os.environ["VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS"] == "1"
+    assert os.environ["VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME"] == "0"
 
     class FullGraphArgs(FakeEngineArgs):
         def __init__(self):

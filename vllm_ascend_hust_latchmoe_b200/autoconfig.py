@@ -210,12 +210,57 @@ def derive_num_slots_defaults(target_offload_gb: float, model_config: dict[str, 
     }
 
 
+# Settings of the seam data plane (fixed slots only, graph-safe staging), set as defaults when
+# it is selected (reference ``moe_offload/autoconfig.py:83-102``): the original expert copies
+# are unused once the host store and slot banks exist, so they are released.
+SEW_DATAPLANE_ENV_VARS = {
+    "VLLM_ASCEND_MOE_OFFLOAD_GRAPH_COMPATIBLE": "1",
+    "VLLM_ASCEND_MOE_OFFLOAD_STAGE_SEAM": "1",
+    "VLLM_ASCEND_MOE_OFFLOAD_B2_WAVE_PREFILL": "1",
+    "VLLM_ASCEND_MOE_OFFLOAD_B2_OVERFLOW_MODE": "multi_wave",
+    "VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME": "0",
+    "VLLM_ASCEND_MOE_OFFLOAD_ASYNC_LOAD": "1",
+    "VLLM_ASCEND_MOE_OFFLOAD_PIN_HOST_MEMORY": "1",
+    "VLLM_ASCEND_MOE_OFFLOAD_TRANSFER_AWARE_SCHEDULE": "1",
+    "VLLM_ASCEND_MOE_OFFLOAD_PREFILL_PREFETCH_DEPTH": "1",
+    "VLLM_ASCEND_MOE_OFFLOAD_PREFILL_BUFFER_COUNT": "2",
+    "VLLM_ASCEND_MOE_OFFLOAD_DEVICE_PAIR_PLANNING": "1",
+    "VLLM_ASCEND_MOE_OFFLOAD_ROUTE_STATS_CACHE": "0",
+    "VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS": "1",
+}
+
+
+def _truthy(value: Any) -> bool:
+    return str(value or "").strip().lower() in ("1", "true", "yes", "on")
+
+
+def check_layered_release_conflict(env: dict | None = None) -> None:
+    """The layered runtime reads the full expert tensors for high-fanout batches, so it cannot
+    run with those tensors released (reference ``moe_offload/autoconfig.py:700-711``)."""
+    env = os.environ if env is None else env
+    if (_truthy(env.get("VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME"))
+            and _truthy(env.get("VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS"))):
+        raise ValueError(
+            "VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS=1 is incompatible with "
+            "VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME=1: the layered runtime needs the full "
+            "expert tensors for high-fanout batches. Unset the release or set "
+            "VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME=0 for the pure fixed-slot path.")
+
+
 def apply_moe_offload_defaults(target_offload_gb: float, model_config: dict[str, Any] | None = None,
                                *, env: dict | None = None, max_num_seqs: int = 1,
-                               max_model_len: int | None = None) -> dict[str, Any]:
+                               max_model_len: int | None = None,
+                               sew_dataplane: bool | None = None) -> dict[str, Any]:
     """Write the derived settings into ``env`` (default ``os.environ``), keeping explicit
-    user overrides of NUM_SLOTS. Returns the plan."""
+    user overrides of NUM_SLOTS and RESIDENT_LAYER_IDS. With the seam data plane selected
+    (``sew_dataplane``, default: ``VLLM_ASCEND_MOE_OFFLOAD_SEW_DATAPLANE``) its settings are
+    the defaults instead of the layered ones. Returns the plan."""
     env = os.environ if env is None else env
+    if sew_dataplane is None:
+        sew_dataplane = _truthy(env.get("VLLM_ASCEND_MOE_OFFLOAD_SEW_DATAPLANE"))
+    if sew_dataplane:
+        for name, value in SEW_DATAPLANE_ENV_VARS.items():
+            env.setdefault(name, value)
     pre = derive_prefetch_defaults(target_offload_gb, model_config)
     slots = derive_num_slots_defaults(target_offload_gb, model_config, pre,
                                       max_num_seqs=max_num_seqs, max_model_len=max_model_len)
@@ -226,8 +271,10 @@ def apply_moe_offload_defaults(target_offload_gb: float, model_config: dict[str,
     env.setdefault("VLLM_ASCEND_MOE_OFFLOAD_B2_WAVE_PREFILL", "1")
     env.setdefault("VLLM_ASCEND_MOE_OFFLOAD_ASYNC_LOAD", "1")
     env.setdefault("VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME", "1")
-    env["VLLM_ASCEND_MOE_OFFLOAD_RESIDENT_LAYER_IDS"] = ",".join(map(str, pre["resident_layer_ids"]))
-    return {"prefetch_defaults": pre, "slot_defaults": slots}
+    check_layered_release_conflict(env)
+    env.setdefault("VLLM_ASCEND_MOE_OFFLOAD_RESIDENT_LAYER_IDS",
+                   ",".join(map(str, pre["resident_layer_ids"])))
+    return {"prefetch_defaults": pre, "slot_defaults": slots, "sew_dataplane": bool(sew_dataplane)}
 
 
 def b200_residency_advice(model_config: dict[str, Any] | None = None,

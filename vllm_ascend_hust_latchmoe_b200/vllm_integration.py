@@ -179,7 +179,8 @@ def apply_engine_args_defaults(engine_args: Any) -> bool:
     apply_moe_offload_defaults(
         gb, _load_model_config_dict(engine_args),
         max_num_seqs=int(getattr(engine_args, "max_num_seqs", None) or 1),
-        max_model_len=getattr(engine_args, "max_model_len", None))
+        max_model_len=getattr(engine_args, "max_model_len", None),
+        sew_dataplane=True if stage_seam_enabled() else None)
     return True
 
 
