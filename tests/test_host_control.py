@@ -231,3 +231,55 @@ def test_release_original_expert_weights_after_the_store_holds_them():
     p = rt.stage_fixed_slot_plan(layer_id=0, active_experts=(4, 1), num_logical_experts=E)
     for e, s in zip(p.mapping.active_experts, p.mapping.active_slot_ids):
         assert torch.equal(p.w1[s], w13[e]) and torch.equal(p.w2[s], w2[e])
+
+
+def test_stage_fixed_slot_plan_rolls_back_a_failed_load(monkeypatch):
+    """A failed copy enqueue leaves every newly assigned slot EMPTY, unmapped, and log2phy
+    unpublished (reference ``tests/test_prefill_stage_runtime.py:1225-1283``)."""
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.expert_key import ExpertKey
+
+    E = 4
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=2, async_load=True,
+                                            graph_compatible_offload=True))
+    rt.register_layer_for_fixed_slots(ExpertLayer(7, torch.zeros(E, 2, 3), torch.zeros(E, 3, 2)),
+                                      slot_device=torch.device("cpu"))
+
+    def fail(*args, **kwargs):
+        raise RuntimeError("enqueue failed")
+
+    monkeypatch.setattr(rt._transfer_engine, "load_many_async", fail)
+    with pytest.raises(RuntimeError, match="enqueue failed"):
+        rt.stage_fixed_slot_plan(layer_id=7, active_experts=(0, 1), num_logical_experts=E)
+    bank = rt.slot_bank(7)
+    assert all(slot.state == SlotState.EMPTY for slot in bank.slots)
+    assert bank.lookup(ExpertKey(7, 0)) is None and bank.lookup(ExpertKey(7, 1)) is None
+    assert rt.log2phy_buffer(7).tolist() == [-1] * E
+    monkeypatch.undo()
+    p = rt.stage_fixed_slot_plan(layer_id=7, active_experts=(0, 1), num_logical_experts=E)
+    assert p.mapping.active_slot_ids == (0, 1)  # the slots are reusable after the rollback
+
+
+def test_log2phy_updates_only_changed_active_entries(monkeypatch):
+    """Only active experts whose slot changed are rewritten; an evicted expert's stale entry
+    stays (it is never routed), and a hit-only stage enqueues no copy (reference
+    ``tests/test_prefill_stage_runtime.py:1782-1900``)."""
+    E = 4
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=3, async_load=True,
+                                            graph_compatible_offload=True))
+    rt.register_layer_for_fixed_slots(ExpertLayer(7, torch.zeros(E, 2, 3), torch.zeros(E, 3, 2)),
+                                      slot_device=torch.device("cpu"))
+    rt.stage_fixed_slot_plan(layer_id=7, active_experts=(0, 1, 2), num_logical_experts=E)
+    before = rt.stage_stats["log2phy_updates"]
+    p = rt.stage_fixed_slot_plan(layer_id=7, active_experts=(1, 3), num_logical_experts=E)
+    assert rt.stage_stats["log2phy_updates"] - before == 1  # only expert 3 -> slot 0
+    assert rt.log2phy_buffer(7).tolist() == [0, 1, 2, 0]  # expert 0's entry is stale
+    assert p.mapping.active_experts == (1, 3) and p.mapping.active_slot_ids == (1, 0)
+
+    def no_copy(*args, **kwargs):
+        raise AssertionError("a hit-only stage must not enqueue a copy")
+
+    monkeypatch.setattr(rt._transfer_engine, "load_many_async", no_copy)
+    before = rt.stage_stats["log2phy_updates"]
+    rt.stage_fixed_slot_plan(layer_id=7, active_experts=(1, 3), num_logical_experts=E)
+    assert rt.stage_stats["log2phy_updates"] == before
+    assert rt.log2phy_buffer(7).tolist() == [0, 1, 2, 0]
