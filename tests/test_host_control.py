@@ -283,3 +283,71 @@ def test_log2phy_updates_only_changed_active_entries(monkeypatch):
     rt.stage_fixed_slot_plan(layer_id=7, active_experts=(1, 3), num_logical_experts=E)
     assert rt.stage_stats["log2phy_updates"] == before
     assert rt.log2phy_buffer(7).tolist() == [0, 1, 2, 0]
+
+
+def test_transfer_ready_event_publishes_after_the_consumer_wait_and_rejects_stale_leases():
+    """A slot becomes READY only once the consumer stream waits on the copy event, and a
+    completion whose slot was reassigned meanwhile is rejected before any stream hand-off
+    (reference ``tests/test_prefill_stage_runtime.py:85-157``)."""
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.expert_key import ExpertKey
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.slot_bank import ExpertSlotBank
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.transfer_engine import TransferReadyEvent
+
+    bank = ExpertSlotBank(1, (1, 1), (1, 1), dtype=torch.float32, device=torch.device("cpu"))
+    slot = bank.allocate_for(ExpertKey(7, 0), step_id=1)
+    event = object()
+    ready = TransferReadyEvent(event, ((slot, slot.lease()),))
+    calls = []
+
+    class Consumer:
+        def wait_event(self, observed):
+            assert observed is event and slot.state == SlotState.LOADING
+            assert not ready.completed
+            calls.append("wait")
+
+    ready.install_consumer_dependency(Consumer())
+    assert calls == ["wait"] and ready.consumer_wait_installed and ready.completed
+    assert slot.state == SlotState.READY
+    ready.mark_ready()  # idempotent
+
+    bank2 = ExpertSlotBank(1, (1, 1), (1, 1), dtype=torch.float32, device=torch.device("cpu"))
+    s2 = bank2.allocate_for(ExpertKey(7, 0), step_id=1)
+    stale = TransferReadyEvent(object(), ((s2, s2.lease()),))
+    bank2.clear_slot(0, force=True)  # a rolled-back load; the slot is then reassigned
+    replacement = bank2.allocate_for(ExpertKey(7, 1), step_id=2)
+
+    class NoHandOff:
+        def wait_event(self, _):
+            raise AssertionError("a stale completion must fail before the stream hand-off")
+
+    with pytest.raises(RuntimeError, match="stale H2D completion"):
+        stale.install_consumer_dependency(NoHandOff())
+    assert replacement.state == SlotState.LOADING
+
+
+def test_prefill_stage_pool_double_buffers_and_sharing_across_equal_layouts():
+    """Two stage buffers never share storage; equal-layout layers share one pool and its
+    release events (reference ``tests/test_prefill_stage_runtime.py:566-658``)."""
+    E = 4
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=2))
+    for lid in (7, 9):
+        rt.register_layer_for_fixed_slots(
+            ExpertLayer(lid, torch.arange(E * 6, dtype=torch.float32).reshape(E, 2, 3),
+                        torch.arange(E * 6, dtype=torch.float32).reshape(E, 3, 2)),
+            slot_device=torch.device("cpu"))
+    first, r0 = rt.prepare_prefill_stage_plan(layer_id=7, active_experts=(0, 1), buffer_index=0)
+    second, r1 = rt.prepare_prefill_stage_plan(layer_id=7, active_experts=(2, 3), buffer_index=1)
+    assert first.w13_slots.data_ptr() != second.w13_slots.data_ptr()
+    assert first.w2_slots.data_ptr() != second.w2_slots.data_ptr()
+    with pytest.raises(RuntimeError, match="cannot be reassigned"):  # still loading
+        rt.prepare_prefill_stage_plan(layer_id=9, active_experts=(3,), buffer_index=0)
+    rt.wait_prefill_stage_plan(r0)
+    other, _ = rt.prepare_prefill_stage_plan(layer_id=9, active_experts=(3,), buffer_index=0)
+    assert other.w13_slots.data_ptr() == first.w13_slots.data_ptr()  # shared pool
+    event = object()
+    rt.remember_prefill_stage_buffer_release(7, 1, event)
+    assert rt.prefill_stage_buffer_release_event(9, 1) is event
+    with pytest.raises(ValueError, match="out of range"):
+        rt.prefill_stage_bank(7, 2)
+    rt.wait_prefill_stage_plan(r1)
+    assert torch.equal(second.w13_slots[0], torch.arange(12, 18, dtype=torch.float32).reshape(2, 3))
