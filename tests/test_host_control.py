@@ -351,3 +351,19 @@ def test_prefill_stage_pool_double_buffers_and_sharing_across_equal_layouts():
         rt.prefill_stage_bank(7, 2)
     rt.wait_prefill_stage_plan(r1)
     assert torch.equal(second.w13_slots[0], torch.arange(12, 18, dtype=torch.float32).reshape(2, 3))
+
+
+def test_host_remap_fails_closed_on_an_unstaged_expert():
+    """A routed expert whose log2phy entry is -1 is refused, never read from a wrong slot
+    (reference ``tests/test_prefill_stage_runtime.py:2098-2111``; on the device the same
+    check sets the error word inside lm_build_groups)."""
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.slot_mapping import ExpertSlotMapping
+
+    m = ExpertSlotMapping(7, (1, 2), torch.tensor([-1, 0, 1, -1], dtype=torch.int32),
+                          (1, 2, None, None), (0, 1))
+    assert m.remap_topk_ids_host(torch.tensor([[1, 2]])).tolist() == [[0, 1]]
+    assert m.physical_slot_for(2) == 1
+    with pytest.raises(RuntimeError, match="not staged"):
+        m.remap_topk_ids_host(torch.tensor([[2, 3]]))
+    with pytest.raises(KeyError):
+        m.physical_slot_for(3)
