@@ -226,6 +226,7 @@ def test_release_original_expert_weights_after_the_store_holds_them():
     assert rt.release_original_expert_weights_if_ready(l1) == (False, ("resident_layer:1",))
     assert rt.release_original_expert_weights_if_ready(l0) == (True, ())
     assert rt.release_original_expert_weights_if_ready(l0) == (True, ())  # idempotent
+    assert rt.released_original_weight_layers == (0,)
     assert tuple(l0.w13_weight.shape) == (0, 2, 3) and tuple(l0.w2_weight.shape) == (0, 3, 2)
     assert tuple(l1.w13_weight.shape) == (E, 2, 3)
     p = rt.stage_fixed_slot_plan(layer_id=0, active_experts=(4, 1), num_logical_experts=E)

@@ -610,6 +610,11 @@ class MoeOffloadRuntime:
         ready.install_consumer_dependency(consumer_stream)
 
     # ------------------------------------------------------------------ ledger
+    @property
+    def released_original_weight_layers(self) -> tuple[int, ...]:
+        """Layers whose original expert tensors were released, ascending."""
+        return tuple(sorted(self._released_original_weight_layers))
+
     def release_original_expert_weights_if_ready(self, layer: torch.nn.Module
                                                  ) -> tuple[bool, tuple[str, ...]]:
         """Opt-in release of a non-resident layer's original expert tensors once its host

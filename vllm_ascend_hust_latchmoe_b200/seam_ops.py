@@ -67,6 +67,12 @@ def unregister_moe_layer(layer_name: str) -> None:
             _LAYERS_BY_ID.pop(int(layer.layer_id), None)
 
 
+def registered_layer_names() -> tuple[str, ...]:
+    """Names of the MoE layers currently registered with the seam."""
+    with _registry_lock:
+        return tuple(_LAYERS_BY_NAME)
+
+
 def get_layer(layer_name: str) -> SlotBankMoE:
     layer = _LAYERS_BY_NAME.get(str(layer_name))
     if layer is None:

@@ -115,9 +115,9 @@ def main(argv=None) -> int:
         graph = {"unavailable": repr(exc)}
     print(json.dumps({
         "model": f"qwen3-30b-a3b-shaped, {args.layers} layers, dummy weights",
-        "attached_moe_layers": len(seam_ops._LAYERS_BY_NAME),
+        "attached_moe_layers": len(seam_ops.registered_layer_names()),
         "offloaded_layers": args.layers - len(resident.split(",")),
-        "released_original_expert_layers": sorted(rt._released_original_weight_layers),
+        "released_original_expert_layers": list(rt.released_original_weight_layers),
         "num_slots": args.slots,
         "engine_build_s": round(build_s, 1),
         "prompt_tokens": args.prompt_tokens,
