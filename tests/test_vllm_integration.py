@@ -289,3 +289,30 @@ def test_traced_seam_entry_splits_into_router_stage_and_mlp_pieces():
     assert any("moe_router_indirect" in t for t in pieces[0])
     assert pieces[1] == ["vllm.moe_offload_stage.default"]
     assert any("moe_mlp" in t for t in pieces[2])
+
+
+def test_captured_mlp_piece_takes_the_path_of_its_layer_tier(monkeypatch):
+    """While vLLM captures an MLP piece, the seam records the path that reads only fixed
+    buffers for the layer's tier: in-place reads for an HBM store, the device slot plan under
+    device staging, the slot bank otherwise; prefill-sized captures under device staging are
+    refused. Outside capture the eager stage decision is consumed once."""
+    from vllm_ascend_hust_latchmoe_b200 import seam_ops
+    from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE, StageDecision
+
+    def layer(resident, device):
+        lay = SlotBankMoE.__new__(SlotBankMoE)
+        lay.resident_tier, lay.device_staging, lay.layer_id, lay.pending = resident, device, 0, None
+        return lay
+
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    assert seam_ops._take_decision(layer(True, False), 4).mode == "resident"
+    assert seam_ops._take_decision(layer(False, True), 4).mode == "device"
+    assert seam_ops._take_decision(layer(False, False), 4).mode == "capturing"
+    with pytest.raises(RuntimeError, match="not captured under device staging"):
+        seam_ops._take_decision(layer(False, True), 512)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: False)
+    lay = layer(False, False)
+    lay.pending = StageDecision("slots")
+    assert seam_ops._take_decision(lay, 4).mode == "slots" and lay.pending is None
+    with pytest.raises(RuntimeError, match="without a preceding"):
+        seam_ops._take_decision(lay, 4)
