@@ -5,6 +5,7 @@ import json
 from pathlib import Path
 
 import numpy as np
+import pytest
 
 from oracle import control as oc
 from oracle import mlp as omlp
@@ -147,3 +148,14 @@ def test_mlp_oracle_linear_in_combine_weights():
     ones = f32_to_bf16_bits(np.ones((T, k), dtype=np.float32))
     out = omlp.combine(y, ones)
     assert np.allclose(out, round_bf16(y.reshape(T, k, H).sum(1)), atol=1e-2)
+
+
+def test_native_combine_index_fails_closed_on_missing_or_duplicate_pairs():
+    """The one combine must see every original top-k pair exactly once (reference
+    ``tests/test_phase_split_b2.py:1106``): a missing or repeated pair is refused."""
+    with pytest.raises(ValueError, match="exactly once"):
+        oc.native_combine_index([[1, 3], [0]], [[1, 0], [0]], 4)  # pair 2 missing
+    with pytest.raises(ValueError, match="exactly once"):
+        oc.native_combine_index([[1, 3], [0, 1]], [[1, 0], [0, 1]], 4)  # pair 1 twice
+    with pytest.raises(ValueError, match="pair count"):
+        oc.native_combine_index([[1, 3]], [[0]], 2)

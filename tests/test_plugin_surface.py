@@ -128,3 +128,33 @@ def test_autoconfig_seam_dataplane_defaults_and_release_conflict():
     assert not ac.apply_moe_offload_defaults(14.0, env=plain)["sew_dataplane"]
     assert plain["VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME"] == "1"
     assert "VLLM_ASCEND_MOE_OFFLOAD_RELEASE_ORIGINAL_EXPERT_WEIGHTS" not in plain
+
+
+def test_capability_admission_fails_closed_on_unimplemented_modes():
+    """Anything the B200 path does not implement is refused with a named blocker, like the
+    reference's admission (``tests/test_capabilities.py:95-179``): overlapped shared-expert
+    streams, Python router callables, tensor / multi-GPU layouts other than the expert-
+    partitioned bank, gated shared activations and unknown scoring functions."""
+    import dataclasses
+
+    base = cap.describe_checkpoint_config({"n_routed_experts": 64, "n_shared_experts": 2,
+                                           "num_experts_per_tok": 6, "n_group": 1,
+                                           "topk_group": 1})
+    assert cap.evaluate_support(base).enabled
+    cases = {
+        "unsupported_overlap_mode:shared_gate_multistream":
+            dataclasses.replace(base, overlap_mode="shared_gate_multistream"),
+        "unsupported_router_adapter:python_callable":
+            dataclasses.replace(base, router_adapter="python_callable"),
+        "unsupported_parallel_mode:tensor_parallel":
+            dataclasses.replace(base, parallel_mode="tensor_parallel"),
+        "unsupported_shared_activation:gated":
+            dataclasses.replace(base, shared_activation="gated"),
+        "unsupported_scoring:sqrtsoftplus": dataclasses.replace(
+            base, selection=dataclasses.replace(base.selection, scoring_function="sqrtsoftplus")),
+    }
+    for blocker, d in cases.items():
+        support = cap.evaluate_support(d)
+        assert support.state == "unsupported" and blocker in support.blockers, (blocker, support)
+    ep = dataclasses.replace(base, parallel_mode="expert_parallel")
+    assert cap.evaluate_support(ep).enabled
