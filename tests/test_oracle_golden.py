@@ -159,3 +159,37 @@ def test_native_combine_index_fails_closed_on_missing_or_duplicate_pairs():
         oc.native_combine_index([[1, 3], [0, 1]], [[1, 0], [0, 1]], 4)  # pair 1 twice
     with pytest.raises(ValueError, match="pair count"):
         oc.native_combine_index([[1, 3]], [[0]], 2)
+
+
+def test_router_oracle_agrees_with_vllm_torch_router():
+    """Third-party cross-check of the routing semantics the oracle restates (the reference's
+    own router lives in the un-vendored fork): vLLM's torch ``grouped_topk`` selects the same
+    expert sets with the same weights for plain softmax + renormalise (Qwen3-MoE), softmax
+    without renormalisation (DeepSeek-V2-Lite, one group) and grouped sigmoid + correction
+    bias + scaling (group-limited routing). vLLM does not order the selected experts, so each
+    token's (id, weight) pairs are compared sorted by id."""
+    mod = pytest.importorskip("vllm.model_executor.layers.fused_moe.router.grouped_topk_router")
+    grouped_topk = getattr(mod.grouped_topk, "__wrapped__", mod.grouped_topk)
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(5)
+    cases = [
+        dict(E=128, k=8, renorm=True, scoring="softmax", groups=1, topk_group=1, scale=1.0, bias=False),
+        dict(E=64, k=6, renorm=False, scoring="softmax", groups=1, topk_group=1, scale=1.0, bias=False),
+        dict(E=256, k=8, renorm=True, scoring="sigmoid", groups=8, topk_group=4, scale=2.5, bias=True),
+    ]
+    for c in cases:
+        logits = rng.standard_normal((64, c["E"])).astype(np.float32)
+        bias = rng.standard_normal(c["E"]).astype(np.float32) * 0.1 if c["bias"] else None
+        _, w, ids = orouter.route(logits, c["k"], renormalize=c["renorm"],
+                                  routed_scaling_factor=c["scale"], scoring_func=c["scoring"],
+                                  e_score_correction_bias=bias, num_expert_group=c["groups"],
+                                  topk_group=c["topk_group"])
+        vw, vids = grouped_topk(torch.zeros(64, 8), torch.from_numpy(logits), c["k"], c["renorm"],
+                                num_expert_group=c["groups"], topk_group=c["topk_group"],
+                                scoring_func=c["scoring"], routed_scaling_factor=c["scale"],
+                                e_score_correction_bias=None if bias is None else torch.from_numpy(bias))
+        vw, vids = vw.float().numpy(), vids.numpy()
+        for t in range(64):
+            a, b = np.argsort(ids[t]), np.argsort(vids[t])
+            assert ids[t][a].tolist() == vids[t][b].tolist(), (c, t)
+            np.testing.assert_allclose(w[t][a], vw[t][b], rtol=1e-5, atol=1e-7)
