@@ -316,3 +316,17 @@ def test_captured_mlp_piece_takes_the_path_of_its_layer_tier(monkeypatch):
     assert seam_ops._take_decision(lay, 4).mode == "slots" and lay.pending is None
     with pytest.raises(RuntimeError, match="without a preceding"):
         seam_ops._take_decision(lay, 4)
+
+
+def test_serve_check_model_config_is_a_qwen3_moe_config():
+    """The synthetic model the serving check hands vLLM parses as a transformers Qwen3-MoE
+    config with Qwen3-30B-A3B's expert shapes."""
+    transformers = pytest.importorskip("transformers")
+    from vllm_ascend_hust_latchmoe_b200.vllm_serve_check import qwen3_moe_config
+
+    raw = qwen3_moe_config(4, 32768)
+    cfg = transformers.AutoConfig.for_model(raw.pop("model_type"), **raw)
+    assert type(cfg).__name__ == "Qwen3MoeConfig"
+    assert (cfg.num_hidden_layers, cfg.hidden_size, cfg.moe_intermediate_size) == (4, 2048, 768)
+    assert (cfg.num_experts, cfg.num_experts_per_tok, cfg.norm_topk_prob) == (128, 8, True)
+    assert (cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim) == (32, 4, 128)
