@@ -318,9 +318,11 @@ def attach_fused_moe_layer(fused_moe: Any, *, runtime=None, layer_id: int | None
     name = str(getattr(fused_moe, "layer_name", "") or "")
     if not name:
         raise ValueError("FusedMoE layer has no layer_name")
-    lid = int(layer_id) if layer_id is not None else int(
-        getattr(fused_moe, "layer_id", -1) if getattr(fused_moe, "layer_id", -1) >= 0
-        else layer_id_from_name(name))
+    if layer_id is None:
+        layer_id = getattr(fused_moe, "layer_id", None)  # vLLM derives it from the name
+        if layer_id is None or int(layer_id) < 0:
+            layer_id = layer_id_from_name(name)
+    lid = int(layer_id)
     for attr in ("tp_size", "ep_size", "dp_size"):
         if int(getattr(fused_moe, attr, 1) or 1) != 1:
             raise RuntimeError(f"LatchMoE seam supports single-GPU MoE layers; {name} has "
