@@ -164,67 +164,223 @@ def _profiled_traffic(name: str) -> int | None:
 
 
 # --------------------------------------------------------------------------- CPU arm
-def cpu_reference_step(cfg, tokens: int, w13_bits, w2_bits, hidden_bits, logits_np) -> float:
-    """One bounded oracle pass (router + grouped MLP + combine) on `tokens` tokens."""
+def use_all_host_threads() -> int:
+    """Give the CPU arm every host core, whatever the launcher set: torchrun exports
+    OMP_NUM_THREADS=1 when it starts more than one process, which numpy's BLAS and torch
+    both honour. Returns the BLAS thread count in effect."""
+    cores = os.cpu_count() or 1
+    import torch
+
+    torch.set_num_threads(cores)
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        threadpool_limits(limits=cores)
+        blas = [int(i["num_threads"]) for i in threadpool_info()
+                if i.get("user_api") == "blas" and i.get("num_threads")]
+        return max(blas) if blas else cores
+    except Exception:
+        return cores
+
+
+def cpu_reference_step(cfg, tokens: int, w13, w2, hidden_bits, logits_np) -> float:
+    """One bounded oracle pass (router + grouped MLP + combine) on `tokens` tokens; expert
+    weights are fp32 arrays indexed by expert id (converted once, like loaded parameters)."""
     from oracle import mlp as omlp
     from oracle import router as orouter
 
     t0 = time.perf_counter()
     wb, _, ids = orouter.route(logits_np[:tokens], cfg.top_k, renormalize=cfg.renormalize,
-                               routed_scaling_factor=cfg.routed_scaling_factor)
-    omlp.moe_layer(hidden_bits[:tokens], ids, wb, w13_bits, w2_bits)
+                               routed_scaling_factor=cfg.routed_scaling_factor,
+                               scoring_func=cfg.scoring_func,
+                               num_expert_group=cfg.num_expert_group, topk_group=cfg.topk_group)
+    omlp.moe_layer(hidden_bits[:tokens], ids, wb, w13, w2)
     return time.perf_counter() - t0
 
 
-def cpu_inputs(cfg, tokens: int):
+def _bits(t):
     import numpy as np
     import torch
 
-    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
 
-    def b(t):
-        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+def cpu_inputs(cfg, tokens: int):
+    """The GPU arm's own seeded inputs (weights, hidden, logits), weights as fp32 numpy."""
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
 
     w13, w2 = syn.make_expert_weights(cfg, 0)
     hidden = syn.make_hidden(cfg, 0, tokens=tokens)
     logits = syn.make_router_logits(cfg, 0, tokens=tokens)
-    # Expert weights are converted to fp32 once (parameter load), outside the timed steps.
-    return w13.float().numpy(), w2.float().numpy(), b(hidden), logits.numpy()
+    return w13.float().numpy(), w2.float().numpy(), _bits(hidden), logits.numpy()
+
+
+def cpu_inputs_routed(cfg, tokens: int):
+    """Inputs for a timing sample of a large layer: seeded hidden states and logits, and
+    N(0, 0.02) fp32 weights for only the experts the sample routes to (the CPU pass touches
+    no other expert), so a Qwen3-235B-shaped sample does not materialise all 128 experts."""
+    import numpy as np
+    import torch
+
+    from oracle import router as orouter
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+    logits = syn.make_router_logits(cfg, 0, tokens=tokens).numpy()
+    hidden = _bits(syn.make_hidden(cfg, 0, tokens=tokens))
+    ids = orouter.route(logits, cfg.top_k, renormalize=cfg.renormalize)[2]
+    g = torch.Generator().manual_seed(0)
+    H, I = cfg.hidden, cfg.intermediate
+    w13, w2 = {}, {}
+    for e in np.unique(ids).tolist():
+        w13[e] = (torch.randn(2 * I, H, generator=g) * 0.02).numpy()
+        w2[e] = (torch.randn(H, I, generator=g) * 0.02).numpy()
+    return w13, w2, hidden, logits
+
+
+# CPU samples of the other benchmark layers: (config, tokens per timed pass)
+CPU_CONFIG_SAMPLES = (("c1_decode", 16), ("c4_shared", 64), ("c5_ep", 64))
+
+
+def cpu_config_times(headline: dict, repeats: int = 3) -> dict:
+    """Median wall time of the CPU pass of each benchmark layer on the host cores; the C2
+    entry is the headline figure measured by the caller (`headline`)."""
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+    out = {}
+    for name, tokens in CPU_CONFIG_SAMPLES:
+        cfg = syn.CONFIGS[name]
+        tokens = min(tokens, cfg.tokens)
+        ins = cpu_inputs_routed(cfg, tokens)
+        cpu_reference_step(cfg, tokens, *ins)
+        tt = sorted(cpu_reference_step(cfg, tokens, *ins) for _ in range(repeats))
+        ms = 1e3 * tt[len(tt) // 2]
+        out[name] = {"workload": cfg.name, "tokens": tokens, "full_tokens": cfg.tokens,
+                     "ms_per_pass": ms, "tokens_per_s": tokens / (ms / 1e3),
+                     "weights": "seeded N(0,0.02) fp32 for the routed experts"}
+        del ins
+    out["c2_prefill"] = headline
+    return out
 
 
 def run_reference(args, cfg) -> dict:
     """The CPU implementation of the path, timed on the host cores (bounded samples)."""
     cores = os.cpu_count() or 1
+    threads = use_all_host_threads()
     sample = args.cpu_sample_tokens
     w13, w2, hid, lg = cpu_inputs(cfg, sample)
     for _ in range(max(0, args.warmup)):
         cpu_reference_step(cfg, sample, w13, w2, hid, lg)
     times = [cpu_reference_step(cfg, sample, w13, w2, hid, lg) for _ in range(args.steps)]
+    del w13, w2
     total = sum(times)
     value = sample * len(times) / total
+    per_config = cpu_config_times({"workload": cfg.name, "tokens": sample,
+                                   "full_tokens": cfg.tokens,
+                                   "ms_per_pass": 1e3 * total / len(times),
+                                   "tokens_per_s": value,
+                                   "weights": "the GPU arm's seeded bf16 weights as fp32"})
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) bf16 weights, Zipf-biased router)",
         "config": {"workload": cfg.name, "tokens_per_step": sample, "full_tokens": cfg.tokens,
+                   "same_config": False,
+                   "sample_rule": "each step is the first 1024 of the 4096 tokens (same seeded "
+                                  "inputs as the GPU arm); tokens/s normalises the sample",
                    "hidden": cfg.hidden, "experts": cfg.num_experts, "top_k": cfg.top_k,
                    "moe_intermediate": cfg.intermediate, "num_slots": cfg.num_slots},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{sample} of {cfg.tokens} tokens per step, numpy fp32 BLAS"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "threads": threads,
+                         "kind": "port",
+                         "sample": f"{sample} of {cfg.tokens} tokens per step, numpy fp32 BLAS",
+                         "per_config": per_config},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return line
 
 
+# --------------------------------------------------------------------------- layer check
+def torch_layer_reference(hidden, ids, weights_bf16, w13_of, w2_of):
+    """fp32 torch restatement of the routed layer, used by the bench to check the outputs it
+    times (the numpy oracle is reserved for the tests and the CPU arm): per routed pair
+    y1 = bf16(x . W13^T), act = bf16(silu(y1[:, :I]) * y1[:, I:]), y2 = bf16(act . W2^T);
+    out[t] = bf16(sum_j f32(w[t, j]) * y2[t, j]) accumulated in fp32 in j order.
+    ``w13_of(e)`` / ``w2_of(e)`` return expert e's row-major bf16 weights."""
+    import torch
+
+    T, k = ids.shape
+    H = hidden.shape[1]
+    x = hidden.float()
+    y = torch.zeros(T, k, H, dtype=torch.float32, device=hidden.device)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for e in torch.unique(ids).tolist():
+            t_idx, j_idx = (ids == e).nonzero(as_tuple=True)
+            w13 = w13_of(e).float()
+            w2 = w2_of(e).float()
+            inter = w2.shape[1]
+            y1 = (x[t_idx] @ w13.T).to(torch.bfloat16).float()
+            gate = y1[:, :inter]
+            act = (gate / (1.0 + torch.exp(-gate)) * y1[:, inter:]).to(torch.bfloat16).float()
+            y[t_idx, j_idx] = (act @ w2.T).to(torch.bfloat16).float()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    w = weights_bf16.float()
+    acc = torch.zeros(T, H, dtype=torch.float32, device=hidden.device)
+    for j in range(k):
+        acc = acc + w[:, j:j + 1] * y[:, j]
+    return acc.to(torch.bfloat16)
+
+
+def torch_route_reference(logits, top_k: int, renormalize: bool = True):
+    """softmax(fp32) -> top-k -> w / max(sum w, eps) -> bf16 weights, int32 ids."""
+    import torch
+
+    p = torch.softmax(logits.float(), dim=-1)
+    w, ids = torch.topk(p, top_k, dim=-1)
+    if renormalize:
+        w = w / w.sum(dim=-1, keepdim=True).clamp_min(torch.finfo(torch.float32).eps)
+    return w.to(torch.bfloat16), ids.to(torch.int32)
+
+
+def compare_outputs(actual, expected) -> dict:
+    """max |a - e| / max |e| and cosine, in fp64."""
+    a = actual.double().reshape(-1)
+    e = expected.double().reshape(-1)
+    denom = max(float(e.abs().max()), 1e-30)
+    cos = float(a @ e / max(float(a.norm() * e.norm()), 1e-30))
+    return {"max_rel_err": float((a - e).abs().max()) / denom, "cosine": cos}
+
+
 # --------------------------------------------------------------------------- C5 (N > 1)
+def ep_expert_weights(e: int, cfg, dev):
+    """Expert e of the expert-partitioned layer: bf16 N(0, 0.02), seeded per expert so any
+    rank can rebuild any expert (its owner's bank, or a checker on another rank)."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(7000 + int(e))
+    I, H = cfg.intermediate, cfg.hidden
+    w13 = (torch.randn(2 * I, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(H, I, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    return w13, w2
+
+
+EP_CHECK_TOKENS = 8  # tokens per rank checked against the torch reference after timing
+EP_MAX_REL_ERR = 1e-2
+EP_MIN_COSINE = 0.9999
+
+
 def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
     """Qwen3-235B-A22B-shaped layer with the expert bank partitioned over the ranks: 256
     decode tokens per step in total (256 / N per rank). Cases: HBM-resident store with the
     exchange over NCCL and over peer memory (the library's dispatch / combine kernels), and a
     pinned-host store staged into half as many slots as the rank owns experts (peer
     exchange). Times are the max over ranks; `hbm_gbs_per_rank` counts the weights of the
-    rank's active experts read once per step."""
+    rank's active experts read once per step. After timing, each case's output for the
+    rank's first tokens is checked against the torch fp32 restatement of the layer (the
+    1-GPU semantics), worst case over ranks."""
     import torch
 
     from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
@@ -234,18 +390,30 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
     cfg = syn.CONFIGS["c5_ep"]
     T = cfg.tokens // world
     per = cfg.num_experts // world
-    g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
     I, H = cfg.intermediate, cfg.hidden
-    w13 = (torch.randn(per, 2 * I, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-    w2 = (torch.randn(per, H, I, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    owned = [ep_expert_weights(rank * per + i, cfg, dev) for i in range(per)]
+    w13 = torch.stack([a for a, _ in owned])
+    w2 = torch.stack([b for _, b in owned])
+    del owned
     hidden = syn.make_hidden(cfg, seed=rank, tokens=T).to(dev)
     all_logits = syn.make_router_logits(cfg, seed=0, tokens=cfg.tokens)
     logits = all_logits[rank * T:(rank + 1) * T].to(dev)
     ids_all = torch.topk(all_logits, cfg.top_k, dim=1).indices
-    owned = ids_all[(ids_all // per) == rank]
-    active_owned = int(torch.unique(owned).numel())
+    owned_ids = ids_all[(ids_all // per) == rank]
+    active_owned = int(torch.unique(owned_ids).numel())
     expert_bytes = 6 * H * I
+    n_chk = min(EP_CHECK_TOKENS, T)
+    w_ref, ids_ref = torch_route_reference(logits[:n_chk], cfg.top_k)
+    cache: dict[int, tuple] = {}
+
+    def weights_of(e):
+        if e not in cache:
+            cache[e] = ep_expert_weights(e, cfg, dev)
+        return cache[e]
+
+    ref = torch_layer_reference(hidden[:n_chk], ids_ref, w_ref, lambda e: weights_of(e)[0],
+                                lambda e: weights_of(e)[1])
+    cache.clear()
     out = {"workload": cfg.name, "tokens_per_step": cfg.tokens, "tokens_per_rank": T,
            "experts_per_rank": per, "active_experts_rank": active_owned}
     cases = (("resident_nccl", True, per, "nccl"), ("resident_peer", True, per, "peer"),
@@ -283,12 +451,25 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
         t_ms = float(ms.item())
         nv = (ep.stats.bytes_sent - sent0) / steps
         h2d = (local.runtime.transfer_engine.stats.bytes_h2d - h2d0) / steps
+        # correctness of what was timed: one more call, its first tokens against the reference
+        got = ep.forward(hidden, logits)
+        torch.cuda.synchronize()
+        local.check_device_errors("bench ep check")
+        ep.check_exchange_errors()
+        m = compare_outputs(got[:n_chk], ref)
+        worst = torch.tensor([m["max_rel_err"], -m["cosine"]], dtype=torch.float64, device=dev)
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+        parity = {"max_rel_err": float(worst[0]), "cosine": -float(worst[1]),
+                  "tokens_checked_per_rank": n_chk, "ranks": world,
+                  "bar": {"max_rel_err": EP_MAX_REL_ERR, "cosine": EP_MIN_COSINE},
+                  "reference": "torch fp32 restatement of the 1-GPU layer"}
+        parity["ok"] = parity["max_rel_err"] <= EP_MAX_REL_ERR and parity["cosine"] >= EP_MIN_COSINE
         out[name] = {"transport": transport, "ms_per_step": t_ms,
                      "tokens_per_s": cfg.tokens / (t_ms / 1e3),
                      "nvlink_bytes_per_rank_step": nv,
                      "hbm_gbs_per_rank": active_owned * expert_bytes / (t_ms / 1e3) / 1e9,
                      "slots_per_rank": slots if not on_dev else None,
-                     "h2d_bytes_rank0_step": int(h2d)}
+                     "h2d_bytes_rank0_step": int(h2d), "parity": parity}
         if exchange is not None:
             exchange.close()
         del ep, local
@@ -381,6 +562,10 @@ def main() -> None:
                     help="comma list of value,decode,c4,tpot,e2e,ep,cpu (profiling runs use one)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        # before numpy / torch load their thread pools (torchrun sets 1 thread per process)
+        for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+            os.environ[var] = str(os.cpu_count() or 1)
     every = {"value", "decode", "c4", "tpot", "e2e", "ep", "cpu"}
     sec = every if args.sections == "all" else set(args.sections.split(","))
     if not sec <= every:
@@ -417,11 +602,11 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
-    from tests.helpers import ExpertLayer
     from vllm_ascend_hust_latchmoe_b200 import _lib
     from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
     from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE
     from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
+    from vllm_ascend_hust_latchmoe_b200.synthetic import ExpertLayer
 
     _lib.load()
     peaks = _peaks()
@@ -677,12 +862,20 @@ def main() -> None:
 
     cpu = None
     if "cpu" in sec:
+        threads = use_all_host_threads()
         sample = args.cpu_sample_tokens
         w13b, w2b, hid, lg = cpu_inputs(cfg, sample)
         cpu_reference_step(cfg, sample, w13b, w2b, hid, lg)
         tt = [cpu_reference_step(cfg, sample, w13b, w2b, hid, lg) for _ in range(2)]
-        cpu = {"value": sample * len(tt) / sum(tt), "unit": UNIT, "cores": os.cpu_count(),
-               "kind": "port", "sample": f"{sample} of {cfg.tokens} tokens, numpy fp32 BLAS"}
+        del w13b, w2b
+        cpu_value = sample * len(tt) / sum(tt)
+        cpu = {"value": cpu_value, "unit": UNIT, "cores": os.cpu_count(),
+               "threads": threads, "kind": "port",
+               "sample": f"{sample} of {cfg.tokens} tokens, numpy fp32 BLAS",
+               "per_config": cpu_config_times({
+                   "workload": cfg.name, "tokens": sample, "full_tokens": cfg.tokens,
+                   "ms_per_pass": 1e3 * sum(tt) / len(tt), "tokens_per_s": cpu_value,
+                   "weights": "the GPU arm's seeded bf16 weights as fp32"})}
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,

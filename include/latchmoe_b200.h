@@ -300,7 +300,11 @@ int lm_moe_mlp_decode_offload(const uint16_t* hidden, int32_t top_k,
  *   lm_ep_combine       waits for every owner (bounded), reads each pair's output row from its
  *                       owner and reduces out[t] = sum_j w[t,j] * y[t,j] in fp32, j in order.
  * done_counter: one device int32, zero before the first call. Waits that run out set
- * LM_DEVERR_WAIT_TIMEOUT. Ranks must be on distinct GPUs.
+ * LM_DEVERR_WAIT_TIMEOUT; after a timed-out output wait lm_ep_combine reads nothing from the
+ * owners and writes zero rows. num_tokens * top_k > cap is rejected with
+ * LM_ERR_INVALID_ARGUMENT by lm_ep_dispatch and lm_ep_combine, and a pair whose position in
+ * its owner's area falls outside [0, cap) is skipped and recorded as LM_DEVERR_BAD_GROUP.
+ * Ranks must be on distinct GPUs.
  * Replaces: nothing in the reference, which is single-device
  * (patches/patch_fused_moe.py:4898-4914); the combine follows token_combine's order
  * (moe_offload/phase_split.py:1765-1856).

@@ -9,6 +9,7 @@ from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
 from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
 from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE
 from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
+from vllm_ascend_hust_latchmoe_b200.synthetic import ExpertLayer  # noqa: F401  (re-exported)
 
 # Tolerance for bf16 outputs against the fp32-accumulating oracle.
 MAX_REL_ERR = 1e-2
@@ -18,15 +19,6 @@ MIN_COSINE = 0.9999
 def bits(t: torch.Tensor) -> np.ndarray:
     """Raw bf16 bit patterns of a bf16 tensor as uint16 numpy."""
     return t.detach().to("cpu").contiguous().view(torch.int16).numpy().view(np.uint16)
-
-
-class ExpertLayer(torch.nn.Module):
-    def __init__(self, layer_id: int, w13: torch.Tensor, w2: torch.Tensor, shared: int = 0):
-        super().__init__()
-        self.layer_id = layer_id
-        self.w13_weight = w13
-        self.w2_weight = w2
-        self.num_fused_shared_experts = shared
 
 
 def build_layer(cfg: syn.LayerConfig, *, seed: int = 0, max_tokens: int | None = None,

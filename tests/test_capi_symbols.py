@@ -36,3 +36,17 @@ def test_abi_version_and_error_strings_without_gpu():
     assert b"num_experts" in lib.lm_last_error()
     rc = lib.lm_stage_copy(None, 16, None, 16, None, None, 1, 16, 7, None)
     assert rc == -1 and b"kind" in lib.lm_last_error()
+
+
+def test_ep_exchange_capacity_is_checked_on_the_host():
+    """More routed pairs than the exchange capacity are refused before any launch (a C-ABI
+    caller could otherwise address rows past an owner's receive area)."""
+    lib = _lib.load()
+    fake = ctypes.c_void_p(0x1000)
+    # 10 tokens x top-8 = 80 pairs > cap 64
+    rc = lib.lm_ep_dispatch(fake, 10, 8, 2048, fake, 16, fake, fake, 0, 2, fake, 64, 1, fake,
+                            None, None)
+    assert rc == -1 and b"capacity" in lib.lm_last_error()
+    rc = lib.lm_ep_combine(fake, fake, 10, 8, 2048, 16, fake, fake, 0, 2, fake, fake, 64, 1,
+                           fake, None, None)
+    assert rc == -1 and b"capacity" in lib.lm_last_error()

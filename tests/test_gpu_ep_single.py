@@ -1,0 +1,82 @@
+"""The peer exchange kernels on one GPU (world size 1: the rank is its own only owner).
+
+Dispatch, receive, signal and combine run in stream order, so every flag a wait reads was
+raised by an earlier launch: nothing waits on a concurrently running kernel. The combine of
+the rows sent back unchanged equals the oracle's top-k combine. A combine whose owners never
+signal (an epoch nobody raised) gives up after its bounded wait, reports
+LM_DEVERR_WAIT_TIMEOUT and writes zero rows instead of reading the owners' areas.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mlp as omlp
+from oracle.bf16 import bf16_bits_to_f32
+from tests.helpers import MAX_REL_ERR, MIN_COSINE, bits
+from vllm_ascend_hust_latchmoe_b200 import _lib
+from vllm_ascend_hust_latchmoe_b200.expert_parallel import _DevicePtrArray
+
+pytestmark = pytest.mark.gpu
+
+T, K, E, H = 16, 4, 8, 256
+
+
+def _setup(cuda):
+    cap = T * K
+    region = _lib.ep_region_alloc(_lib.ep_region_bytes(1, cap, H))
+    peers = torch.tensor([region], dtype=torch.int64, device=cuda)
+    off = _lib.ep_out_rows_offset(1, cap, H)
+    out_rows = torch.as_tensor(_DevicePtrArray(region + off, (cap, H), "<i2"),
+                               device=cuda).view(torch.bfloat16)
+    rng = np.random.default_rng(3)
+    ids_np = np.stack([rng.permutation(E)[:K] for _ in range(T)]).astype(np.int32)
+    w = torch.from_numpy(rng.random((T, K)).astype(np.float32)).to(torch.bfloat16).to(cuda)
+    ids = torch.from_numpy(ids_np).to(cuda)
+    hidden = torch.randn(T, H, device=cuda).to(torch.bfloat16)
+    owner = torch.zeros(E, dtype=torch.int32, device=cuda)
+    offsets = torch.empty(2, dtype=torch.int32, device=cuda)
+    p2r = torch.empty(cap, dtype=torch.int32, device=cuda)
+    r2p = torch.empty(cap, dtype=torch.int32, device=cuda)
+    scratch = torch.empty(_lib.build_groups_scratch_elems(cap, 1), dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    _lib.build_groups(ids, E, owner, 1, offsets, p2r, r2p, scratch, err)
+    return dict(cap=cap, region=region, peers=peers, out_rows=out_rows, ids=ids, ids_np=ids_np,
+                w=w, hidden=hidden, offsets=offsets, p2r=p2r, err=err)
+
+
+def test_single_rank_exchange_round_trip_and_timeout(cuda):
+    c = _setup(cuda)
+    cap, err = c["cap"], c["err"]
+    rows = torch.empty(cap, H, dtype=torch.bfloat16, device=cuda)
+    rids = torch.empty(cap, dtype=torch.int32, device=cuda)
+    total = torch.zeros(1, dtype=torch.int32, device=cuda)
+    done = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=cuda)
+    try:
+        for epoch in (1, 2):  # a second call reuses every area
+            _lib.ep_dispatch(c["hidden"], c["ids"], E, c["p2r"], c["offsets"], 0, 1, c["peers"],
+                             cap, epoch, done, err)
+            _lib.ep_receive(c["region"], 1, cap, H, epoch, rows, rids, total, err)
+            c["out_rows"].copy_(rows)  # the "expert" returns each row unchanged
+            _lib.ep_signal_outputs(c["peers"], 0, 1, cap, H, epoch)
+            out.fill_(7.0)
+            _lib.ep_combine(c["ids"], c["w"], E, c["p2r"], c["offsets"], 0, 1, c["peers"],
+                            c["region"], cap, epoch, out, err)
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0 and int(total.item()) == T * K
+            pairs = np.repeat(bf16_bits_to_f32(bits(c["hidden"])), K, axis=0)
+            ref = omlp.combine(pairs, bits(c["w"]))
+            m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)
+            assert m["max_rel_err"] <= MAX_REL_ERR and m["cosine"] >= MIN_COSINE, m
+        # epoch 3 was never signalled: the bounded wait gives up, nothing is read
+        out.fill_(7.0)
+        _lib.ep_combine(c["ids"], c["w"], E, c["p2r"], c["offsets"], 0, 1, c["peers"],
+                        c["region"], cap, 3, out, err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 3  # LM_DEVERR_WAIT_TIMEOUT
+        assert bool((out.float() == 0).all())
+    finally:
+        torch.cuda.synchronize()
+        c["out_rows"] = None
+        _lib.ep_region_free(c["region"])

@@ -156,3 +156,40 @@ def test_wave_fallback_reruns_full_layer(cuda, monkeypatch):
     _check(out, ref)
     m = omlp.compare(bf16_bits_to_f32(bits(out)), bf16_bits_to_f32(bits(good)))
     assert m["max_rel_err"] <= MAX_REL_ERR, m
+
+
+def test_overflow_at_a_captured_size_fails_closed(cuda):
+    """A slot-bank MLP piece captured at T tokens is replayed for every later T-token call,
+    reading log2phy for all routed experts. When a later T-token stage call finds more active
+    experts than slots it must raise (an evicted expert's stale log2phy entry would silently
+    select another expert's weights), while an uncaptured size still runs its waves."""
+    cfg = syn.CONFIGS["c1_decode"].with_tokens(4)
+    layer, rt, (w13, w2) = build_layer(cfg, max_tokens=16, num_slots=8)
+    E = cfg.num_experts
+    narrow = torch.full((4, E), -5.0)
+    narrow[:, :8] = torch.arange(8, 0, -1, dtype=torch.float32)  # every token: experts 0..7
+    hidden4 = syn.make_hidden(cfg, seed=1).to(cuda)
+    layer.forward(hidden4, narrow.to(cuda))  # 8 active experts: fits the 8 slots
+    torch.cuda.synchronize()
+    assert layer.stage(layer.topk_ids[:4]).mode == "slots"
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        layer.mlp_slots(hidden4, 4)
+    assert 4 in layer.captured_mlp_tokens
+    wide = syn.make_router_logits(cfg, seed=2)  # 4 tokens x top-8 over many experts
+    _, ids = layer.route(hidden4, wide.to(cuda))
+    torch.cuda.synchronize()
+    assert len(set(ids.cpu().reshape(-1).tolist())) > 8
+    with pytest.raises(RuntimeError, match="replayed from a CUDA graph"):
+        layer.stage(ids)
+    # an uncaptured size overflows into waves as usual, with the oracle's result
+    cfg5 = cfg.with_tokens(5)
+    hidden5 = syn.make_hidden(cfg5, seed=3)
+    logits5 = syn.make_router_logits(cfg5, seed=3)
+    _, _, ref = _oracle_layer(cfg5, hidden5, logits5, w13, w2)
+    out = layer.forward(hidden5.to(cuda), logits5.to(cuda))
+    torch.cuda.synchronize()
+    layer.check_device_errors()
+    assert len(layer.last_waves.waves) >= 2
+    _check(out, ref)
+    del g

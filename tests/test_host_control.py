@@ -368,3 +368,20 @@ def test_host_remap_fails_closed_on_an_unstaged_expert():
         m.remap_topk_ids_host(torch.tensor([[2, 3]]))
     with pytest.raises(KeyError):
         m.physical_slot_for(3)
+
+
+def test_slot_piece_replay_detection_follows_vllm_graph_mode(monkeypatch):
+    """The overflow guard applies to token counts with a captured slot-bank MLP piece, unless
+    vLLM runs the forward pass eagerly (cudagraph mode NONE)."""
+    import types
+
+    from vllm_ascend_hust_latchmoe_b200 import layer as layer_mod
+
+    fake = types.SimpleNamespace(captured_mlp_tokens={4})
+    replays = layer_mod.SlotBankMoE._slot_piece_replays
+    monkeypatch.setattr(layer_mod, "_vllm_cudagraph_mode", lambda: None)
+    assert replays(fake, 4) and not replays(fake, 5)
+    monkeypatch.setattr(layer_mod, "_vllm_cudagraph_mode", lambda: "PIECEWISE")
+    assert replays(fake, 4)
+    monkeypatch.setattr(layer_mod, "_vllm_cudagraph_mode", lambda: "NONE")
+    assert not replays(fake, 4)

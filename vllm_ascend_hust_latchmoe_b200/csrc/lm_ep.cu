@@ -27,9 +27,9 @@
 namespace lm {
 namespace {
 
-constexpr int kLayoutFields = 8;
-enum : int { F_FLAG_DISPATCH = 0, F_FLAG_OUT, F_COUNTS, F_PREFIX, F_RECV_IDS, F_RECV_ROWS,
-             F_OUT_ROWS, F_TOTAL };
+constexpr int kLayoutFields = 9;
+enum : int { F_FLAG_DISPATCH = 0, F_FLAG_OUT, F_COUNTS, F_PREFIX, F_WAIT_STATUS, F_RECV_IDS,
+             F_RECV_ROWS, F_OUT_ROWS, F_TOTAL };
 
 int64_t align256(int64_t v) { return (v + 255) & ~static_cast<int64_t>(255); }
 
@@ -43,6 +43,8 @@ void layout(int G, int cap, int H, int64_t* off) {
   o = align256(o + 4ll * G);
   off[F_PREFIX] = o;
   o = align256(o + 4ll * (G + 1));
+  off[F_WAIT_STATUS] = o;  // this rank's last output wait: 0 every owner answered, 1 timed out
+  o = align256(o + 4);
   off[F_RECV_IDS] = o;
   o = align256(o + 4ll * G * cap);
   off[F_RECV_ROWS] = o;
@@ -191,31 +193,45 @@ __global__ void ep_signal_kernel(void* const* __restrict__ peers, Layout L, int 
     st_release_sys(field<long long>(peers[o], L, F_FLAG_OUT) + rank, epoch);
 }
 
+// Waits for every owner's output flag; the outcome goes to the region's wait-status word,
+// which the combine reads so that a timed-out call never reads rows that may still change.
 __global__ void __launch_bounds__(32)
     ep_wait_out_kernel(void* region, Layout L, int G, long long epoch, int32_t* err_word) {
-  wait_flags(field<long long>(region, L, F_FLAG_OUT), G, epoch, err_word);
+  const bool ok = wait_flags(field<long long>(region, L, F_FLAG_OUT), G, epoch, err_word);
+  if (threadIdx.x == 0) *field<int32_t>(region, L, F_WAIT_STATUS) = ok ? 0 : 1;
 }
 
 // One block per token; the same accumulation order and arithmetic as combine_kernel.
+// After a timed-out output wait (the local wait-status word) nothing is read from the owners
+// and the token's row is written as zeros; a pair whose position lies outside [0, cap) is
+// recorded as LM_DEVERR_BAD_GROUP and contributes nothing (the same rule as the dispatch).
 __global__ void ep_combine_kernel(const int32_t* __restrict__ ids,
                                   const uint16_t* __restrict__ w_bf16, int top_k, int H,
                                   int per_rank, const int32_t* __restrict__ pair_to_row,
                                   const int32_t* __restrict__ send_offsets, int rank, int G,
-                                  void* const* __restrict__ peers, Layout L,
-                                  uint16_t* __restrict__ out) {
+                                  void* const* __restrict__ peers, const void* local_region,
+                                  Layout L, int cap, uint16_t* __restrict__ out,
+                                  int32_t* __restrict__ err_word) {
   __shared__ const uint16_t* s_src[32];
   __shared__ float s_w[32];
   const int64_t t = blockIdx.x;
+  const bool waited = *field<const int32_t>(const_cast<void*>(local_region), L, F_WAIT_STATUS) == 0;
   if (threadIdx.x < top_k) {
     const int64_t p = t * top_k + threadIdx.x;
     const int e = ids[p];
     const int o = e / per_rank;
     const uint16_t* src = nullptr;
-    if (e >= 0 && o < G) {
+    if (e < 0 || o >= G) {
+      record_error(err_word, LM_DEVERR_BAD_EXPERT_ID);
+    } else if (waited) {
       const int pos = pair_to_row[p] - send_offsets[o];
-      const int32_t* prefix = field<int32_t>(peers[o], L, F_PREFIX);
-      const int64_t row = __ldcg(prefix + rank) + pos;
-      src = field<uint16_t>(peers[o], L, F_OUT_ROWS) + row * H;
+      if (pos < 0 || pos >= cap) {
+        record_error(err_word, LM_DEVERR_BAD_GROUP);
+      } else {
+        const int32_t* prefix = field<int32_t>(peers[o], L, F_PREFIX);
+        const int64_t row = __ldcg(prefix + rank) + pos;
+        src = field<uint16_t>(peers[o], L, F_OUT_ROWS) + row * H;
+      }
     }
     s_src[threadIdx.x] = src;
     s_w[threadIdx.x] = bf16_bits_to_f32(w_bf16[p]);
@@ -335,6 +351,9 @@ extern "C" int lm_ep_dispatch(const uint16_t* hidden, int64_t num_tokens, int32_
       send_offsets == nullptr || (num_tokens > 0 && (hidden == nullptr || topk_ids == nullptr ||
                                                      pair_to_row == nullptr)))
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_dispatch: bad arguments");
+  if (num_tokens * top_k > cap)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_ep_dispatch: num_tokens * top_k exceeds the exchange capacity cap");
   if (reinterpret_cast<uintptr_t>(hidden) & 15)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_dispatch: hidden must be 16-byte aligned");
   const int64_t pairs = num_tokens * top_k;
@@ -400,6 +419,9 @@ extern "C" int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weigh
       (num_tokens > 0 && (topk_ids == nullptr || topk_weights_bf16 == nullptr ||
                           pair_to_row == nullptr || send_offsets == nullptr || out == nullptr)))
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_combine: bad arguments");
+  if (num_tokens * top_k > cap)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_ep_combine: num_tokens * top_k exceeds the exchange capacity cap");
   if (reinterpret_cast<uintptr_t>(out) & 15)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_combine: out must be 16-byte aligned");
   const Layout L = make_layout(world, cap, hidden_size);
@@ -412,6 +434,6 @@ extern "C" int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weigh
   if (threads < 32) threads = 32;
   ep_combine_kernel<<<static_cast<unsigned>(num_tokens), threads, 0, s>>>(
       topk_ids, topk_weights_bf16, top_k, hidden_size, experts_per_rank, pair_to_row,
-      send_offsets, rank, world, peer_regions, L, out);
+      send_offsets, rank, world, peer_regions, local_region, L, cap, out, err_word);
   return launch_status("lm_ep_combine");
 }

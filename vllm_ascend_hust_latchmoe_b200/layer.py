@@ -61,6 +61,19 @@ def group_launches(pairs: int) -> int:
     return 1 if 0 < pairs <= 512 else 3
 
 
+def _vllm_cudagraph_mode() -> str | None:
+    """vLLM's CUDA-graph mode of the forward pass in flight ("NONE", "PIECEWISE", ...), or
+    None outside a vLLM forward pass."""
+    try:
+        from vllm.forward_context import get_forward_context, is_forward_context_available
+    except Exception:
+        return None
+    if not is_forward_context_available():
+        return None
+    mode = getattr(get_forward_context(), "cudagraph_runtime_mode", None)
+    return None if mode is None else str(getattr(mode, "name", mode))
+
+
 @dataclass
 class StageDecision:
     mode: str  # "capturing" | "static" | "slots" | "waves" | "resident" | "device" | "passthrough"
@@ -123,6 +136,7 @@ class SlotBankMoE:
         self.counts = torch.zeros(self.E, dtype=i32, device=d)
         self.counts_host = torch.zeros(self.E, dtype=i32, pin_memory=True)
         self.err = torch.zeros(1, dtype=i32, device=d)
+        self.err_host = torch.zeros(1, dtype=i32, pin_memory=True)
         self.tables_host = torch.zeros(self.E_total + self.G_max, dtype=i32, pin_memory=True)
         self.tables = torch.zeros(self.E_total + self.G_max, dtype=i32, device=d)
         self.expert_to_group = self.tables[: self.E_total]
@@ -158,6 +172,10 @@ class SlotBankMoE:
             self.hit_miss = torch.zeros(2, dtype=torch.int64, device=d)
         self.last_full_layer: dict | None = None
         self.kernel_launches = 0
+        # Token counts whose slot-bank MLP piece (mlp_slots) was captured into a CUDA graph.
+        # A replayed piece reads log2phy for every routed expert, so a stage call at one of
+        # these sizes must never leave the working set unstaged (see stage()).
+        self.captured_mlp_tokens: set[int] = set()
         self.pending: StageDecision | None = None
         self.shared_w13 = None
         self.shared_w2 = None
@@ -178,12 +196,29 @@ class SlotBankMoE:
         return self.topk_w[:T], self.topk_ids[:T]
 
     def active_counts(self, topk_ids: torch.Tensor) -> tuple[int, ...]:
-        """K2 histogram + one small D2H: per-expert pair counts of this call."""
+        """K2 histogram + one small D2H: per-expert pair counts of this call. The layer's
+        device error word comes back in the same round trip and a set word raises here,
+        before anything is staged or published (an out-of-range id would otherwise be
+        dropped from the working set silently)."""
         _lib.expert_histogram(topk_ids, self.E, self.counts, self.err)
         self.kernel_launches += 1
         self.counts_host.copy_(self.counts, non_blocking=True)
+        self.err_host.copy_(self.err, non_blocking=True)
         torch.cuda.current_stream().synchronize()
+        code = int(self.err_host[0])
+        if code:
+            raise RuntimeError(f"layer {self.layer_id}: device error {code} "
+                               f"({_lib.DEVERR_NAMES.get(code, '?')}) before staging")
         return tuple(self.counts_host.tolist())
+
+    def _slot_piece_replays(self, T: int) -> bool:
+        """True when the MLP piece that follows this stage call is a replay of a captured
+        slot-bank piece: one was captured at this token count and the caller is not running
+        vLLM's forward pass eagerly (cudagraph mode NONE)."""
+        if int(T) not in self.captured_mlp_tokens:
+            return False
+        return _vllm_cudagraph_mode() in (None, "PIECEWISE", "FULL", "FULL_AND_PIECEWISE",
+                                          "FULL_DECODE_ONLY")
 
     def stage(self, topk_ids: torch.Tensor, phase: int = PHASE_UNKNOWN,
               capturing: bool = False) -> StageDecision:
@@ -219,6 +254,16 @@ class SlotBankMoE:
         counts = self.active_counts(topk_ids)
         active = tuple(e for e, c in enumerate(counts) if c > 0)
         if len(active) > rt.config.num_slots:
+            if self._slot_piece_replays(T):
+                # Fail closed: the replayed piece would read log2phy for all routed experts,
+                # and an evicted expert's entry still names a slot that now holds another.
+                raise RuntimeError(
+                    f"layer {self.layer_id}: {len(active)} active experts exceed "
+                    f"num_slots={rt.config.num_slots} at {T} tokens, a size whose slot-bank "
+                    "MLP piece is replayed from a CUDA graph; multi-wave execution cannot run "
+                    "inside a captured piece. Raise VLLM_ASCEND_MOE_OFFLOAD_NUM_SLOTS to at "
+                    "least top_k * max_num_seqs, enable device staging "
+                    "(VLLM_ASCEND_MOE_OFFLOAD_DEVICE_STAGING=1), or run this batch size eagerly")
             if not rt.config.b2_wave_prefill:
                 raise RuntimeError(
                     f"active expert working set size {len(active)} exceeds "
@@ -250,6 +295,8 @@ class SlotBankMoE:
         """Captured MLP piece: log2phy remap + grouping, grouped MLP on the slot bank, combine.
 
         Reads only fixed addresses (slot bank, log2phy, this layer's buffers)."""
+        if torch.cuda.is_current_stream_capturing():
+            self.captured_mlp_tokens.add(int(T))
         rt = self.runtime
         bank = rt.slot_bank(self.layer_id)
         log2phy = rt.log2phy_buffer(self.layer_id)

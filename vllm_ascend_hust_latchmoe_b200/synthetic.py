@@ -68,6 +68,20 @@ CONFIGS: dict[str, LayerConfig] = {
 }
 
 
+class ExpertLayer(torch.nn.Module):
+    """The attributes the runtime reads from a MoE layer when it registers the layer's
+    experts (``register_layer_for_fixed_slots``): ``layer_id``, ``w13_weight [E, 2I, H]``,
+    ``w2_weight [E, H, I]`` and ``num_fused_shared_experts``. Stands in for a loaded model's
+    FusedMoE module when the weights are synthetic."""
+
+    def __init__(self, layer_id: int, w13: torch.Tensor, w2: torch.Tensor, shared: int = 0):
+        super().__init__()
+        self.layer_id = layer_id
+        self.w13_weight = w13
+        self.w2_weight = w2
+        self.num_fused_shared_experts = shared
+
+
 def _gen(seed: int, index: int) -> torch.Generator:
     g = torch.Generator(device="cpu")
     g.manual_seed(int(seed) * 1_000_003 + int(index))
