@@ -562,6 +562,213 @@ def run_value(args, cfg, make_layer, hidden, logits, dist, dev, world, local_ran
     return value, ms_step, roofline, int(launches_per_step * args.steps), waves, clocks
 
 
+# --------------------------------------------------------------------------- N > 1 value
+def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
+    """``value`` at N > 1: the same C2 layer (Qwen3-30B-A3B shape, 4096 tokens per rank: weak
+    scaling) with its 128 experts partitioned over the N GPUs. Experts are placed on ranks by
+    a load-balanced placement of a profiled routing sample (the router's gate columns and the
+    expert bank permuted together at load time); each rank holds its E / N experts in HBM.
+    One step on every rank: route its tokens, dispatch each routed pair's row straight into its
+    owner's receive area over NVLink (peer memory), run the owner's grouped MLP on what it
+    received (the row count stays on the device), signal, and combine every token's pairs from
+    the owners in top-k order. Time = max over ranks; after timing, each rank's first tokens
+    are checked against the torch fp32 restatement of the 1-GPU layer. Also returns the same
+    step from host buffers (``e2e``)."""
+    import torch
+
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+    from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE, PeerExchange,
+                                                                balanced_expert_placement,
+                                                                build_rank_layer, cuda_ops)
+
+    T, E, k, H, I = cfg.tokens, cfg.num_experts, cfg.top_k, cfg.hidden, cfg.intermediate
+    per = E // world
+    prof = torch.topk(syn.make_router_logits(cfg, seed=0, tokens=1024), k, dim=1).indices
+    perm = torch.tensor(balanced_expert_placement(
+        torch.bincount(prof.reshape(-1), minlength=E).tolist(), world))
+    w13, w2 = syn.make_expert_weights(cfg, 0)
+    owned = perm[rank * per:(rank + 1) * per]
+    local = build_rank_layer(w13_owned=w13[owned].to(dev), w2_owned=w2[owned].to(dev),
+                             rank=rank, device=dev, max_rows=world * T * k, num_slots=per,
+                             store_on_device=True)
+    exchange = PeerExchange(world_size=world, rank=rank, max_tokens=T, top_k=k, hidden_size=H,
+                            device=dev)
+    ep = ExpertParallelMoE(num_experts=E, top_k=k, hidden_size=H, rank=rank, world_size=world,
+                           device=dev, exchange=exchange,
+                           ops=cuda_ops(local, num_experts=E, top_k=k, max_tokens=T))
+    hidden_cpu = syn.make_hidden(cfg, seed=rank)
+    logits_cpu = syn.make_router_logits(cfg, seed=rank, bias_seed=0)
+    placed_cpu = logits_cpu[:, perm].contiguous()
+    hidden, logits = hidden_cpu.to(dev), placed_cpu.to(dev)
+    for _ in range(args.warmup):
+        ep.forward(hidden, logits)
+    torch.cuda.synchronize()
+    local.check_device_errors("bench ep value warmup")
+    ep.check_exchange_errors()
+    sent0 = ep.stats.bytes_sent
+    launches0 = local.kernel_launches
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        t0.record()
+        for _ in range(args.steps):
+            ep.forward(hidden, logits)
+        t1.record()
+        barrier()
+    local.check_device_errors("bench ep value")
+    ep.check_exchange_errors()
+    ms = torch.tensor([t0.elapsed_time(t1)], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_total = float(ms.item())
+    ms_step = ms_total / args.steps
+    value = world * T * args.steps / (ms_total / 1e3)
+    nvlink = (ep.stats.bytes_sent - sent0) / args.steps
+    # per step: route, owner grouping, dispatch, receive (wait + compact), the owner MLP's
+    # grouping / gather / grouped-MLP / unit combine, signal, combine (wait + reduce)
+    launches_per_step = 2 + 1 + 2 + (local.kernel_launches - launches0) // args.steps + 1 + 2
+
+    # correctness of what was timed: one more call, first tokens against the reference
+    got = ep.forward(hidden, logits)
+    torch.cuda.synchronize()
+    local.check_device_errors("bench ep value check")
+    ep.check_exchange_errors()
+    n_chk = EP_CHECK_TOKENS
+    w_ref, ids_ref = torch_route_reference(logits_cpu[:n_chk].to(dev), k)
+    ref = torch_layer_reference(hidden[:n_chk], ids_ref, w_ref, lambda e: w13[e].to(dev),
+                                lambda e: w2[e].to(dev))
+    m = compare_outputs(got[:n_chk], ref)
+    worst = torch.tensor([m["max_rel_err"], -m["cosine"]], dtype=torch.float64, device=dev)
+    dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+    parity = {"max_rel_err": float(worst[0]), "cosine": -float(worst[1]),
+              "tokens_checked_per_rank": n_chk, "ranks": world,
+              "bar": {"max_rel_err": EP_MAX_REL_ERR, "cosine": EP_MIN_COSINE},
+              "reference": "torch fp32 restatement of the 1-GPU layer (original expert order)"}
+    parity["ok"] = parity["max_rel_err"] <= EP_MAX_REL_ERR and parity["cosine"] >= EP_MIN_COSINE
+
+    # the owner's grouped MLP alone on the rows it received in the last step (roofline)
+    x = exchange
+    rows_recv = int(x.total.item())
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        local.mlp_rows_count(x.rows, x.ids, x.total, x.out_rows)
+    a.record()
+    for _ in range(args.steps):
+        local.mlp_rows_count(x.rows, x.ids, x.total, x.out_rows)
+    b.record()
+    torch.cuda.synchronize()
+    mlp_ms = a.elapsed_time(b) / args.steps
+    local.check_device_errors("bench ep owner mlp")
+    flops = rows_recv * cfg.flops_per_pair
+    achieved = flops / (mlp_ms / 1e3) / 1e12
+    loads = torch.tensor([rows_recv], dtype=torch.float64, device=dev)
+    gathered = [torch.zeros_like(loads) for _ in range(world)]
+    dist.all_gather(gathered, loads)
+    rows_all = [float(g.item()) for g in gathered]
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
+                "peak_source": peaks["source"], "traffic": None,
+                "kernel": "rank 0's grouped MLP (owner side: grouping, gather, lm_moe_mlp_prefill, "
+                          "unit-weight combine) on the rows it received",
+                "ms_per_call": mlp_ms, "flops_per_call": flops, "rows_rank0": rows_recv}
+
+    # e2e: the same step from pinned host buffers (inputs in, output out, every step)
+    h_host = hidden_cpu.pin_memory()
+    lg_host = placed_cpu.pin_memory()
+    out_host = torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True)
+    h_dev, lg_dev = torch.empty_like(hidden), torch.empty_like(logits)
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier()
+    a.record()
+    for _ in range(e2e_steps):
+        h_dev.copy_(h_host, non_blocking=True)
+        lg_dev.copy_(lg_host, non_blocking=True)
+        o = ep.forward(h_dev, lg_dev)
+        out_host.copy_(o, non_blocking=True)
+    b.record()
+    barrier()
+    ep.check_exchange_errors()
+    e_ms = torch.tensor([a.elapsed_time(b)], device=dev)
+    dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e_ms.item()) / e2e_steps
+    e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": int(h_host.numel() * 2 + lg_host.numel() * 4),
+           "d2h_bytes_per_step": int(out_host.numel() * 2), "ms_per_step": e2e_ms,
+           "path": "ExpertParallelMoE.forward per rank from pinned host buffers"}
+    ep_info = {"placement": "load-balanced (profiled routing sample; gate columns and expert "
+                            "bank permuted at load time)",
+               "experts_per_rank": per, "rows_received_per_rank": rows_all,
+               "rank_load_max_over_mean": max(rows_all) / (sum(rows_all) / world),
+               "nvlink_bytes_sent_rank0_per_step": nvlink, "transport": "peer memory (IPC)",
+               "parity": parity}
+    exchange.close()
+    del ep, local
+    torch.cuda.empty_cache()
+    return value, ms_step, roofline, int(launches_per_step * args.steps), clocks, e2e, ep_info
+
+
+def run_c5_single(args, dev) -> dict:
+    """Single-GPU baseline of the Qwen3-235B-A22B-shaped layer of the expert-partitioned
+    configuration: all 128 experts (4.8 GB) HBM-resident on one GPU, 256 tokens per step,
+    the layer (route, wave plan, grouping, permute, tcgen05 MLP, combine) captured as a CUDA
+    graph and replayed; its first tokens checked against the torch fp32 restatement."""
+    import torch
+
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+    from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
+    from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
+    from vllm_ascend_hust_latchmoe_b200.weight_layout import to_tiled
+
+    cfg = syn.CONFIGS["c5_ep"]
+    E, H, I, T = cfg.num_experts, cfg.hidden, cfg.intermediate, cfg.tokens
+    w13 = torch.empty(E, 2 * I, H, dtype=torch.bfloat16, device=dev)
+    w2 = torch.empty(E, H, I, dtype=torch.bfloat16, device=dev)
+    for e in range(E):
+        w13[e], w2[e] = ep_expert_weights(e, cfg, dev)
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=cfg.num_slots,
+                                            async_load=True, b2_wave_prefill=True))
+    rt.register_layer_with_store(0, to_tiled(w13), to_tiled(w2), slot_device=dev, num_slots=1)
+    layer = SlotBankMoE(rt, 0, hidden_size=H, intermediate_size=I, num_experts=E,
+                        top_k=cfg.top_k, max_tokens=T, device=dev)
+    hidden = syn.make_hidden(cfg, seed=0).to(dev)
+    logits = syn.make_router_logits(cfg, seed=0).to(dev)
+    for _ in range(3):
+        layer.forward(hidden, logits)
+    torch.cuda.synchronize()
+    layer.check_device_errors("bench c5 single")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        layer.route(hidden, logits)
+        layer.mlp_resident(hidden, T)
+    for _ in range(3):
+        g.replay()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(50):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / 50
+    out = layer.out[:T]
+    n_chk = EP_CHECK_TOKENS
+    w_ref, ids_ref = torch_route_reference(logits[:n_chk], cfg.top_k)
+    ref = torch_layer_reference(hidden[:n_chk], ids_ref, w_ref, lambda e: w13[e],
+                                lambda e: w2[e])
+    m = compare_outputs(out[:n_chk], ref)
+    active = int((torch.bincount(layer.topk_ids[:T].reshape(-1).long(), minlength=E) > 0).sum())
+    del g
+    res = {"workload": cfg.name + " on one GPU (all 128 experts in HBM)", "ms_per_step": ms,
+           "tokens_per_s": T / (ms / 1e3), "active_experts": active,
+           "hbm_gbs": active * cfg.expert_bytes / (ms / 1e3) / 1e9,
+           "timing": "CUDA-graph replay x50 of the whole layer",
+           "parity": dict(m, tokens_checked=n_chk,
+                          ok=m["max_rel_err"] <= EP_MAX_REL_ERR and m["cosine"] >= EP_MIN_COSINE)}
+    del layer, rt, w13, w2
+    torch.cuda.empty_cache()
+    return res
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -583,7 +790,10 @@ def main() -> None:
         for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
             os.environ[var] = str(os.cpu_count() or 1)
     every = {"value", "decode", "c4", "tpot", "e2e", "ep", "cpu"}
-    sec = every if args.sections == "all" else set(args.sections.split(","))
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    # at N > 1 the single-GPU sections (decode, C4, TPOT) would only repeat BENCH's figures
+    default = every if world_env == 1 else {"value", "e2e", "ep"}
+    sec = default if args.sections == "all" else set(args.sections.split(","))
     if not sec <= every:
         ap.error(f"unknown sections {sorted(sec - every)}")
     if args.no_tpot:
@@ -651,9 +861,13 @@ def main() -> None:
     value = ms_step = roofline = None
     launches = waves = 0
     clocks = ClockSampler(local_rank)
-    if "value" in sec:
+    ep_value = e2e_ep = None
+    if "value" in sec and world == 1:
         value, ms_step, roofline, launches, waves, clocks = run_value(
             args, cfg, make_layer, hidden, logits, dist, dev, world, local_rank, peaks, barrier)
+    elif "value" in sec:
+        value, ms_step, roofline, launches, clocks, e2e_ep, ep_value = run_value_ep(
+            args, cfg, dist, dev, rank, world, local_rank, peaks, barrier)
     # ----------------------------------------------------------------- decode layer (C1)
     decode = None
     if "decode" in sec:
@@ -824,8 +1038,8 @@ def main() -> None:
                 "data": "random-init weights and KV; synthetic routing"}
 
     # ----------------------------------------------------------------- e2e (host buffers)
-    e2e = None
-    if "e2e" in sec:
+    e2e = e2e_ep
+    if "e2e" in sec and world == 1:
         off = make_layer(False)
         h_host = hidden_cpu.pin_memory()
         lg_host = logits_cpu.pin_memory()
@@ -870,6 +1084,8 @@ def main() -> None:
     ep_report = None
     if dist is not None and "ep" in sec:
         ep_report = run_expert_parallel(dist, rank, world, dev, args)
+    elif "ep" in sec:
+        ep_report = {"single_gpu": run_c5_single(args, dev)}
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -902,11 +1118,17 @@ def main() -> None:
                    "hidden": cfg.hidden, "experts": cfg.num_experts, "top_k": cfg.top_k,
                    "moe_intermediate": cfg.intermediate,
                    "tier": "HBM-resident experts read in place (no staging)",
-                   "wave_plan": {"num_slots": cfg.num_slots, "waves": waves,
-                                 "executed_as": "the device wave plan orders the groups; all "
-                                                "waves run in one grouped-MLP pass"},
-                   "launch": "layer step captured once as a CUDA graph, replayed per step",
-                   "parallelism": f"replica x{world}",
+                   "wave_plan": ({"num_slots": cfg.num_slots, "waves": waves,
+                                  "executed_as": "the device wave plan orders the groups; all "
+                                                 "waves run in one grouped-MLP pass"}
+                                 if world == 1 else None),
+                   "launch": ("layer step captured once as a CUDA graph, replayed per step"
+                              if world == 1 else "eager (the exchange epochs advance per call)"),
+                   "parallelism": ("single GPU" if world == 1 else
+                                   f"expert-partitioned x{world}: 128 experts over {world} GPUs, "
+                                   "4096 tokens per rank, dispatch/combine over NVLink peer "
+                                   "memory"),
+                   "expert_partition": ep_value,
                    "l2": "weights 1.2 GB per step > 126 MB L2 (no flush needed)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode, "c4": c4, "tpot": tpot,
         "expert_parallel": ep_report,

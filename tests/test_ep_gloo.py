@@ -16,7 +16,8 @@ from oracle import control as oc
 from oracle import mlp as omlp
 from oracle import router as orouter
 from oracle.bf16 import bf16_bits_to_f32, f32_to_bf16_bits
-from vllm_ascend_hust_latchmoe_b200.expert_parallel import EPOps, ExpertParallelMoE
+from vllm_ascend_hust_latchmoe_b200.expert_parallel import (EPOps, ExpertParallelMoE,
+                                                            balanced_expert_placement)
 
 E, K, H, I, T = 16, 4, 64, 32, 24
 
@@ -67,15 +68,27 @@ def _oracle_ops(w13, w2, rank, per_rank):
     return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine)
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, placed=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         logits, hidden, w13, w2 = _data(rank)
-        ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank, world_size=world,
-                               ops=_oracle_ops(w13, w2, rank, E // world), device="cpu")
-        out = ep.forward(_bf16(hidden), torch.from_numpy(logits))
+        if placed:
+            # placement from a profiled sample (rank 0's routing), applied to the gate columns
+            # and the expert bank; the layer's result must not change
+            ids0 = orouter.route(_data(0)[0], K)[2]
+            perm = np.asarray(balanced_expert_placement(np.bincount(ids0.reshape(-1),
+                                                                    minlength=E), world))
+            ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
+                                   world_size=world, device="cpu",
+                                   ops=_oracle_ops(w13[perm], w2[perm], rank, E // world))
+            out = ep.forward(_bf16(hidden), torch.from_numpy(np.ascontiguousarray(logits[:, perm])))
+        else:
+            ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
+                                   world_size=world, ops=_oracle_ops(w13, w2, rank, E // world),
+                                   device="cpu")
+            out = ep.forward(_bf16(hidden), torch.from_numpy(logits))
         wb, _, ids = orouter.route(logits, K)
         ref = omlp.moe_layer(hidden, ids, wb, w13, w2)
         m = omlp.compare(bf16_bits_to_f32(_bits(out)), ref)
@@ -90,12 +103,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_exchange_matches_single_process_oracle(world):
+@pytest.mark.parametrize("world,placed", [(2, False), (4, False), (4, True)])
+def test_ep_exchange_matches_single_process_oracle(world, placed):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, placed)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=120) for _ in procs]
@@ -108,3 +121,22 @@ def test_ep_exchange_matches_single_process_oracle(world):
     assert sum(r[2] for r in results) == sum(r[3] for r in results) == world * T * K
     for rank, m, *_ in results:
         assert m["max_rel_err"] <= 1e-2 and m["cosine"] >= 0.9999, (rank, m)
+
+
+def test_balanced_placement_is_a_permutation_with_even_load():
+    rng = np.random.default_rng(0)
+    load = np.floor(4000.0 / np.arange(1, 129) ** 1.1)[rng.permutation(128)]
+    for world in (1, 2, 4, 8):
+        perm = balanced_expert_placement(load, world)
+        assert sorted(perm) == list(range(128))
+        per = 128 // world
+        ranks = np.asarray(load)[perm].reshape(world, per).sum(1)
+        # within a few percent of the lower bound (the mean, or the heaviest single expert)
+        assert ranks.max() <= 1.08 * max(ranks.mean(), load.max()), (world, ranks)
+        contiguous = np.asarray(load).reshape(world, per).sum(1)
+        assert ranks.max() <= contiguous.max()
+        for r in range(world):  # each rank's experts in id order
+            assert perm[r * per:(r + 1) * per] == sorted(perm[r * per:(r + 1) * per])
+    assert balanced_expert_placement([5, 5, 5, 5], 2) == [0, 2, 1, 3]  # ties: lowest rank
+    with pytest.raises(ValueError):
+        balanced_expert_placement(load[:10], 4)

@@ -93,10 +93,15 @@ def zipf_bias(num_experts: int, s: float, seed: int) -> torch.Tensor:
     return (-s * torch.log(rank)).to(torch.float32)
 
 
-def make_router_logits(cfg: LayerConfig, seed: int = 0, tokens: int | None = None) -> torch.Tensor:
+def make_router_logits(cfg: LayerConfig, seed: int = 0, tokens: int | None = None,
+                       bias_seed: int | None = None) -> torch.Tensor:
+    """Router logits: N(0, 1) noise from ``seed`` plus the Zipf bias of ``bias_seed``
+    (default ``seed``). Ranks of one expert-parallel model share the bias seed (the experts'
+    popularity is a property of the model) and differ in the noise (their tokens)."""
     T = cfg.tokens if tokens is None else int(tokens)
     noise = torch.randn(T, cfg.num_experts, generator=_gen(seed, 2), dtype=torch.float32)
-    return noise + zipf_bias(cfg.num_experts, cfg.zipf_s, seed)[None, :]
+    bseed = seed if bias_seed is None else bias_seed
+    return noise + zipf_bias(cfg.num_experts, cfg.zipf_s, bseed)[None, :]
 
 
 def make_hidden(cfg: LayerConfig, seed: int = 0, tokens: int | None = None) -> torch.Tensor:
