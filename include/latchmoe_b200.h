@@ -84,6 +84,23 @@ int lm_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts,
                   int32_t* topk_ids, void* stream);
 
 /*
+ * K1 router with the fused mix-placement shared suffix: the same routed selection as
+ * lm_route_topk over the num_experts routed experts, written as rows of top_k + num_shared
+ * entries: the routed top-k, then the shared experts' logical ids num_experts ..
+ * num_experts + num_shared - 1 with weight 1 (the slot bank's pinned suffix serves them).
+ * topk_weights_bf16 / topk_weights_f32 / topk_ids are [T, top_k + num_shared];
+ * top_k + num_shared <= 32.
+ * Replaces: ops/fused_moe/moe_router_op.py:72-125 with mix_placement=True (select_experts
+ * appending num_shared_experts pairs per token, moe_router_op.py:152-161).
+ */
+int lm_route_topk_shared(const float* logits, int64_t num_tokens, int32_t num_experts,
+                         int32_t top_k, int32_t scoring_func, int32_t renormalize,
+                         float routed_scaling_factor, const float* e_score_correction_bias,
+                         int32_t num_expert_group, int32_t topk_group, int32_t num_shared,
+                         uint16_t* topk_weights_bf16, float* topk_weights_f32,
+                         int32_t* topk_ids, void* stream);
+
+/*
  * K2 active-expert histogram: counts[e] = #pairs routed to expert e (counts is
  * overwritten). Invalid ids set LM_DEVERR_BAD_EXPERT_ID in err_word (may be NULL).
  * Replaces: ops/fused_moe/moe_offload_stage_op.py:297-302,474-508 (D2H of all top-k ids

@@ -158,3 +158,27 @@ def test_capability_admission_fails_closed_on_unimplemented_modes():
         assert support.state == "unsupported" and blocker in support.blockers, (blocker, support)
     ep = dataclasses.replace(base, parallel_mode="expert_parallel")
     assert cap.evaluate_support(ep).enabled
+
+
+def test_fused_mix_placement_lane_is_admitted_and_the_router_widens():
+    """The fused mix-placement shared lane is admitted, like the reference
+    (``tests/test_capabilities.py:121-144``); it returns a routed tensor only. With
+    mix_placement the router op's rows hold top_k + num_shared_experts entries."""
+    import dataclasses
+
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    base = cap.describe_checkpoint_config({"n_routed_experts": 64, "n_shared_experts": 2,
+                                           "num_experts_per_tok": 6})
+    fused = dataclasses.replace(base, shared_mode="fused_mix_placement",
+                                output_contract="routed_tensor")
+    assert cap.evaluate_support(fused).enabled
+    tuple_out = dataclasses.replace(fused, output_contract="shared_routed_tuple")
+    assert "fused_mix_placement_returns_routed_tensor" in cap.evaluate_support(tuple_out).blockers
+    plugin.register()
+    with FakeTensorMode():
+        h = torch.empty(5, 64, dtype=torch.bfloat16)
+        lg = torch.empty(5, 64)
+        w, ids = torch.ops.vllm.moe_router(h, lg, 6, False, False, None, None, "softmax", 1.0,
+                                           None, 64, True, 2)
+        assert tuple(w.shape) == (5, 8) and tuple(ids.shape) == (5, 8)

@@ -42,6 +42,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _P, _P, _P, _P],
     ),
+    "lm_route_topk_shared": (
+        ctypes.c_int,
+        [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _I32, _P, _P, _P, _P],
+    ),
     "lm_expert_histogram": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _P]),
     "lm_ep_region_bytes": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_ep_out_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
@@ -165,13 +169,30 @@ def route_topk(
     weights_bf16: torch.Tensor,
     ids: torch.Tensor,
     weights_f32: torch.Tensor | None = None,
+    num_shared: int = 0,
 ) -> None:
+    """Top-k routing into ``weights_bf16`` / ``ids`` ``[T, top_k]``; with ``num_shared`` > 0
+    the rows are ``top_k + num_shared`` wide and end with the fused shared experts' ids
+    (``E .. E + num_shared - 1``, weight 1)."""
     _require_cuda(logits, weights_bf16, ids, weights_f32, e_score_correction_bias)
     assert logits.dtype == torch.float32 and logits.is_contiguous()
     T, E = logits.shape
     scoring = {"softmax": LM_SCORING_SOFTMAX, "sigmoid": LM_SCORING_SIGMOID}.get(scoring_func)
     if scoring is None:
         raise ValueError(f"unsupported scoring_func {scoring_func!r}")
+    if num_shared:
+        if ids.shape[-1] != top_k + num_shared or weights_bf16.shape[-1] != top_k + num_shared:
+            raise ValueError("mix-placement outputs need top_k + num_shared columns")
+        _check(
+            "lm_route_topk_shared",
+            lib().lm_route_topk_shared(
+                _ptr(logits), T, E, int(top_k), scoring, int(bool(renormalize)),
+                float(routed_scaling_factor), _ptr(e_score_correction_bias),
+                int(num_expert_group or 0), int(topk_group or 0), int(num_shared),
+                _ptr(weights_bf16), _ptr(weights_f32), _ptr(ids), _stream(),
+            ),
+        )
+        return
     _check(
         "lm_route_topk",
         lib().lm_route_topk(

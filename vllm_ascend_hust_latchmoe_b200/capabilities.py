@@ -36,7 +36,7 @@ class RouterSelection:
 class MoeCapabilityDescriptor:
     schema_version: str
     output_contract: str        # "routed_tensor" | "shared_routed_tuple"
-    shared_mode: str            # "none" | "external_resident"
+    shared_mode: str            # "none" | "external_resident" | "fused_mix_placement"
     shared_activation: str
     shared_expert_count: int
     routed_expert_count: int
@@ -138,18 +138,25 @@ def describe_checkpoint_config(config: dict[str, Any], *, parallel_mode: str = "
 def describe_layer_capability(layer: Any) -> MoeCapabilityDescriptor:
     """Descriptor of a constructed :class:`~vllm_ascend_hust_latchmoe_b200.layer.SlotBankMoE`."""
     shared = 1 if getattr(layer, "shared_w13", None) is not None else 0
+    fused = int(getattr(layer, "num_fused_shared", 0) or 0)
     n_group = int(getattr(layer, "num_expert_group", 0) or 0)
+    if shared:
+        shared_mode, contract, count = "external_resident", "shared_routed_tuple", shared
+    elif fused:
+        shared_mode, contract, count = "fused_mix_placement", "routed_tensor", fused
+    else:
+        shared_mode, contract, count = "none", "routed_tensor", 0
     return MoeCapabilityDescriptor(
         schema_version=SCHEMA_VERSION,
-        output_contract="shared_routed_tuple" if shared else "routed_tensor",
-        shared_mode="external_resident" if shared else "none",
-        shared_activation="always_on" if shared else "none",
-        shared_expert_count=shared,
+        output_contract=contract,
+        shared_mode=shared_mode,
+        shared_activation="always_on" if count else "none",
+        shared_expert_count=count,
         routed_expert_count=int(layer.E),
         router_owner="external_logits",
         router_adapter="builtin",
         selection=RouterSelection(
-            top_k=int(layer.k), grouped_top_k=n_group > 1,
+            top_k=int(getattr(layer, "k_route", layer.k)), grouped_top_k=n_group > 1,
             topk_group=int(getattr(layer, "topk_group", 0) or 0) or None,
             num_expert_group=n_group or None, renormalize=bool(layer.renormalize),
             scoring_function=str(layer.scoring_func),
@@ -168,8 +175,10 @@ def evaluate_support(d: MoeCapabilityDescriptor) -> CapabilitySupport:
     b: list[str] = []
     if d.output_contract not in ("routed_tensor", "shared_routed_tuple"):
         b.append(f"unknown_output_contract:{d.output_contract}")
-    if d.shared_mode not in ("none", "external_resident"):
+    if d.shared_mode not in ("none", "external_resident", "fused_mix_placement"):
         b.append(f"unsupported_shared_mode:{d.shared_mode}")
+    if d.shared_mode == "fused_mix_placement" and d.output_contract != "routed_tensor":
+        b.append("fused_mix_placement_returns_routed_tensor")
     if d.shared_mode == "external_resident" and d.shared_activation not in ("always_on",):
         b.append(f"unsupported_shared_activation:{d.shared_activation}")
     if d.router_owner not in ("external_logits", "internal_gate"):

@@ -63,7 +63,8 @@ __device__ __forceinline__ int route_one_token(const float* __restrict__ logits,
                                                const float* __restrict__ bias, int n_group,
                                                int topk_group, uint16_t* __restrict__ w_bf16,
                                                float* __restrict__ w_f32,
-                                               int32_t* __restrict__ ids, int lane) {
+                                               int32_t* __restrict__ ids, int lane,
+                                               int num_shared = 0, int shared_base = 0) {
   const float* row = logits + t * num_experts;
 
   float lg[EPL], sc[EPL], key[EPL];
@@ -209,11 +210,19 @@ __device__ __forceinline__ int route_one_token(const float* __restrict__ logits,
     my_w = my_w / fmaxf(s, FLT_EPSILON);
   }
   my_w *= scale;
+  // Rows hold the routed top-k followed by the fused shared suffix (num_shared > 0): ids
+  // shared_base .. shared_base + num_shared - 1, each with weight 1.
+  const int ld = top_k + num_shared;
   if (lane < top_k) {
-    const int64_t o = t * top_k + lane;
+    const int64_t o = t * ld + lane;
     w_bf16[o] = f32_to_bf16_bits(my_w);
     if (w_f32 != nullptr) w_f32[o] = my_w;
     ids[o] = my_id;
+  } else if (lane < ld) {
+    const int64_t o = t * ld + lane;
+    w_bf16[o] = f32_to_bf16_bits(1.0f);
+    if (w_f32 != nullptr) w_f32[o] = 1.0f;
+    ids[o] = shared_base + (lane - top_k);
   }
   return my_id;
 }
@@ -225,14 +234,14 @@ __global__ void __launch_bounds__(kRouteWarpsPerBlock * 32)
                       int top_k, int scoring, int renorm, float scale,
                       const float* __restrict__ bias, int n_group, int topk_group,
                       uint16_t* __restrict__ w_bf16, float* __restrict__ w_f32,
-                      int32_t* __restrict__ ids) {
+                      int32_t* __restrict__ ids, int num_shared, int shared_base) {
   pdl_wait();
   pdl_trigger();
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kRouteWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= num_tokens) return;
   route_one_token<EPL>(logits, t, num_experts, top_k, scoring, renorm, scale, bias, n_group,
-                       topk_group, w_bf16, w_f32, ids, lane);
+                       topk_group, w_bf16, w_f32, ids, lane, num_shared, shared_base);
 }
 
 __global__ void histogram_kernel(const int32_t* __restrict__ ids, int64_t num_pairs,
@@ -596,15 +605,13 @@ int check_route_args(int64_t num_tokens, int32_t num_experts, int32_t top_k,
 }
 }  // namespace
 
-extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts,
-                             int32_t top_k, int32_t scoring_func, int32_t renormalize,
-                             float routed_scaling_factor, const float* e_score_correction_bias,
-                             int32_t num_expert_group, int32_t topk_group,
-                             uint16_t* topk_weights_bf16, float* topk_weights_f32,
-                             int32_t* topk_ids, void* stream) {
-  int rc = check_route_args(num_tokens, num_experts, top_k, scoring_func, num_expert_group,
-                            topk_group, logits, topk_weights_bf16, topk_ids);
-  if (rc) return rc;
+namespace {
+int route_launch(const float* logits, int64_t num_tokens, int32_t num_experts, int32_t top_k,
+                 int32_t scoring_func, int32_t renormalize, float routed_scaling_factor,
+                 const float* e_score_correction_bias, int32_t num_expert_group,
+                 int32_t topk_group, uint16_t* topk_weights_bf16, float* topk_weights_f32,
+                 int32_t* topk_ids, int32_t num_shared, int32_t shared_base, void* stream,
+                 const char* who) {
   if (num_tokens == 0) return LM_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned blocks =
@@ -615,7 +622,8 @@ extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t nu
   e = launch_dependent(route_topk_kernel<N>, dim3(blocks), dim3(kRouteWarpsPerBlock * 32), 0, s, \
                        logits, num_tokens, num_experts, top_k, scoring_func, renormalize,    \
                        routed_scaling_factor, e_score_correction_bias, num_expert_group,     \
-                       topk_group, topk_weights_bf16, topk_weights_f32, topk_ids)
+                       topk_group, topk_weights_bf16, topk_weights_f32, topk_ids, num_shared, \
+                       shared_base)
   if (epl <= 1) {
     LM_ROUTE_LAUNCH(1);
   } else if (epl <= 2) {
@@ -626,8 +634,43 @@ extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t nu
     LM_ROUTE_LAUNCH(8);
   }
 #undef LM_ROUTE_LAUNCH
-  if (e != cudaSuccess) return check_cuda(e, "lm_route_topk");
-  return launch_status("lm_route_topk");
+  if (e != cudaSuccess) return check_cuda(e, who);
+  return launch_status(who);
+}
+}  // namespace
+
+extern "C" int lm_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts,
+                             int32_t top_k, int32_t scoring_func, int32_t renormalize,
+                             float routed_scaling_factor, const float* e_score_correction_bias,
+                             int32_t num_expert_group, int32_t topk_group,
+                             uint16_t* topk_weights_bf16, float* topk_weights_f32,
+                             int32_t* topk_ids, void* stream) {
+  int rc = check_route_args(num_tokens, num_experts, top_k, scoring_func, num_expert_group,
+                            topk_group, logits, topk_weights_bf16, topk_ids);
+  if (rc) return rc;
+  return route_launch(logits, num_tokens, num_experts, top_k, scoring_func, renormalize,
+                      routed_scaling_factor, e_score_correction_bias, num_expert_group,
+                      topk_group, topk_weights_bf16, topk_weights_f32, topk_ids, 0, 0, stream,
+                      "lm_route_topk");
+}
+
+extern "C" int lm_route_topk_shared(const float* logits, int64_t num_tokens,
+                                    int32_t num_experts, int32_t top_k, int32_t scoring_func,
+                                    int32_t renormalize, float routed_scaling_factor,
+                                    const float* e_score_correction_bias,
+                                    int32_t num_expert_group, int32_t topk_group,
+                                    int32_t num_shared, uint16_t* topk_weights_bf16,
+                                    float* topk_weights_f32, int32_t* topk_ids, void* stream) {
+  int rc = check_route_args(num_tokens, num_experts, top_k, scoring_func, num_expert_group,
+                            topk_group, logits, topk_weights_bf16, topk_ids);
+  if (rc) return rc;
+  if (num_shared < 0 || top_k + num_shared > 32)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_route_topk_shared: need 0 <= num_shared and top_k + num_shared <= 32");
+  return route_launch(logits, num_tokens, num_experts, top_k, scoring_func, renormalize,
+                      routed_scaling_factor, e_score_correction_bias, num_expert_group,
+                      topk_group, topk_weights_bf16, topk_weights_f32, topk_ids, num_shared,
+                      num_experts, stream, "lm_route_topk_shared");
 }
 
 extern "C" int lm_expert_histogram(const int32_t* topk_ids, int64_t num_pairs,

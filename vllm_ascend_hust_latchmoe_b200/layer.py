@@ -119,6 +119,7 @@ class SlotBankMoE:
         self.renormalize = bool(renormalize)
         self.routed_scaling_factor = float(routed_scaling_factor)
         self.scoring_func = scoring_func
+        self.k_route = self.k
         self.num_expert_group = int(num_expert_group or 0)
         self.topk_group = int(topk_group or 0)
         self.device = torch.device(device) if device is not None else torch.device("cuda")
@@ -128,13 +129,18 @@ class SlotBankMoE:
         self.E_total = runtime.total_logical_expert_count_for_layer(layer_id=self.layer_id,
                                                                     fallback=self.E)
         self.num_bank_rows = bank.physical_expert_count
+        # Fused mix-placement shared lane: logical ids E .. E_total-1 are shared experts held in
+        # the bank's pinned suffix; the router appends them to every token's top-k (weight 1),
+        # so a pair row is k_route + num_fused_shared wide.
+        self.num_fused_shared = self.E_total - self.E
+        self.k = self.k_route + self.num_fused_shared
         d, i32 = self.device, torch.int32
         P = self.max_tokens * self.k
         self.G_max = max(self.E_total, self.num_bank_rows)
         self.topk_ids = torch.zeros(self.max_tokens, self.k, dtype=i32, device=d)
         self.topk_w = torch.zeros(self.max_tokens, self.k, dtype=torch.bfloat16, device=d)
-        self.counts = torch.zeros(self.E, dtype=i32, device=d)
-        self.counts_host = torch.zeros(self.E, dtype=i32, pin_memory=True)
+        self.counts = torch.zeros(self.E_total, dtype=i32, device=d)
+        self.counts_host = torch.zeros(self.E_total, dtype=i32, pin_memory=True)
         self.err = torch.zeros(1, dtype=i32, device=d)
         self.err_host = torch.zeros(1, dtype=i32, pin_memory=True)
         self.tables_host = torch.zeros(self.E_total + self.G_max, dtype=i32, pin_memory=True)
@@ -155,6 +161,19 @@ class SlotBankMoE:
         self.identity_groups = torch.arange(self.E_total, dtype=i32, device=d)
         self.wave_offsets = torch.zeros(self.E + 1, dtype=i32, device=d)
         self.num_waves = torch.zeros(1, dtype=i32, device=d)
+        # Shared experts are groups E .. E_total-1 on every path, reading the bank's pinned
+        # rows; the device wave plan only writes the first E entries of these tables.
+        self.pinned_rows = torch.zeros(self.E_total, dtype=i32, device=d)
+        if self.num_fused_shared:
+            pinned = [bank.pinned_slot_for_logical_id(e) for e in range(self.E, self.E_total)]
+            if any(r is None for r in pinned):
+                raise RuntimeError(f"layer {self.layer_id}: shared experts lack pinned slots")
+            self.pinned_rows[self.E:] = torch.tensor(pinned, dtype=i32)
+            self.tables[self.E:self.E_total] = torch.arange(self.E, self.E_total, dtype=i32,
+                                                            device=d)
+            self.tables[self.E_total + self.E:2 * self.E_total] = torch.tensor(
+                pinned, dtype=i32).to(d)
+        self.pinned_rows_host = self.pinned_rows.cpu()
         self.resident_tier = runtime.host_layer(self.layer_id).on_device
         self.last_waves = WaveReport()
         self.last_fallback_reason: str | None = None
@@ -191,7 +210,8 @@ class SlotBankMoE:
                         routed_scaling_factor=self.routed_scaling_factor,
                         e_score_correction_bias=self.e_bias,
                         num_expert_group=self.num_expert_group, topk_group=self.topk_group,
-                        weights_bf16=self.topk_w[:T], ids=self.topk_ids[:T])
+                        weights_bf16=self.topk_w[:T], ids=self.topk_ids[:T],
+                        num_shared=self.num_fused_shared)
         self.kernel_launches += 1
         return self.topk_w[:T], self.topk_ids[:T]
 
@@ -200,7 +220,7 @@ class SlotBankMoE:
         device error word comes back in the same round trip and a set word raises here,
         before anything is staged or published (an out-of-range id would otherwise be
         dropped from the working set silently)."""
-        _lib.expert_histogram(topk_ids, self.E, self.counts, self.err)
+        _lib.expert_histogram(topk_ids, self.E_total, self.counts, self.err)
         self.kernel_launches += 1
         self.counts_host.copy_(self.counts, non_blocking=True)
         self.err_host.copy_(self.err, non_blocking=True)
@@ -209,7 +229,8 @@ class SlotBankMoE:
         if code:
             raise RuntimeError(f"layer {self.layer_id}: device error {code} "
                                f"({_lib.DEVERR_NAMES.get(code, '?')}) before staging")
-        return tuple(self.counts_host.tolist())
+        # routed experts only: the pinned shared suffix is never staged
+        return tuple(self.counts_host[: self.E].tolist())
 
     def _slot_piece_replays(self, T: int) -> bool:
         """True when the MLP piece that follows this stage call is a replay of a captured
@@ -341,25 +362,40 @@ class SlotBankMoE:
         if T <= DECODE_MAX_TOKENS:
             # group = expert id, bank row = expert id: no histogram or wave plan needed
             self.resident_planned = False
-            _lib.build_groups(ids, self.E_total, self.identity_groups, self.E, self.group_offsets,
-                              self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+            _lib.build_groups(ids, self.E_total, self.identity_groups, self.E_total,
+                              self.group_offsets, self.pair_to_row, self.row_to_pair,
+                              self.scratch, self.err)
             self._grouped_mlp(hidden, T, self.identity_groups, 0, self.E, store.w13, store.w2)
+            self._shared_groups_mlp(hidden, T, self.pinned_rows)
             self.kernel_launches += group_launches(T * self.k) + mlp_launches(T) + 1
             return self._combine(T, out)
         self.resident_planned = True
-        _lib.expert_histogram(ids, self.E, self.counts, self.err)
-        _lib.plan_waves(self.counts, self.runtime.config.num_slots, self.expert_to_group,
-                        self.group_bank_row, self.wave_offsets, self.num_waves,
-                        in_place_rows=True)
-        _lib.build_groups(ids, self.E_total, self.expert_to_group, self.E, self.group_offsets,
-                          self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+        _lib.expert_histogram(ids, self.E_total, self.counts, self.err)
+        _lib.plan_waves(self.counts[: self.E], self.runtime.config.num_slots,
+                        self.expert_to_group, self.group_bank_row, self.wave_offsets,
+                        self.num_waves, in_place_rows=True)
+        _lib.build_groups(ids, self.E_total, self.expert_to_group, self.E_total,
+                          self.group_offsets, self.pair_to_row, self.row_to_pair, self.scratch,
+                          self.err)
         launches = 2 + group_launches(T * self.k)  # histogram, plan, grouping
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
         self._grouped_mlp(hidden, T, self.group_bank_row, 0, self.E, store.w13, store.w2)
+        self._shared_groups_mlp(hidden, T, self.group_bank_row)
         self.kernel_launches += launches + mlp_launches(T) + 1
         return self._combine(T, out)
+
+    def _shared_groups_mlp(self, hidden, T, bank_rows_dev) -> None:
+        """Fused mix-placement lane: the shared experts' groups (E .. E_total-1) on the
+        bank's pinned rows, once per call, into the same pair rows as the routed groups (the
+        single combine then sums routed and shared pairs in top-k order)."""
+        if not self.num_fused_shared:
+            return
+        bank = self.runtime.slot_bank(self.layer_id)
+        self._grouped_mlp(hidden, T, bank_rows_dev, self.E, self.E_total, bank.w13_slots,
+                          bank.w2_slots)
+        self.kernel_launches += mlp_launches(T)
 
     def mlp_rows_count(self, rows: torch.Tensor, ids: torch.Tensor, count_dev: torch.Tensor,
                        out: torch.Tensor) -> torch.Tensor:
@@ -452,14 +488,16 @@ class SlotBankMoE:
         bank, ready, payload = rt.prepare_full_layer_prefill_plan(layer_id=self.layer_id)
         rt.wait_prefill_stage_plan(ready, torch.cuda.current_stream())
         ids = self.topk_ids[:T]
-        _lib.build_groups(ids, self.E_total, self.identity_groups, self.E, self.group_offsets,
-                          self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+        _lib.build_groups(ids, self.E_total, self.identity_groups, self.E_total,
+                          self.group_offsets, self.pair_to_row, self.row_to_pair, self.scratch,
+                          self.err)
         launches = group_launches(T * self.k)
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
         self._grouped_mlp(hidden, T, self.identity_groups, 0, self.E, bank.w13_slots,
                           bank.w2_slots)
+        self._shared_groups_mlp(hidden, T, self.pinned_rows)
         launches += mlp_launches(T) + 1
         self.kernel_launches += launches
         self.last_full_layer = payload
@@ -485,6 +523,13 @@ class SlotBankMoE:
                 rows[g] = e if zero_copy else pos
                 g += 1
             wave_groups.append((g0, g))
+        g_routed = g
+        if self.num_fused_shared:
+            # fused shared lane: groups E .. E_total-1 (as on every path) on the pinned rows
+            for e in range(self.E, self.E_total):
+                e2g[e] = e
+                rows[e] = int(self.pinned_rows_host[e])
+            g = self.E_total
         self.tables.copy_(self.tables_host, non_blocking=True)
         ids = self.topk_ids[:T]
         _lib.build_groups(ids, self.E_total, self.expert_to_group, g, self.group_offsets,
@@ -496,7 +541,7 @@ class SlotBankMoE:
         report = WaveReport(waves=waves, zero_copy=zero_copy)
         if zero_copy:
             # Every expert already has an HBM copy: read it in place, all waves in one pass.
-            self._grouped_mlp(hidden, T, self.group_bank_row, 0, g, store.w13, store.w2)
+            self._grouped_mlp(hidden, T, self.group_bank_row, 0, g_routed, store.w13, store.w2)
             launches += mlp_launches(T)
         else:
             main = rt.slot_bank(self.layer_id)
@@ -525,6 +570,13 @@ class SlotBankMoE:
                     release = torch.cuda.Event()
                     release.record(compute_stream)
                     rt.remember_prefill_stage_buffer_release(self.layer_id, buf, release)
+        if self.num_fused_shared:
+            # the pinned shared suffix once, after the routed waves (never counted against
+            # the slots, never repeated per wave)
+            bank = rt.slot_bank(self.layer_id)
+            self._grouped_mlp(hidden, T, self.group_bank_row, self.E, self.E_total,
+                              bank.w13_slots, bank.w2_slots)
+            launches += mlp_launches(T)
         dst = self._combine(T, out)
         launches += 1
         report.launches = launches

@@ -92,25 +92,33 @@ def get_layer_by_id(layer_id: int) -> SlotBankMoE:
 def _moe_router(hidden_states, router_logits, top_k, use_grouped_topk, renormalize, topk_group,
                 num_expert_group, scoring_func, routed_scaling_factor, e_score_correction_bias,
                 num_experts, mix_placement=False, num_shared_experts=0):
-    if mix_placement:
-        raise RuntimeError("mix_placement routing (shared experts appended to top-k) is not "
-                           "supported by the B200 seam")
+    # mix_placement: the shared experts' ids num_experts .. num_experts + num_shared - 1 are
+    # appended to every token's top-k with weight 1 (the fused shared lane's pinned suffix)
+    shared = int(num_shared_experts or 0) if mix_placement else 0
+    if mix_placement and shared <= 0:
+        raise RuntimeError("mix_placement routing needs num_shared_experts > 0")
     T = router_logits.shape[0]
-    w = torch.empty(T, top_k, dtype=torch.bfloat16, device=router_logits.device)
-    ids = torch.empty(T, top_k, dtype=torch.int32, device=router_logits.device)
+    width = int(top_k) + shared
+    w = torch.empty(T, width, dtype=torch.bfloat16, device=router_logits.device)
+    ids = torch.empty(T, width, dtype=torch.int32, device=router_logits.device)
     _lib.route_topk(router_logits.float().contiguous(), int(top_k), scoring_func=scoring_func,
                     renormalize=renormalize, routed_scaling_factor=routed_scaling_factor,
                     e_score_correction_bias=e_score_correction_bias,
                     num_expert_group=(num_expert_group or 0) if use_grouped_topk else 0,
                     topk_group=(topk_group or 0) if use_grouped_topk else 0,
-                    weights_bf16=w, ids=ids)
+                    weights_bf16=w, ids=ids, num_shared=shared)
     return w.to(hidden_states.dtype), ids
 
 
-def _moe_router_fake(hidden_states, router_logits, top_k, *args, **kwargs):
+def _moe_router_fake(hidden_states, router_logits, top_k, use_grouped_topk=False,
+                     renormalize=True, topk_group=None, num_expert_group=None,
+                     scoring_func="softmax", routed_scaling_factor=1.0,
+                     e_score_correction_bias=None, num_experts=0, mix_placement=False,
+                     num_shared_experts=0):
     T = hidden_states.shape[0]
-    return (hidden_states.new_empty((T, top_k)),
-            torch.empty((T, top_k), dtype=torch.int32, device=hidden_states.device))
+    width = int(top_k) + (int(num_shared_experts) if mix_placement else 0)
+    return (hidden_states.new_empty((T, width)),
+            torch.empty((T, width), dtype=torch.int32, device=hidden_states.device))
 
 
 def _moe_router_indirect(hidden_states, router_logits, layer_name):
