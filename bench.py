@@ -562,6 +562,56 @@ def run_value(args, cfg, make_layer, hidden, logits, dist, dev, world, local_ran
     return value, ms_step, roofline, int(launches_per_step * args.steps), waves, clocks
 
 
+# --------------------------------------------------------------------------- wave executor
+def run_waves_hbm(args, cfg, w13, w2, dev) -> dict:
+    """The capacity-bounded wave executor on the device: the C2 layer with its store in HBM but
+    staged wave by wave (canonical waves of at most 32 experts, double-buffered stage banks
+    filled device-to-device on the copy stream, one tcgen05 pass per wave, stage-buffer
+    release events, one combine), eager as the seam runs it (one 4*E-byte count read-back per
+    call for the host wave plan). CUDA events around the steps."""
+    import torch
+
+    from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
+    from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
+    from vllm_ascend_hust_latchmoe_b200.synthetic import ExpertLayer
+
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=cfg.num_slots,
+                                            async_load=True, b2_wave_prefill=True,
+                                            graph_compatible_offload=True,
+                                            stage_waves_from_hbm_store=True))
+    rt.register_layer_for_fixed_slots(ExpertLayer(0, w13, w2), slot_device=dev, store_device=dev)
+    layer = SlotBankMoE(rt, 0, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
+                        num_experts=cfg.num_experts, top_k=cfg.top_k, max_tokens=cfg.tokens,
+                        renormalize=cfg.renormalize, device=dev)
+    hidden = syn.make_hidden(cfg, seed=0).to(dev)
+    logits = syn.make_router_logits(cfg, seed=0).to(dev)
+    for _ in range(args.warmup):
+        layer.forward(hidden, logits)
+    torch.cuda.synchronize()
+    layer.check_device_errors("bench waves")
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        layer.forward(hidden, logits)
+    b.record()
+    torch.cuda.synchronize()
+    layer.check_device_errors("bench waves")
+    ms = a.elapsed_time(b) / args.steps
+    rep = layer.last_waves
+    res = {"workload": cfg.name + ", store in HBM, staged wave by wave",
+           "ms_per_step": ms, "tokens_per_s": cfg.tokens / (ms / 1e3),
+           "waves": len(rep.waves), "wave_sizes": [len(w) for w in rep.waves],
+           "staged_bytes_per_step": int(rep.staged_bytes),
+           "d2d_gbs": rep.staged_bytes / (ms / 1e3) / 1e9, "launches_per_step": rep.launches,
+           "timing": f"eager layer calls x{args.steps}, CUDA events"}
+    del layer, rt
+    torch.cuda.empty_cache()
+    return res
+
+
 # --------------------------------------------------------------------------- N > 1 value
 def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     """``value`` at N > 1: the same C2 layer (Qwen3-30B-A3B shape, 4096 tokens per rank: weak
@@ -782,14 +832,15 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=0,
                     help="profiling override of the layer's token count (default: the config's)")
     ap.add_argument("--sections", default="all",
-                    help="comma list of value,decode,c4,tpot,e2e,ep,cpu (profiling runs use one)")
+                    help="comma list of value,decode,c4,tpot,e2e,ep,cpu,waves (profiling runs "
+                         "use one)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         # before numpy / torch load their thread pools (torchrun sets 1 thread per process)
         for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
             os.environ[var] = str(os.cpu_count() or 1)
-    every = {"value", "decode", "c4", "tpot", "e2e", "ep", "cpu"}
+    every = {"value", "decode", "c4", "tpot", "e2e", "ep", "cpu", "waves"}
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     # at N > 1 the single-GPU sections (decode, C4, TPOT) would only repeat BENCH's figures
     default = every if world_env == 1 else {"value", "e2e", "ep"}
@@ -868,6 +919,9 @@ def main() -> None:
     elif "value" in sec:
         value, ms_step, roofline, launches, clocks, e2e_ep, ep_value = run_value_ep(
             args, cfg, dist, dev, rank, world, local_rank, peaks, barrier)
+    waves_hbm = None
+    if "waves" in sec:
+        waves_hbm = run_waves_hbm(args, cfg, w13, w2, dev)
     # ----------------------------------------------------------------- decode layer (C1)
     decode = None
     if "decode" in sec:
@@ -918,6 +972,30 @@ def main() -> None:
         d_mlp_ms = replay_ms(g_mlp)
         del g_layer, g_mlp
         dl.check_device_errors("bench decode")
+        # The same layer on the slot bank: pinned host store, 64 slots (the 16 tokens route to
+        # 33 experts, one more than 32 slots hold), every active expert staged once, then the
+        # router + captured slot-bank MLP piece (log2phy remap, grouping, MLP, combine)
+        # replayed: all hits.
+        srt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=64, async_load=True,
+                                                 b2_wave_prefill=True,
+                                                 graph_compatible_offload=True,
+                                                 pin_host_memory=True))
+        srt.register_layer_for_fixed_slots(ExpertLayer(0, w13, w2), slot_device=dev)
+        sl = SlotBankMoE(srt, 0, hidden_size=dcfg.hidden, intermediate_size=dcfg.intermediate,
+                         num_experts=dcfg.num_experts, top_k=dcfg.top_k, max_tokens=dcfg.tokens,
+                         device=dev)
+        for _ in range(2):
+            sl.forward(dh, dlg)
+        torch.cuda.synchronize()
+        assert sl.stage(sl.topk_ids[:T1]).mode == "slots"
+        g_slots = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_slots):
+            sl.route(dh, dlg)
+            sl.mlp_slots(dh, T1)
+        slot_layer_ms = replay_ms(g_slots)
+        del g_slots
+        sl.check_device_errors("bench decode slots")
+        del sl, srt
         from vllm_ascend_hust_latchmoe_b200.moe_offload.phase_split import plan_balanced_b2_waves
 
         d_counts = torch.bincount(dl.topk_ids[: dcfg.tokens].reshape(-1).long().cpu(),
@@ -935,6 +1013,13 @@ def main() -> None:
                   "mlp_hbm_gbs": d_bytes / (d_mlp_ms / 1e3) / 1e9,
                   "mlp_frac_hbm": d_bytes / (d_mlp_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
                   "algorithmic_bytes_per_call": d_bytes,
+                  "slot_bank": {"layer_ms": slot_layer_ms,
+                                "layer_hbm_frac":
+                                    d_bytes / (slot_layer_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                                "num_slots": 64,
+                                "timing": "router + captured slot-bank MLP piece (log2phy "
+                                          "remap, grouping, MLP, combine), graph replay x50; "
+                                          "every active expert a slot hit"},
                   "kernel": "gemv_persistent_kernel (lm_moe_mlp_decode: gate_up and down in one "
                             "persistent launch)"}
         del dl, drt
@@ -1131,7 +1216,7 @@ def main() -> None:
                    "expert_partition": ep_value,
                    "l2": "weights 1.2 GB per step > 126 MB L2 (no flush needed)"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode, "c4": c4, "tpot": tpot,
-        "expert_parallel": ep_report,
+        "expert_parallel": ep_report, "wave_executor": waves_hbm,
         "clocks": clocks.summary(), "gpu_launches": int(launches),
     }
     print(json.dumps(line), flush=True)

@@ -174,3 +174,31 @@ def test_c5_shape_owner_rows_count(cuda, c5_bank, R, live):
     ref = omlp.moe_layer(bits(rows)[:live], ids_np[:live, None], unit, _ExpertBits(w13),
                          _ExpertBits(w2))
     _check(out[:live], ref)
+
+
+def test_c2_waves_staged_from_hbm_store(cuda, c2_case):
+    """The capacity-bounded wave executor with an HBM-resident store (stage banks filled
+    device-to-device, one GEMM pass per wave on its stage bank, one combine): the canonical
+    waves, each within the 32 slots, and the oracle's output."""
+    from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
+    from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE
+    from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
+
+    cfg, (w13, w2), hidden, logits, ids_ref, ref, waves = c2_case
+    rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=cfg.num_slots,
+                                            async_load=True, b2_wave_prefill=True,
+                                            graph_compatible_offload=True,
+                                            stage_waves_from_hbm_store=True))
+    rt.register_layer_for_fixed_slots(syn.ExpertLayer(0, w13, w2), slot_device=cuda,
+                                      store_device=cuda)
+    layer = SlotBankMoE(rt, 0, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
+                        num_experts=cfg.num_experts, top_k=cfg.top_k, max_tokens=cfg.tokens,
+                        device=cuda)
+    for _ in range(2):
+        out = layer.forward(hidden.to(cuda), logits.to(cuda))
+        torch.cuda.synchronize()
+        layer.check_device_errors("c2 staged waves")
+        assert not layer.last_waves.zero_copy
+        assert [tuple(w) for w in layer.last_waves.waves] == [tuple(w) for w in waves]
+        assert layer.last_waves.staged_bytes == sum(len(w) for w in waves) * cfg.expert_bytes
+        _check(out, ref)

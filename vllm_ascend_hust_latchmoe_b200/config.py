@@ -30,6 +30,10 @@ class MoeOffloadConfig:
     # B200 addition: decode staging decided on the device (lm_slot_plan) and missed experts
     # read over PCIe by the MLP itself; no host round trip per layer.
     device_staging: bool = False
+    # B200 addition: a layer whose expert store is HBM-resident still runs prefill overflow
+    # through the capacity-bounded wave executor (stage banks filled device-to-device on the
+    # copy stream) instead of reading every expert in place in one pass.
+    stage_waves_from_hbm_store: bool = False
     pin_host_memory: bool | None = None
     transfer_aware_wave_schedule: bool = True
     prefill_prefetch_depth: int = 1

@@ -260,7 +260,7 @@ class SlotBankMoE:
             if rt.should_use_fixed_slot_plan_for_layer(self.layer_id) and not rt.is_layer_registered(self.layer_id):
                 raise RuntimeError(f"graph capture reached an unregistered fixed-slot MoE layer {self.layer_id}")
             return StageDecision("capturing")
-        if self.resident_tier:
+        if self.resident_tier and not rt.config.stage_waves_from_hbm_store:
             # Every expert already has an HBM copy: nothing to stage, and the wave plan is
             # made on the device inside the MLP piece (no host round trip).
             return StageDecision("resident")
@@ -510,7 +510,7 @@ class SlotBankMoE:
         cfg = rt.config
         waves = plan.waves
         store = rt.host_layer(self.layer_id)
-        zero_copy = store.on_device
+        zero_copy = store.on_device and not cfg.stage_waves_from_hbm_store
         e2g = self.tables_host[: self.E_total]
         e2g.fill_(-1)
         rows = self.tables_host[self.E_total:]
