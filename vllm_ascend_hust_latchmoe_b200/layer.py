@@ -205,7 +205,7 @@ class SlotBankMoE:
         T = int(router_logits.shape[0])
         self._check_tokens(T)
         logits = router_logits if router_logits.dtype == torch.float32 else router_logits.float()
-        _lib.route_topk(logits.contiguous(), self.k, scoring_func=self.scoring_func,
+        _lib.route_topk(logits.contiguous(), self.k_route, scoring_func=self.scoring_func,
                         renormalize=self.renormalize,
                         routed_scaling_factor=self.routed_scaling_factor,
                         e_score_correction_bias=self.e_bias,
