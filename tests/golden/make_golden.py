@@ -238,6 +238,62 @@ def _autoconfig_cases():
     return out
 
 
+def _residency_cases():
+    """Profiles in the reference's JSONL schema (with malformed lines, other events and bad
+    layer ids mixed in) -> the reference loader's per-layer costs and its placement."""
+    import tempfile
+
+    from vllm_moe_offload_ascend.moe_offload import prefill_residency as pr
+
+    rng = random.Random(4242)
+    out = []
+    for case in range(40):
+        layers = rng.choice([4, 12, 48])
+        offloaded = sorted(rng.sample(range(layers), rng.randint(1, layers - 1)))
+        lines = []
+        for _ in range(rng.randint(0 if case < 2 else 1, 30)):
+            kind = rng.random()
+            lid = rng.randrange(-1, layers + 2)
+            if kind < 0.45:
+                payload = {"n_pairs": rng.randint(0, 32768), "n_waves": rng.randint(1, 6),
+                           "n_active": rng.randint(1, 128),
+                           "control_ms": {"end_to_end": round(rng.uniform(1, 200), 3)}
+                           if rng.random() < 0.8 else {},
+                           "waves": [{"gmm_ms": rng.uniform(0, 9), "stage_wait_ms":
+                                      rng.uniform(0, 3), "h2d_bytes": rng.randint(0, 10**9)}
+                                     for _ in range(rng.randint(0, 3))]}
+                if rng.random() < 0.5:
+                    payload["wave_summary"] = {"gmm_ms": rng.uniform(0, 50),
+                                               "stage_wait_ms": rng.uniform(0, 9),
+                                               "h2d_bytes": rng.randint(0, 10**10)}
+                    payload["control_ms"]["loop"] = rng.uniform(0, 5)
+                rec = {"name": "b2_work_conserving_prefill", "layer_id": lid,
+                       "seconds": rng.uniform(0.001, 0.3), "payload": payload}
+            elif kind < 0.8:
+                rec = {"name": "prefill_resident_native", "layer_id": lid,
+                       "seconds": rng.uniform(0.001, 0.3),
+                       "payload": {"n_tokens": rng.randint(1, 8192)}}
+            elif kind < 0.9:
+                rec = {"name": "decode_step", "layer_id": lid, "seconds": 0.5}
+            else:
+                lines.append("{not json")
+                continue
+            lines.append(json.dumps(rec))
+        with tempfile.NamedTemporaryFile("w", suffix=".jsonl", delete=False) as fh:
+            fh.write("\n".join(lines) + "\n")
+            path = fh.name
+        try:
+            costs = pr.load_prefill_layer_costs(path)
+        finally:
+            os.unlink(path)
+        plan = pr.plan_profile_guided_prefill_residency(
+            num_layers=layers, default_offloaded_layer_ids=tuple(offloaded), layer_costs=costs)
+        out.append({"lines": lines, "num_layers": layers, "default_offloaded": offloaded,
+                    "costs": {str(k): v.to_jsonable() for k, v in sorted(costs.items())},
+                    "placement": plan.to_jsonable()})
+    return out
+
+
 def main() -> None:
     # the reference checkout: first argument, else LATCHMOE_REFERENCE_ROOT
     root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LATCHMOE_REFERENCE_ROOT", "")
@@ -255,6 +311,7 @@ def main() -> None:
         "pair_plans.json": _pair_plans(ps),
         "combine_index.json": _combine_index(ps),
         "autoconfig.json": _autoconfig_cases(),
+        "residency.json": _residency_cases(),
     }
     for name, data in blobs.items():
         (HERE / name).write_text(json.dumps(data, separators=(",", ":")) + "\n")

@@ -23,16 +23,16 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 def build_layer(cfg: syn.LayerConfig, *, seed: int = 0, max_tokens: int | None = None,
                 device="cuda", store_on_device: bool = False, num_slots: int | None = None,
-                experts=None, reference_full_layer: bool = False):
+                experts=None, reference_full_layer: bool = False, layer_id: int = 0):
     w13, w2 = syn.make_expert_weights(cfg, seed) if experts is None else experts
     runtime = MoeOffloadRuntime(MoeOffloadConfig(
         enabled=True, num_slots=int(num_slots or cfg.num_slots), async_load=True,
         b2_wave_prefill=True, graph_compatible_offload=True,
         b2_reference_full_layer=reference_full_layer))
     runtime.register_layer_for_fixed_slots(
-        ExpertLayer(0, w13, w2), slot_device=torch.device(device),
+        ExpertLayer(layer_id, w13, w2), slot_device=torch.device(device),
         store_device=torch.device(device) if store_on_device else None)
-    layer = SlotBankMoE(runtime, 0, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
+    layer = SlotBankMoE(runtime, layer_id, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
                         num_experts=cfg.num_experts, top_k=cfg.top_k,
                         max_tokens=int(max_tokens or cfg.tokens), renormalize=cfg.renormalize,
                         routed_scaling_factor=cfg.routed_scaling_factor,

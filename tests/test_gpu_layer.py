@@ -193,3 +193,29 @@ def test_overflow_at_a_captured_size_fails_closed(cuda):
     assert len(layer.last_waves.waves) >= 2
     _check(out, ref)
     del g
+
+
+def test_prefill_profile_drives_residency(cuda, tmp_path):
+    """Prefill calls of an offloaded layer (staged waves) and of a resident layer are recorded
+    as profile records (CUDA events, read back on flush); the planner then makes the costlier
+    offloaded layer resident in exchange for the cheaper resident one."""
+    from vllm_ascend_hust_latchmoe_b200.moe_offload import prefill_residency as pr
+
+    cfg = syn.CONFIGS["c2_prefill"].with_tokens(512)
+    path = tmp_path / "prefill.jsonl"
+    hidden = syn.make_hidden(cfg).to(cuda)
+    logits = syn.make_router_logits(cfg).to(cuda)
+    for lid, on_dev in ((1, False), (0, True)):
+        layer, rt, _ = build_layer(cfg, store_on_device=on_dev, layer_id=lid)
+        rt.prefill_profiler = pr.PrefillProfileRecorder(str(path))
+        for _ in range(2):
+            layer.forward(hidden, logits)
+        torch.cuda.synchronize()
+        layer.check_device_errors()
+        assert rt.prefill_profiler.flush() == 2
+    costs = pr.load_prefill_layer_costs(path)
+    assert costs[1].b2_calls == 2 and costs[1].waves >= 8 and costs[1].h2d_bytes > 0
+    assert costs[0].resident_native_calls == 2
+    plan = pr.plan_profile_guided_prefill_residency(num_layers=2, default_offloaded_layer_ids=(1,),
+                                                    layer_costs=costs)
+    assert plan.reason == "profile_guided_swaps" and plan.offloaded_layer_ids == (0,)

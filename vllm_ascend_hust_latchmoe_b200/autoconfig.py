@@ -247,6 +247,43 @@ def check_layered_release_conflict(env: dict | None = None) -> None:
             "VLLM_ASCEND_MOE_OFFLOAD_LAYERED_RUNTIME=0 for the pure fixed-slot path.")
 
 
+PREFILL_RESIDENCY_PROFILE_ENV = "VLLM_ASCEND_MOE_OFFLOAD_PREFILL_RESIDENCY_PROFILE"
+
+
+def apply_profile_guided_residency(defaults: dict[str, Any], *, profile_path: str | None,
+                                   model_config: dict[str, Any] | None = None) -> dict[str, Any]:
+    """Refine the default resident / offloaded layer split with prefill profiles
+    (``os.pathsep``-separated JSONL paths; reference ``moe_offload/autoconfig.py:585-640``).
+    The swap keeps the number of offloaded layers, so the offload budget is unchanged. Without
+    profile evidence the defaults are returned as they are."""
+    if not profile_path:
+        return defaults
+    from .moe_offload.prefill_residency import (load_prefill_layer_costs_many,
+                                                plan_profile_guided_prefill_residency)
+
+    paths = tuple(p.strip() for p in str(profile_path).split(os.pathsep) if p.strip())
+    if not paths:
+        return defaults
+    cfg = model_config or QWEN3_30B_A3B
+    plan = plan_profile_guided_prefill_residency(
+        num_layers=_get(cfg, "num_hidden_layers"),
+        default_offloaded_layer_ids=tuple(defaults["offloaded_layer_ids"]),
+        layer_costs=load_prefill_layer_costs_many(paths))
+    if not plan.profiled_layer_ids:
+        return defaults
+    out = dict(defaults)
+    out.update({
+        "resident_layer_ids": plan.resident_layer_ids,
+        "offloaded_layer_ids": plan.offloaded_layer_ids,
+        "estimated_offloaded_layers": len(plan.offloaded_layer_ids),
+        "estimated_offloaded_gb": len(plan.offloaded_layer_ids) * float(defaults["expert_layer_gb"]),
+        "prefill_residency_profile": os.pathsep.join(paths),
+        "prefill_residency_profiles": paths,
+        "prefill_residency_plan": plan.to_jsonable(),
+    })
+    return out
+
+
 def apply_moe_offload_defaults(target_offload_gb: float, model_config: dict[str, Any] | None = None,
                                *, env: dict | None = None, max_num_seqs: int = 1,
                                max_model_len: int | None = None,
@@ -262,6 +299,8 @@ def apply_moe_offload_defaults(target_offload_gb: float, model_config: dict[str,
         for name, value in SEW_DATAPLANE_ENV_VARS.items():
             env.setdefault(name, value)
     pre = derive_prefetch_defaults(target_offload_gb, model_config)
+    pre = apply_profile_guided_residency(pre, profile_path=env.get(PREFILL_RESIDENCY_PROFILE_ENV),
+                                         model_config=model_config)
     slots = derive_num_slots_defaults(target_offload_gb, model_config, pre,
                                       max_num_seqs=max_num_seqs, max_model_len=max_model_len)
     if not env.get("VLLM_ASCEND_MOE_OFFLOAD_NUM_SLOTS"):

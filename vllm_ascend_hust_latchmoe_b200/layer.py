@@ -646,7 +646,19 @@ class SlotBankMoE:
         if hidden.dtype != torch.bfloat16 or not hidden.is_contiguous():
             raise ValueError("hidden_states must be a contiguous bf16 tensor")
         _, ids = self.route(hidden, router_logits)
-        return self.run_mlp(hidden, self.stage(ids, phase))
+        prof = self.runtime.prefill_profiler
+        if prof is None or T <= DECODE_MAX_TOKENS:
+            return self.run_mlp(hidden, self.stage(ids, phase))
+        # prefill call recorded for profile-guided residency (events only; no sync here)
+        start = prof.begin()
+        decision = self.stage(ids, phase)
+        out = self.run_mlp(hidden, decision)
+        resident = decision.mode == "resident"
+        prof.end(start, layer_id=self.layer_id, resident=resident, tokens=T, pairs=T * self.k,
+                 waves=0 if resident else len(self.last_waves.waves),
+                 active=len(decision.active_experts),
+                 h2d_bytes=0 if resident else int(self.last_waves.staged_bytes))
+        return out
 
     def check_device_errors(self, where: str = "SlotBankMoE") -> None:
         _lib.raise_on_device_error(self.err, f"{where} layer {self.layer_id}")

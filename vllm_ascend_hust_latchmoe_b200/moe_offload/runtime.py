@@ -117,6 +117,13 @@ class MoeOffloadRuntime:
         self._capturing = False
         self._released_original_weight_layers: set[int] = set()
         self.stage_stats = {"calls": 0, "hits": 0, "misses": 0, "h2d_bytes": 0, "log2phy_updates": 0}
+        # Prefill layer calls are recorded (CUDA events, read back on flush) into the profile
+        # JSONL that profile-guided residency reads, when a profile path is configured.
+        self.prefill_profiler = None
+        if self.config.profile_path:
+            from .prefill_residency import PrefillProfileRecorder
+
+            self.prefill_profiler = PrefillProfileRecorder(str(self.config.profile_path))
 
     # ------------------------------------------------------------------ registration
     @property
