@@ -1069,7 +1069,51 @@ def main() -> None:
         c_active = int((torch.bincount(cl.topk_ids[:Tc].reshape(-1).long(),
                                        minlength=ccfg.num_experts) > 0).sum())
         c_bytes = c_active * ccfg.expert_bytes + ccfg.num_shared * ccfg.expert_bytes
+        ext_out = (cl.out[:Tc].float() + shared_out.float()).to(torch.bfloat16)
+        # The same layer through the fused mix-placement lane: the 2 shared experts become
+        # logical experts 64, 65 (each one I=1408 slice of the fused shared MLP), held in the
+        # HBM store beside the routed ones, appended to every token's top-k by the router and
+        # run in the same grouped-MLP launch; one combine.
+        Is = ccfg.intermediate
+        sh13 = torch.stack([torch.cat([sw13[s * Is:(s + 1) * Is], sw13[2 * Is + s * Is:
+                                                                       2 * Is + (s + 1) * Is]])
+                            for s in range(ccfg.num_shared)])
+        sh2 = torch.stack([sw2[:, s * Is:(s + 1) * Is] for s in range(ccfg.num_shared)])
+        frt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=ccfg.num_slots,
+                                                 async_load=True, b2_wave_prefill=True))
+        frt.register_layer_for_fixed_slots(
+            ExpertLayer(0, torch.cat([cw13, sh13]), torch.cat([cw2, sh2]), shared=ccfg.num_shared),
+            slot_device=dev, store_device=dev)
+        fl = SlotBankMoE(frt, 0, hidden_size=ccfg.hidden, intermediate_size=Is,
+                         num_experts=ccfg.num_experts, top_k=ccfg.top_k, max_tokens=Tc,
+                         renormalize=ccfg.renormalize,
+                         routed_scaling_factor=ccfg.routed_scaling_factor,
+                         scoring_func=ccfg.scoring_func, num_expert_group=ccfg.num_expert_group,
+                         topk_group=ccfg.topk_group, device=dev)
+        for _ in range(args.warmup):
+            fl.forward(ch, clg)
+        torch.cuda.synchronize()
+        g_f = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_f):
+            fl.route(ch, clg)
+            fl.mlp_resident(ch, Tc)
+        for _ in range(3):
+            g_f.replay()
+        a4.record()
+        for _ in range(50):
+            g_f.replay()
+        b4.record()
+        torch.cuda.synchronize()
+        fused_ms = a4.elapsed_time(b4) / 50
+        fl.check_device_errors("bench c4 fused lane")
+        fused_vs_external = compare_outputs(fl.out[:Tc], ext_out)
+        del g_f, fl, frt
         c4 = {"workload": ccfg.name + " + 2 resident shared experts", "layer_ms": c4_ms,
+              "fused_lane": {"layer_ms": fused_ms,
+                             "frac_hbm": c_bytes / (fused_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+                             "lane": "mix placement: shared experts as groups 64, 65 of the "
+                                     "same grouped-MLP launch (HBM store), one combine",
+                             "vs_external_lane": fused_vs_external},
               "timing": "CUDA-graph replay x50: route, grouping, routed MLP (experts read in "
                         "place), combine, shared-expert MLP",
               "active_experts": c_active, "algorithmic_bytes_per_call": c_bytes,

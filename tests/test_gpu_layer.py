@@ -214,7 +214,7 @@ def test_prefill_profile_drives_residency(cuda, tmp_path):
         layer.check_device_errors()
         assert rt.prefill_profiler.flush() == 2
     costs = pr.load_prefill_layer_costs(path)
-    assert costs[1].b2_calls == 2 and costs[1].waves >= 8 and costs[1].h2d_bytes > 0
+    assert costs[1].b2_calls == 2 and costs[1].waves >= 4 and costs[1].h2d_bytes > 0
     assert costs[0].resident_native_calls == 2
     plan = pr.plan_profile_guided_prefill_residency(num_layers=2, default_offloaded_layer_ids=(1,),
                                                     layer_costs=costs)

@@ -164,8 +164,17 @@ class SlotBankMoE:
         # Shared experts are groups E .. E_total-1 on every path, reading the bank's pinned
         # rows; the device wave plan only writes the first E entries of these tables.
         self.pinned_rows = torch.zeros(self.E_total, dtype=i32, device=d)
+        store = runtime.host_layer(self.layer_id)
+        # An HBM store that holds the shared rows serves them in place (row = logical id),
+        # in the same launch as the routed groups; otherwise they come from the bank's
+        # pinned suffix.
+        self.shared_in_store = bool(self.num_fused_shared) and store.on_device and \
+            int(store.w13.shape[0]) >= self.E_total
         if self.num_fused_shared:
-            pinned = [bank.pinned_slot_for_logical_id(e) for e in range(self.E, self.E_total)]
+            if self.shared_in_store:
+                pinned = list(range(self.E, self.E_total))
+            else:
+                pinned = [bank.pinned_slot_for_logical_id(e) for e in range(self.E, self.E_total)]
             if any(r is None for r in pinned):
                 raise RuntimeError(f"layer {self.layer_id}: shared experts lack pinned slots")
             self.pinned_rows[self.E:] = torch.tensor(pinned, dtype=i32)
@@ -365,8 +374,10 @@ class SlotBankMoE:
             _lib.build_groups(ids, self.E_total, self.identity_groups, self.E_total,
                               self.group_offsets, self.pair_to_row, self.row_to_pair,
                               self.scratch, self.err)
-            self._grouped_mlp(hidden, T, self.identity_groups, 0, self.E, store.w13, store.w2)
-            self._shared_groups_mlp(hidden, T, self.pinned_rows)
+            g_end = self.E_total if self.shared_in_store else self.E
+            self._grouped_mlp(hidden, T, self.identity_groups, 0, g_end, store.w13, store.w2)
+            if not self.shared_in_store:
+                self._shared_groups_mlp(hidden, T, self.pinned_rows)
             self.kernel_launches += group_launches(T * self.k) + mlp_launches(T) + 1
             return self._combine(T, out)
         self.resident_planned = True
@@ -381,8 +392,10 @@ class SlotBankMoE:
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
-        self._grouped_mlp(hidden, T, self.group_bank_row, 0, self.E, store.w13, store.w2)
-        self._shared_groups_mlp(hidden, T, self.group_bank_row)
+        g_end = self.E_total if self.shared_in_store else self.E
+        self._grouped_mlp(hidden, T, self.group_bank_row, 0, g_end, store.w13, store.w2)
+        if not self.shared_in_store:
+            self._shared_groups_mlp(hidden, T, self.group_bank_row)
         self.kernel_launches += launches + mlp_launches(T) + 1
         return self._combine(T, out)
 
@@ -392,10 +405,17 @@ class SlotBankMoE:
         single combine then sums routed and shared pairs in top-k order)."""
         if not self.num_fused_shared:
             return
-        bank = self.runtime.slot_bank(self.layer_id)
-        self._grouped_mlp(hidden, T, bank_rows_dev, self.E, self.E_total, bank.w13_slots,
-                          bank.w2_slots)
+        w13, w2 = self._shared_weights()
+        self._grouped_mlp(hidden, T, bank_rows_dev, self.E, self.E_total, w13, w2)
         self.kernel_launches += mlp_launches(T)
+
+    def _shared_weights(self):
+        """The tensors the shared groups' rows index: the HBM store, or the slot bank."""
+        if self.shared_in_store:
+            store = self.runtime.host_layer(self.layer_id)
+            return store.w13, store.w2
+        bank = self.runtime.slot_bank(self.layer_id)
+        return bank.w13_slots, bank.w2_slots
 
     def mlp_rows_count(self, rows: torch.Tensor, ids: torch.Tensor, count_dev: torch.Tensor,
                        out: torch.Tensor) -> torch.Tensor:
@@ -573,9 +593,8 @@ class SlotBankMoE:
         if self.num_fused_shared:
             # the pinned shared suffix once, after the routed waves (never counted against
             # the slots, never repeated per wave)
-            bank = rt.slot_bank(self.layer_id)
-            self._grouped_mlp(hidden, T, self.group_bank_row, self.E, self.E_total,
-                              bank.w13_slots, bank.w2_slots)
+            sw13, sw2 = self._shared_weights()
+            self._grouped_mlp(hidden, T, self.group_bank_row, self.E, self.E_total, sw13, sw2)
             launches += mlp_launches(T)
         dst = self._combine(T, out)
         launches += 1

@@ -182,10 +182,14 @@ class MoeOffloadRuntime:
                     f"of 128 and H and I multiples of 64; got {tuple(w13.shape)}, {tuple(w2.shape)}")
             w13t, w2t = w13.detach(), w2.detach()
         self._tiled_layout[layer_id] = bool(tiled13 and tiled2)
+        # A host store holds the routed rows only (the shared suffix lives in the bank). An HBM
+        # store also keeps the shared rows, so a resident layer reads routed and shared experts
+        # in place in one grouped-MLP launch.
+        on_hbm = store_device is not None and torch.device(store_device).type == "cuda"
         self._host_store.register_layer(
             SimpleNamespace(layer_id=layer_id, w13_weight=w13t, w2_weight=w2t),
             pin_memory=self.config.should_pin_host_memory or torch.cuda.is_available(),
-            routed_expert_count=routed, device=store_device)
+            routed_expert_count=total if on_hbm else routed, device=store_device)
         w13, w2 = w13t, w2t
         pinned = tuple(range(routed, total))
         bank = ExpertSlotBank(self.config.num_slots, tuple(w13.shape[1:]), tuple(w2.shape[1:]),
