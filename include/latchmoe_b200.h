@@ -235,6 +235,12 @@ int lm_build_groups_count(const int32_t* topk_ids, int64_t max_pairs,
 int lm_permute_rows_count(const uint16_t* hidden, int32_t hidden_size,
                           const int32_t* row_to_pair, int32_t top_k, int64_t max_rows,
                           const int32_t* num_rows_dev, uint16_t* x_perm, void* stream);
+/* Row gather through a second index, for rows another GPU wrote this call (read at L2):
+ * x_perm[r, :] = src[pair_src[row_to_pair[r]], :] for r < min(max_rows, *num_rows_dev). */
+int lm_permute_rows_gather_count(const uint16_t* src, int32_t hidden_size,
+                                 const int32_t* row_to_pair, const int32_t* pair_src,
+                                 int64_t max_rows, const int32_t* num_rows_dev, uint16_t* x_perm,
+                                 void* stream);
 int lm_moe_combine_count(const uint16_t* y_perm, const int32_t* pair_to_row,
                          const uint16_t* topk_weights_bf16, int64_t max_tokens,
                          const int32_t* num_tokens_dev, int32_t top_k, int32_t hidden_size,
@@ -313,9 +319,15 @@ int lm_moe_mlp_decode_offload(const uint16_t* hidden, int32_t top_k,
  *   lm_ep_receive       waits for every source's dispatch (bounded), compacts the received rows
  *                       and ids into rows_out / ids_out; *total_out = their number (device).
  *   (local expert MLP, outputs written in received order at region + lm_ep_out_rows_offset)
+ *   (or lm_ep_receive_index: the same wait, then only the received pairs' receive-area slots
+ *    and ids in received order; the owner gathers its rows from the receive area itself,
+ *    region + lm_ep_recv_rows_offset, with lm_permute_rows_gather_count, and writes the output
+ *    row of received pair d to the int32 table at region + lm_ep_pair_rows_offset)
  *   lm_ep_signal_outputs  tells every source the outputs are there.
  *   lm_ep_combine       waits for every owner (bounded), reads each pair's output row from its
- *                       owner and reduces out[t] = sum_j w[t,j] * y[t,j] in fp32, j in order.
+ *                       owner (row = the owner's pair-row table entry; lm_ep_receive writes
+ *                       received order there) and reduces out[t] = sum_j w[t,j] * y[t,j] in
+ *                       fp32, j in order.
  * done_counter: one device int32, zero before the first call. Waits that run out set
  * LM_DEVERR_WAIT_TIMEOUT; after a timed-out output wait lm_ep_combine reads nothing from the
  * owners and writes zero rows. num_tokens * top_k > cap is rejected with
@@ -341,6 +353,11 @@ int lm_ep_dispatch(const uint16_t* hidden, int64_t num_tokens, int32_t top_k,
 int lm_ep_receive(void* region, int32_t world, int32_t cap, int32_t hidden_size, int64_t epoch,
                   uint16_t* rows_out, int32_t* ids_out, int32_t* total_out, int32_t* err_word,
                   void* stream);
+int lm_ep_receive_index(void* region, int32_t world, int32_t cap, int32_t hidden_size,
+                        int64_t epoch, int32_t* slot_out, int32_t* ids_out, int32_t* total_out,
+                        int32_t* err_word, void* stream);
+int64_t lm_ep_recv_rows_offset(int32_t world, int32_t cap, int32_t hidden_size);
+int64_t lm_ep_pair_rows_offset(int32_t world, int32_t cap, int32_t hidden_size);
 int lm_ep_signal_outputs(void* const* peer_regions, int32_t rank, int32_t world, int32_t cap,
                          int32_t hidden_size, int64_t epoch, void* stream);
 int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,

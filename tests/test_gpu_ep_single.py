@@ -80,3 +80,63 @@ def test_single_rank_exchange_round_trip_and_timeout(cuda):
         torch.cuda.synchronize()
         c["out_rows"] = None
         _lib.ep_region_free(c["region"])
+
+
+def test_single_rank_gather_path_matches_oracle(cuda):
+    """The owner path without row copies: index-only receive, the grouped MLP gathering its
+    rows from the receive area, outputs left in grouped order with the pair-row table, and the
+    combine reading through that table -- against the oracle layer, twice in a row."""
+    from oracle import router as orouter
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+    from vllm_ascend_hust_latchmoe_b200.expert_parallel import build_rank_layer
+
+    T2, K2, E2, H2, I2 = 32, 4, 8, 256, 128
+    cap = T2 * K2
+    cfg = syn.LayerConfig("g", hidden=H2, num_experts=E2, top_k=K2, intermediate=I2,
+                          num_slots=E2, tokens=T2)
+    w13, w2 = syn.make_expert_weights(cfg, seed=9)
+    layer = build_rank_layer(w13_owned=w13.to(cuda), w2_owned=w2.to(cuda), rank=0, device=cuda,
+                             max_rows=cap, num_slots=E2, store_on_device=True)
+    region = _lib.ep_region_alloc(_lib.ep_region_bytes(1, cap, H2))
+    try:
+        peers = torch.tensor([region], dtype=torch.int64, device=cuda)
+
+        def view(off, shape, ts):
+            return torch.as_tensor(_DevicePtrArray(region + off, shape, ts), device=cuda)
+
+        recv_rows = view(_lib.ep_recv_rows_offset(1, cap, H2), (cap, H2), "<i2").view(torch.bfloat16)
+        out_rows = view(_lib.ep_out_rows_offset(1, cap, H2), (cap, H2), "<i2").view(torch.bfloat16)
+        pair_rows = view(_lib.ep_pair_rows_offset(1, cap, H2), (cap,), "<i4")
+        slots = torch.empty(cap, dtype=torch.int32, device=cuda)
+        rids = torch.empty(cap, dtype=torch.int32, device=cuda)
+        total = torch.zeros(1, dtype=torch.int32, device=cuda)
+        done = torch.zeros(1, dtype=torch.int32, device=cuda)
+        err = torch.zeros(1, dtype=torch.int32, device=cuda)
+        owner = torch.zeros(E2, dtype=torch.int32, device=cuda)
+        offsets = torch.empty(2, dtype=torch.int32, device=cuda)
+        p2r = torch.empty(cap, dtype=torch.int32, device=cuda)
+        r2p = torch.empty(cap, dtype=torch.int32, device=cuda)
+        scratch = torch.empty(_lib.build_groups_scratch_elems(cap, 1), dtype=torch.int32,
+                              device=cuda)
+        out = torch.empty(T2, H2, dtype=torch.bfloat16, device=cuda)
+        for epoch, seed in ((1, 1), (2, 2)):
+            hidden = syn.make_hidden(cfg, seed=seed)
+            wb, _, ids_np = orouter.route(syn.make_router_logits(cfg, seed=seed).numpy(), K2)
+            ids = torch.from_numpy(ids_np).to(cuda)
+            w = torch.from_numpy(wb.view(np.int16)).view(torch.bfloat16).to(cuda)
+            h = hidden.to(cuda)
+            _lib.build_groups(ids, E2, owner, 1, offsets, p2r, r2p, scratch, err)
+            _lib.ep_dispatch(h, ids, E2, p2r, offsets, 0, 1, peers, cap, epoch, done, err)
+            _lib.ep_receive_index(region, 1, cap, H2, epoch, slots, rids, total, err)
+            layer.mlp_rows_gather_count(recv_rows, slots, rids, total, pair_rows, out_rows)
+            _lib.ep_signal_outputs(peers, 0, 1, cap, H2, epoch)
+            _lib.ep_combine(ids, w, E2, p2r, offsets, 0, 1, peers, region, cap, epoch, out, err)
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0 and int(total.item()) == cap
+            layer.check_device_errors("gather path")
+            ref = omlp.moe_layer(bits(hidden), ids_np, wb, bits(w13), bits(w2))
+            m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)
+            assert m["max_rel_err"] <= MAX_REL_ERR and m["cosine"] >= MIN_COSINE, m
+    finally:
+        torch.cuda.synchronize()
+        _lib.ep_region_free(region)

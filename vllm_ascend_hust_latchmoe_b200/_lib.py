@@ -60,6 +60,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "lm_ep_receive": (ctypes.c_int, [_P, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P]),
     "lm_ep_signal_outputs": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _I64, _P]),
+    "lm_ep_receive_index": (ctypes.c_int, [_P, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P]),
+    "lm_ep_recv_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
+    "lm_ep_pair_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
+    "lm_permute_rows_gather_count": (ctypes.c_int, [_P, _I32, _P, _P, _I64, _P, _P, _P]),
     "lm_ep_combine": (
         ctypes.c_int,
         [_P, _P, _I64, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _P, _I32, _I64, _P, _P, _P],
@@ -397,6 +401,29 @@ def ep_receive(region: int, world, cap, hidden_size, epoch, rows_out, ids_out, t
     _check("lm_ep_receive", lib().lm_ep_receive(
         region, int(world), int(cap), int(hidden_size), int(epoch), _ptr(rows_out),
         _ptr(ids_out), _ptr(total_out), _ptr(err_word), _stream()))
+
+
+def ep_receive_index(region: int, world, cap, hidden_size, epoch, slot_out, ids_out, total_out,
+                     err_word=None) -> None:
+    _check("lm_ep_receive_index", lib().lm_ep_receive_index(
+        region, int(world), int(cap), int(hidden_size), int(epoch), _ptr(slot_out),
+        _ptr(ids_out), _ptr(total_out), _ptr(err_word), _stream()))
+
+
+def ep_recv_rows_offset(world, cap, hidden_size) -> int:
+    return int(lib().lm_ep_recv_rows_offset(int(world), int(cap), int(hidden_size)))
+
+
+def ep_pair_rows_offset(world, cap, hidden_size) -> int:
+    return int(lib().lm_ep_pair_rows_offset(int(world), int(cap), int(hidden_size)))
+
+
+def permute_rows_gather_count(src, row_to_pair, pair_src, max_rows, count_dev, x_perm) -> None:
+    """x_perm[r] = src[pair_src[row_to_pair[r]]] for r < *count_dev (rows read at L2)."""
+    _require_cuda(src, row_to_pair, pair_src, count_dev, x_perm)
+    _check("lm_permute_rows_gather_count", lib().lm_permute_rows_gather_count(
+        _ptr(src), src.shape[-1], _ptr(row_to_pair), _ptr(pair_src), int(max_rows),
+        _ptr(count_dev), _ptr(x_perm), _stream()))
 
 
 def ep_signal_outputs(peer_regions, rank, world, cap, hidden_size, epoch) -> None:

@@ -27,9 +27,9 @@
 namespace lm {
 namespace {
 
-constexpr int kLayoutFields = 9;
+constexpr int kLayoutFields = 10;
 enum : int { F_FLAG_DISPATCH = 0, F_FLAG_OUT, F_COUNTS, F_PREFIX, F_WAIT_STATUS, F_RECV_IDS,
-             F_RECV_ROWS, F_OUT_ROWS, F_TOTAL };
+             F_PAIR_ROW, F_RECV_ROWS, F_OUT_ROWS, F_TOTAL };
 
 int64_t align256(int64_t v) { return (v + 255) & ~static_cast<int64_t>(255); }
 
@@ -46,6 +46,8 @@ void layout(int G, int cap, int H, int64_t* off) {
   off[F_WAIT_STATUS] = o;  // this rank's last output wait: 0 every owner answered, 1 timed out
   o = align256(o + 4);
   off[F_RECV_IDS] = o;
+  o = align256(o + 4ll * G * cap);
+  off[F_PAIR_ROW] = o;  // owner: output row of its received pair d (read by the sources)
   o = align256(o + 4ll * G * cap);
   off[F_RECV_ROWS] = o;
   o = align256(o + 2ll * G * cap * H);
@@ -171,6 +173,7 @@ __global__ void __launch_bounds__(256)
   const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
   const int32_t* recv_ids = field<int32_t>(region, L, F_RECV_IDS);
   const uint16_t* recv_rows = field<uint16_t>(region, L, F_RECV_ROWS);
+  int32_t* pair_row = field<int32_t>(region, L, F_PAIR_ROW);
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t q = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -179,10 +182,30 @@ __global__ void __launch_bounds__(256)
     const int n = prefix[s + 1] - prefix[s];
     if (i >= n) continue;
     const int64_t d = prefix[s] + i;
-    if (lane == 0) ids_out[d] = __ldcg(recv_ids + q);
+    if (lane == 0) {
+      ids_out[d] = __ldcg(recv_ids + q);
+      pair_row[d] = static_cast<int32_t>(d);  // outputs land in received order
+    }
     const uint4* src = reinterpret_cast<const uint4*>(recv_rows + q * H);
     uint4* dst = reinterpret_cast<uint4*>(rows_out + d * H);
     for (int c = lane; c < H / 8; c += 32) dst[c] = __ldcg(src + c);
+  }
+}
+
+// Index-only compaction: the received pairs' receive-area slots and owner-local ids in
+// received order (no row copy; the owner's grouped MLP gathers its rows from the slots).
+__global__ void __launch_bounds__(256)
+    ep_index_kernel(void* region, Layout L, int G, int cap, int32_t* __restrict__ slot_out,
+                    int32_t* __restrict__ ids_out) {
+  const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
+  const int32_t* recv_ids = field<int32_t>(region, L, F_RECV_IDS);
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       q < static_cast<int64_t>(G) * cap; q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(q / cap), i = static_cast<int>(q - static_cast<int64_t>(s) * cap);
+    if (i >= prefix[s + 1] - prefix[s]) continue;
+    const int64_t d = prefix[s] + i;
+    slot_out[d] = static_cast<int32_t>(q);
+    ids_out[d] = __ldcg(recv_ids + q);
   }
 }
 
@@ -229,7 +252,8 @@ __global__ void ep_combine_kernel(const int32_t* __restrict__ ids,
         record_error(err_word, LM_DEVERR_BAD_GROUP);
       } else {
         const int32_t* prefix = field<int32_t>(peers[o], L, F_PREFIX);
-        const int64_t row = __ldcg(prefix + rank) + pos;
+        const int32_t* prow = field<int32_t>(peers[o], L, F_PAIR_ROW);
+        const int64_t row = __ldcg(prow + __ldcg(prefix + rank) + pos);
         src = field<uint16_t>(peers[o], L, F_OUT_ROWS) + row * H;
       }
     }
@@ -385,6 +409,41 @@ extern "C" int lm_ep_receive(void* region, int32_t world, int32_t cap, int32_t h
   ep_compact_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(region, L, world, cap,
                                                                  hidden_size, rows_out, ids_out);
   return launch_status("lm_ep_receive: compact");
+}
+
+extern "C" int lm_ep_receive_index(void* region, int32_t world, int32_t cap,
+                                   int32_t hidden_size, int64_t epoch, int32_t* slot_out,
+                                   int32_t* ids_out, int32_t* total_out, int32_t* err_word,
+                                   void* stream) {
+  int rc = check_ep("lm_ep_receive_index", world, cap, hidden_size);
+  if (rc) return rc;
+  if (region == nullptr || slot_out == nullptr || ids_out == nullptr || total_out == nullptr ||
+      epoch <= 0)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_receive_index: bad arguments");
+  const Layout L = make_layout(world, cap, hidden_size);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ep_receive_wait_kernel<<<1, 32, 0, s>>>(region, L, world, cap, epoch, total_out, err_word);
+  rc = launch_status("lm_ep_receive_index: wait");
+  if (rc) return rc;
+  int64_t blocks = (static_cast<int64_t>(world) * cap + 255) / 256;
+  if (blocks > 1184) blocks = 1184;
+  ep_index_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(region, L, world, cap,
+                                                                slot_out, ids_out);
+  return launch_status("lm_ep_receive_index: index");
+}
+
+extern "C" int64_t lm_ep_recv_rows_offset(int32_t world, int32_t cap, int32_t hidden_size) {
+  if (world <= 0 || cap <= 0 || hidden_size <= 0) return -1;
+  int64_t off[kLayoutFields];
+  layout(world, cap, hidden_size, off);
+  return off[F_RECV_ROWS];
+}
+
+extern "C" int64_t lm_ep_pair_rows_offset(int32_t world, int32_t cap, int32_t hidden_size) {
+  if (world <= 0 || cap <= 0 || hidden_size <= 0) return -1;
+  int64_t off[kLayoutFields];
+  layout(world, cap, hidden_size, off);
+  return off[F_PAIR_ROW];
 }
 
 extern "C" int64_t lm_ep_out_rows_offset(int32_t world, int32_t cap, int32_t hidden_size) {

@@ -496,6 +496,25 @@ __global__ void __launch_bounds__(kGroupTile)
                  pair_to_row, row_to_pair, err_word, sm);
 }
 
+// Row gather through a second index: x_perm[r] = src[pair_src[row_to_pair[r]]], the source
+// rows read at L2 (another GPU may have written them for this call; no stale L1 lines).
+__global__ void permute_rows_gather_kernel(const uint16_t* __restrict__ src, int hidden_size,
+                                           const int32_t* __restrict__ row_to_pair,
+                                           const int32_t* __restrict__ pair_src,
+                                           int64_t num_rows, uint16_t* __restrict__ x_perm,
+                                           const int32_t* __restrict__ count) {
+  pdl_wait();
+  pdl_trigger();
+  num_rows = live_count(num_rows, count);
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= num_rows) return;
+  const int64_t row = pair_src[row_to_pair[r]];
+  const uint4* in = reinterpret_cast<const uint4*>(src + row * hidden_size);
+  uint4* dst = reinterpret_cast<uint4*>(x_perm + r * hidden_size);
+  for (int c = lane; c < hidden_size / 8; c += 32) dst[c] = __ldcg(in + c);
+}
+
 __global__ void permute_rows_kernel(const uint16_t* __restrict__ hidden, int hidden_size,
                                     const int32_t* __restrict__ row_to_pair, int top_k,
                                     int64_t num_rows, uint16_t* __restrict__ x_perm,
@@ -877,6 +896,26 @@ extern "C" int lm_permute_rows(const uint16_t* hidden, int32_t hidden_size,
       static_cast<const int32_t*>(nullptr));
   if (e != cudaSuccess) return check_cuda(e, "lm_permute_rows");
   return launch_status("lm_permute_rows");
+}
+
+extern "C" int lm_permute_rows_gather_count(const uint16_t* src, int32_t hidden_size,
+                                            const int32_t* row_to_pair, const int32_t* pair_src,
+                                            int64_t max_rows, const int32_t* num_rows_dev,
+                                            uint16_t* x_perm, void* stream) {
+  if (hidden_size <= 0 || hidden_size % 8 != 0 || max_rows < 0 || num_rows_dev == nullptr ||
+      (max_rows > 0 && (src == nullptr || row_to_pair == nullptr || pair_src == nullptr ||
+                        x_perm == nullptr)))
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_permute_rows_gather_count: need hidden_size % 8 == 0, tables and a count");
+  if (max_rows == 0) return LM_OK;
+  const int warps = 8;
+  const unsigned blocks = static_cast<unsigned>((max_rows + warps - 1) / warps);
+  const cudaError_t e = launch_dependent(
+      permute_rows_gather_kernel, dim3(blocks), dim3(warps * 32), 0,
+      static_cast<cudaStream_t>(stream), src, hidden_size, row_to_pair, pair_src, max_rows,
+      x_perm, num_rows_dev);
+  if (e != cudaSuccess) return check_cuda(e, "lm_permute_rows_gather_count");
+  return launch_status("lm_permute_rows_gather_count");
 }
 
 extern "C" int lm_permute_rows_count(const uint16_t* hidden, int32_t hidden_size,

@@ -43,6 +43,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
+from .layer import DECODE_MAX_TOKENS
 
 
 def balanced_expert_placement(expert_load, world_size: int) -> list[int]:
@@ -92,6 +93,10 @@ class EPOps:
     # (rows [Rmax,H], local_ids [Rmax], count int32 [1] on the device, out [Rmax,H]): the
     # owner's MLP with the received row count kept on the device (None: not available)
     expert_mlp_count: Callable | None = None
+    # (receive area [Rmax,H], slot of pair [Rmax], local_ids [Rmax], count [1], pair-row table
+    # out [Rmax], output rows [Rmax,H]): the owner's MLP gathering its rows straight from the
+    # receive area and leaving them grouped, with the table the sources read (None: n/a)
+    expert_mlp_gather: Callable | None = None
 
 
 class _DevicePtrArray:
@@ -130,6 +135,14 @@ class PeerExchange:
         self.out_rows = torch.as_tensor(
             _DevicePtrArray(self.region + off, (rows, self.H), "<i2"),
             device=self.device).view(torch.bfloat16)
+        roff = _lib.ep_recv_rows_offset(self.G, self.cap, self.H)
+        self.recv_rows = torch.as_tensor(
+            _DevicePtrArray(self.region + roff, (rows, self.H), "<i2"),
+            device=self.device).view(torch.bfloat16)
+        poff = _lib.ep_pair_rows_offset(self.G, self.cap, self.H)
+        self.pair_rows = torch.as_tensor(_DevicePtrArray(self.region + poff, (rows,), "<i4"),
+                                         device=self.device)
+        self.slots = torch.empty(rows, dtype=torch.int32, device=self.device)
         self.rows = torch.empty(rows, self.H, dtype=torch.bfloat16, device=self.device)
         self.ids = torch.empty(rows, dtype=torch.int32, device=self.device)
         self.total = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -150,7 +163,7 @@ class PeerExchange:
             if r != self.rank:
                 _lib.ipc_close_handle(ptr)
         dist.barrier(group=self.group)
-        self.out_rows = None
+        self.out_rows = self.recv_rows = self.pair_rows = None
         _lib.ep_region_free(self.region)
         self.region = None
 
@@ -237,15 +250,25 @@ class ExpertParallelMoE:
         x.epoch += 1
         _lib.ep_dispatch(hidden, ids, self.per_rank, p2r, offsets, self.rank, self.G, x.peers,
                          x.cap, x.epoch, x.done, x.err)
-        _lib.ep_receive(x.region, self.G, x.cap, self.H, x.epoch, x.rows, x.ids, x.total, x.err)
-        no_sync = self.ops.expert_mlp_count is not None
-        if no_sync:
-            # the received count stays on the device: no host round trip in the step
-            self.ops.expert_mlp_count(x.rows, x.ids, x.total, x.out_rows)
+        gather = self.ops.expert_mlp_gather is not None and x.rows.shape[0] > DECODE_MAX_TOKENS
+        no_sync = gather or self.ops.expert_mlp_count is not None
+        if gather:
+            # no row copies on the owner: slots only, the MLP gathers from the receive area and
+            # its grouped outputs stay put; the sources read them through the pair-row table
+            _lib.ep_receive_index(x.region, self.G, x.cap, self.H, x.epoch, x.slots, x.ids,
+                                  x.total, x.err)
+            self.ops.expert_mlp_gather(x.recv_rows, x.slots, x.ids, x.total, x.pair_rows,
+                                       x.out_rows)
         else:
-            R = int(x.total.item())  # sizes (and stages) the local expert MLP
-            if R:
-                self.ops.expert_mlp(x.rows[:R], x.ids[:R], out=x.out_rows[:R])
+            _lib.ep_receive(x.region, self.G, x.cap, self.H, x.epoch, x.rows, x.ids, x.total,
+                            x.err)
+            if no_sync:
+                # the received count stays on the device: no host round trip in the step
+                self.ops.expert_mlp_count(x.rows, x.ids, x.total, x.out_rows)
+            else:
+                R = int(x.total.item())  # sizes (and stages) the local expert MLP
+                if R:
+                    self.ops.expert_mlp(x.rows[:R], x.ids[:R], out=x.out_rows[:R])
         _lib.ep_signal_outputs(x.peers, self.rank, self.G, x.cap, self.H, x.epoch)
         out = torch.empty(T, self.H, dtype=hidden.dtype, device=hidden.device)
         _lib.ep_combine(ids, w, self.per_rank, p2r, offsets, self.rank, self.G, x.peers,
@@ -318,12 +341,16 @@ def cuda_ops(local_moe, *, num_experts: int, top_k: int, renormalize: bool = Tru
         _lib.moe_combine(back, p2r_, w, out)
         return out
 
-    expert_mlp_count = None
+    expert_mlp_count = expert_mlp_gather = None
     if local_moe.runtime.host_layer(local_moe.layer_id).on_device:
         def expert_mlp_count(rows, local_ids, count, out):
             return local_moe.mlp_rows_count(rows, local_ids, count, out)
 
-    return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine, expert_mlp_count)
+        def expert_mlp_gather(src, slots, local_ids, count, pair_rows, out):
+            return local_moe.mlp_rows_gather_count(src, slots, local_ids, count, pair_rows, out)
+
+    return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine, expert_mlp_count,
+                 expert_mlp_gather)
 
 
 def build_rank_layer(*, w13_owned: torch.Tensor, w2_owned: torch.Tensor, rank: int,

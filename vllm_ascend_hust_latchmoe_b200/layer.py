@@ -446,6 +446,30 @@ class SlotBankMoE:
         self.kernel_launches += group_launches(R) + mlp_launches(R) + 1 + (R > DECODE_MAX_TOKENS)
         return out
 
+    def mlp_rows_gather_count(self, src_rows: torch.Tensor, pair_src: torch.Tensor,
+                              ids: torch.Tensor, count_dev: torch.Tensor,
+                              pair_to_row_out: torch.Tensor, y_out: torch.Tensor) -> None:
+        """Top-1 MLP over the first ``count_dev`` pairs whose rows sit in ``src_rows`` at
+        ``pair_src[p]`` (the receive area an exchange filled; nothing is compacted first):
+        grouping by expert, a gather straight from ``src_rows`` into the grouped order, the
+        tcgen05 MLP writing its rows into ``y_out`` and pair p's row index into
+        ``pair_to_row_out[p]`` (the table the exchange's sources read). Needs a top-1 layer
+        with an HBM-resident store and a capacity above the decode size."""
+        store = self.runtime.host_layer(self.layer_id)
+        R = int(ids.shape[0])
+        if self.k != 1 or not store.on_device:
+            raise RuntimeError("mlp_rows_gather_count needs a top-1 layer with an HBM store")
+        if R > self.max_tokens or R <= DECODE_MAX_TOKENS:
+            raise ValueError(f"{R} pairs outside ({DECODE_MAX_TOKENS}, {self.max_tokens}]")
+        _lib.build_groups_count(ids.view(R, 1), count_dev, self.E_total, self.identity_groups,
+                                self.E, self.group_offsets, pair_to_row_out, self.row_to_pair,
+                                self.scratch, self.err)
+        _lib.permute_rows_gather_count(src_rows, self.row_to_pair, pair_src, R, count_dev,
+                                       self.x_perm)
+        _lib.moe_mlp_prefill(self.x_perm, R, self.group_offsets, self.identity_groups, 0,
+                             self.E, store.w13, store.w2, self.act, y_out, self.err)
+        self.kernel_launches += group_launches(R) + 1 + mlp_launches(R)
+
     def resident_wave_plan(self) -> tuple[tuple[int, ...], ...]:
         """Read back the last device wave plan (synchronises; diagnostics and tests). Empty
         after a decode-sized resident call, which groups by expert id without waves."""
