@@ -618,10 +618,11 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     scaling) with its 128 experts partitioned over the N GPUs. Experts are placed on ranks by
     a load-balanced placement of a profiled routing sample (the router's gate columns and the
     expert bank permuted together at load time); each rank holds its E / N experts in HBM.
-    One step on every rank: route its tokens, dispatch each routed pair's row straight into its
-    owner's receive area over NVLink (peer memory), run the owner's grouped MLP on what it
-    received (the row count stays on the device), signal, and combine every token's pairs from
-    the owners in top-k order. Time = max over ranks; after timing, each rank's first tokens
+    One step on every rank: route its tokens, store each token's row once into every owner that
+    holds any of its experts over NVLink (peer memory), with each pair's owner-local id and
+    receive-row index; the owner's grouped MLP gathers its rows from the receive area (the row
+    count stays on the device) and leaves its outputs grouped; signal, and combine every
+    token's pairs from the owners in top-k order. Time = max over ranks; after timing, each rank's first tokens
     are checked against the torch fp32 restatement of the 1-GPU layer. Also returns the same
     step from host buffers (``e2e``)."""
     import torch
@@ -673,9 +674,12 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     ms_step = ms_total / args.steps
     value = world * T * args.steps / (ms_total / 1e3)
     nvlink = (ep.stats.bytes_sent - sent0) / args.steps
-    # per step: route, owner grouping, dispatch, receive (wait + compact), the owner MLP's
-    # grouping / gather / grouped-MLP / unit combine, signal, combine (wait + reduce)
-    launches_per_step = 2 + 1 + 2 + (local.kernel_launches - launches0) // args.steps + 1 + 2
+    # per step: route, owner grouping, dispatch (token slots + stores when deduplicated),
+    # receive (wait + index), the owner MLP's grouping / gather / grouped MLP, signal, combine
+    # (wait + reduce)
+    dispatch_launches = 2 if ep.dedupe_dispatch else 1
+    launches_per_step = (1 + 1 + dispatch_launches + 2
+                         + (local.kernel_launches - launches0) // args.steps + 1 + 2)
 
     # correctness of what was timed: one more call, first tokens against the reference
     got = ep.forward(hidden, logits)
@@ -699,11 +703,17 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     x = exchange
     rows_recv = int(x.total.item())
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # the gather path the step runs (every rank's combine of the last step has completed: the
+    # all-reduce above follows it in each rank's stream; the rewrite stores the same values)
+    def owner_mlp():
+        local.mlp_rows_gather_count(x.recv_rows, x.slots, x.ids, x.total, x.pair_rows,
+                                    x.out_rows)
+
     for _ in range(3):
-        local.mlp_rows_count(x.rows, x.ids, x.total, x.out_rows)
+        owner_mlp()
     a.record()
     for _ in range(args.steps):
-        local.mlp_rows_count(x.rows, x.ids, x.total, x.out_rows)
+        owner_mlp()
     b.record()
     torch.cuda.synchronize()
     mlp_ms = a.elapsed_time(b) / args.steps
@@ -718,8 +728,8 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
                 "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                 "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
                 "peak_source": peaks["source"], "traffic": None,
-                "kernel": "rank 0's grouped MLP (owner side: grouping, gather, lm_moe_mlp_prefill, "
-                          "unit-weight combine) on the rows it received",
+                "kernel": "rank 0's grouped MLP (owner side: grouping, gather from the receive "
+                          "area, lm_moe_mlp_prefill) on the rows it received",
                 "ms_per_call": mlp_ms, "flops_per_call": flops, "rows_rank0": rows_recv}
 
     # e2e: the same step from pinned host buffers (inputs in, output out, every step)
@@ -750,6 +760,8 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
                "experts_per_rank": per, "rows_received_per_rank": rows_all,
                "rank_load_max_over_mean": max(rows_all) / (sum(rows_all) / world),
                "nvlink_bytes_sent_rank0_per_step": nvlink, "transport": "peer memory (IPC)",
+               "dispatch": "token-deduplicated (one row per token and owner)"
+                           if ep.dedupe_dispatch else "one row per routed pair",
                "parity": parity}
     exchange.close()
     del ep, local

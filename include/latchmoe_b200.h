@@ -200,6 +200,17 @@ int lm_moe_mlp_decode(const uint16_t* hidden, int32_t top_k, const int32_t* row_
                       int32_t hidden_size, int32_t intermediate_size,
                       uint16_t* act, uint16_t* y_perm, int32_t* err_word, void* stream);
 
+/*
+ * The persistent decode kernel keeps its work queue in one of 16 counter sets per device, one
+ * per stream. A set moves to another stream once its stream's last eager launch has
+ * completed; a set used inside a stream capture stays with that stream. When no set can be
+ * freed, the launch runs the two-kernel decode path (same outputs) and is counted here.
+ * Reports the current device's sets in use, those held by captures, sets moved so far and
+ * launches that fell back (any pointer may be NULL).
+ */
+int lm_decode_counter_sets(int32_t* in_use, int32_t* pinned, int64_t* recycled,
+                           int64_t* fallbacks);
+
 int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
                        const int32_t* group_offsets, const int32_t* group_bank_row,
                        int32_t group_begin, int32_t group_end,
@@ -316,6 +327,11 @@ int lm_moe_mlp_decode_offload(const uint16_t* hidden, int32_t top_k,
  *   lm_ep_dispatch      pairs grouped by owner (pair_to_row / send_offsets from
  *                       lm_build_groups with expert -> owner); each pair's hidden row and
  *                       owner-local expert id go straight into the owner's region.
+ *   (or lm_ep_dispatch_tokens: the same pair metadata, but each token's row is stored once
+ *    per owner that holds any of its experts, at receive row rank * (cap / top_k) + its token
+ *    slot; tok_slot [num_tokens * world] (-1: no pair there) and tok_count [world] are
+ *    written on the device. Owners read rows through each pair's receive-row index, so the
+ *    receive side is the same for both dispatches.)
  *   lm_ep_receive       waits for every source's dispatch (bounded), compacts the received rows
  *                       and ids into rows_out / ids_out; *total_out = their number (device).
  *   (local expert MLP, outputs written in received order at region + lm_ep_out_rows_offset)
@@ -350,6 +366,13 @@ int lm_ep_dispatch(const uint16_t* hidden, int64_t num_tokens, int32_t top_k,
                    const int32_t* pair_to_row, const int32_t* send_offsets, int32_t rank,
                    int32_t world, void* const* peer_regions, int32_t cap, int64_t epoch,
                    int32_t* done_counter, int32_t* err_word, void* stream);
+int lm_ep_dispatch_tokens(const uint16_t* hidden, int64_t num_tokens, int32_t top_k,
+                          int32_t hidden_size, const int32_t* topk_ids,
+                          int32_t experts_per_rank, const int32_t* pair_to_row,
+                          const int32_t* send_offsets, int32_t rank, int32_t world,
+                          void* const* peer_regions, int32_t cap, int64_t epoch,
+                          int32_t* tok_slot, int32_t* tok_count, int32_t* done_counter,
+                          int32_t* err_word, void* stream);
 int lm_ep_receive(void* region, int32_t world, int32_t cap, int32_t hidden_size, int64_t epoch,
                   uint16_t* rows_out, int32_t* ids_out, int32_t* total_out, int32_t* err_word,
                   void* stream);

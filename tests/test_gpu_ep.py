@@ -1,6 +1,7 @@
 """Expert-parallel layer on 2 GPUs: each rank owns half of the experts in its own slot bank
 (pinned host store, staged, or HBM-resident) and the outputs match the single-GPU oracle,
-with the exchange over NCCL or over peer memory (the library's dispatch / combine kernels).
+with the exchange over NCCL or over peer memory (the library's dispatch / combine kernels,
+the dispatch per token or per routed pair).
 Skipped with fewer than 2 GPUs."""
 
 import os
@@ -51,11 +52,12 @@ def _worker(rank, world, port, store_on_device, transport, q):
                                  device=dev, max_rows=world * T * K, num_slots=S,
                                  store_on_device=store_on_device)
         exchange = None
-        if transport == "peer":
+        if transport.startswith("peer"):
             exchange = PeerExchange(world_size=world, rank=rank, max_tokens=T, top_k=K,
                                     hidden_size=H, device=dev)
         ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
                                world_size=world, device=dev, exchange=exchange,
+                               dedupe_dispatch=transport == "peer",
                                ops=cuda_ops(local, num_experts=E, top_k=K, max_tokens=T))
         # a call with other routing first: the checked call reuses every area and flag
         ep.forward(syn.make_hidden(cfg, seed=30 + rank).to(dev),
@@ -82,7 +84,8 @@ def _worker(rank, world, port, store_on_device, transport, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["nccl", "peer"])
+# "peer": token-deduplicated dispatch; "peer_pairs": one row per routed pair
+@pytest.mark.parametrize("transport", ["nccl", "peer", "peer_pairs"])
 @pytest.mark.parametrize("store_on_device", [False, True])
 def test_ep_two_gpus_matches_oracle(store_on_device, transport):
     if torch.cuda.device_count() < 2:

@@ -54,9 +54,15 @@ def test_single_rank_exchange_round_trip_and_timeout(cuda):
     done = torch.zeros(1, dtype=torch.int32, device=cuda)
     out = torch.empty(T, H, dtype=torch.bfloat16, device=cuda)
     try:
-        for epoch in (1, 2):  # a second call reuses every area
-            _lib.ep_dispatch(c["hidden"], c["ids"], E, c["p2r"], c["offsets"], 0, 1, c["peers"],
-                             cap, epoch, done, err)
+        tok_slot = torch.empty(T, dtype=torch.int32, device=cuda)
+        tok_count = torch.zeros(1, dtype=torch.int32, device=cuda)
+        for epoch in (1, 2):  # a second call reuses every area; epoch 2 dispatches per token
+            if epoch == 1:
+                _lib.ep_dispatch(c["hidden"], c["ids"], E, c["p2r"], c["offsets"], 0, 1,
+                                 c["peers"], cap, epoch, done, err)
+            else:
+                _lib.ep_dispatch_tokens(c["hidden"], c["ids"], E, c["p2r"], c["offsets"], 0, 1,
+                                        c["peers"], cap, epoch, tok_slot, tok_count, done, err)
             _lib.ep_receive(c["region"], 1, cap, H, epoch, rows, rids, total, err)
             c["out_rows"].copy_(rows)  # the "expert" returns each row unchanged
             _lib.ep_signal_outputs(c["peers"], 0, 1, cap, H, epoch)
@@ -65,6 +71,9 @@ def test_single_rank_exchange_round_trip_and_timeout(cuda):
                             c["region"], cap, epoch, out, err)
             torch.cuda.synchronize()
             assert int(err.item()) == 0 and int(total.item()) == T * K
+            if epoch == 2:  # one owner: every token once, in token order
+                assert int(tok_count.item()) == T
+                assert tok_slot.tolist() == list(range(T))
             pairs = np.repeat(bf16_bits_to_f32(bits(c["hidden"])), K, axis=0)
             ref = omlp.combine(pairs, bits(c["w"]))
             m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)
@@ -82,10 +91,12 @@ def test_single_rank_exchange_round_trip_and_timeout(cuda):
         _lib.ep_region_free(c["region"])
 
 
-def test_single_rank_gather_path_matches_oracle(cuda):
+@pytest.mark.parametrize("dedupe", [False, True])
+def test_single_rank_gather_path_matches_oracle(cuda, dedupe):
     """The owner path without row copies: index-only receive, the grouped MLP gathering its
     rows from the receive area, outputs left in grouped order with the pair-row table, and the
-    combine reading through that table -- against the oracle layer, twice in a row."""
+    combine reading through that table -- against the oracle layer, twice in a row. With
+    ``dedupe`` each token row is stored once and all its pairs read that one row."""
     from oracle import router as orouter
     from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
     from vllm_ascend_hust_latchmoe_b200.expert_parallel import build_rank_layer
@@ -119,6 +130,8 @@ def test_single_rank_gather_path_matches_oracle(cuda):
         scratch = torch.empty(_lib.build_groups_scratch_elems(cap, 1), dtype=torch.int32,
                               device=cuda)
         out = torch.empty(T2, H2, dtype=torch.bfloat16, device=cuda)
+        tok_slot = torch.empty(T2, dtype=torch.int32, device=cuda)
+        tok_count = torch.zeros(1, dtype=torch.int32, device=cuda)
         for epoch, seed in ((1, 1), (2, 2)):
             hidden = syn.make_hidden(cfg, seed=seed)
             wb, _, ids_np = orouter.route(syn.make_router_logits(cfg, seed=seed).numpy(), K2)
@@ -126,13 +139,20 @@ def test_single_rank_gather_path_matches_oracle(cuda):
             w = torch.from_numpy(wb.view(np.int16)).view(torch.bfloat16).to(cuda)
             h = hidden.to(cuda)
             _lib.build_groups(ids, E2, owner, 1, offsets, p2r, r2p, scratch, err)
-            _lib.ep_dispatch(h, ids, E2, p2r, offsets, 0, 1, peers, cap, epoch, done, err)
+            if dedupe:
+                _lib.ep_dispatch_tokens(h, ids, E2, p2r, offsets, 0, 1, peers, cap, epoch,
+                                        tok_slot, tok_count, done, err)
+            else:
+                _lib.ep_dispatch(h, ids, E2, p2r, offsets, 0, 1, peers, cap, epoch, done, err)
             _lib.ep_receive_index(region, 1, cap, H2, epoch, slots, rids, total, err)
             layer.mlp_rows_gather_count(recv_rows, slots, rids, total, pair_rows, out_rows)
             _lib.ep_signal_outputs(peers, 0, 1, cap, H2, epoch)
             _lib.ep_combine(ids, w, E2, p2r, offsets, 0, 1, peers, region, cap, epoch, out, err)
             torch.cuda.synchronize()
             assert int(err.item()) == 0 and int(total.item()) == cap
+            if dedupe:  # the token rows sit once each at the head of the receive area
+                assert int(tok_count.item()) == T2
+                assert torch.equal(recv_rows[:T2], h)
             layer.check_device_errors("gather path")
             ref = omlp.moe_layer(bits(hidden), ids_np, wb, bits(w13), bits(w2))
             m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)

@@ -228,6 +228,44 @@ def test_decode_mlp_concurrent_streams(cuda):
             assert torch.equal(c["y"], ref)
 
 
+def test_decode_counter_sets_move_between_streams(cuda):
+    """More streams than counter sets, each used eagerly in turn: a set whose stream's last
+    launch has finished moves to the next stream, so every launch stays on the persistent
+    kernel (no fallback) and gives the same output."""
+    E, H, I, k, T = 16, 256, 128, 8, 4
+    g = torch.Generator().manual_seed(5)
+    W13 = to_tiled((torch.randn(E, 2 * I, H, generator=g) * 0.05).to(torch.bfloat16)).to(cuda)
+    W2 = to_tiled((torch.randn(E, H, I, generator=g) * 0.05).to(torch.bfloat16)).to(cuda)
+    ident = torch.arange(E, dtype=torch.int32, device=cuda)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    h = (torch.randn(T, H, generator=g) * 0.5).to(torch.bfloat16).to(cuda)
+    off = torch.empty(E + 1, dtype=torch.int32, device=cuda)
+    p2r = torch.empty(T * k, dtype=torch.int32, device=cuda)
+    r2p = torch.empty(T * k, dtype=torch.int32, device=cuda)
+    scratch = torch.empty(_lib.build_groups_scratch_elems(T * k, E), dtype=torch.int32,
+                          device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    _lib.build_groups(ids.to(cuda), E, ident, E, off, p2r, r2p, scratch, err)
+    act = torch.empty(T * k, I, dtype=torch.bfloat16, device=cuda)
+    y = torch.empty(T * k, H, dtype=torch.bfloat16, device=cuda)
+    _lib.moe_mlp_decode(h, k, r2p, off, ident, 0, E, T, W13, W2, act, y, err)
+    torch.cuda.synchronize()
+    ref = y.clone()
+    before = _lib.decode_counter_sets()
+    streams = [torch.cuda.Stream() for _ in range(20)]  # kept alive: distinct handles
+    for st in streams:
+        y.zero_()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(st):
+            _lib.moe_mlp_decode(h, k, r2p, off, ident, 0, E, T, W13, W2, act, y, err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0 and torch.equal(y, ref)
+    after = _lib.decode_counter_sets()
+    assert after["fallbacks"] == before["fallbacks"], (before, after)
+    assert after["recycled"] >= before["recycled"] + 4, (before, after)
+    assert after["in_use"] <= 16
+
+
 @pytest.mark.parametrize("T,k,E,H,I", [(256, 8, 32, 2048, 768), (300, 8, 128, 2048, 768),
                                        (129, 2, 4, 256, 128), (512, 6, 64, 2048, 1408)])
 def test_prefill_tcgen05_mlp_matches_oracle(cuda, T, k, E, H, I):

@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _I32, _P, _P, _P, _P],
     ),
     "lm_expert_histogram": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _P]),
+    "lm_decode_counter_sets": (ctypes.c_int, [_P, _P, _P, _P]),
     "lm_ep_region_bytes": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_ep_out_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_ep_region_alloc": (ctypes.c_int, [_I64, ctypes.POINTER(ctypes.c_void_p)]),
@@ -57,6 +58,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lm_ep_dispatch": (
         ctypes.c_int,
         [_P, _I64, _I32, _I32, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _I64, _P, _P, _P],
+    ),
+    "lm_ep_dispatch_tokens": (
+        ctypes.c_int,
+        [_P, _I64, _I32, _I32, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _I64, _P, _P, _P, _P, _P],
     ),
     "lm_ep_receive": (ctypes.c_int, [_P, _I32, _I32, _I32, _I64, _P, _P, _P, _P, _P]),
     "lm_ep_signal_outputs": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _I64, _P]),
@@ -396,6 +401,19 @@ def ep_dispatch(hidden, topk_ids, experts_per_rank, pair_to_row, send_offsets, r
         int(cap), int(epoch), _ptr(done_counter), _ptr(err_word), _stream()))
 
 
+def ep_dispatch_tokens(hidden, topk_ids, experts_per_rank, pair_to_row, send_offsets, rank,
+                       world, peer_regions, cap, epoch, tok_slot, tok_count, done_counter,
+                       err_word=None) -> None:
+    """Token-deduplicated dispatch: each token row goes once to each owner holding any of its
+    experts (tok_slot [T * world], tok_count [world] are written, on the device)."""
+    T, k = topk_ids.shape
+    _check("lm_ep_dispatch_tokens", lib().lm_ep_dispatch_tokens(
+        _ptr(hidden), T, k, hidden.shape[-1], _ptr(topk_ids), int(experts_per_rank),
+        _ptr(pair_to_row), _ptr(send_offsets), int(rank), int(world), _ptr(peer_regions),
+        int(cap), int(epoch), _ptr(tok_slot), _ptr(tok_count), _ptr(done_counter),
+        _ptr(err_word), _stream()))
+
+
 def ep_receive(region: int, world, cap, hidden_size, epoch, rows_out, ids_out, total_out,
                err_word=None) -> None:
     _check("lm_ep_receive", lib().lm_ep_receive(
@@ -458,6 +476,15 @@ def slot_plan(topk_ids, num_experts, slot_owner, slot_last_used, expert_slot, st
             _ptr(log2phy), _ptr(group_src), _ptr(hit_miss), _ptr(err_word), _stream(),
         ),
     )
+
+
+def decode_counter_sets() -> dict:
+    """Counter sets of the persistent decode kernel on the current device."""
+    u, p = ctypes.c_int32(0), ctypes.c_int32(0)
+    r, f = ctypes.c_int64(0), ctypes.c_int64(0)
+    _check("lm_decode_counter_sets", lib().lm_decode_counter_sets(
+        ctypes.byref(u), ctypes.byref(p), ctypes.byref(r), ctypes.byref(f)))
+    return {"in_use": u.value, "pinned": p.value, "recycled": r.value, "fallbacks": f.value}
 
 
 def moe_mlp_decode_offload(hidden, top_k, row_to_pair, group_offsets, group_src, group_expert,

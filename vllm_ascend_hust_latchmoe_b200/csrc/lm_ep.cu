@@ -27,9 +27,9 @@
 namespace lm {
 namespace {
 
-constexpr int kLayoutFields = 10;
+constexpr int kLayoutFields = 11;
 enum : int { F_FLAG_DISPATCH = 0, F_FLAG_OUT, F_COUNTS, F_PREFIX, F_WAIT_STATUS, F_RECV_IDS,
-             F_PAIR_ROW, F_RECV_ROWS, F_OUT_ROWS, F_TOTAL };
+             F_RECV_ROWIDX, F_PAIR_ROW, F_RECV_ROWS, F_OUT_ROWS, F_TOTAL };
 
 int64_t align256(int64_t v) { return (v + 255) & ~static_cast<int64_t>(255); }
 
@@ -46,6 +46,8 @@ void layout(int G, int cap, int H, int64_t* off) {
   off[F_WAIT_STATUS] = o;  // this rank's last output wait: 0 every owner answered, 1 timed out
   o = align256(o + 4);
   off[F_RECV_IDS] = o;
+  o = align256(o + 4ll * G * cap);
+  off[F_RECV_ROWIDX] = o;  // receive-area row of each received pair (rows may be shared)
   o = align256(o + 4ll * G * cap);
   off[F_PAIR_ROW] = o;  // owner: output row of its received pair d (read by the sources)
   o = align256(o + 4ll * G * cap);
@@ -117,10 +119,124 @@ __global__ void __launch_bounds__(256)
     }
     void* region = peers[o];
     const int64_t slot = static_cast<int64_t>(rank) * cap + pos;
-    if (lane == 0) field<int32_t>(region, L, F_RECV_IDS)[slot] = e - o * per_rank;
+    if (lane == 0) {
+      field<int32_t>(region, L, F_RECV_IDS)[slot] = e - o * per_rank;
+      field<int32_t>(region, L, F_RECV_ROWIDX)[slot] = static_cast<int32_t>(slot);
+    }
     const uint4* src = reinterpret_cast<const uint4*>(hidden + (p / top_k) * static_cast<int64_t>(H));
     uint4* dst = reinterpret_cast<uint4*>(field<uint16_t>(region, L, F_RECV_ROWS) + slot * H);
     for (int c = lane; c < H / 8; c += 32) dst[c] = __ldg(src + c);
+  }
+  __threadfence_system();
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) last = atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence_system();
+  for (int o = threadIdx.x; o < G; o += blockDim.x)
+    field<int32_t>(peers[o], L, F_COUNTS)[rank] = send_offsets[o + 1] - send_offsets[o];
+  __threadfence_system();
+  __syncthreads();
+  for (int o = threadIdx.x; o < G; o += blockDim.x)
+    st_release_sys(field<long long>(peers[o], L, F_FLAG_DISPATCH) + rank, epoch);
+  if (threadIdx.x == 0) *done = 0;  // ready for the next call
+}
+
+// Token slots of a deduplicated dispatch: block o walks the tokens in order and numbers those
+// with at least one pair owned by o (tok_slot[t * G + o], -1 otherwise); tok_count[o] = their
+// number. A token's row then crosses to owner o once, whatever its number of pairs there.
+__global__ void __launch_bounds__(1024)
+    ep_token_slots_kernel(const int32_t* __restrict__ ids, int64_t num_tokens, int top_k,
+                          int per_rank, int G, int32_t* __restrict__ tok_slot,
+                          int32_t* __restrict__ tok_count) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  const int o = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int64_t base = 0; base < num_tokens; base += blockDim.x) {
+    const int64_t t = base + threadIdx.x;
+    int mine = 0;
+    if (t < num_tokens) {
+      for (int j = 0; j < top_k; ++j) {
+        const int e = ids[t * top_k + j];
+        if (e >= 0 && e / per_rank == o) mine = 1;
+      }
+    }
+    // block exclusive scan of the flags
+    const unsigned ball = __ballot_sync(0xffffffffu, mine);
+    const int before_in_warp = __popc(ball & ((1u << lane) - 1u));
+    if (lane == 0) warp_sums[wid] = __popc(ball);
+    __syncthreads();
+    if (wid == 0) {
+      int v = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += u;
+      }
+      if (lane < nw) warp_sums[lane] = v;  // inclusive
+    }
+    __syncthreads();
+    const int warp_base = wid ? warp_sums[wid - 1] : 0;
+    if (t < num_tokens) tok_slot[t * G + o] = mine ? carry + warp_base + before_in_warp : -1;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += warp_sums[nw - 1];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tok_count[o] = carry;
+}
+
+// Deduplicated dispatch: warps over (token, owner) copy each needed token row once into the
+// owner's receive area at [rank * tok_cap + token slot]; threads over pairs store each pair's
+// owner-local id and receive-area row index. Same flags / counts protocol as
+// ep_dispatch_kernel (counts are pairs per owner).
+__global__ void __launch_bounds__(256)
+    ep_dispatch_tokens_kernel(const uint16_t* __restrict__ hidden, int64_t num_tokens,
+                              int top_k, int H, const int32_t* __restrict__ ids, int per_rank,
+                              const int32_t* __restrict__ pair_to_row,
+                              const int32_t* __restrict__ send_offsets,
+                              const int32_t* __restrict__ tok_slot, int rank, int G,
+                              void* const* __restrict__ peers, Layout L, int cap, int tok_cap,
+                              long long epoch, int32_t* __restrict__ done,
+                              int32_t* __restrict__ err_word) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t w0 = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t num_pairs = num_tokens * top_k;
+  for (int64_t q = w0; q < num_tokens * G; q += warps) {
+    const int64_t t = q / G;
+    const int o = static_cast<int>(q - t * G);
+    const int ts = tok_slot[q];
+    if (ts < 0) continue;
+    if (ts >= tok_cap) {
+      if (lane == 0) record_error(err_word, LM_DEVERR_BAD_GROUP);
+      continue;
+    }
+    const int64_t row = static_cast<int64_t>(rank) * tok_cap + ts;
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + t * static_cast<int64_t>(H));
+    uint4* dst = reinterpret_cast<uint4*>(field<uint16_t>(peers[o], L, F_RECV_ROWS) + row * H);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = __ldg(src + c);
+  }
+  for (int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; p < num_pairs;
+       p += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[p];
+    const int o = e / per_rank;
+    if (e < 0 || o >= G) {
+      record_error(err_word, LM_DEVERR_BAD_EXPERT_ID);
+      continue;
+    }
+    const int pos = pair_to_row[p] - send_offsets[o];
+    const int ts = tok_slot[(p / top_k) * G + o];
+    if (pos < 0 || pos >= cap || ts < 0 || ts >= tok_cap) {
+      record_error(err_word, LM_DEVERR_BAD_GROUP);
+      continue;
+    }
+    const int64_t slot = static_cast<int64_t>(rank) * cap + pos;
+    field<int32_t>(peers[o], L, F_RECV_IDS)[slot] = e - o * per_rank;
+    field<int32_t>(peers[o], L, F_RECV_ROWIDX)[slot] = rank * tok_cap + ts;
   }
   __threadfence_system();
   __syncthreads();
@@ -172,6 +288,7 @@ __global__ void __launch_bounds__(256)
                       uint16_t* __restrict__ rows_out, int32_t* __restrict__ ids_out) {
   const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
   const int32_t* recv_ids = field<int32_t>(region, L, F_RECV_IDS);
+  const int32_t* recv_rowidx = field<int32_t>(region, L, F_RECV_ROWIDX);
   const uint16_t* recv_rows = field<uint16_t>(region, L, F_RECV_ROWS);
   int32_t* pair_row = field<int32_t>(region, L, F_PAIR_ROW);
   const int lane = threadIdx.x & 31;
@@ -186,7 +303,8 @@ __global__ void __launch_bounds__(256)
       ids_out[d] = __ldcg(recv_ids + q);
       pair_row[d] = static_cast<int32_t>(d);  // outputs land in received order
     }
-    const uint4* src = reinterpret_cast<const uint4*>(recv_rows + q * H);
+    const int64_t srow = __ldcg(recv_rowidx + q);
+    const uint4* src = reinterpret_cast<const uint4*>(recv_rows + srow * H);
     uint4* dst = reinterpret_cast<uint4*>(rows_out + d * H);
     for (int c = lane; c < H / 8; c += 32) dst[c] = __ldcg(src + c);
   }
@@ -199,12 +317,13 @@ __global__ void __launch_bounds__(256)
                     int32_t* __restrict__ ids_out) {
   const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
   const int32_t* recv_ids = field<int32_t>(region, L, F_RECV_IDS);
+  const int32_t* recv_rowidx = field<int32_t>(region, L, F_RECV_ROWIDX);
   for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        q < static_cast<int64_t>(G) * cap; q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int s = static_cast<int>(q / cap), i = static_cast<int>(q - static_cast<int64_t>(s) * cap);
     if (i >= prefix[s + 1] - prefix[s]) continue;
     const int64_t d = prefix[s] + i;
-    slot_out[d] = static_cast<int32_t>(q);
+    slot_out[d] = __ldcg(recv_rowidx + q);
     ids_out[d] = __ldcg(recv_ids + q);
   }
 }
@@ -389,6 +508,42 @@ extern "C" int lm_ep_dispatch(const uint16_t* hidden, int64_t num_tokens, int32_
       rank, world, peer_regions, make_layout(world, cap, hidden_size), cap, epoch, done_counter,
       err_word);
   return launch_status("lm_ep_dispatch");
+}
+
+extern "C" int lm_ep_dispatch_tokens(const uint16_t* hidden, int64_t num_tokens, int32_t top_k,
+                                     int32_t hidden_size, const int32_t* topk_ids,
+                                     int32_t experts_per_rank, const int32_t* pair_to_row,
+                                     const int32_t* send_offsets, int32_t rank, int32_t world,
+                                     void* const* peer_regions, int32_t cap, int64_t epoch,
+                                     int32_t* tok_slot, int32_t* tok_count,
+                                     int32_t* done_counter, int32_t* err_word, void* stream) {
+  int rc = check_ep("lm_ep_dispatch_tokens", world, cap, hidden_size);
+  if (rc) return rc;
+  if (num_tokens < 0 || top_k <= 0 || experts_per_rank <= 0 || rank < 0 || rank >= world ||
+      epoch <= 0 || done_counter == nullptr || peer_regions == nullptr ||
+      send_offsets == nullptr || tok_slot == nullptr || tok_count == nullptr ||
+      (num_tokens > 0 && (hidden == nullptr || topk_ids == nullptr || pair_to_row == nullptr)))
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_dispatch_tokens: bad arguments");
+  if (num_tokens * top_k > cap)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_ep_dispatch_tokens: num_tokens * top_k exceeds the exchange capacity cap");
+  if (reinterpret_cast<uintptr_t>(hidden) & 15)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_dispatch_tokens: hidden must be 16-byte aligned");
+  // a source's token rows start at rank * tok_cap inside the world * cap receive rows
+  const int tok_cap = cap / top_k;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ep_token_slots_kernel<<<world, 1024, 0, s>>>(topk_ids, num_tokens, top_k, experts_per_rank,
+                                               world, tok_slot, tok_count);
+  rc = launch_status("lm_ep_dispatch_tokens: token slots");
+  if (rc) return rc;
+  int64_t blocks = (num_tokens * world + 7) / 8;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 1184) blocks = 1184;
+  ep_dispatch_tokens_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+      hidden, num_tokens, top_k, hidden_size, topk_ids, experts_per_rank, pair_to_row,
+      send_offsets, tok_slot, rank, world, peer_regions, make_layout(world, cap, hidden_size),
+      cap, tok_cap, epoch, done_counter, err_word);
+  return launch_status("lm_ep_dispatch_tokens");
 }
 
 extern "C" int lm_ep_receive(void* region, int32_t world, int32_t cap, int32_t hidden_size,

@@ -13,6 +13,7 @@
 // down: warp rows = 16 consecutive output columns of the hidden dimension.
 // Weights are in the tile-contiguous bank layout [N/128][K/64][128][64]: a row's 64-element
 // K chunk is 128 contiguous bytes and the 8 rows a load instruction touches share a tile.
+#include <cstdio>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -806,20 +807,93 @@ __global__ void __launch_bounds__(kPdThreads)
   }
 }
 
-// Counter set of (device, stream): at most kPdCounterSets streams per device use the
-// persistent kernel; further streams take the register-streaming launch pair.
-int pd_counter_set(cudaStream_t s) {
-  static std::mutex mu;
-  static std::vector<std::pair<std::pair<int, cudaStream_t>, int>> reg;
-  static int used[64] = {0};
+// Counter-set registry, per device. A stream keeps its set while it launches the persistent
+// kernel. When every set is taken, a set whose stream's last eager launch has completed (an
+// event recorded after each launch) moves to the new stream; a set launched inside a stream
+// capture stays with its stream for good, since the graph replays it later. Only when no set
+// can be freed does a launch take the register-streaming pair, and that is counted
+// (lm_decode_counter_sets) and reported once on stderr.
+struct PdSetEntry {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t last = nullptr;  // recorded after the stream's latest eager launch
+  bool used = false;
+  bool pinned = false;  // launched during capture: never moves
+  bool launched = false;
+};
+std::mutex g_pd_mu;
+PdSetEntry g_pd_sets[64][kPdCounterSets];
+long long g_pd_recycled = 0;
+long long g_pd_fallbacks = 0;
+
+bool stream_capturing(cudaStream_t s) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &st) != cudaSuccess) return true;  // unknown: treat as captured
+  return st != cudaStreamCaptureStatusNone;
+}
+
+// -1: no set (take the two-kernel path)
+int pd_counter_set(cudaStream_t s, bool capturing) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
-  std::lock_guard<std::mutex> lk(mu);
-  for (const auto& e : reg)
-    if (e.first.first == dev && e.first.second == s) return e.second;
-  if (used[dev] >= kPdCounterSets) return -1;
-  reg.push_back({{dev, s}, used[dev]});
-  return used[dev]++;
+  std::lock_guard<std::mutex> lk(g_pd_mu);
+  PdSetEntry* sets = g_pd_sets[dev];
+  int free_set = -1;
+  for (int i = 0; i < kPdCounterSets; ++i) {
+    if (sets[i].used && sets[i].stream == s) return i;
+    if (!sets[i].used && free_set < 0) free_set = i;
+  }
+  if (free_set < 0 && !capturing) {
+    // a set whose owner's last eager launch has finished can move (no event query while
+    // this stream captures: the query is not allowed there)
+    for (int i = 0; i < kPdCounterSets && free_set < 0; ++i) {
+      if (sets[i].pinned || sets[i].last == nullptr) continue;
+      const cudaError_t q = sets[i].launched ? cudaEventQuery(sets[i].last) : cudaSuccess;
+      if (q == cudaSuccess) {
+        free_set = i;
+        ++g_pd_recycled;
+      } else if (cudaPeekAtLastError() == q) {
+        (void)cudaGetLastError();  // not-ready is a status, not this launch's error
+      }
+    }
+  }
+  if (free_set < 0) {
+    if (g_pd_fallbacks++ == 0)
+      fprintf(stderr,
+              "latchmoe_b200: lm_moe_mlp_decode: all %d counter sets of device %d are held by "
+              "other streams (captured graphs or launches in flight); this and later such "
+              "launches take the two-kernel decode path\n",
+              kPdCounterSets, dev);
+    return -1;
+  }
+  PdSetEntry& e = sets[free_set];
+  if (e.last == nullptr &&
+      cudaEventCreateWithFlags(&e.last, cudaEventDisableTiming) != cudaSuccess) {
+    (void)cudaGetLastError();
+    e.last = nullptr;
+  }
+  e.stream = s;
+  e.used = true;
+  e.pinned = false;
+  e.launched = false;
+  return free_set;
+}
+
+// After a launch with counter set `set` on stream s: pin it (capture) or record its event.
+void pd_counter_set_launched(int set, cudaStream_t s, bool capturing) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+  std::lock_guard<std::mutex> lk(g_pd_mu);
+  PdSetEntry& e = g_pd_sets[dev][set];
+  if (capturing || e.last == nullptr) {
+    e.pinned = true;  // no event to tell when it is free: keep it
+    return;
+  }
+  if (cudaEventRecord(e.last, s) == cudaSuccess) {
+    e.launched = true;
+  } else {
+    (void)cudaGetLastError();
+    e.pinned = true;
+  }
 }
 
 template <int NC, int S>
@@ -830,7 +904,11 @@ int launch_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_p
                              int64_t bank_rows, int H, int I, uint16_t* act, uint16_t* y_perm,
                              int32_t* err_word, int per_sm_cap, cudaStream_t s) {
   const int max_passes = (max_rows + 8 * NC - 1) / (8 * NC);
-  const int set = pd_counter_set(s);
+  const bool capturing = stream_capturing(s);
+  const int set = (num_groups > kPdMaxGroups ||
+                   static_cast<int64_t>(num_groups) * max_passes > kPdMaxSlots)
+                      ? -1
+                      : pd_counter_set(s, capturing);
   if (num_groups > kPdMaxGroups || static_cast<int64_t>(num_groups) * max_passes > kPdMaxSlots ||
       set < 0)
     return launch_decode<NC>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
@@ -888,7 +966,9 @@ int launch_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_p
       launch_dependent(gemv_persistent_kernel<NC, S>, dim3(info[dev].grid), dim3(kPdThreads),
                        pd_smem_bytes<NC, S>(num_groups), s, prm);
   if (e != cudaSuccess) return check_cuda(e, "lm_moe_mlp_decode: persistent");
-  return launch_status("lm_moe_mlp_decode: persistent");
+  rc = launch_status("lm_moe_mlp_decode: persistent");
+  if (rc == LM_OK) pd_counter_set_launched(set, s, capturing);
+  return rc;
 }
 
 // Few pairs (batch 1 or 2): few items, each CTA streaming a long run, so deeper rings (5
@@ -1011,6 +1091,25 @@ extern "C" int lm_moe_mlp_decode_offload(
                                     o13, o2, H, I, act, y_perm, err_word, s);
   return launch_decode_offload<8>(hidden, top_k, row_to_pair, group_offsets, group_begin, ng,
                                   o13, o2, H, I, act, y_perm, err_word, s);
+}
+
+extern "C" int lm_decode_counter_sets(int32_t* in_use, int32_t* pinned, int64_t* recycled,
+                                      int64_t* fallbacks) {
+  int dev = 0;
+  int rc = lm::check_cuda(cudaGetDevice(&dev), "lm_decode_counter_sets");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) return lm::fail(LM_ERR_CUDA, "lm_decode_counter_sets: device");
+  std::lock_guard<std::mutex> lk(lm::g_pd_mu);
+  int u = 0, p = 0;
+  for (const auto& e : lm::g_pd_sets[dev]) {
+    u += e.used;
+    p += e.used && e.pinned;
+  }
+  if (in_use) *in_use = u;
+  if (pinned) *pinned = p;
+  if (recycled) *recycled = lm::g_pd_recycled;
+  if (fallbacks) *fallbacks = lm::g_pd_fallbacks;
+  return LM_OK;
 }
 
 extern "C" int lm_moe_mlp_decode(const uint16_t* hidden, int32_t top_k,

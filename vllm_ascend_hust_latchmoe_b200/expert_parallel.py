@@ -25,8 +25,10 @@ CPU ranks with gloo against the oracle; the default ``ops`` are the CUDA kernels
 Two transports carry the exchange. ``"nccl"``: ``all_to_all_single`` of counts, rows and ids
 and back (the collective library; one host sync for the counts). ``"peer"`` (a
 :class:`PeerExchange`): the library's own kernels over peer memory mapped with CUDA IPC.
-``lm_ep_dispatch`` gathers each pair's row straight into the owner's receive area (no
-permute, no staging buffer), ``lm_ep_receive`` compacts on the owner, and ``lm_ep_combine``
+``lm_ep_dispatch_tokens`` stores each token's row once into every owner that holds any of
+its experts (a token routed to 8 experts on 3 ranks crosses NVLink 3 times, not 8) and each
+pair's owner-local id and receive-row index beside it (``lm_ep_dispatch``, the per-pair form,
+stays selectable); the owner reads its rows through those indices, and ``lm_ep_combine``
 reads every pair's output row from its owner and reduces it in the original top-k order
 (no return collective). With an HBM-resident local store the owner's MLP takes the received
 row count on the device (grouping, gather and combine read it there), so a peer step has no
@@ -116,7 +118,8 @@ class PeerExchange:
     def __init__(self, *, world_size: int, rank: int, max_tokens: int, top_k: int,
                  hidden_size: int, device: torch.device, group=None) -> None:
         self.G, self.rank, self.H = int(world_size), int(rank), int(hidden_size)
-        self.cap = int(max_tokens) * int(top_k)
+        self.max_tokens = int(max_tokens)
+        self.cap = self.max_tokens * int(top_k)
         self.device = torch.device(device)
         uuids = [None] * self.G
         dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(self.device).uuid),
@@ -146,6 +149,10 @@ class PeerExchange:
         self.rows = torch.empty(rows, self.H, dtype=torch.bfloat16, device=self.device)
         self.ids = torch.empty(rows, dtype=torch.int32, device=self.device)
         self.total = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # token-deduplicated dispatch: each token's slot in each owner's area, rows per owner
+        self.tok_slot = torch.empty(self.max_tokens * self.G, dtype=torch.int32,
+                                    device=self.device)
+        self.tok_count = torch.zeros(self.G, dtype=torch.int32, device=self.device)
         self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.epoch = 0
@@ -172,7 +179,7 @@ class ExpertParallelMoE:
     def __init__(self, *, num_experts: int, top_k: int, hidden_size: int, rank: int,
                  world_size: int, ops: EPOps, group: dist.ProcessGroup | None = None,
                  device: torch.device | str = "cuda",
-                 exchange: PeerExchange | None = None) -> None:
+                 exchange: PeerExchange | None = None, dedupe_dispatch: bool = True) -> None:
         if num_experts % world_size != 0:
             raise ValueError(f"{num_experts} experts do not split evenly over {world_size} ranks")
         self.E = int(num_experts)
@@ -188,22 +195,27 @@ class ExpertParallelMoE:
         self.owner = (torch.arange(self.E, dtype=torch.int32) // self.per_rank).to(self.device)
         self._stats = EPStats()
         # peer steps without a host sync: per-step figures accumulate on the device
-        self._dev_rows = torch.zeros(2, dtype=torch.int64, device=self.device)  # recv, local
+        # pairs received, pairs kept local, token rows stored into other ranks
+        self._dev_rows = torch.zeros(3, dtype=torch.int64, device=self.device)
         self._dev_steps = 0
         self._dev_pairs = 0
         self.exchange = exchange
         self.transport = "peer" if exchange is not None else "nccl"
+        # peer transport: a token's row crosses to an owner once, not once per routed pair
+        self.dedupe_dispatch = bool(dedupe_dispatch)
 
     @property
     def stats(self) -> EPStats:
         """Exchange totals (reads the device-side part of peer steps: synchronises)."""
         st = EPStats(**vars(self._stats))
         if self._dev_steps:
-            recv, local_rows = (int(v) for v in self._dev_rows.tolist())
+            recv, local_rows, token_rows = (int(v) for v in self._dev_rows.tolist())
             elt = 2  # bf16 rows
             st.send_rows += self._dev_pairs
             st.recv_rows += recv
-            st.bytes_sent += 2 * (self._dev_pairs - local_rows) * self.H * elt
+            # dispatch stores (token rows, or one row per remote pair) + outputs read back
+            st.bytes_sent += (token_rows + self._dev_pairs - local_rows) * self.H * elt
+            # counted per pair: an upper bound on the dispatch side when tokens are deduplicated
             st.bytes_received += 2 * (recv - local_rows) * self.H * elt
         return st
 
@@ -248,8 +260,13 @@ class ExpertParallelMoE:
         w, ids = self.ops.route(router_logits)
         offsets, p2r, _ = self.ops.group_by_owner(ids, self.owner, self.G)
         x.epoch += 1
-        _lib.ep_dispatch(hidden, ids, self.per_rank, p2r, offsets, self.rank, self.G, x.peers,
-                         x.cap, x.epoch, x.done, x.err)
+        if self.dedupe_dispatch:
+            _lib.ep_dispatch_tokens(hidden, ids, self.per_rank, p2r, offsets, self.rank, self.G,
+                                    x.peers, x.cap, x.epoch, x.tok_slot[: T * self.G],
+                                    x.tok_count, x.done, x.err)
+        else:
+            _lib.ep_dispatch(hidden, ids, self.per_rank, p2r, offsets, self.rank, self.G,
+                             x.peers, x.cap, x.epoch, x.done, x.err)
         gather = self.ops.expert_mlp_gather is not None and x.rows.shape[0] > DECODE_MAX_TOKENS
         no_sync = gather or self.ops.expert_mlp_count is not None
         if gather:
@@ -275,8 +292,13 @@ class ExpertParallelMoE:
                         x.region, x.cap, x.epoch, out, x.err)
         if no_sync:
             # rows received, and rows this rank kept for itself (its own experts' pairs)
+            local = offsets[self.rank + 1] - offsets[self.rank]
             self._dev_rows[0] += x.total[0]
-            self._dev_rows[1] += offsets[self.rank + 1] - offsets[self.rank]
+            self._dev_rows[1] += local
+            if self.dedupe_dispatch:
+                self._dev_rows[2] += x.tok_count.sum() - x.tok_count[self.rank]
+            else:
+                self._dev_rows[2] += T * self.k - local
             self._dev_steps += 1
             self._dev_pairs += T * self.k
         else:
@@ -286,7 +308,12 @@ class ExpertParallelMoE:
             st.send_rows += T * self.k
             st.recv_rows += R
             remote = (T * self.k - counts[self.rank]) * self.H * elt
-            st.bytes_sent += 2 * remote       # rows stored into owners + outputs read back
+            if self.dedupe_dispatch:
+                tc = x.tok_count.tolist()
+                stored = (sum(tc) - tc[self.rank]) * self.H * elt
+            else:
+                stored = remote
+            st.bytes_sent += stored + remote  # rows stored into owners + outputs read back
             st.bytes_received += 2 * (R - int(counts[self.rank])) * self.H * elt
         return out
 
