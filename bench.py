@@ -375,7 +375,8 @@ EP_MIN_COSINE = 0.9999
 def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
     """Qwen3-235B-A22B-shaped layer with the expert bank partitioned over the ranks: 256
     decode tokens per step in total (256 / N per rank). Cases: HBM-resident store with the
-    exchange over NCCL and over peer memory (the library's dispatch / combine kernels), and a
+    exchange over NCCL (exact splits read on the host, or fixed-size blocks sized from the
+    routing with no host read) and over peer memory (the library's dispatch / combine kernels), and a
     pinned-host store staged into half as many slots as the rank owns experts (peer
     exchange). Times are the max over ranks; `hbm_gbs_per_rank` counts the weights of the
     rank's active experts read once per step. After timing, each case's output for the
@@ -401,6 +402,11 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
     ids_all = torch.topk(all_logits, cfg.top_k, dim=1).indices
     owned_ids = ids_all[(ids_all // per) == rank]
     active_owned = int(torch.unique(owned_ids).numel())
+    # fixed NCCL block size: the largest (source, owner) pair count of this routing, plus a
+    # quarter (the capacity an expert-parallel deployment provisions from a profile)
+    block_counts = torch.stack([torch.bincount((ids_all[r * T:(r + 1) * T] // per).reshape(-1),
+                                               minlength=world) for r in range(world)])
+    rows_per_peer = min(T * cfg.top_k, -(-int(block_counts.max()) * 5 // 4))
     expert_bytes = 6 * H * I
     n_chk = min(EP_CHECK_TOKENS, T)
     w_ref, ids_ref = torch_route_reference(logits[:n_chk], cfg.top_k)
@@ -416,7 +422,8 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
     cache.clear()
     out = {"workload": cfg.name, "tokens_per_step": cfg.tokens, "tokens_per_rank": T,
            "experts_per_rank": per, "active_experts_rank": active_owned}
-    cases = (("resident_nccl", True, per, "nccl"), ("resident_peer", True, per, "peer"),
+    cases = (("resident_nccl", True, per, "nccl"), ("resident_nccl_fixed", True, per, "nccl_fixed"),
+             ("resident_peer", True, per, "peer"),
              ("offloaded_peer", False, max(1, per // 2), "peer"))
     for name, on_dev, slots, transport in cases:
         local = build_rank_layer(w13_owned=w13 if on_dev else w13.cpu(),
@@ -430,7 +437,9 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
         ep = ExpertParallelMoE(num_experts=cfg.num_experts, top_k=cfg.top_k, hidden_size=H,
                                rank=rank, world_size=world, device=dev, exchange=exchange,
                                ops=cuda_ops(local, num_experts=cfg.num_experts, top_k=cfg.top_k,
-                                            max_tokens=T))
+                                            max_tokens=T),
+                               nccl_rows_per_peer=rows_per_peer
+                               if transport == "nccl_fixed" else None)
         for _ in range(3):
             ep.forward(hidden, logits)
         torch.cuda.synchronize()
@@ -470,6 +479,8 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
                      "hbm_gbs_per_rank": active_owned * expert_bytes / (t_ms / 1e3) / 1e9,
                      "slots_per_rank": slots if not on_dev else None,
                      "h2d_bytes_rank0_step": int(h2d), "parity": parity}
+        if transport == "nccl_fixed":
+            out[name]["rows_per_peer"] = rows_per_peer
         if exchange is not None:
             exchange.close()
         del ep, local
@@ -732,19 +743,53 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
                           "area, lm_moe_mlp_prefill) on the rows it received",
                 "ms_per_call": mlp_ms, "flops_per_call": flops, "rows_rank0": rows_recv}
 
-    # e2e: the same step from pinned host buffers (inputs in, output out, every step)
+    # e2e: the same step from pinned host buffers (inputs in, output out, every step). The
+    # copies run on two copy streams, double-buffered: step i+1's inputs go up and step i-1's
+    # output comes down while step i computes (what a serving loop does); the timed region
+    # opens before the first upload and closes after the last download.
     h_host = hidden_cpu.pin_memory()
     lg_host = placed_cpu.pin_memory()
-    out_host = torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True)
-    h_dev, lg_dev = torch.empty_like(hidden), torch.empty_like(logits)
+    out_host = [torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+    h_dev = [torch.empty_like(hidden) for _ in range(2)]
+    lg_dev = [torch.empty_like(logits) for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    c_in, c_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    buf_free = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(i):
+        j = i % 2
+        if i >= 2:
+            c_in.wait_event(buf_free[j])  # step i-2 has finished reading buffer j
+        with torch.cuda.stream(c_in):
+            h_dev[j].copy_(h_host, non_blocking=True)
+            lg_dev[j].copy_(lg_host, non_blocking=True)
+        in_ready[j].record(c_in)
+
+    def e2e_run(n):
+        c_in.wait_event(a)
+        upload(0)
+        for i in range(n):
+            j = i % 2
+            if i + 1 < n:
+                upload(i + 1)
+            comp.wait_event(in_ready[j])
+            o = ep.forward(h_dev[j], lg_dev[j])
+            buf_free[j].record(comp)
+            c_out.wait_stream(comp)
+            with torch.cuda.stream(c_out):
+                out_host[j].copy_(o, non_blocking=True)
+            o.record_stream(c_out)
+        comp.wait_stream(c_out)
+        comp.wait_stream(c_in)
+
     e2e_steps = max(3, min(args.steps, 10))
+    a.record()
+    e2e_run(3)  # warm-up of the pipelined loop
+    torch.cuda.synchronize()
     barrier()
     a.record()
-    for _ in range(e2e_steps):
-        h_dev.copy_(h_host, non_blocking=True)
-        lg_dev.copy_(lg_host, non_blocking=True)
-        o = ep.forward(h_dev, lg_dev)
-        out_host.copy_(o, non_blocking=True)
+    e2e_run(e2e_steps)
     b.record()
     barrier()
     ep.check_exchange_errors()
@@ -753,8 +798,9 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     e2e_ms = float(e_ms.item()) / e2e_steps
     e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": int(h_host.numel() * 2 + lg_host.numel() * 4),
-           "d2h_bytes_per_step": int(out_host.numel() * 2), "ms_per_step": e2e_ms,
-           "path": "ExpertParallelMoE.forward per rank from pinned host buffers"}
+           "d2h_bytes_per_step": int(out_host[0].numel() * 2), "ms_per_step": e2e_ms,
+           "path": "ExpertParallelMoE.forward per rank from pinned host buffers; uploads and "
+                   "downloads on two copy streams, overlapped with the neighbouring steps"}
     ep_info = {"placement": "load-balanced (profiled routing sample; gate columns and expert "
                             "bank permuted at load time)",
                "experts_per_rank": per, "rows_received_per_rank": rows_all,

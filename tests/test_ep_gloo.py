@@ -68,7 +68,7 @@ def _oracle_ops(w13, w2, rank, per_rank):
     return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine)
 
 
-def _worker(rank, world, port, q, placed=False):
+def _worker(rank, world, port, q, placed=False, rows_per_peer=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -87,12 +87,25 @@ def _worker(rank, world, port, q, placed=False):
         else:
             ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
                                    world_size=world, ops=_oracle_ops(w13, w2, rank, E // world),
-                                   device="cpu")
+                                   device="cpu", nccl_rows_per_peer=rows_per_peer)
             out = ep.forward(_bf16(hidden), torch.from_numpy(logits))
+            if rows_per_peer is not None:
+                try:
+                    ep.check_exchange_errors()
+                    overflow = False
+                except RuntimeError as exc:
+                    overflow = "nccl_rows_per_peer" in str(exc)
+                q.put((rank, overflow, ep.stats.send_rows, ep.stats.recv_rows,
+                       list(ep.owned_experts())))
+                if overflow:
+                    return
         wb, _, ids = orouter.route(logits, K)
         ref = omlp.moe_layer(hidden, ids, wb, w13, w2)
         m = omlp.compare(bf16_bits_to_f32(_bits(out)), ref)
-        q.put((rank, m, ep.stats.send_rows, ep.stats.recv_rows, list(ep.owned_experts())))
+        if rows_per_peer is None:
+            q.put((rank, m, ep.stats.send_rows, ep.stats.recv_rows, list(ep.owned_experts())))
+        else:
+            q.put((rank, m, 0, 0, []))
     finally:
         dist.destroy_process_group()
 
@@ -121,6 +134,35 @@ def test_ep_exchange_matches_single_process_oracle(world, placed):
     assert sum(r[2] for r in results) == sum(r[3] for r in results) == world * T * K
     for rank, m, *_ in results:
         assert m["max_rel_err"] <= 1e-2 and m["cosine"] >= 0.9999, (rank, m)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_fixed_splits_match_oracle_and_report_overflow(world):
+    """NCCL exchange with fixed-size blocks (no host-read counts): with room for every pair the
+    output equals the oracle; with blocks smaller than some owner's share the step reports the
+    overflow instead of passing it silently."""
+    ctx = mp.get_context("spawn")
+    for rows, expect_overflow in ((T * K, False), (3, True)):
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, world, port, q, False, rows))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        results = [q.get(timeout=120) for _ in range(2 * world if not expect_overflow else world)]
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+        flags = [r for r in results if isinstance(r[1], bool)]
+        assert len(flags) == world
+        if expect_overflow:
+            assert any(f[1] for f in flags)
+            continue
+        assert not any(f[1] for f in flags)
+        assert sum(f[3] for f in flags) == world * world * rows  # fixed blocks
+        for rank, m, *_ in results:
+            if isinstance(m, dict):
+                assert m["max_rel_err"] <= 1e-2 and m["cosine"] >= 0.9999, (rank, m)
 
 
 def test_balanced_placement_is_a_permutation_with_even_load():

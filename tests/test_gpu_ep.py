@@ -58,6 +58,7 @@ def _worker(rank, world, port, store_on_device, transport, q):
         ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
                                world_size=world, device=dev, exchange=exchange,
                                dedupe_dispatch=transport == "peer",
+                               nccl_rows_per_peer=T * K if transport == "nccl_fixed" else None,
                                ops=cuda_ops(local, num_experts=E, top_k=K, max_tokens=T))
         # a call with other routing first: the checked call reuses every area and flag
         ep.forward(syn.make_hidden(cfg, seed=30 + rank).to(dev),
@@ -85,7 +86,8 @@ def _worker(rank, world, port, store_on_device, transport, q):
 
 
 # "peer": token-deduplicated dispatch; "peer_pairs": one row per routed pair
-@pytest.mark.parametrize("transport", ["nccl", "peer", "peer_pairs"])
+# "nccl_fixed": fixed-size all-to-all blocks, counts never read on the host
+@pytest.mark.parametrize("transport", ["nccl", "nccl_fixed", "peer", "peer_pairs"])
 @pytest.mark.parametrize("store_on_device", [False, True])
 def test_ep_two_gpus_matches_oracle(store_on_device, transport):
     if torch.cuda.device_count() < 2:

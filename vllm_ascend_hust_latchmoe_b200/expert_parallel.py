@@ -179,7 +179,8 @@ class ExpertParallelMoE:
     def __init__(self, *, num_experts: int, top_k: int, hidden_size: int, rank: int,
                  world_size: int, ops: EPOps, group: dist.ProcessGroup | None = None,
                  device: torch.device | str = "cuda",
-                 exchange: PeerExchange | None = None, dedupe_dispatch: bool = True) -> None:
+                 exchange: PeerExchange | None = None, dedupe_dispatch: bool = True,
+                 nccl_rows_per_peer: int | None = None) -> None:
         if num_experts % world_size != 0:
             raise ValueError(f"{num_experts} experts do not split evenly over {world_size} ranks")
         self.E = int(num_experts)
@@ -203,6 +204,12 @@ class ExpertParallelMoE:
         self.transport = "peer" if exchange is not None else "nccl"
         # peer transport: a token's row crosses to an owner once, not once per routed pair
         self.dedupe_dispatch = bool(dedupe_dispatch)
+        # nccl transport with fixed splits: every (source, owner) block holds this many rows,
+        # so the all-to-alls need no host-known counts (None: exact splits, read on the host)
+        self.nccl_rows_per_peer = None if nccl_rows_per_peer is None else int(nccl_rows_per_peer)
+        if self.nccl_rows_per_peer is not None and self.nccl_rows_per_peer <= 0:
+            raise ValueError("nccl_rows_per_peer must be positive")
+        self._overflow = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     @property
     def stats(self) -> EPStats:
@@ -225,6 +232,8 @@ class ExpertParallelMoE:
     def forward(self, hidden: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         if self.exchange is not None:
             return self._forward_peer(hidden, router_logits)
+        if self.nccl_rows_per_peer is not None:
+            return self._forward_fixed(hidden, router_logits)
         T = int(hidden.shape[0])
         w, ids = self.ops.route(router_logits)
         offsets, p2r, r2p = self.ops.group_by_owner(ids, self.owner, self.G)
@@ -251,6 +260,87 @@ class ExpertParallelMoE:
         st.bytes_sent += (P - s_split[self.rank]) * self.H * elt * 2
         st.bytes_received += (R - r_split[self.rank]) * self.H * elt * 2
         return self.ops.combine(back, p2r[:P], w)
+
+    def _forward_fixed(self, hidden: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        """NCCL exchange with fixed splits: block (source, owner) of both all-to-alls holds
+        ``C = nccl_rows_per_peer`` rows (the first ``count`` real, the rest padding with local
+        id -1), so counts travel as a device tensor beside the rows and no step reads them on
+        the host (with the gather MLP). Pairs beyond C for one owner are not sent: they add
+        nothing to the output and raise the overflow flag that :meth:`check_exchange_errors`
+        reports."""
+        T = int(hidden.shape[0])
+        G, C, k, dev = self.G, self.nccl_rows_per_peer, self.k, hidden.device
+        P = T * k
+        w, ids = self.ops.route(router_logits)
+        offsets, p2r, r2p = self.ops.group_by_owner(ids, self.owner, G)
+        off = offsets.long()
+        counts = off[1:] - off[:-1]
+        self._overflow |= (counts > C).any().to(torch.int32)
+        # grouped row r -> block slot q = owner * C + position (G * C: not sent)
+        r = torch.arange(P, dtype=torch.int64, device=dev)
+        o_r = torch.searchsorted(off[1:].contiguous(), r, right=True)
+        pos = r - off[o_r]
+        q_r = torch.where(pos < C, o_r * C + pos, torch.full_like(r, G * C))
+        pair_of_slot = torch.zeros(G * C + 1, dtype=torch.int32, device=dev)
+        pair_of_slot.index_copy_(0, q_r, r2p[:P].to(torch.int32))
+        send_ids = torch.full((G * C + 1,), -1, dtype=torch.int32, device=dev)
+        local_ids = (ids.reshape(-1).long().index_select(0, r2p[:P].long())
+                     % self.per_rank).to(torch.int32)
+        send_ids.index_copy_(0, q_r, local_ids)
+        send_rows = self.ops.gather_rows(hidden, pair_of_slot[:G * C], k)
+        sent = torch.minimum(counts, torch.full_like(counts, C))
+        recv_counts = torch.empty_like(sent)
+        dist.all_to_all_single(recv_counts, sent, group=self.group)
+        recv_rows = torch.empty(G * C, self.H, dtype=hidden.dtype, device=dev)
+        recv_ids = torch.empty(G * C, dtype=torch.int32, device=dev)
+        dist.all_to_all_single(recv_rows, send_rows, group=self.group)
+        dist.all_to_all_single(recv_ids, send_ids[:G * C].contiguous(), group=self.group)
+        # received blocks compacted in source order: slot list, ids, count (all on the device)
+        q = torch.arange(G * C, dtype=torch.int64, device=dev)
+        src, j = q // C, q % C
+        prefix = torch.cumsum(recv_counts, 0) - recv_counts
+        valid = j < recv_counts[src]
+        dest = torch.where(valid, prefix[src] + j, torch.full_like(q, G * C))
+        slots = torch.zeros(G * C + 1, dtype=torch.int32, device=dev)
+        slots.index_copy_(0, dest, q.to(torch.int32))
+        cids = torch.zeros(G * C + 1, dtype=torch.int32, device=dev)
+        cids.index_copy_(0, dest, recv_ids)
+        total = recv_counts.sum().to(torch.int32).reshape(1)
+        n = G * C
+        if self.ops.expert_mlp_gather is not None and n > DECODE_MAX_TOKENS:
+            # rows gathered straight from the received blocks; outputs stay grouped
+            out_rows = torch.empty(n, self.H, dtype=hidden.dtype, device=dev)
+            pair_rows = torch.empty(n, dtype=torch.int32, device=dev)
+            self.ops.expert_mlp_gather(recv_rows, slots[:n], cids[:n], total, pair_rows,
+                                       out_rows)
+        elif self.ops.expert_mlp_count is not None:
+            out_rows = torch.empty(n, self.H, dtype=hidden.dtype, device=dev)
+            self.ops.expert_mlp_count(recv_rows.index_select(0, slots[:n].long()), cids[:n],
+                                      total, out_rows)
+            pair_rows = torch.arange(n, dtype=torch.int32, device=dev)
+        else:
+            R = int(total.item())  # host-sized owner MLP (the injectable CPU steps)
+            out_rows = torch.zeros(n, self.H, dtype=hidden.dtype, device=dev)
+            if R:
+                out_rows[:R] = self.ops.expert_mlp(
+                    recv_rows.index_select(0, slots[:R].long()), cids[:R])
+            pair_rows = torch.arange(n, dtype=torch.int32, device=dev)
+        # block slot q's output row (padding slots send row 0, which nobody reads)
+        d = torch.where(valid, dest, torch.zeros_like(dest))
+        back_idx = torch.where(valid, pair_rows.long().index_select(0, d), torch.zeros_like(q))
+        back_send = out_rows.index_select(0, back_idx)
+        back = torch.empty(G * C, self.H, dtype=hidden.dtype, device=dev)
+        dist.all_to_all_single(back, back_send, group=self.group)
+        # pair -> its output row in the returned blocks (-1: not sent, contributes nothing)
+        q_pair = torch.where(q_r < G * C, q_r, torch.full_like(q_r, -1)).index_select(
+            0, p2r[:P].long()).to(torch.int32)
+        st = self._stats
+        elt = hidden.element_size()
+        st.send_rows += P
+        st.recv_rows += G * C  # block rows, padding included
+        st.bytes_sent += 2 * (G - 1) * C * self.H * elt
+        st.bytes_received += 2 * (G - 1) * C * self.H * elt
+        return self.ops.combine(back, q_pair, w)
 
     def _forward_peer(self, hidden: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         x = self.exchange
@@ -318,6 +408,10 @@ class ExpertParallelMoE:
         return out
 
     def check_exchange_errors(self) -> None:
+        if self.nccl_rows_per_peer is not None and int(self._overflow.item()):
+            raise RuntimeError(
+                f"expert-parallel rank {self.rank}: more than {self.nccl_rows_per_peer} routed "
+                "pairs for one owner in a step (fixed NCCL splits); raise nccl_rows_per_peer")
         if self.exchange is not None:
             _lib.raise_on_device_error(self.exchange.err, f"expert-parallel rank {self.rank}")
 
