@@ -638,6 +638,7 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     step from host buffers (``e2e``)."""
     import torch
 
+    from vllm_ascend_hust_latchmoe_b200 import _lib
     from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
     from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE, PeerExchange,
                                                                 balanced_expert_placement,
@@ -686,8 +687,8 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     value = world * T * args.steps / (ms_total / 1e3)
     nvlink = (ep.stats.bytes_sent - sent0) / args.steps
     # per step: route, owner grouping, dispatch (token slots + stores when deduplicated),
-    # receive (wait + index), the owner MLP's grouping / gather / grouped MLP, signal, combine
-    # (wait + reduce)
+    # receive (wait + index), the owner MLP's grouping / row pointers / gather / grouped MLP,
+    # signal, combine (wait + reduce)
     dispatch_launches = 2 if ep.dedupe_dispatch else 1
     launches_per_step = (1 + 1 + dispatch_launches + 2
                          + (local.kernel_launches - launches0) // args.steps + 1 + 2)
@@ -716,9 +717,16 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # the gather path the step runs (every rank's combine of the last step has completed: the
     # all-reduce above follows it in each rank's stream; the rewrite stores the same values)
+    def row_ptrs(row_to_pair, count, ptrs):
+        _lib.ep_output_row_ptrs(x.region, world, x.cap, H, rank, x.peers, row_to_pair, count,
+                                ptrs.shape[0], ptrs, x.err)
+
     def owner_mlp():
-        local.mlp_rows_gather_count(x.recv_rows, x.slots, x.ids, x.total, x.pair_rows,
-                                    x.out_rows)
+        if ep.push_outputs:  # outputs stored into the sources' areas (same values again)
+            local.mlp_rows_gather_push(x.recv_rows, x.slots, x.ids, x.total, row_ptrs)
+        else:
+            local.mlp_rows_gather_count(x.recv_rows, x.slots, x.ids, x.total, x.pair_rows,
+                                        x.out_rows)
 
     for _ in range(3):
         owner_mlp()
@@ -740,6 +748,10 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
                 "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"],
                 "peak_source": peaks["source"], "traffic": None,
                 "kernel": "rank 0's grouped MLP (owner side: grouping, gather from the receive "
+                          "area, tcgen05 MLP whose down-GEMM epilogue stores each output row "
+                          "into its source's memory over NVLink) on the rows it received"
+                          if ep.push_outputs else
+                          "rank 0's grouped MLP (owner side: grouping, gather from the receive "
                           "area, lm_moe_mlp_prefill) on the rows it received",
                 "ms_per_call": mlp_ms, "flops_per_call": flops, "rows_rank0": rows_recv}
 
@@ -1198,10 +1210,12 @@ def main() -> None:
         rep_dev = dec.run(shape.max_new, warmup=8)
         for lay in dec.moe:
             lay.check_device_errors("bench tpot (device staging)")
+        share_dev = dec.moe_share()
         del dec
         torch.cuda.empty_cache()
         dec = SyntheticMoEDecoder(shape, offloaded_layers=[], device=dev, seed=rank)
         rep_res = dec.run(shape.max_new, warmup=8)
+        share_res = dec.moe_share()
         del dec
         torch.cuda.empty_cache()
         tpot = {"workload": "qwen3-30b-a3b-shaped 48-layer decoder, batch 1, 1024-token context, "
@@ -1219,9 +1233,14 @@ def main() -> None:
                         rep_dev.h2d_bytes_per_step / (rep_dev.tpot_ms_p50 / 1e3) / 1e9,
                     "slot_hit_rate": rep_dev.slot_hit_rate, "graphs_per_token": rep_dev.graphs,
                     "staging": "slot decision on the GPU (lm_slot_plan); misses read over "
-                               "PCIe by the MLP and written through into their slots"},
+                               "PCIe by the MLP and written through into their slots",
+                    "moe_share": share_dev},
                 "all_resident_tpot_ms_p50": rep_res.tpot_ms_p50,
                 "all_resident_tpot_ms_p95": rep_res.tpot_ms_p95,
+                "all_resident_moe_share": share_res,
+                "moe_share_method": "each layer's attention and MoE piece captured as its own "
+                                    "graph, replayed in token order with an event after each; "
+                                    "MoE piece times summed per token (median over 32 tokens)",
                 "data": "random-init weights and KV; synthetic routing"}
 
     # ----------------------------------------------------------------- e2e (host buffers)

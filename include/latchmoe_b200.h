@@ -219,6 +219,20 @@ int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
                        uint16_t* act, uint16_t* y_perm, int32_t* err_word, void* stream);
 
 /*
+ * lm_moe_mlp_prefill_rows: the same MLP with the down GEMM's output row r stored at
+ * y_row_ptrs[r] (a device array of total_rows 16-byte-aligned row pointers, which may address
+ * another GPU's memory mapped into this process) instead of y_perm[r]. The kernel ends with a
+ * system-scope fence, so a flag raised by a later kernel in the stream orders those stores.
+ */
+int lm_moe_mlp_prefill_rows(const uint16_t* x_perm, int64_t total_rows,
+                            const int32_t* group_offsets, const int32_t* group_bank_row,
+                            int32_t group_begin, int32_t group_end,
+                            const uint16_t* w13_bank, const uint16_t* w2_bank, int64_t bank_rows,
+                            int32_t hidden_size, int32_t intermediate_size,
+                            uint16_t* act, uint16_t* const* y_row_ptrs, int32_t* err_word,
+                            void* stream);
+
+/*
  * K8 weighted combine in the original flattened top-k pair order:
  *   out[t, :] = bf16( sum_{j<k} f32(topk_weights[t, j]) * f32(y_perm[pair_to_row[t*k+j], :]) )
  * accumulated in fp32 in j order (deterministic, no atomics). pair_to_row < 0 contributes 0.
@@ -339,6 +353,10 @@ int lm_moe_mlp_decode_offload(const uint16_t* hidden, int32_t top_k,
  *    and ids in received order; the owner gathers its rows from the receive area itself,
  *    region + lm_ep_recv_rows_offset, with lm_permute_rows_gather_count, and writes the output
  *    row of received pair d to the int32 table at region + lm_ep_pair_rows_offset)
+ *   (or the owner pushes: lm_ep_output_row_ptrs turns the grouped rows' received pairs
+ *    (row_to_pair, *count_dev rows) into row pointers into each source's output area, block
+ *    rank, at the pair's position, and lm_moe_mlp_prefill_rows stores the outputs there;
+ *    the sources then combine with lm_ep_combine_local, which reads only their own region)
  *   lm_ep_signal_outputs  tells every source the outputs are there.
  *   lm_ep_combine       waits for every owner (bounded), reads each pair's output row from its
  *                       owner (row = the owner's pair-row table entry; lm_ep_receive writes
@@ -381,6 +399,16 @@ int lm_ep_receive_index(void* region, int32_t world, int32_t cap, int32_t hidden
                         int32_t* err_word, void* stream);
 int64_t lm_ep_recv_rows_offset(int32_t world, int32_t cap, int32_t hidden_size);
 int64_t lm_ep_pair_rows_offset(int32_t world, int32_t cap, int32_t hidden_size);
+int lm_ep_output_row_ptrs(void* region, int32_t world, int32_t cap, int32_t hidden_size,
+                          int32_t rank, void* const* peer_regions, const int32_t* row_to_pair,
+                          const int32_t* count_dev, int32_t max_rows, uint16_t** row_ptrs_out,
+                          int32_t* err_word, void* stream);
+int lm_ep_combine_local(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,
+                        int64_t num_tokens, int32_t top_k, int32_t hidden_size,
+                        int32_t experts_per_rank, const int32_t* pair_to_row,
+                        const int32_t* send_offsets, int32_t rank, int32_t world,
+                        void* const* peer_regions, void* local_region, int32_t cap,
+                        int64_t epoch, uint16_t* out, int32_t* err_word, void* stream);
 int lm_ep_signal_outputs(void* const* peer_regions, int32_t rank, int32_t world, int32_t cap,
                          int32_t hidden_size, int64_t epoch, void* stream);
 int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,

@@ -57,7 +57,8 @@ def _worker(rank, world, port, store_on_device, transport, q):
                                     hidden_size=H, device=dev)
         ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
                                world_size=world, device=dev, exchange=exchange,
-                               dedupe_dispatch=transport == "peer",
+                               dedupe_dispatch=transport in ("peer", "peer_pull"),
+                               push_outputs=transport == "peer",
                                nccl_rows_per_peer=T * K if transport == "nccl_fixed" else None,
                                ops=cuda_ops(local, num_experts=E, top_k=K, max_tokens=T))
         # a call with other routing first: the checked call reuses every area and flag
@@ -85,9 +86,11 @@ def _worker(rank, world, port, store_on_device, transport, q):
         dist.destroy_process_group()
 
 
-# "peer": token-deduplicated dispatch; "peer_pairs": one row per routed pair
+# "peer": token-deduplicated dispatch, owners push outputs into the sources' memory;
+# "peer_pull": the same dispatch, sources read the outputs from the owners;
+# "peer_pairs": one row per routed pair, outputs read from the owners
 # "nccl_fixed": fixed-size all-to-all blocks, counts never read on the host
-@pytest.mark.parametrize("transport", ["nccl", "nccl_fixed", "peer", "peer_pairs"])
+@pytest.mark.parametrize("transport", ["nccl", "nccl_fixed", "peer", "peer_pull", "peer_pairs"])
 @pytest.mark.parametrize("store_on_device", [False, True])
 def test_ep_two_gpus_matches_oracle(store_on_device, transport):
     if torch.cuda.device_count() < 2:

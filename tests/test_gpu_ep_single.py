@@ -91,12 +91,14 @@ def test_single_rank_exchange_round_trip_and_timeout(cuda):
         _lib.ep_region_free(c["region"])
 
 
-@pytest.mark.parametrize("dedupe", [False, True])
-def test_single_rank_gather_path_matches_oracle(cuda, dedupe):
+@pytest.mark.parametrize("dedupe,push", [(False, False), (True, False), (True, True)])
+def test_single_rank_gather_path_matches_oracle(cuda, dedupe, push):
     """The owner path without row copies: index-only receive, the grouped MLP gathering its
     rows from the receive area, outputs left in grouped order with the pair-row table, and the
     combine reading through that table -- against the oracle layer, twice in a row. With
-    ``dedupe`` each token row is stored once and all its pairs read that one row."""
+    ``dedupe`` each token row is stored once and all its pairs read that one row; with
+    ``push`` the MLP stores every output row into the source's own area (row pointers from
+    ``lm_ep_output_row_ptrs``) and the combine reads only that area."""
     from oracle import router as orouter
     from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
     from vllm_ascend_hust_latchmoe_b200.expert_parallel import build_rank_layer
@@ -145,9 +147,18 @@ def test_single_rank_gather_path_matches_oracle(cuda, dedupe):
             else:
                 _lib.ep_dispatch(h, ids, E2, p2r, offsets, 0, 1, peers, cap, epoch, done, err)
             _lib.ep_receive_index(region, 1, cap, H2, epoch, slots, rids, total, err)
-            layer.mlp_rows_gather_count(recv_rows, slots, rids, total, pair_rows, out_rows)
+            if push:
+                def row_ptrs(row_to_pair, count, ptrs):
+                    _lib.ep_output_row_ptrs(region, 1, cap, H2, 0, peers, row_to_pair, count,
+                                            ptrs.shape[0], ptrs, err)
+
+                out_rows.fill_(7.0)  # every pair's row must be rewritten
+                layer.mlp_rows_gather_push(recv_rows, slots, rids, total, row_ptrs)
+            else:
+                layer.mlp_rows_gather_count(recv_rows, slots, rids, total, pair_rows, out_rows)
             _lib.ep_signal_outputs(peers, 0, 1, cap, H2, epoch)
-            _lib.ep_combine(ids, w, E2, p2r, offsets, 0, 1, peers, region, cap, epoch, out, err)
+            combine = _lib.ep_combine_local if push else _lib.ep_combine
+            combine(ids, w, E2, p2r, offsets, 0, 1, peers, region, cap, epoch, out, err)
             torch.cuda.synchronize()
             assert int(err.item()) == 0 and int(total.item()) == cap
             if dedupe:  # the token rows sit once each at the head of the receive area

@@ -69,6 +69,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lm_ep_recv_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_ep_pair_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_permute_rows_gather_count": (ctypes.c_int, [_P, _I32, _P, _P, _I64, _P, _P, _P]),
+    "lm_ep_output_row_ptrs": (
+        ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P]),
+    "lm_ep_combine_local": (
+        ctypes.c_int,
+        [_P, _P, _I64, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _P, _I32, _I64, _P, _P, _P],
+    ),
     "lm_ep_combine": (
         ctypes.c_int,
         [_P, _P, _I64, _I32, _I32, _I32, _P, _P, _I32, _I32, _P, _P, _I32, _I64, _P, _P, _P],
@@ -101,6 +107,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _I32, _P, _P, _P, _I32, _I32, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
     ),
     "lm_moe_mlp_prefill": (
+        ctypes.c_int,
+        [_P, _I64, _P, _P, _I32, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
+    ),
+    "lm_moe_mlp_prefill_rows": (
         ctypes.c_int,
         [_P, _I64, _P, _P, _I32, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
     ),
@@ -357,6 +367,22 @@ def moe_mlp_prefill(x_perm, total_rows, group_offsets, group_bank_row, group_beg
     )
 
 
+def moe_mlp_prefill_rows(x_perm, total_rows, group_offsets, group_bank_row, group_begin,
+                         group_end, w13_bank, w2_bank, act, y_row_ptrs, err_word=None) -> None:
+    """The prefill MLP with output row r stored at the address ``y_row_ptrs[r]`` (int64)."""
+    _require_cuda(x_perm, group_offsets, group_bank_row, w13_bank, w2_bank, act, y_row_ptrs)
+    H = x_perm.shape[-1]
+    I = w2_bank.shape[-1]
+    _check(
+        "lm_moe_mlp_prefill_rows",
+        lib().lm_moe_mlp_prefill_rows(
+            _ptr(x_perm), int(total_rows), _ptr(group_offsets), _ptr(group_bank_row),
+            int(group_begin), int(group_end), _ptr(w13_bank), _ptr(w2_bank),
+            w13_bank.shape[0], H, I, _ptr(act), _ptr(y_row_ptrs), _ptr(err_word), _stream(),
+        ),
+    )
+
+
 def ep_region_bytes(world: int, cap: int, hidden: int) -> int:
     return int(lib().lm_ep_region_bytes(int(world), int(cap), int(hidden)))
 
@@ -448,6 +474,26 @@ def ep_signal_outputs(peer_regions, rank, world, cap, hidden_size, epoch) -> Non
     _check("lm_ep_signal_outputs", lib().lm_ep_signal_outputs(
         _ptr(peer_regions), int(rank), int(world), int(cap), int(hidden_size), int(epoch),
         _stream()))
+
+
+def ep_output_row_ptrs(region: int, world, cap, hidden_size, rank, peer_regions, row_to_pair,
+                       count_dev, max_rows, row_ptrs_out, err_word=None) -> None:
+    """Row pointers (int64 tensor) of an owner's grouped output rows in the sources' areas."""
+    _check("lm_ep_output_row_ptrs", lib().lm_ep_output_row_ptrs(
+        region, int(world), int(cap), int(hidden_size), int(rank), _ptr(peer_regions),
+        _ptr(row_to_pair), _ptr(count_dev), int(max_rows), _ptr(row_ptrs_out), _ptr(err_word),
+        _stream()))
+
+
+def ep_combine_local(topk_ids, topk_weights_bf16, experts_per_rank, pair_to_row, send_offsets,
+                     rank, world, peer_regions, local_region: int, cap, epoch, out,
+                     err_word=None) -> None:
+    """Combine of outputs the owners pushed into this rank's own output area."""
+    T, k = topk_ids.shape
+    _check("lm_ep_combine_local", lib().lm_ep_combine_local(
+        _ptr(topk_ids), _ptr(topk_weights_bf16), T, k, out.shape[-1], int(experts_per_rank),
+        _ptr(pair_to_row), _ptr(send_offsets), int(rank), int(world), _ptr(peer_regions),
+        local_region, int(cap), int(epoch), _ptr(out), _ptr(err_word), _stream()))
 
 
 def ep_combine(topk_ids, topk_weights_bf16, experts_per_rank, pair_to_row, send_offsets, rank,

@@ -53,8 +53,8 @@ void layout(int G, int cap, int H, int64_t* off) {
   o = align256(o + 4ll * G * cap);
   off[F_RECV_ROWS] = o;
   o = align256(o + 2ll * G * cap * H);
-  off[F_OUT_ROWS] = o;
-  o = align256(o + 2ll * G * cap * H);
+  off[F_OUT_ROWS] = o;  // + one spare row at G * cap that no one reads
+  o = align256(o + 2ll * (static_cast<int64_t>(G) * cap + 1) * H);
   off[F_TOTAL] = o;
 }
 
@@ -328,6 +328,38 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Output row pointers for an owner that pushes its MLP outputs to the sources: grouped row r
+// holds received pair d = row_to_pair[r], which source s sent at position pos (d = prefix[s]
+// + pos); its output goes to source s's region, row rank * cap + pos of the output area. A
+// row whose pair is out of range points at this region's spare row instead (and is recorded).
+__global__ void __launch_bounds__(256)
+    ep_output_ptrs_kernel(void* region, void* const* __restrict__ peers, Layout L, int G,
+                          int cap, int H, int rank, const int32_t* __restrict__ row_to_pair,
+                          const int32_t* __restrict__ count_dev, int max_rows,
+                          uint16_t** __restrict__ ptrs, int32_t* __restrict__ err_word) {
+  const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
+  uint16_t* spare = field<uint16_t>(region, L, F_OUT_ROWS) + static_cast<int64_t>(G) * cap * H;
+  int n = *count_dev;
+  if (n > max_rows) n = max_rows;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x) {
+    const int d = row_to_pair[r];
+    uint16_t* dst = spare;
+    if (d >= 0 && d < prefix[G]) {
+      int src = 0;
+      while (src + 1 < G && prefix[src + 1] <= d) ++src;
+      const int pos = d - prefix[src];
+      if (pos < cap)
+        dst = field<uint16_t>(peers[src], L, F_OUT_ROWS) +
+              (static_cast<int64_t>(rank) * cap + pos) * H;
+      else
+        record_error(err_word, LM_DEVERR_BAD_GROUP);
+    } else {
+      record_error(err_word, LM_DEVERR_BAD_GROUP);
+    }
+    ptrs[r] = dst;
+  }
+}
+
 __global__ void ep_signal_kernel(void* const* __restrict__ peers, Layout L, int rank, int G,
                                  long long epoch) {
   __threadfence_system();
@@ -353,7 +385,7 @@ __global__ void ep_combine_kernel(const int32_t* __restrict__ ids,
                                   const int32_t* __restrict__ send_offsets, int rank, int G,
                                   void* const* __restrict__ peers, const void* local_region,
                                   Layout L, int cap, uint16_t* __restrict__ out,
-                                  int32_t* __restrict__ err_word) {
+                                  int32_t* __restrict__ err_word, int pushed) {
   __shared__ const uint16_t* s_src[32];
   __shared__ float s_w[32];
   const int64_t t = blockIdx.x;
@@ -369,6 +401,10 @@ __global__ void ep_combine_kernel(const int32_t* __restrict__ ids,
       const int pos = pair_to_row[p] - send_offsets[o];
       if (pos < 0 || pos >= cap) {
         record_error(err_word, LM_DEVERR_BAD_GROUP);
+      } else if (pushed) {
+        // the owner stored the output into this rank's own area, block o
+        src = field<uint16_t>(const_cast<void*>(local_region), L, F_OUT_ROWS) +
+              (static_cast<int64_t>(o) * cap + pos) * H;
       } else {
         const int32_t* prefix = field<int32_t>(peers[o], L, F_PREFIX);
         const int32_t* prow = field<int32_t>(peers[o], L, F_PAIR_ROW);
@@ -620,12 +656,12 @@ extern "C" int lm_ep_signal_outputs(void* const* peer_regions, int32_t rank, int
   return launch_status("lm_ep_signal_outputs");
 }
 
-extern "C" int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,
-                             int64_t num_tokens, int32_t top_k, int32_t hidden_size,
-                             int32_t experts_per_rank, const int32_t* pair_to_row,
-                             const int32_t* send_offsets, int32_t rank, int32_t world,
-                             void* const* peer_regions, void* local_region, int32_t cap,
-                             int64_t epoch, uint16_t* out, int32_t* err_word, void* stream) {
+namespace {
+int combine_impl(const int32_t* topk_ids, const uint16_t* topk_weights_bf16, int64_t num_tokens,
+                 int32_t top_k, int32_t hidden_size, int32_t experts_per_rank,
+                 const int32_t* pair_to_row, const int32_t* send_offsets, int32_t rank,
+                 int32_t world, void* const* peer_regions, void* local_region, int32_t cap,
+                 int64_t epoch, uint16_t* out, int32_t* err_word, void* stream, int pushed) {
   int rc = check_ep("lm_ep_combine", world, cap, hidden_size);
   if (rc) return rc;
   if (top_k <= 0 || top_k > 32 || num_tokens < 0 || experts_per_rank <= 0 || rank < 0 ||
@@ -648,6 +684,50 @@ extern "C" int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weigh
   if (threads < 32) threads = 32;
   ep_combine_kernel<<<static_cast<unsigned>(num_tokens), threads, 0, s>>>(
       topk_ids, topk_weights_bf16, top_k, hidden_size, experts_per_rank, pair_to_row,
-      send_offsets, rank, world, peer_regions, local_region, L, cap, out, err_word);
+      send_offsets, rank, world, peer_regions, local_region, L, cap, out, err_word, pushed);
   return launch_status("lm_ep_combine");
+}
+}  // namespace
+
+extern "C" int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,
+                             int64_t num_tokens, int32_t top_k, int32_t hidden_size,
+                             int32_t experts_per_rank, const int32_t* pair_to_row,
+                             const int32_t* send_offsets, int32_t rank, int32_t world,
+                             void* const* peer_regions, void* local_region, int32_t cap,
+                             int64_t epoch, uint16_t* out, int32_t* err_word, void* stream) {
+  return combine_impl(topk_ids, topk_weights_bf16, num_tokens, top_k, hidden_size,
+                      experts_per_rank, pair_to_row, send_offsets, rank, world, peer_regions,
+                      local_region, cap, epoch, out, err_word, stream, 0);
+}
+
+extern "C" int lm_ep_combine_local(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,
+                                   int64_t num_tokens, int32_t top_k, int32_t hidden_size,
+                                   int32_t experts_per_rank, const int32_t* pair_to_row,
+                                   const int32_t* send_offsets, int32_t rank, int32_t world,
+                                   void* const* peer_regions, void* local_region, int32_t cap,
+                                   int64_t epoch, uint16_t* out, int32_t* err_word,
+                                   void* stream) {
+  return combine_impl(topk_ids, topk_weights_bf16, num_tokens, top_k, hidden_size,
+                      experts_per_rank, pair_to_row, send_offsets, rank, world, peer_regions,
+                      local_region, cap, epoch, out, err_word, stream, 1);
+}
+
+extern "C" int lm_ep_output_row_ptrs(void* region, int32_t world, int32_t cap,
+                                     int32_t hidden_size, int32_t rank,
+                                     void* const* peer_regions, const int32_t* row_to_pair,
+                                     const int32_t* count_dev, int32_t max_rows,
+                                     uint16_t** row_ptrs_out, int32_t* err_word, void* stream) {
+  int rc = check_ep("lm_ep_output_row_ptrs", world, cap, hidden_size);
+  if (rc) return rc;
+  if (region == nullptr || peer_regions == nullptr || rank < 0 || rank >= world ||
+      max_rows < 0 || (max_rows > 0 && (row_to_pair == nullptr || count_dev == nullptr ||
+                                        row_ptrs_out == nullptr)))
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_output_row_ptrs: bad arguments");
+  if (max_rows == 0) return LM_OK;
+  int blocks = (max_rows + 255) / 256;
+  if (blocks > 1184) blocks = 1184;
+  ep_output_ptrs_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      region, peer_regions, make_layout(world, cap, hidden_size), world, cap, hidden_size, rank,
+      row_to_pair, count_dev, max_rows, row_ptrs_out, err_word);
+  return launch_status("lm_ep_output_row_ptrs");
 }

@@ -103,6 +103,7 @@ struct UmmaParams {
   const int32_t* group_offsets;
   const int32_t* group_bank_row;
   uint16_t* out;
+  uint16_t* const* row_ptr;  // mode 1: output row r goes to row_ptr[r] (may be a peer's memory)
   int32_t* err_word;
   int32_t group_begin;
   int32_t num_groups;
@@ -181,6 +182,30 @@ __device__ __forceinline__ void store_chunk_coalesced(uint4* xbuf, uint16_t* out
     const int row = 8 * i + (lane >> 2);
     const uint4 v = xbuf[row * 4 + (cc ^ ((row >> 1) & 3))];
     if (row < valid_rows) *reinterpret_cast<uint4*>(out0 + row * ld + cc * 8) = v;
+  }
+  __syncwarp();
+}
+
+// The same chunk stored through per-row pointers (lane_row = the pointer of this warp's row
+// `lane`, which may address another GPU's memory): each store instruction still writes 8 rows
+// x 64 contiguous bytes.
+__device__ __forceinline__ void store_chunk_rows(uint4* xbuf, uint16_t* lane_row, int col,
+                                                 int valid_rows, const uint32_t (&packed)[16]) {
+  const int lane = threadIdx.x & 31;
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    xbuf[lane * 4 + (c ^ sw)] =
+        make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+  __syncwarp();
+  const int cc = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = 8 * i + (lane >> 2);
+    const uint4 v = xbuf[row * 4 + (cc ^ ((row >> 1) & 3))];
+    uint16_t* rp = reinterpret_cast<uint16_t*>(
+        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(lane_row), row));
+    if (row < valid_rows) *reinterpret_cast<uint4*>(rp + col + cc * 8) = v;
   }
   __syncwarp();
 }
@@ -472,6 +497,23 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
             store_chunk_coalesced(c.xpose[quad], out_warp + tc.nt * 128 + ch * 32, p.out_ld,
                                   warp_rows, packed);
           }
+        } else if (p.row_ptr != nullptr) {
+          // this lane's row: its output pointer (the rows past the tile's are never stored)
+          const int rr = quad * 32 + lane;
+          uint16_t* lane_row = rr < my_valid
+                                   ? p.row_ptr[tc.row0 + static_cast<int>(rank) * BM + rr]
+                                   : nullptr;
+#pragma unroll 1
+          for (int ch = 0; ch < 8; ++ch) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tbase + ch * 32, v);
+            tmem_ld_wait();
+            uint32_t packed[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              packed[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+            store_chunk_rows(c.xpose[quad], lane_row, tc.nt * BN + ch * 32, warp_rows, packed);
+          }
         } else {
 #pragma unroll 1
           for (int ch = 0; ch < 8; ++ch) {
@@ -498,6 +540,9 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // stores through row pointers may have gone to other GPUs: order them before anything
+    // this thread's stream does next (the exchange's signal follows this kernel)
+    if (p.row_ptr != nullptr) __threadfence_system();
   }
 
   tc_fence_before();
@@ -637,13 +682,12 @@ int make_row_maps(CUtensorMap* maps, const void* ptr, uint64_t k, uint64_t rows)
 
 using namespace lm;
 
-extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
-                                  const int32_t* group_offsets, const int32_t* group_bank_row,
-                                  int32_t group_begin, int32_t group_end,
-                                  const uint16_t* w13_bank, const uint16_t* w2_bank,
-                                  int64_t bank_rows, int32_t hidden_size,
-                                  int32_t intermediate_size, uint16_t* act, uint16_t* y_perm,
-                                  int32_t* err_word, void* stream) {
+namespace {
+int prefill_impl(const uint16_t* x_perm, int64_t total_rows, const int32_t* group_offsets,
+                 const int32_t* group_bank_row, int32_t group_begin, int32_t group_end,
+                 const uint16_t* w13_bank, const uint16_t* w2_bank, int64_t bank_rows,
+                 int32_t hidden_size, int32_t intermediate_size, uint16_t* act,
+                 uint16_t* y_perm, uint16_t* const* y_rows, int32_t* err_word, void* stream) {
   const int H = hidden_size, I = intermediate_size;
   if (H <= 0 || I <= 0 || H % BN != 0 || I % 128 != 0)
     return fail(LM_ERR_INVALID_ARGUMENT,
@@ -655,7 +699,8 @@ extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_moe_mlp_prefill: bad bank_rows or total_rows");
   if (group_end == group_begin || total_rows == 0) return LM_OK;
   if (x_perm == nullptr || group_offsets == nullptr || group_bank_row == nullptr ||
-      w13_bank == nullptr || w2_bank == nullptr || act == nullptr || y_perm == nullptr)
+      w13_bank == nullptr || w2_bank == nullptr || act == nullptr ||
+      (y_perm == nullptr) == (y_rows == nullptr))
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_moe_mlp_prefill: null pointer");
   if ((reinterpret_cast<uintptr_t>(x_perm) | reinterpret_cast<uintptr_t>(w13_bank) |
        reinterpret_cast<uintptr_t>(w2_bank) | reinterpret_cast<uintptr_t>(act) |
@@ -695,6 +740,7 @@ extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
   if (!rc) rc = make_map(&p2.tmap_w1, w2_bank, 3, w2_tiles, 0, 128, 1);
   if (rc) return rc;
   p2.out = y_perm;
+  p2.row_ptr = y_rows;
   p2.k_blocks = I / BK;
   p2.n_tiles = H / BN;
   p2.mode = 1;
@@ -726,4 +772,32 @@ extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
   const int rj = check_cuda(cudaEventRecord(ss->join, ss->stream), "lm_moe_mlp_prefill: join");
   const int rw = rj ? rj : check_cuda(cudaStreamWaitEvent(s, ss->join, 0), "lm_moe_mlp_prefill: join wait");
   return rc ? rc : rw;
+}
+}  // namespace
+
+extern "C" int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
+                                  const int32_t* group_offsets, const int32_t* group_bank_row,
+                                  int32_t group_begin, int32_t group_end,
+                                  const uint16_t* w13_bank, const uint16_t* w2_bank,
+                                  int64_t bank_rows, int32_t hidden_size,
+                                  int32_t intermediate_size, uint16_t* act, uint16_t* y_perm,
+                                  int32_t* err_word, void* stream) {
+  return prefill_impl(x_perm, total_rows, group_offsets, group_bank_row, group_begin, group_end,
+                      w13_bank, w2_bank, bank_rows, hidden_size, intermediate_size, act, y_perm,
+                      nullptr, err_word, stream);
+}
+
+extern "C" int lm_moe_mlp_prefill_rows(const uint16_t* x_perm, int64_t total_rows,
+                                       const int32_t* group_offsets,
+                                       const int32_t* group_bank_row, int32_t group_begin,
+                                       int32_t group_end, const uint16_t* w13_bank,
+                                       const uint16_t* w2_bank, int64_t bank_rows,
+                                       int32_t hidden_size, int32_t intermediate_size,
+                                       uint16_t* act, uint16_t* const* y_row_ptrs,
+                                       int32_t* err_word, void* stream) {
+  if (y_row_ptrs == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_moe_mlp_prefill_rows: null row pointers");
+  return prefill_impl(x_perm, total_rows, group_offsets, group_bank_row, group_begin, group_end,
+                      w13_bank, w2_bank, bank_rows, hidden_size, intermediate_size, act, nullptr,
+                      y_row_ptrs, err_word, stream);
 }

@@ -297,6 +297,73 @@ class SyntheticMoEDecoder:
         rt.end_slot_compute(pending)
         return stage_s
 
+    def moe_share(self, steps: int = 32, warmup: int = 4) -> dict:
+        """Device time of the MoE blocks in a decode token beside the rest of the token.
+
+        Each layer's attention piece and MoE piece (router output -> grouped expert MLP ->
+        residual) is captured as its own graph and the pieces are replayed in token order
+        with an event after each; a token of MoE piece times is summed. Needs a decoder
+        without host stage seams (every layer resident or device-staged), so the host
+        enqueues whole tokens ahead of the GPU and the intervals hold device time only. The
+        per-piece split adds launch gaps the token graphs do not have; the share, not the
+        absolute, is the figure."""
+        if self.offloaded and not self.device_staging:
+            raise ValueError("moe_share needs resident or device-staged layers")
+        s = self.s
+        pieces = []
+        for i in range(s.layers):
+            pieces.append(("attn", lambda i=i: self._attention(i)))
+            pieces.append(("moe", lambda i=i: self._moe(i)))
+        pieces.append(("head", self._head))
+        self.logits.copy_(self.logit_table[0].to(self.device))
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                for _, fn in pieces:
+                    fn()
+        torch.cuda.synchronize()
+        self.reset_position()
+        pool = torch.cuda.graph_pool_handle()
+        graphs = []
+        for kind, fn in pieces:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                fn()
+            graphs.append((kind, g))
+        torch.cuda.synchronize()
+        self.reset_position()
+
+        def token(t, evs=None):
+            self.forced.fill_(t % s.vocab)
+            self.logits.copy_(self.logit_table[t % self.logit_table.shape[0]], non_blocking=True)
+            if evs is not None:
+                evs[0].record()
+            for n, (_, g) in enumerate(graphs):
+                g.replay()
+                if evs is not None:
+                    evs[n + 1].record()
+
+        for t in range(warmup):
+            token(t)
+        torch.cuda.synchronize()
+        self.reset_position()
+        moe_ms, tok_ms = [], []
+        for t in range(steps):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(graphs) + 1)]
+            token(t, evs)
+            evs[-1].synchronize()
+            gaps = [evs[n].elapsed_time(evs[n + 1]) for n in range(len(graphs))]
+            moe_ms.append(sum(x for x, (kind, _) in zip(gaps, graphs) if kind == "moe"))
+            tok_ms.append(sum(gaps))
+        del graphs
+        self.reset_position()
+        moe = statistics.median(moe_ms)
+        tok = statistics.median(tok_ms)
+        return {"moe_ms_per_token_p50": moe, "token_ms_split_p50": tok,
+                "moe_share": moe / tok if tok else None, "steps": steps,
+                "pieces_per_token": 2 * s.layers + 1}
+
     def _stage_counts(self) -> dict:
         """Hits, misses and H2D bytes so far (device counters under device staging)."""
         if not self.device_staging:

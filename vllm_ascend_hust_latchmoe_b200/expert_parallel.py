@@ -99,6 +99,10 @@ class EPOps:
     # out [Rmax], output rows [Rmax,H]): the owner's MLP gathering its rows straight from the
     # receive area and leaving them grouped, with the table the sources read (None: n/a)
     expert_mlp_gather: Callable | None = None
+    # (receive area, slot of pair, local_ids, count, make_row_ptrs(row_to_pair, count, ptrs)):
+    # the gather MLP whose outputs are stored wherever the callback points each grouped row
+    # (straight into the sources' memory); None: not available
+    expert_mlp_push: Callable | None = None
 
 
 class _DevicePtrArray:
@@ -180,6 +184,7 @@ class ExpertParallelMoE:
                  world_size: int, ops: EPOps, group: dist.ProcessGroup | None = None,
                  device: torch.device | str = "cuda",
                  exchange: PeerExchange | None = None, dedupe_dispatch: bool = True,
+                 push_outputs: bool = True,
                  nccl_rows_per_peer: int | None = None) -> None:
         if num_experts % world_size != 0:
             raise ValueError(f"{num_experts} experts do not split evenly over {world_size} ranks")
@@ -204,6 +209,9 @@ class ExpertParallelMoE:
         self.transport = "peer" if exchange is not None else "nccl"
         # peer transport: a token's row crosses to an owner once, not once per routed pair
         self.dedupe_dispatch = bool(dedupe_dispatch)
+        # peer transport: owners store outputs into the sources' memory from the MLP epilogue
+        # (the combine then reads only local memory) instead of the sources reading them
+        self.push_outputs = bool(push_outputs)
         # nccl transport with fixed splits: every (source, owner) block holds this many rows,
         # so the all-to-alls need no host-known counts (None: exact splits, read on the host)
         self.nccl_rows_per_peer = None if nccl_rows_per_peer is None else int(nccl_rows_per_peer)
@@ -357,9 +365,21 @@ class ExpertParallelMoE:
         else:
             _lib.ep_dispatch(hidden, ids, self.per_rank, p2r, offsets, self.rank, self.G,
                              x.peers, x.cap, x.epoch, x.done, x.err)
-        gather = self.ops.expert_mlp_gather is not None and x.rows.shape[0] > DECODE_MAX_TOKENS
-        no_sync = gather or self.ops.expert_mlp_count is not None
-        if gather:
+        big = x.rows.shape[0] > DECODE_MAX_TOKENS
+        push = self.push_outputs and self.ops.expert_mlp_push is not None and big
+        gather = not push and self.ops.expert_mlp_gather is not None and big
+        no_sync = push or gather or self.ops.expert_mlp_count is not None
+        if push:
+            # outputs go from the down GEMM's epilogue straight into each source's area
+            _lib.ep_receive_index(x.region, self.G, x.cap, self.H, x.epoch, x.slots, x.ids,
+                                  x.total, x.err)
+
+            def row_ptrs(row_to_pair, count, ptrs):
+                _lib.ep_output_row_ptrs(x.region, self.G, x.cap, self.H, self.rank, x.peers,
+                                        row_to_pair, count, ptrs.shape[0], ptrs, x.err)
+
+            self.ops.expert_mlp_push(x.recv_rows, x.slots, x.ids, x.total, row_ptrs)
+        elif gather:
             # no row copies on the owner: slots only, the MLP gathers from the receive area and
             # its grouped outputs stay put; the sources read them through the pair-row table
             _lib.ep_receive_index(x.region, self.G, x.cap, self.H, x.epoch, x.slots, x.ids,
@@ -378,8 +398,9 @@ class ExpertParallelMoE:
                     self.ops.expert_mlp(x.rows[:R], x.ids[:R], out=x.out_rows[:R])
         _lib.ep_signal_outputs(x.peers, self.rank, self.G, x.cap, self.H, x.epoch)
         out = torch.empty(T, self.H, dtype=hidden.dtype, device=hidden.device)
-        _lib.ep_combine(ids, w, self.per_rank, p2r, offsets, self.rank, self.G, x.peers,
-                        x.region, x.cap, x.epoch, out, x.err)
+        combine = _lib.ep_combine_local if push else _lib.ep_combine
+        combine(ids, w, self.per_rank, p2r, offsets, self.rank, self.G, x.peers, x.region, x.cap,
+                x.epoch, out, x.err)
         if no_sync:
             # rows received, and rows this rank kept for itself (its own experts' pairs)
             local = offsets[self.rank + 1] - offsets[self.rank]
@@ -470,8 +491,13 @@ def cuda_ops(local_moe, *, num_experts: int, top_k: int, renormalize: bool = Tru
         def expert_mlp_gather(src, slots, local_ids, count, pair_rows, out):
             return local_moe.mlp_rows_gather_count(src, slots, local_ids, count, pair_rows, out)
 
+        def expert_mlp_push(src, slots, local_ids, count, make_row_ptrs):
+            return local_moe.mlp_rows_gather_push(src, slots, local_ids, count, make_row_ptrs)
+    else:
+        expert_mlp_push = None
+
     return EPOps(route, group_by_owner, gather_rows, expert_mlp, combine, expert_mlp_count,
-                 expert_mlp_gather)
+                 expert_mlp_gather, expert_mlp_push)
 
 
 def build_rank_layer(*, w13_owned: torch.Tensor, w2_owned: torch.Tensor, rank: int,

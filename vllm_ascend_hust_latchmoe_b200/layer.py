@@ -470,6 +470,34 @@ class SlotBankMoE:
                              self.E, store.w13, store.w2, self.act, y_out, self.err)
         self.kernel_launches += group_launches(R) + 1 + mlp_launches(R)
 
+    def mlp_rows_gather_push(self, src_rows: torch.Tensor, pair_src: torch.Tensor,
+                             ids: torch.Tensor, count_dev: torch.Tensor, make_row_ptrs) -> None:
+        """:meth:`mlp_rows_gather_count` whose output rows go wherever
+        ``make_row_ptrs(row_to_pair, count_dev, row_ptrs)`` points them: after grouping, the
+        callback fills ``row_ptrs`` (int64 device addresses, one per grouped row, from the
+        row's pair index) and the down GEMM's epilogue stores each row there -- an exchange
+        uses it to store every output straight into its source's memory."""
+        store = self.runtime.host_layer(self.layer_id)
+        R = int(ids.shape[0])
+        if self.k != 1 or not store.on_device:
+            raise RuntimeError("mlp_rows_gather_push needs a top-1 layer with an HBM store")
+        if R > self.max_tokens or R <= DECODE_MAX_TOKENS:
+            raise ValueError(f"{R} pairs outside ({DECODE_MAX_TOKENS}, {self.max_tokens}]")
+        if getattr(self, "_row_ptrs", None) is None:
+            self._row_ptrs = torch.empty(self.max_tokens, dtype=torch.int64, device=self.device)
+            self._pair_rows_scratch = torch.empty(self.max_tokens, dtype=torch.int32,
+                                                  device=self.device)
+        _lib.build_groups_count(ids.view(R, 1), count_dev, self.E_total, self.identity_groups,
+                                self.E, self.group_offsets, self._pair_rows_scratch[:R],
+                                self.row_to_pair, self.scratch, self.err)
+        make_row_ptrs(self.row_to_pair, count_dev, self._row_ptrs[:R])
+        _lib.permute_rows_gather_count(src_rows, self.row_to_pair, pair_src, R, count_dev,
+                                       self.x_perm)
+        _lib.moe_mlp_prefill_rows(self.x_perm, R, self.group_offsets, self.identity_groups, 0,
+                                  self.E, store.w13, store.w2, self.act, self._row_ptrs[:R],
+                                  self.err)
+        self.kernel_launches += group_launches(R) + 2 + mlp_launches(R)
+
     def resident_wave_plan(self) -> tuple[tuple[int, ...], ...]:
         """Read back the last device wave plan (synchronises; diagnostics and tests). Empty
         after a decode-sized resident call, which groups by expert id without waves."""
