@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lm_ep_recv_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_ep_pair_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_permute_rows_gather_count": (ctypes.c_int, [_P, _I32, _P, _P, _I64, _P, _P, _P]),
+    "lm_ep_step_stats": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P, _P]),
     "lm_ep_output_row_ptrs": (
         ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P]),
     "lm_ep_combine_local": (
@@ -474,6 +475,13 @@ def ep_signal_outputs(peer_regions, rank, world, cap, hidden_size, epoch) -> Non
     _check("lm_ep_signal_outputs", lib().lm_ep_signal_outputs(
         _ptr(peer_regions), int(rank), int(world), int(cap), int(hidden_size), int(epoch),
         _stream()))
+
+
+def ep_step_stats(total, send_offsets, tok_count, num_pairs, rank, world, stats) -> None:
+    """Accumulate one exchange step's figures into ``stats`` (int64 [3], on the device)."""
+    _check("lm_ep_step_stats", lib().lm_ep_step_stats(
+        _ptr(total), _ptr(send_offsets), _ptr(tok_count), int(num_pairs), int(rank), int(world),
+        _ptr(stats), _stream()))
 
 
 def ep_output_row_ptrs(region: int, world, cap, hidden_size, rank, peer_regions, row_to_pair,

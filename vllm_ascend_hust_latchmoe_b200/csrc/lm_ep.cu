@@ -360,6 +360,26 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Per-step exchange figures kept on the device (one launch instead of several small ones):
+// stats[0] += pairs received, stats[1] += pairs kept local, stats[2] += rows stored into
+// other ranks by the dispatch (token rows when tok_count is given, else remote pairs).
+__global__ void ep_stats_kernel(const int32_t* __restrict__ total,
+                                const int32_t* __restrict__ send_offsets,
+                                const int32_t* __restrict__ tok_count, int64_t num_pairs,
+                                int rank, int G, long long* __restrict__ stats) {
+  if (threadIdx.x != 0) return;
+  const long long local = send_offsets[rank + 1] - send_offsets[rank];
+  long long stored = num_pairs - local;
+  if (tok_count != nullptr) {
+    stored = 0;
+    for (int o = 0; o < G; ++o)
+      if (o != rank) stored += tok_count[o];
+  }
+  stats[0] += *total;
+  stats[1] += local;
+  stats[2] += stored;
+}
+
 __global__ void ep_signal_kernel(void* const* __restrict__ peers, Layout L, int rank, int G,
                                  long long epoch) {
   __threadfence_system();
@@ -710,6 +730,18 @@ extern "C" int lm_ep_combine_local(const int32_t* topk_ids, const uint16_t* topk
   return combine_impl(topk_ids, topk_weights_bf16, num_tokens, top_k, hidden_size,
                       experts_per_rank, pair_to_row, send_offsets, rank, world, peer_regions,
                       local_region, cap, epoch, out, err_word, stream, 1);
+}
+
+extern "C" int lm_ep_step_stats(const int32_t* total, const int32_t* send_offsets,
+                                const int32_t* tok_count, int64_t num_pairs, int32_t rank,
+                                int32_t world, int64_t* stats, void* stream) {
+  if (total == nullptr || send_offsets == nullptr || stats == nullptr || rank < 0 ||
+      rank >= world || num_pairs < 0)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_step_stats: bad arguments");
+  ep_stats_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      total, send_offsets, tok_count, num_pairs, rank, world,
+      reinterpret_cast<long long*>(stats));
+  return launch_status("lm_ep_step_stats");
 }
 
 extern "C" int lm_ep_output_row_ptrs(void* region, int32_t world, int32_t cap,

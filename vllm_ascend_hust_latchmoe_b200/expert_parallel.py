@@ -403,13 +403,8 @@ class ExpertParallelMoE:
                 x.epoch, out, x.err)
         if no_sync:
             # rows received, and rows this rank kept for itself (its own experts' pairs)
-            local = offsets[self.rank + 1] - offsets[self.rank]
-            self._dev_rows[0] += x.total[0]
-            self._dev_rows[1] += local
-            if self.dedupe_dispatch:
-                self._dev_rows[2] += x.tok_count.sum() - x.tok_count[self.rank]
-            else:
-                self._dev_rows[2] += T * self.k - local
+            _lib.ep_step_stats(x.total, offsets, x.tok_count if self.dedupe_dispatch else None,
+                               T * self.k, self.rank, self.G, self._dev_rows)
             self._dev_steps += 1
             self._dev_pairs += T * self.k
         else:
