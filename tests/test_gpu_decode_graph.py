@@ -69,3 +69,22 @@ def test_device_staged_decoder_is_one_graph_and_matches_host_staging(cuda):
         layer.check_device_errors()
     rep = a.run(steps=8, warmup=2)
     assert rep.graphs == 1 and rep.tpot_ms_p50 > 0 and rep.slot_hit_rate is not None
+
+
+def test_moe_share_after_a_full_run(cuda):
+    """The MoE share of a token (each layer's attention and MoE piece as their own graphs):
+    measured right after a run that used the whole KV cache (it starts again from the first
+    generated position), between 0 and 1, and refused for a host-staged decoder."""
+    d = SyntheticMoEDecoder(TINY, offloaded_layers=(1, 3), device=cuda, seed=5,
+                            device_staging=True)
+    d.run(steps=TINY.max_new, warmup=2)
+    share = d.moe_share(steps=8, warmup=2)
+    assert 0.0 < share["moe_share"] < 1.0 and share["pieces_per_token"] == 2 * TINY.layers + 1
+    assert share["moe_ms_per_token_p50"] > 0
+    for layer in d.moe:
+        layer.check_device_errors()
+    with pytest.raises(ValueError):
+        d.moe_share(steps=TINY.max_new)
+    host = SyntheticMoEDecoder(TINY, offloaded_layers=(1,), device=cuda, seed=5)
+    with pytest.raises(ValueError):
+        host.moe_share(steps=4, warmup=1)

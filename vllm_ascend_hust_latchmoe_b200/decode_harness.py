@@ -310,6 +310,11 @@ class SyntheticMoEDecoder:
         if self.offloaded and not self.device_staging:
             raise ValueError("moe_share needs resident or device-staged layers")
         s = self.s
+        if steps + 2 > s.max_new or warmup + 2 > s.max_new:
+            raise ValueError(f"at most {s.max_new - 2} decode steps fit the KV cache")
+        # every pass below starts from the first generated position (a previous run() may
+        # have left the position at the end of the KV cache)
+        self.reset_position()
         pieces = []
         for i in range(s.layers):
             pieces.append(("attn", lambda i=i: self._attention(i)))
