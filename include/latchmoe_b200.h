@@ -101,6 +101,23 @@ int lm_route_topk_shared(const float* logits, int64_t num_tokens, int32_t num_ex
                          int32_t* topk_ids, void* stream);
 
 /*
+ * K1 + K3 for a decode-sized call in one launch: the routing of lm_route_topk_shared
+ * (num_shared may be 0) followed by the grouping of lm_build_groups over the
+ * num_tokens * (top_k + num_shared) <= 512 pairs with expert_to_group [num_experts_total],
+ * num_groups groups. Outputs are identical to the two calls. For a layer whose experts are
+ * read in place, where the grouping does not depend on staging.
+ */
+int lm_route_group_small(const float* logits, int64_t num_tokens, int32_t num_experts,
+                         int32_t top_k, int32_t scoring_func, int32_t renormalize,
+                         float routed_scaling_factor, const float* e_score_correction_bias,
+                         int32_t num_expert_group, int32_t topk_group, int32_t num_shared,
+                         uint16_t* topk_weights_bf16, float* topk_weights_f32,
+                         int32_t* topk_ids, int32_t num_experts_total,
+                         const int32_t* expert_to_group, int32_t num_groups,
+                         int32_t* group_offsets, int32_t* pair_to_row, int32_t* row_to_pair,
+                         int32_t* err_word, void* stream);
+
+/*
  * K2 active-expert histogram: counts[e] = #pairs routed to expert e (counts is
  * overwritten). Invalid ids set LM_DEVERR_BAD_EXPERT_ID in err_word (may be NULL).
  * Replaces: ops/fused_moe/moe_offload_stage_op.py:297-302,474-508 (D2H of all top-k ids

@@ -110,6 +110,39 @@ def test_build_groups_empty_and_unmapped(cuda):
     assert _groups_case(cuda, ids, e2g, 2, 4) == 2  # LM_DEVERR_UNMAPPED_EXPERT
 
 
+@pytest.mark.parametrize("T,k,E,P", [(16, 8, 128, 0), (1, 8, 128, 0), (64, 8, 128, 0),
+                                     (20, 6, 64, 2), (40, 4, 16, 0)])
+def test_route_group_small_equals_route_then_group(cuda, T, k, E, P):
+    """The one-launch router + grouping of a decode-sized call writes exactly what
+    lm_route_topk(_shared) followed by lm_build_groups writes (identity expert -> group)."""
+    g = torch.Generator().manual_seed(T * 131 + E)
+    logits = (torch.randn(T, E, generator=g) * 2.0).to(cuda)
+    Et = E + P
+    ident = torch.arange(Et, dtype=torch.int32, device=cuda)
+    n = T * (k + P)
+
+    def bufs():
+        return (torch.zeros(T, k + P, dtype=torch.bfloat16, device=cuda),
+                torch.zeros(T, k + P, dtype=torch.int32, device=cuda),
+                torch.full((Et + 1,), -7, dtype=torch.int32, device=cuda),
+                torch.full((n,), -7, dtype=torch.int32, device=cuda),
+                torch.full((n,), -7, dtype=torch.int32, device=cuda),
+                torch.zeros(1, dtype=torch.int32, device=cuda))
+
+    w1, i1, o1, p1, r1, e1 = bufs()
+    _lib.route_topk(logits, k, weights_bf16=w1, ids=i1, num_shared=P)
+    scratch = torch.empty(_lib.build_groups_scratch_elems(n, Et), dtype=torch.int32, device=cuda)
+    _lib.build_groups(i1, Et, ident, Et, o1, p1, r1, scratch, e1)
+    w2, i2, o2, p2, r2, e2 = bufs()
+    _lib.route_group_small(logits, k, num_shared=P, weights_bf16=w2, ids=i2,
+                           num_experts_total=Et, expert_to_group=ident, num_groups=Et,
+                           group_offsets=o2, pair_to_row=p2, row_to_pair=r2, err_word=e2)
+    torch.cuda.synchronize()
+    assert int(e1.item()) == 0 and int(e2.item()) == 0
+    for a, b in ((w1, w2), (i1, i2), (o1, o2), (p1, p2), (r1, r2)):
+        assert torch.equal(a, b)
+
+
 def test_histogram(cuda):
     rng = np.random.default_rng(5)
     ids = rng.integers(0, 128, size=(4096, 8)).astype(np.int32)

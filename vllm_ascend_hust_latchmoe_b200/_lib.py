@@ -46,6 +46,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _I32, _P, _P, _P, _P],
     ),
+    "lm_route_group_small": (
+        ctypes.c_int,
+        [_P, _I64, _I32, _I32, _I32, _I32, _F32, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P,
+         _I32, _P, _P, _P, _P, _P],
+    ),
     "lm_expert_histogram": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _P]),
     "lm_decode_counter_sets": (ctypes.c_int, [_P, _P, _P, _P]),
     "lm_ep_region_bytes": (ctypes.c_int64, [_I32, _I32, _I32]),
@@ -174,6 +179,35 @@ def _require_cuda(*tensors: torch.Tensor | None) -> None:
     for t in tensors:
         if t is not None and not t.is_cuda:
             raise RuntimeError("liblatchmoe_b200 kernels take CUDA tensors only")
+
+
+def route_group_small(logits, top_k, *, scoring_func="softmax", renormalize=True,
+                      routed_scaling_factor=1.0, e_score_correction_bias=None,
+                      num_expert_group=None, topk_group=None, num_shared=0, weights_bf16,
+                      ids, num_experts_total, expert_to_group, num_groups, group_offsets,
+                      pair_to_row, row_to_pair, err_word=None, weights_f32=None) -> None:
+    """Routing and grouping of a decode-sized call in one launch (same outputs as
+    :func:`route_topk` followed by :func:`build_groups`)."""
+    _require_cuda(logits, weights_bf16, ids, expert_to_group, group_offsets, pair_to_row,
+                  row_to_pair)
+    assert logits.dtype == torch.float32 and logits.is_contiguous()
+    T, E = logits.shape
+    scoring = {"softmax": LM_SCORING_SOFTMAX, "sigmoid": LM_SCORING_SIGMOID}.get(scoring_func)
+    if scoring is None:
+        raise ValueError(f"unsupported scoring_func {scoring_func!r}")
+    if ids.shape[-1] != top_k + num_shared or weights_bf16.shape[-1] != top_k + num_shared:
+        raise ValueError("outputs need top_k + num_shared columns")
+    _check(
+        "lm_route_group_small",
+        lib().lm_route_group_small(
+            _ptr(logits), T, E, int(top_k), scoring, int(bool(renormalize)),
+            float(routed_scaling_factor), _ptr(e_score_correction_bias),
+            int(num_expert_group or 0), int(topk_group or 0), int(num_shared),
+            _ptr(weights_bf16), _ptr(weights_f32), _ptr(ids), int(num_experts_total),
+            _ptr(expert_to_group), int(num_groups), _ptr(group_offsets), _ptr(pair_to_row),
+            _ptr(row_to_pair), _ptr(err_word), _stream(),
+        ),
+    )
 
 
 def route_topk(

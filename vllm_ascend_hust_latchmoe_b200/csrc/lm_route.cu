@@ -496,6 +496,32 @@ __global__ void __launch_bounds__(kGroupTile)
                  pair_to_row, row_to_pair, err_word, sm);
 }
 
+// Router and grouping of a decode-sized call in one block (T * (top_k + num_shared) <=
+// kGroupTile pairs): the warps route the tokens with the same device function as
+// route_topk_kernel, the block synchronises (the ids it wrote are then visible to all its
+// threads), and the pairs are grouped exactly as group_single_tile_kernel groups them. A
+// layer whose experts are read in place groups by expert id, so its router can do both.
+template <int EPL>
+__global__ void __launch_bounds__(kGroupTile)
+    route_group_kernel(const float* __restrict__ logits, int64_t num_tokens, int num_experts,
+                       int top_k, int scoring, int renorm, float scale,
+                       const float* __restrict__ bias, int n_group, int topk_group,
+                       uint16_t* w_bf16, float* w_f32, int32_t* ids, int num_shared,
+                       int num_experts_total, const int32_t* __restrict__ e2g, int num_groups,
+                       int32_t* group_offsets, int32_t* pair_to_row, int32_t* row_to_pair,
+                       int32_t* err_word) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ int32_t sm[];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int64_t t = w; t < num_tokens; t += kGroupTileWarps)
+    route_one_token<EPL>(logits, t, num_experts, top_k, scoring, renorm, scale, bias, n_group,
+                         topk_group, w_bf16, w_f32, ids, lane, num_shared, num_experts);
+  __syncthreads();
+  group_one_tile(ids, num_tokens * (top_k + num_shared), num_experts_total, e2g, num_groups,
+                 group_offsets, pair_to_row, row_to_pair, err_word, sm);
+}
+
 // Row gather through a second index: x_perm[r] = src[pair_src[row_to_pair[r]]], the source
 // rows read at L2 (another GPU may have written them for this call; no stale L1 lines).
 __global__ void permute_rows_gather_kernel(const uint16_t* __restrict__ src, int hidden_size,
@@ -690,6 +716,65 @@ extern "C" int lm_route_topk_shared(const float* logits, int64_t num_tokens,
                       routed_scaling_factor, e_score_correction_bias, num_expert_group,
                       topk_group, topk_weights_bf16, topk_weights_f32, topk_ids, num_shared,
                       num_experts, stream, "lm_route_topk_shared");
+}
+
+extern "C" int lm_route_group_small(const float* logits, int64_t num_tokens,
+                                    int32_t num_experts, int32_t top_k, int32_t scoring_func,
+                                    int32_t renormalize, float routed_scaling_factor,
+                                    const float* e_score_correction_bias,
+                                    int32_t num_expert_group, int32_t topk_group,
+                                    int32_t num_shared, uint16_t* topk_weights_bf16,
+                                    float* topk_weights_f32, int32_t* topk_ids,
+                                    int32_t num_experts_total, const int32_t* expert_to_group,
+                                    int32_t num_groups, int32_t* group_offsets,
+                                    int32_t* pair_to_row, int32_t* row_to_pair,
+                                    int32_t* err_word, void* stream) {
+  int rc = check_route_args(num_tokens, num_experts, top_k, scoring_func, num_expert_group,
+                            topk_group, logits, topk_weights_bf16, topk_ids);
+  if (rc) return rc;
+  if (num_shared < 0 || top_k + num_shared > 32)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_route_group_small: need 0 <= num_shared and top_k + num_shared <= 32");
+  const int64_t pairs = num_tokens * (top_k + num_shared);
+  if (pairs <= 0 || pairs > kGroupTile)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_route_group_small: need 0 < num_tokens * (top_k + num_shared) <= 512");
+  if (num_experts_total < num_experts + num_shared || num_groups <= 0 || num_groups > 16384 ||
+      expert_to_group == nullptr || group_offsets == nullptr || pair_to_row == nullptr ||
+      row_to_pair == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_route_group_small: bad grouping arguments");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t smem = sizeof(int32_t) * (1 + kGroupTileWarps) * num_groups;
+  const int epl = (num_experts + 31) / 32;
+  cudaError_t e = cudaSuccess;
+#define LM_ROUTE_GROUP_LAUNCH(N)                                                               \
+  do {                                                                                         \
+    if (smem > 48 * 1024) {                                                                    \
+      rc = check_cuda(cudaFuncSetAttribute(route_group_kernel<N>,                              \
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,        \
+                                           static_cast<int>(smem)),                            \
+                      "lm_route_group_small: smem attribute");                                \
+      if (rc) return rc;                                                                       \
+    }                                                                                          \
+    e = launch_dependent(route_group_kernel<N>, dim3(1), dim3(kGroupTile), smem, s, logits,   \
+                         num_tokens, num_experts, top_k, scoring_func, renormalize,            \
+                         routed_scaling_factor, e_score_correction_bias, num_expert_group,     \
+                         topk_group, topk_weights_bf16, topk_weights_f32, topk_ids,            \
+                         num_shared, num_experts_total, expert_to_group, num_groups,           \
+                         group_offsets, pair_to_row, row_to_pair, err_word);                   \
+  } while (0)
+  if (epl <= 1) {
+    LM_ROUTE_GROUP_LAUNCH(1);
+  } else if (epl <= 2) {
+    LM_ROUTE_GROUP_LAUNCH(2);
+  } else if (epl <= 4) {
+    LM_ROUTE_GROUP_LAUNCH(4);
+  } else {
+    LM_ROUTE_GROUP_LAUNCH(8);
+  }
+#undef LM_ROUTE_GROUP_LAUNCH
+  if (e != cudaSuccess) return check_cuda(e, "lm_route_group_small");
+  return launch_status("lm_route_group_small");
 }
 
 extern "C" int lm_expert_histogram(const int32_t* topk_ids, int64_t num_pairs,

@@ -214,6 +214,24 @@ class SlotBankMoE:
         T = int(router_logits.shape[0])
         self._check_tokens(T)
         logits = router_logits if router_logits.dtype == torch.float32 else router_logits.float()
+        if (self.resident_tier and T <= DECODE_MAX_TOKENS and 0 < T * self.k <= 512
+                and not self.runtime.config.stage_waves_from_hbm_store):
+            # experts read in place: a decode-sized call groups by expert id, which does not
+            # depend on staging, so the router groups its pairs in the same launch and the
+            # MLP piece (mlp_resident) skips its grouping launch
+            _lib.route_group_small(
+                logits.contiguous(), self.k_route, scoring_func=self.scoring_func,
+                renormalize=self.renormalize, routed_scaling_factor=self.routed_scaling_factor,
+                e_score_correction_bias=self.e_bias, num_expert_group=self.num_expert_group,
+                topk_group=self.topk_group, num_shared=self.num_fused_shared,
+                weights_bf16=self.topk_w[:T], ids=self.topk_ids[:T],
+                num_experts_total=self.E_total, expert_to_group=self.identity_groups,
+                num_groups=self.E_total, group_offsets=self.group_offsets,
+                pair_to_row=self.pair_to_row, row_to_pair=self.row_to_pair, err_word=self.err)
+            self.kernel_launches += 1
+            self._grouped_by_router = T
+            return self.topk_w[:T], self.topk_ids[:T]
+        self._grouped_by_router = None
         _lib.route_topk(logits.contiguous(), self.k_route, scoring_func=self.scoring_func,
                         renormalize=self.renormalize,
                         routed_scaling_factor=self.routed_scaling_factor,
@@ -369,16 +387,21 @@ class SlotBankMoE:
         store = self.runtime.host_layer(self.layer_id)
         ids = self.topk_ids[:T]
         if T <= DECODE_MAX_TOKENS:
-            # group = expert id, bank row = expert id: no histogram or wave plan needed
+            # group = expert id, bank row = expert id: no histogram or wave plan needed; the
+            # router of this call may have grouped the pairs already (route_group_small)
             self.resident_planned = False
-            _lib.build_groups(ids, self.E_total, self.identity_groups, self.E_total,
-                              self.group_offsets, self.pair_to_row, self.row_to_pair,
-                              self.scratch, self.err)
+            grouped = getattr(self, "_grouped_by_router", None) == T
+            self._grouped_by_router = None
+            if not grouped:
+                _lib.build_groups(ids, self.E_total, self.identity_groups, self.E_total,
+                                  self.group_offsets, self.pair_to_row, self.row_to_pair,
+                                  self.scratch, self.err)
+                self.kernel_launches += group_launches(T * self.k)
             g_end = self.E_total if self.shared_in_store else self.E
             self._grouped_mlp(hidden, T, self.identity_groups, 0, g_end, store.w13, store.w2)
             if not self.shared_in_store:
                 self._shared_groups_mlp(hidden, T, self.pinned_rows)
-            self.kernel_launches += group_launches(T * self.k) + mlp_launches(T) + 1
+            self.kernel_launches += mlp_launches(T) + 1
             return self._combine(T, out)
         self.resident_planned = True
         _lib.expert_histogram(ids, self.E_total, self.counts, self.err)
