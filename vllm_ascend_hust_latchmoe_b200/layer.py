@@ -214,11 +214,13 @@ class SlotBankMoE:
         T = int(router_logits.shape[0])
         self._check_tokens(T)
         logits = router_logits if router_logits.dtype == torch.float32 else router_logits.float()
-        if (self.resident_tier and T <= DECODE_MAX_TOKENS and 0 < T * self.k <= 512
+        if (self.resident_tier and T <= 16 and 0 < T * self.k <= 512
                 and not self.runtime.config.stage_waves_from_hbm_store):
             # experts read in place: a decode-sized call groups by expert id, which does not
             # depend on staging, so the router groups its pairs in the same launch and the
-            # MLP piece (mlp_resident) skips its grouping launch
+            # MLP piece (mlp_resident) skips its grouping launch. Up to 16 tokens (one per
+            # warp of the block); more tokens route faster over several blocks (64 tokens:
+            # 0.205 ms fused vs 0.199 ms for the C4 layer)
             _lib.route_group_small(
                 logits.contiguous(), self.k_route, scoring_func=self.scoring_func,
                 renormalize=self.renormalize, routed_scaling_factor=self.routed_scaling_factor,
