@@ -112,3 +112,91 @@ def test_ep_two_gpus_matches_oracle(store_on_device, transport):
         assert m["max_rel_err"] <= 1e-2 and m["cosine"] >= 0.9999, (rank, m)
         assert sent > 0
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _edge_worker(rank, world, port, case, q):
+    """Peer exchange (dispatch by token, outputs pushed by the owners) on edge routings:
+    every pair owned by rank 0 (rank 1 receives nothing), one token per rank, and a rank
+    with no tokens at all."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from oracle import mlp as omlp
+    from oracle import router as orouter
+    from oracle.bf16 import bf16_bits_to_f32
+    from tests.helpers import bits
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+    from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE, PeerExchange,
+                                                                build_rank_layer, cuda_ops)
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        cfg = syn.LayerConfig("ep", hidden=H, num_experts=E, top_k=K, intermediate=I,
+                              num_slots=S, tokens=T)
+        w13, w2 = syn.make_expert_weights(cfg, seed=1)
+        per = E // world
+        local = build_rank_layer(w13_owned=w13[rank * per:(rank + 1) * per],
+                                 w2_owned=w2[rank * per:(rank + 1) * per], rank=rank,
+                                 device=dev, max_rows=world * T * K, num_slots=S,
+                                 store_on_device=True)
+        exchange = PeerExchange(world_size=world, rank=rank, max_tokens=T, top_k=K,
+                                hidden_size=H, device=dev)
+        ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
+                               world_size=world, device=dev, exchange=exchange,
+                               ops=cuda_ops(local, num_experts=E, top_k=K, max_tokens=T))
+        n = {"one_owner": T, "single_token": 1, "empty_rank": 0 if rank == 1 else T}[case]
+        hidden = syn.make_hidden(cfg, seed=40 + rank)[:n].contiguous()
+        logits = syn.make_router_logits(cfg, seed=40 + rank)[:n].contiguous()
+        if case == "one_owner":
+            logits[:, per:] -= 100.0  # every token's top-k among rank 0's experts
+        outs = [ep.forward(hidden.to(dev), logits.to(dev)).clone() for _ in range(2)]
+        torch.cuda.synchronize()
+        local.check_device_errors("ep edge")
+        ep.check_exchange_errors()
+        received = int(exchange.total.item())
+        exchange.close()
+        m = {"max_rel_err": 0.0, "cosine": 1.0}
+        if n:
+            wb, _, ids = orouter.route(logits.numpy(), K)
+            ref = omlp.moe_layer(bits(hidden), ids, wb, bits(w13), bits(w2))
+            m = omlp.compare(bf16_bits_to_f32(bits(outs[1])), ref)
+            assert torch.equal(outs[0], outs[1])
+        dist.barrier()
+        q.put((rank, m, received))
+    except Exception as exc:  # report instead of hanging the peer
+        q.put((rank, {"error": repr(exc)}, -1))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", ["one_owner", "single_token", "empty_rank"])
+def test_ep_two_gpus_edge_routings(case):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_edge_worker, args=(r, 2, port, case, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for rank, m, _ in results:
+        assert "error" not in m, m
+        assert m["max_rel_err"] <= 1e-2 and m["cosine"] >= 0.9999, (rank, m)
+    if case == "one_owner":  # rank 0 owns every pair of both ranks, rank 1 none
+        assert results[0][2] == 2 * T * K and results[1][2] == 0
+    if case == "empty_rank":
+        assert results[0][2] + results[1][2] == T * K
+    assert all(p.exitcode == 0 for p in procs)
