@@ -36,6 +36,12 @@ def test_abi_version_and_error_strings_without_gpu():
     assert b"num_experts" in lib.lm_last_error()
     rc = lib.lm_stage_copy(None, 16, None, 16, None, None, 1, 16, 7, None)
     assert rc == -1 and b"kind" in lib.lm_last_error()
+    # an empty call may pass empty (null) tensors: nothing to do, no CUDA call
+    assert lib.lm_route_topk(None, 0, 128, 8, 0, 1, 1.0, None, 0, 0, None, None, None,
+                             None) == 0
+    rc = lib.lm_ep_dispatch_tokens(None, 10, 8, 2048, None, 16, None, None, 0, 2, None, 160, 1,
+                                   None, None, None, None, None)
+    assert rc == -1  # tokens present: every pointer is required
 
 
 def test_ep_exchange_capacity_is_checked_on_the_host():
@@ -49,4 +55,10 @@ def test_ep_exchange_capacity_is_checked_on_the_host():
     assert rc == -1 and b"capacity" in lib.lm_last_error()
     rc = lib.lm_ep_combine(fake, fake, 10, 8, 2048, 16, fake, fake, 0, 2, fake, fake, 64, 1,
                            fake, None, None)
+    assert rc == -1 and b"capacity" in lib.lm_last_error()
+    rc = lib.lm_ep_dispatch_tokens(fake, 10, 8, 2048, fake, 16, fake, fake, 0, 2, fake, 64, 1,
+                                   fake, fake, fake, None, None)
+    assert rc == -1 and b"capacity" in lib.lm_last_error()
+    rc = lib.lm_ep_combine_local(fake, fake, 10, 8, 2048, 16, fake, fake, 0, 2, fake, fake, 64,
+                                 1, fake, None, None)
     assert rc == -1 and b"capacity" in lib.lm_last_error()

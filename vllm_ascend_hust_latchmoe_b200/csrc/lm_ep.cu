@@ -577,8 +577,9 @@ extern "C" int lm_ep_dispatch_tokens(const uint16_t* hidden, int64_t num_tokens,
   if (rc) return rc;
   if (num_tokens < 0 || top_k <= 0 || experts_per_rank <= 0 || rank < 0 || rank >= world ||
       epoch <= 0 || done_counter == nullptr || peer_regions == nullptr ||
-      send_offsets == nullptr || tok_slot == nullptr || tok_count == nullptr ||
-      (num_tokens > 0 && (hidden == nullptr || topk_ids == nullptr || pair_to_row == nullptr)))
+      send_offsets == nullptr || tok_count == nullptr ||
+      (num_tokens > 0 && (hidden == nullptr || topk_ids == nullptr || pair_to_row == nullptr ||
+                          tok_slot == nullptr)))
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_dispatch_tokens: bad arguments");
   if (num_tokens * top_k > cap)
     return fail(LM_ERR_INVALID_ARGUMENT,

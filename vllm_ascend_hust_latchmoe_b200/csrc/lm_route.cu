@@ -644,7 +644,9 @@ int check_route_args(int64_t num_tokens, int32_t num_experts, int32_t top_k,
       return fail(LM_ERR_INVALID_ARGUMENT,
                   "lm_route_topk: topk_group groups hold fewer than top_k experts");
   }
-  if (topk_weights_bf16 == nullptr || topk_ids == nullptr || (num_tokens > 0 && logits == nullptr))
+  // an empty call may pass empty (null) tensors
+  if (num_tokens > 0 &&
+      (topk_weights_bf16 == nullptr || topk_ids == nullptr || logits == nullptr))
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_route_topk: null output or input pointer");
   return LM_OK;
 }
