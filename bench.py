@@ -491,8 +491,8 @@ def run_expert_parallel(dist, rank: int, world: int, dev, args) -> dict:
 def run_value(args, cfg, make_layer, hidden, logits, dist, dev, world, local_rank, peaks,
               barrier):
     """``value``: the C2 layer with hidden states, logits and the expert store in HBM. The
-    layer step (route, histogram, device wave plan, grouping, row permute, grouped MLP,
-    combine; no host synchronisation on this tier) is captured once as a CUDA graph, as vLLM's
+    layer step (route, grouping by expert id, row permute, grouped MLP, combine; no host
+    synchronisation on this tier) is captured once as a CUDA graph, as vLLM's
     piecewise capture runs it, and replayed `steps` times. The grouped MLP alone is captured
     as a second graph and replayed right after the timed steps, bracketed by CUDA events on
     the replay stream: its mean duration is the roofline's kernel time."""
@@ -513,8 +513,9 @@ def run_value(args, cfg, make_layer, hidden, logits, dist, dev, world, local_ran
         layer.route(hidden, logits)
         layer.mlp_resident(hidden, T)
     launches_per_step = layer.kernel_launches - launches0
+    bank_rows = layer.group_bank_row if layer.resident_planned else layer.identity_groups
     with torch.cuda.graph(g_mlp):
-        layer._grouped_mlp(hidden, T, layer.group_bank_row, 0, layer.E, store.w13, store.w2)
+        layer._grouped_mlp(hidden, T, bank_rows, 0, layer.E, store.w13, store.w2)
     for _ in range(3):
         g_layer.replay()
         g_mlp.replay()
@@ -1324,10 +1325,11 @@ def main() -> None:
                    "hidden": cfg.hidden, "experts": cfg.num_experts, "top_k": cfg.top_k,
                    "moe_intermediate": cfg.intermediate,
                    "tier": "HBM-resident experts read in place (no staging)",
-                   "wave_plan": ({"num_slots": cfg.num_slots, "waves": waves,
-                                  "executed_as": "the device wave plan orders the groups; all "
-                                                 "waves run in one grouped-MLP pass"}
-                                 if world == 1 else None),
+                   "group_order": ("expert id: experts read in place need no wave plan; "
+                                   "all groups in one grouped-MLP pass" if not waves else
+                                   f"device wave plan ({waves} waves of at most "
+                                   f"{cfg.num_slots}), all groups in one grouped-MLP pass")
+                                  if world == 1 else None,
                    "launch": ("layer step captured once as a CUDA graph, replayed per step"
                               if world == 1 else "eager (the exchange epochs advance per call)"),
                    "parallelism": ("single GPU" if world == 1 else

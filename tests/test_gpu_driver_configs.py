@@ -53,6 +53,7 @@ def c2_case():
 def test_c2_full_layer_4096_tokens(cuda, c2_case, store_on_device):
     cfg, experts, hidden, logits, ids_ref, ref, waves = c2_case
     layer, rt, _ = build_layer(cfg, store_on_device=store_on_device, experts=experts)
+    layer.resident_wave_order = True  # groups in the device wave plan's order (checked below)
     out = layer.forward(hidden.to(cuda), logits.to(cuda))
     torch.cuda.synchronize()
     layer.check_device_errors("c2 full")
@@ -64,6 +65,12 @@ def test_c2_full_layer_4096_tokens(cuda, c2_case, store_on_device):
     out2 = layer.forward(hidden.to(cuda), logits.to(cuda))
     torch.cuda.synchronize()
     assert torch.equal(out, out2)
+    if store_on_device:  # groups by expert id (the default): the same output, bit for bit
+        layer.resident_wave_order = False
+        out3 = layer.forward(hidden.to(cuda), logits.to(cuda))
+        torch.cuda.synchronize()
+        layer.check_device_errors("c2 full, expert-id order")
+        assert torch.equal(out, out3) and layer.resident_wave_plan() == ()
 
 
 # ----------------------------------------------------------------------------- C5 shape

@@ -78,6 +78,7 @@ def test_prefill_waves_tcgen05_matches_oracle(cuda, store_on_device):
     """C2-shaped multi-wave prefill on a 1024-token slice (>= 4 waves, one combine)."""
     cfg = syn.CONFIGS["c2_prefill"].with_tokens(1024)
     layer, rt, (w13, w2) = build_layer(cfg, store_on_device=store_on_device)
+    layer.resident_wave_order = True  # the resident tier orders its groups by the plan
     hidden = syn.make_hidden(cfg)
     logits = syn.make_router_logits(cfg)
     ids_ref, _, ref = _oracle_layer(cfg, hidden, logits, w13, w2)

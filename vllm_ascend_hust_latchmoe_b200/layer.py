@@ -184,6 +184,9 @@ class SlotBankMoE:
                 pinned, dtype=i32).to(d)
         self.pinned_rows_host = self.pinned_rows.cpu()
         self.resident_tier = runtime.host_layer(self.layer_id).on_device
+        # prefill on the resident tier: order the groups by the device wave plan (as a staged
+        # layer's waves would run) instead of by expert id; the results are the same
+        self.resident_wave_order = False
         self.last_waves = WaveReport()
         self.last_fallback_reason: str | None = None
         # Device staging (decode): slot state kept on the GPU, see lm_slot_plan.
@@ -383,9 +386,10 @@ class SlotBankMoE:
         return self._combine(T, out)
 
     def mlp_resident(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
-        """MLP piece for an HBM-resident expert tier: histogram -> device wave plan ->
-        grouping (rows wave by wave) -> grouped MLP reading each expert in place -> one
-        combine. No host synchronisation; fixed buffers only, so it can be captured."""
+        """MLP piece for an HBM-resident expert tier: grouping by expert id (or, with
+        ``resident_wave_order``, histogram -> device wave plan -> grouping wave by wave) ->
+        grouped MLP reading each expert in place -> one combine. No host synchronisation;
+        fixed buffers only, so it can be captured."""
         store = self.runtime.host_layer(self.layer_id)
         ids = self.topk_ids[:T]
         if T <= DECODE_MAX_TOKENS:
@@ -405,22 +409,33 @@ class SlotBankMoE:
                 self._shared_groups_mlp(hidden, T, self.pinned_rows)
             self.kernel_launches += mlp_launches(T) + 1
             return self._combine(T, out)
-        self.resident_planned = True
-        _lib.expert_histogram(ids, self.E_total, self.counts, self.err)
-        _lib.plan_waves(self.counts[: self.E], self.runtime.config.num_slots,
-                        self.expert_to_group, self.group_bank_row, self.wave_offsets,
-                        self.num_waves, in_place_rows=True)
-        _lib.build_groups(ids, self.E_total, self.expert_to_group, self.E_total,
-                          self.group_offsets, self.pair_to_row, self.row_to_pair, self.scratch,
-                          self.err)
-        launches = 2 + group_launches(T * self.k)  # histogram, plan, grouping
+        if self.resident_wave_order:
+            # groups in the canonical wave order of the device planner (the order of the
+            # groups changes no pair's result; the plan is kept for inspection)
+            self.resident_planned = True
+            _lib.expert_histogram(ids, self.E_total, self.counts, self.err)
+            _lib.plan_waves(self.counts[: self.E], self.runtime.config.num_slots,
+                            self.expert_to_group, self.group_bank_row, self.wave_offsets,
+                            self.num_waves, in_place_rows=True)
+            e2g, bank_rows, shared_rows = self.expert_to_group, self.group_bank_row, \
+                self.group_bank_row
+            launches = 2  # histogram, plan
+        else:
+            # group = expert id, bank row = expert id: nothing to plan for experts read in place
+            self.resident_planned = False
+            e2g, bank_rows, shared_rows = self.identity_groups, self.identity_groups, \
+                self.pinned_rows
+            launches = 0
+        _lib.build_groups(ids, self.E_total, e2g, self.E_total, self.group_offsets,
+                          self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+        launches += group_launches(T * self.k)
         if T > DECODE_MAX_TOKENS:
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             launches += 1
         g_end = self.E_total if self.shared_in_store else self.E
-        self._grouped_mlp(hidden, T, self.group_bank_row, 0, g_end, store.w13, store.w2)
+        self._grouped_mlp(hidden, T, bank_rows, 0, g_end, store.w13, store.w2)
         if not self.shared_in_store:
-            self._shared_groups_mlp(hidden, T, self.group_bank_row)
+            self._shared_groups_mlp(hidden, T, shared_rows)
         self.kernel_launches += launches + mlp_launches(T) + 1
         return self._combine(T, out)
 
