@@ -292,8 +292,10 @@ int lm_moe_combine_count(const uint16_t* y_perm, const int32_t* pair_to_row,
  * K10 expert staging: for i < n, copy bytes_per_expert bytes from
  * src + src_rows_host[i]*src_row_stride to dst + dst_rows_host[i]*dst_row_stride with
  * cudaMemcpyAsync on `stream`, coalescing runs where both row sequences are consecutive
- * into one copy. kind = LM_COPY_H2D (src is pinned host memory) or LM_COPY_D2D.
- * Returns the number of cudaMemcpyAsync calls issued (>= 0) or a negative error.
+ * into one copy. kind = LM_COPY_H2D (src is pinned host memory) or LM_COPY_D2D. A D2D copy
+ * whose bases, strides and size are multiples of 16 bytes runs as one copy kernel per 64
+ * rows instead. Returns the number of copies issued (cudaMemcpyAsync calls or kernel
+ * launches, >= 0) or a negative error.
  * Replaces: moe_offload/transfer_engine.py:139-187,205-228,246-303 (load_many_async,
  * _copy_loads, _try_batch_view).
  */

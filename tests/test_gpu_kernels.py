@@ -332,6 +332,31 @@ def test_stage_copy_coalesces_runs(cuda):
     assert torch.equal(dst[[0, 1, 2, 4, 5]].cpu(), src[[3, 4, 5, 9, 0]])
 
 
+def test_stage_copy_device_to_device_kernel(cuda):
+    """D2D staging runs as a copy kernel (one launch per 64 rows) and moves exactly the rows
+    asked for, rows larger than one CTA's chunk included; a copy whose row size is not a
+    multiple of 16 bytes goes through cudaMemcpyAsync."""
+    g = torch.Generator().manual_seed(3)
+    src = torch.randn(10, 100_003 * 4, generator=g).to(cuda)  # 1.6 MB rows, many chunks
+    dst = torch.zeros(6, src.shape[1], device=cuda)
+    n = _lib.stage_copy(dst, src, [3, 4, 5, 9, 0], [0, 1, 2, 4, 5])
+    torch.cuda.synchronize()
+    assert n == 1
+    assert torch.equal(dst[[0, 1, 2, 4, 5]], src[[3, 4, 5, 9, 0]])
+    assert bool((dst[3] == 0).all())
+    many_src = torch.randn(200, 64, generator=g).to(cuda)
+    many_dst = torch.zeros(200, 64, device=cuda)
+    rows = list(range(199, -1, -1))
+    assert _lib.stage_copy(many_dst, many_src, rows, list(range(200))) == 4  # 64 rows a launch
+    torch.cuda.synchronize()
+    assert torch.equal(many_dst, many_src.flip(0))
+    odd_src = torch.randn(4, 5, generator=g).to(cuda)  # 20-byte rows
+    odd_dst = torch.zeros(4, 5, device=cuda)
+    assert _lib.stage_copy(odd_dst, odd_src, [1, 2], [2, 3]) == 1  # one memcpy of the run
+    torch.cuda.synchronize()
+    assert torch.equal(odd_dst[2:], odd_src[1:3])
+
+
 def test_device_wave_planner_matches_reference_golden(cuda):
     """lm_plan_waves reproduces the reference's canonical wave plans bit for bit."""
     import json

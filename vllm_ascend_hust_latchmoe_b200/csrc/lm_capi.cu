@@ -1,6 +1,8 @@
 // C-ABI glue of liblatchmoe_b200: per-thread error messages, version, and the expert
-// staging copy (K10) that moves experts from the pinned host store (or another HBM bank)
-// into slot-bank rows with one cudaMemcpyAsync per run of consecutive rows.
+// staging copy (K10) that moves experts from the pinned host store into slot-bank rows with
+// one cudaMemcpyAsync per run of consecutive rows, or from another HBM bank with a copy
+// kernel (the copy engine moves device-to-device bytes at a fraction of HBM bandwidth; the
+// kernel's CTAs need no shared memory, so they run beside the grouped MLP's CTAs).
 #include <string>
 
 #include "lm_common.cuh"
@@ -27,6 +29,45 @@ int launch_status(const char* what) { return check_cuda(cudaGetLastError(), what
 
 }  // namespace lm
 
+namespace lm {
+namespace {
+
+constexpr int kCopyRowsPerLaunch = 64;
+constexpr int64_t kCopyChunk = 64 * 1024;  // bytes per CTA
+constexpr int kCopyThreads = 256;
+
+struct CopyRows {
+  int32_t src[kCopyRowsPerLaunch];
+  int32_t dst[kCopyRowsPerLaunch];
+};
+
+// Block (x, y): chunk x of row y; each thread moves 4 x 16 bytes per iteration (four loads in
+// flight before the stores). The source is read once (evict-first).
+__global__ void __launch_bounds__(kCopyThreads)
+    stage_copy_kernel(char* __restrict__ dst, int64_t dst_stride, const char* __restrict__ src,
+                      int64_t src_stride, const __grid_constant__ CopyRows rows,
+                      int64_t bytes) {
+  const int i = blockIdx.y;
+  const int64_t off0 = static_cast<int64_t>(blockIdx.x) * kCopyChunk;
+  if (off0 >= bytes) return;
+  const int64_t len = bytes - off0 < kCopyChunk ? bytes - off0 : kCopyChunk;
+  const uint4* s = reinterpret_cast<const uint4*>(src + rows.src[i] * src_stride + off0);
+  uint4* d = reinterpret_cast<uint4*>(dst + rows.dst[i] * dst_stride + off0);
+  const int64_t n = len / 16;
+  for (int64_t c = threadIdx.x; c < n; c += 4 * kCopyThreads) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (c + u * kCopyThreads < n) v[u] = __ldcs(s + c + u * kCopyThreads);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (c + u * kCopyThreads < n) d[c + u * kCopyThreads] = v[u];
+  }
+}
+
+}  // namespace
+}  // namespace lm
+
 using namespace lm;
 
 extern "C" int lm_abi_version(void) { return LM_ABI_VERSION; }
@@ -50,6 +91,30 @@ extern "C" int lm_stage_copy(void* dst, int64_t dst_row_stride, const void* src,
       return fail(LM_ERR_INVALID_ARGUMENT, "lm_stage_copy: negative row index");
   const cudaMemcpyKind ck = kind == LM_COPY_H2D ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kind == LM_COPY_D2D &&
+      ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) |
+        static_cast<uintptr_t>(dst_row_stride) | static_cast<uintptr_t>(src_row_stride) |
+        static_cast<uintptr_t>(bytes_per_expert)) & 15) == 0) {
+    // device to device: one copy kernel per 64 rows
+    int launches = 0;
+    for (int i0 = 0; i0 < n; i0 += kCopyRowsPerLaunch) {
+      const int m = n - i0 < kCopyRowsPerLaunch ? n - i0 : kCopyRowsPerLaunch;
+      CopyRows rows{};
+      for (int i = 0; i < m; ++i) {
+        rows.src[i] = src_rows_host[i0 + i];
+        rows.dst[i] = dst_rows_host[i0 + i];
+      }
+      const dim3 grid(static_cast<unsigned>((bytes_per_expert + kCopyChunk - 1) / kCopyChunk),
+                      static_cast<unsigned>(m));
+      stage_copy_kernel<<<grid, kCopyThreads, 0, s>>>(static_cast<char*>(dst), dst_row_stride,
+                                                      static_cast<const char*>(src),
+                                                      src_row_stride, rows, bytes_per_expert);
+      const int rc = launch_status("lm_stage_copy: copy kernel");
+      if (rc) return rc;
+      ++launches;
+    }
+    return launches;
+  }
   // A run may be merged into one copy only when both sides are densely packed
   // (stride == bytes) and both row sequences advance by one.
   const bool dense = dst_row_stride == bytes_per_expert && src_row_stride == bytes_per_expert;
