@@ -579,8 +579,9 @@ def run_waves_hbm(args, cfg, w13, w2, dev) -> dict:
     """The capacity-bounded wave executor on the device: the C2 layer with its store in HBM but
     staged wave by wave (canonical waves of at most 32 experts, double-buffered stage banks
     filled device-to-device on the copy stream, one tcgen05 pass per wave, stage-buffer
-    release events, one combine), eager as the seam runs it (one 4*E-byte count read-back per
-    call for the host wave plan). CUDA events around the steps."""
+    release events, one combine). The waves are planned and staged on the device (no host
+    read); the same layer with the host-planned executor (one 4*E-byte count read-back per
+    call, copies issued per wave) is timed after it. CUDA events around the steps."""
     import torch
 
     from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
@@ -612,14 +613,46 @@ def run_waves_hbm(args, cfg, w13, w2, dev) -> dict:
     torch.cuda.synchronize()
     layer.check_device_errors("bench waves")
     ms = a.elapsed_time(b) / args.steps
-    rep = layer.last_waves
+    waves = layer.device_wave_plan()  # the device plan of the last call (reads it back)
+    staged = sum(len(w) for w in waves) * cfg.expert_bytes
+    # the same layer with the waves planned and staged by the host (count read-back, host
+    # wave plan, copies issued per wave), for comparison
+    del layer, rt
+    torch.cuda.empty_cache()
+    hrt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=cfg.num_slots,
+                                             async_load=True, b2_wave_prefill=True,
+                                             graph_compatible_offload=True,
+                                             stage_waves_from_hbm_store=True,
+                                             stage_waves_on_device=False))
+    hrt.register_layer_for_fixed_slots(ExpertLayer(0, w13, w2), slot_device=dev,
+                                       store_device=dev)
+    hlayer = SlotBankMoE(hrt, 0, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
+                         num_experts=cfg.num_experts, top_k=cfg.top_k, max_tokens=cfg.tokens,
+                         renormalize=cfg.renormalize, device=dev)
+    for _ in range(args.warmup):
+        hlayer.forward(hidden, logits)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(args.steps):
+        hlayer.forward(hidden, logits)
+    b.record()
+    torch.cuda.synchronize()
+    hlayer.check_device_errors("bench waves (host plan)")
+    host_ms = a.elapsed_time(b) / args.steps
+    host_waves = hlayer.last_waves.waves
     res = {"workload": cfg.name + ", store in HBM, staged wave by wave",
            "ms_per_step": ms, "tokens_per_s": cfg.tokens / (ms / 1e3),
-           "waves": len(rep.waves), "wave_sizes": [len(w) for w in rep.waves],
-           "staged_bytes_per_step": int(rep.staged_bytes),
-           "d2d_gbs": rep.staged_bytes / (ms / 1e3) / 1e9, "launches_per_step": rep.launches,
+           "waves": len(waves), "wave_sizes": [len(w) for w in waves],
+           "staged_bytes_per_step": int(staged),
+           "d2d_gbs": staged / (ms / 1e3) / 1e9,
+           "plan": "device wave plan; copy kernels into the stage banks; per-wave group ranges "
+                   "read on the device; no host read between router and combine",
+           "host_plan": {"ms_per_step": host_ms, "same_waves": [tuple(w) for w in host_waves]
+                         == [tuple(w) for w in waves],
+                         "plan": "count read-back, host wave plan, stage copies issued per "
+                                 "wave by the host"},
            "timing": f"eager layer calls x{args.steps}, CUDA events"}
-    del layer, rt
+    del hlayer, hrt
     torch.cuda.empty_cache()
     return res
 

@@ -250,6 +250,28 @@ int lm_moe_mlp_prefill_rows(const uint16_t* x_perm, int64_t total_rows,
                             void* stream);
 
 /*
+ * Multi-wave execution from a device wave plan (lm_plan_waves with bank_row_mode 1), with no
+ * host step between the waves:
+ *   lm_stage_wave_copy: expert e joins stage row expert_to_group[e] - wave_offsets[wave] when
+ *     the plan put it in wave `wave` (rows of bytes_per_expert bytes; dst holds dst_rows rows;
+ *     bases, strides and size multiples of 16 bytes); nothing happens for wave >= *num_waves.
+ *   lm_moe_mlp_prefill_wave: lm_moe_mlp_prefill over the groups of wave `wave`
+ *     [wave_offsets[wave], wave_offsets[wave + 1]) read on the device (none when
+ *     wave >= *num_waves; at most 256 groups).
+ * A caller launches ceil(E / S) waves; the plan decides how many do any work.
+ */
+int lm_stage_wave_copy(void* dst, int64_t dst_row_stride, int32_t dst_rows, const void* src,
+                       int64_t src_row_stride, int32_t num_experts, int64_t bytes_per_expert,
+                       const int32_t* expert_to_group, const int32_t* wave_offsets,
+                       const int32_t* num_waves, int32_t wave, void* stream);
+int lm_moe_mlp_prefill_wave(const uint16_t* x_perm, int64_t total_rows,
+                            const int32_t* group_offsets, const int32_t* group_bank_row,
+                            const int32_t* wave_offsets, const int32_t* num_waves, int32_t wave,
+                            const uint16_t* w13_bank, const uint16_t* w2_bank, int64_t bank_rows,
+                            int32_t hidden_size, int32_t intermediate_size, uint16_t* act,
+                            uint16_t* y_perm, int32_t* err_word, void* stream);
+
+/*
  * K8 weighted combine in the original flattened top-k pair order:
  *   out[t, :] = bf16( sum_{j<k} f32(topk_weights[t, j]) * f32(y_perm[pair_to_row[t*k+j], :]) )
  * accumulated in fp32 in j order (deterministic, no atomics). pair_to_row < 0 contributes 0.

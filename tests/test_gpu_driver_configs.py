@@ -183,10 +183,13 @@ def test_c5_shape_owner_rows_count(cuda, c5_bank, R, live):
     _check(out[:live], ref)
 
 
-def test_c2_waves_staged_from_hbm_store(cuda, c2_case):
+@pytest.mark.parametrize("on_device", [False, True], ids=["host_plan", "device_plan"])
+def test_c2_waves_staged_from_hbm_store(cuda, c2_case, on_device):
     """The capacity-bounded wave executor with an HBM-resident store (stage banks filled
     device-to-device, one GEMM pass per wave on its stage bank, one combine): the canonical
-    waves, each within the 32 slots, and the oracle's output."""
+    waves, each within the 32 slots, and the oracle's output -- planned and staged by the
+    host, or planned on the device with copy kernels and per-wave group ranges read on the
+    device (then also replayed from a CUDA graph)."""
     from vllm_ascend_hust_latchmoe_b200.config import MoeOffloadConfig
     from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE
     from vllm_ascend_hust_latchmoe_b200.moe_offload.runtime import MoeOffloadRuntime
@@ -195,17 +198,33 @@ def test_c2_waves_staged_from_hbm_store(cuda, c2_case):
     rt = MoeOffloadRuntime(MoeOffloadConfig(enabled=True, num_slots=cfg.num_slots,
                                             async_load=True, b2_wave_prefill=True,
                                             graph_compatible_offload=True,
-                                            stage_waves_from_hbm_store=True))
+                                            stage_waves_from_hbm_store=True,
+                                            stage_waves_on_device=on_device))
     rt.register_layer_for_fixed_slots(syn.ExpertLayer(0, w13, w2), slot_device=cuda,
                                       store_device=cuda)
     layer = SlotBankMoE(rt, 0, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
                         num_experts=cfg.num_experts, top_k=cfg.top_k, max_tokens=cfg.tokens,
                         device=cuda)
+    h, lg = hidden.to(cuda), logits.to(cuda)
     for _ in range(2):
-        out = layer.forward(hidden.to(cuda), logits.to(cuda))
+        out = layer.forward(h, lg)
         torch.cuda.synchronize()
         layer.check_device_errors("c2 staged waves")
-        assert not layer.last_waves.zero_copy
-        assert [tuple(w) for w in layer.last_waves.waves] == [tuple(w) for w in waves]
-        assert layer.last_waves.staged_bytes == sum(len(w) for w in waves) * cfg.expert_bytes
+        if on_device:
+            assert [tuple(w) for w in layer.device_wave_plan()] == [tuple(w) for w in waves]
+        else:
+            assert not layer.last_waves.zero_copy
+            assert [tuple(w) for w in layer.last_waves.waves] == [tuple(w) for w in waves]
+            assert layer.last_waves.staged_bytes == sum(len(w) for w in waves) * cfg.expert_bytes
         _check(out, ref)
+    if on_device:  # no host step: the whole layer replays from a CUDA graph, same output
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            layer.route(h, lg)
+            gout = layer.run_mlp(h, layer.stage(layer.topk_ids[: cfg.tokens]))
+        for _ in range(2):
+            gout.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            layer.check_device_errors("c2 device waves, graph")
+            assert torch.equal(gout, out)

@@ -299,13 +299,19 @@ def test_captured_mlp_piece_takes_the_path_of_its_layer_tier(monkeypatch):
     from vllm_ascend_hust_latchmoe_b200 import seam_ops
     from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE, StageDecision
 
-    def layer(resident, device):
+    def layer(resident, device, waves_from_store=False):
         lay = SlotBankMoE.__new__(SlotBankMoE)
         lay.resident_tier, lay.device_staging, lay.layer_id, lay.pending = resident, device, 0, None
+        lay.num_fused_shared = 0
+        lay.runtime = SimpleNamespace(config=SimpleNamespace(
+            stage_waves_from_hbm_store=waves_from_store, stage_waves_on_device=True))
         return lay
 
     monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
     assert seam_ops._take_decision(layer(True, False), 4).mode == "resident"
+    # an HBM store staged wave by wave: prefill sizes plan and stage their waves on the device
+    assert seam_ops._take_decision(layer(True, False, True), 512).mode == "device_waves"
+    assert seam_ops._take_decision(layer(True, False, True), 4).mode == "resident"
     assert seam_ops._take_decision(layer(False, True), 4).mode == "device"
     assert seam_ops._take_decision(layer(False, False), 4).mode == "capturing"
     with pytest.raises(RuntimeError, match="not captured under device staging"):

@@ -120,6 +120,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _P, _P, _I32, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
     ),
+    "lm_stage_wave_copy": (
+        ctypes.c_int, [_P, _I64, _I32, _P, _I64, _I32, _I64, _P, _P, _P, _I32, _P]),
+    "lm_moe_mlp_prefill_wave": (
+        ctypes.c_int,
+        [_P, _I64, _P, _P, _P, _P, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
+    ),
     "lm_moe_combine": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P, _P]),
     "lm_stage_copy": (
         ctypes.c_int,
@@ -416,6 +422,32 @@ def moe_mlp_prefill_rows(x_perm, total_rows, group_offsets, group_bank_row, grou
             w13_bank.shape[0], H, I, _ptr(act), _ptr(y_row_ptrs), _ptr(err_word), _stream(),
         ),
     )
+
+
+def stage_wave_copy(dst: torch.Tensor, src: torch.Tensor, expert_to_group, wave_offsets,
+                    num_waves, wave: int, stream: torch.cuda.Stream | None = None) -> None:
+    """Copy the experts a device wave plan put in wave ``wave`` from ``src`` (row e = expert
+    e) into ``dst`` rows 0.. in group order (no host read of the plan)."""
+    _require_cuda(dst, src, expert_to_group, wave_offsets, num_waves)
+    row_bytes = dst[0].numel() * dst.element_size()
+    if src[0].numel() * src.element_size() != row_bytes or src.dtype != dst.dtype:
+        raise ValueError("stage_wave_copy: source and destination rows differ")
+    _check("lm_stage_wave_copy", lib().lm_stage_wave_copy(
+        _ptr(dst), dst.stride(0) * dst.element_size(), dst.shape[0], _ptr(src),
+        src.stride(0) * src.element_size(), src.shape[0], row_bytes, _ptr(expert_to_group),
+        _ptr(wave_offsets), _ptr(num_waves), int(wave), _stream(stream)))
+
+
+def moe_mlp_prefill_wave(x_perm, total_rows, group_offsets, group_bank_row, wave_offsets,
+                         num_waves, wave, w13_bank, w2_bank, act, y_perm, err_word=None) -> None:
+    """The prefill MLP over the groups of wave ``wave`` of a device wave plan."""
+    _require_cuda(x_perm, group_offsets, group_bank_row, wave_offsets, num_waves, w13_bank,
+                  w2_bank, act, y_perm)
+    _check("lm_moe_mlp_prefill_wave", lib().lm_moe_mlp_prefill_wave(
+        _ptr(x_perm), int(total_rows), _ptr(group_offsets), _ptr(group_bank_row),
+        _ptr(wave_offsets), _ptr(num_waves), int(wave), _ptr(w13_bank), _ptr(w2_bank),
+        w13_bank.shape[0], x_perm.shape[-1], w2_bank.shape[-1], _ptr(act), _ptr(y_perm),
+        _ptr(err_word), _stream()))
 
 
 def ep_region_bytes(world: int, cap: int, hidden: int) -> int:

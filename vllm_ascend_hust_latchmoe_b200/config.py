@@ -34,6 +34,10 @@ class MoeOffloadConfig:
     # through the capacity-bounded wave executor (stage banks filled device-to-device on the
     # copy stream) instead of reading every expert in place in one pass.
     stage_waves_from_hbm_store: bool = False
+    # B200 addition: such waves are planned and staged on the device (device wave plan, copy
+    # kernels into the stage banks, grouped MLP over each wave's groups read on the device),
+    # with no host read between the router and the combine, so the layer can be captured.
+    stage_waves_on_device: bool = True
     pin_host_memory: bool | None = None
     transfer_aware_wave_schedule: bool = True
     prefill_prefetch_depth: int = 1

@@ -65,12 +65,69 @@ __global__ void __launch_bounds__(kCopyThreads)
   }
 }
 
+// Wave staging driven by a device wave plan: block (x, e) copies chunk x of expert e's row
+// into stage row (group - first group of the wave) when the plan put e in wave `wave`
+// (expert_to_group[e] in [wave_offsets[wave], wave_offsets[wave + 1])); every other block
+// returns at once. Nothing is read on the host, so the staging can be captured.
+__global__ void __launch_bounds__(kCopyThreads)
+    stage_wave_copy_kernel(char* __restrict__ dst, int64_t dst_stride,
+                           const char* __restrict__ src, int64_t src_stride, int64_t bytes,
+                           const int32_t* __restrict__ expert_to_group,
+                           const int32_t* __restrict__ wave_offsets,
+                           const int32_t* __restrict__ num_waves, int wave, int max_rows) {
+  if (wave >= *num_waves) return;
+  const int e = blockIdx.y;
+  const int g = expert_to_group[e];
+  const int g0 = wave_offsets[wave], g1 = wave_offsets[wave + 1];
+  if (g < g0 || g >= g1 || g - g0 >= max_rows) return;
+  const int64_t off0 = static_cast<int64_t>(blockIdx.x) * kCopyChunk;
+  if (off0 >= bytes) return;
+  const int64_t len = bytes - off0 < kCopyChunk ? bytes - off0 : kCopyChunk;
+  const uint4* s = reinterpret_cast<const uint4*>(src + e * src_stride + off0);
+  uint4* d = reinterpret_cast<uint4*>(dst + (g - g0) * dst_stride + off0);
+  const int64_t n = len / 16;
+  for (int64_t c = threadIdx.x; c < n; c += 4 * kCopyThreads) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (c + u * kCopyThreads < n) v[u] = __ldcs(s + c + u * kCopyThreads);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (c + u * kCopyThreads < n) d[c + u * kCopyThreads] = v[u];
+  }
+}
+
 }  // namespace
 }  // namespace lm
 
 using namespace lm;
 
 extern "C" int lm_abi_version(void) { return LM_ABI_VERSION; }
+
+extern "C" int lm_stage_wave_copy(void* dst, int64_t dst_row_stride, int32_t dst_rows,
+                                  const void* src, int64_t src_row_stride, int32_t num_experts,
+                                  int64_t bytes_per_expert, const int32_t* expert_to_group,
+                                  const int32_t* wave_offsets, const int32_t* num_waves,
+                                  int32_t wave, void* stream) {
+  if (num_experts <= 0 || num_experts > 65535 || dst_rows <= 0 || wave < 0 ||
+      bytes_per_expert <= 0 || dst_row_stride < bytes_per_expert ||
+      src_row_stride < bytes_per_expert)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_stage_wave_copy: bad sizes");
+  if (dst == nullptr || src == nullptr || expert_to_group == nullptr ||
+      wave_offsets == nullptr || num_waves == nullptr)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_stage_wave_copy: null pointer");
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) |
+        static_cast<uintptr_t>(dst_row_stride) | static_cast<uintptr_t>(src_row_stride) |
+        static_cast<uintptr_t>(bytes_per_expert)) & 15) != 0)
+    return fail(LM_ERR_INVALID_ARGUMENT,
+                "lm_stage_wave_copy: bases, strides and size must be multiples of 16 bytes");
+  const dim3 grid(static_cast<unsigned>((bytes_per_expert + kCopyChunk - 1) / kCopyChunk),
+                  static_cast<unsigned>(num_experts));
+  stage_wave_copy_kernel<<<grid, kCopyThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<char*>(dst), dst_row_stride, static_cast<const char*>(src), src_row_stride,
+      bytes_per_expert, expert_to_group, wave_offsets, num_waves, wave, dst_rows);
+  return launch_status("lm_stage_wave_copy");
+}
 
 extern "C" const char* lm_last_error(void) { return g_last_error.c_str(); }
 

@@ -104,6 +104,11 @@ struct UmmaParams {
   const int32_t* group_bank_row;
   uint16_t* out;
   uint16_t* const* row_ptr;  // mode 1: output row r goes to row_ptr[r] (may be a peer's memory)
+  // device-side group range: the groups of wave `wave` of a device wave plan,
+  // [wave_offsets[wave], wave_offsets[wave + 1]), none when wave >= *num_waves
+  const int32_t* wave_offsets;
+  const int32_t* num_waves;
+  int32_t wave;
   int32_t* err_word;
   int32_t group_begin;
   int32_t num_groups;
@@ -242,7 +247,20 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
   SmemCtl& c = *reinterpret_cast<SmemCtl*>(smem + C::STAGES * C::STAGE_BYTES);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int G = p.num_groups;
+  int G = p.num_groups;
+  int gbeg = p.group_begin;
+  if (p.wave_offsets != nullptr) {
+    G = 0;
+    if (p.wave < *p.num_waves) {
+      gbeg = p.wave_offsets[p.wave];
+      const int n = p.wave_offsets[p.wave + 1] - gbeg;
+      if (n > MAX_G) {
+        if (threadIdx.x == 0 && p.role != ROLE_LIGHT) record_error(p.err_word, LM_DEVERR_BAD_GROUP);
+      } else if (n > 0 && gbeg >= 0) {
+        G = n;
+      }
+    }
+  }
   const uint32_t rank = PAIR == 2 ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
   const int cluster_id = blockIdx.x / PAIR;
@@ -262,7 +280,7 @@ __device__ __forceinline__ void umma_grouped_body(const UmmaParams& p) {
     fence_mbarrier_init();
   }
   for (int i = threadIdx.x; i < G; i += NUM_THREADS) {
-    const int g = p.group_begin + i;
+    const int g = gbeg + i;
     const int r0 = p.group_offsets[g];
     int n = p.group_offsets[g + 1] - r0;
     int bank = p.group_bank_row[g];
@@ -687,7 +705,9 @@ int prefill_impl(const uint16_t* x_perm, int64_t total_rows, const int32_t* grou
                  const int32_t* group_bank_row, int32_t group_begin, int32_t group_end,
                  const uint16_t* w13_bank, const uint16_t* w2_bank, int64_t bank_rows,
                  int32_t hidden_size, int32_t intermediate_size, uint16_t* act,
-                 uint16_t* y_perm, uint16_t* const* y_rows, int32_t* err_word, void* stream) {
+                 uint16_t* y_perm, uint16_t* const* y_rows, int32_t* err_word, void* stream,
+                 const int32_t* wave_offsets = nullptr, const int32_t* num_waves = nullptr,
+                 int32_t wave = 0) {
   const int H = hidden_size, I = intermediate_size;
   if (H <= 0 || I <= 0 || H % BN != 0 || I % 128 != 0)
     return fail(LM_ERR_INVALID_ARGUMENT,
@@ -731,6 +751,9 @@ int prefill_impl(const uint16_t* x_perm, int64_t total_rows, const int32_t* grou
   p1.bank_rows = static_cast<int32_t>(bank_rows);
   p1.w_ntiles = 2 * I / 128;
   p1.split_sms = grid;
+  p1.wave_offsets = wave_offsets;
+  p1.num_waves = num_waves;
+  p1.wave = wave;
   split_costs(0, &p1.heavy_tile_cost, &p1.light_tile_cost);
 
   UmmaParams p2 = p1;
@@ -800,4 +823,21 @@ extern "C" int lm_moe_mlp_prefill_rows(const uint16_t* x_perm, int64_t total_row
   return prefill_impl(x_perm, total_rows, group_offsets, group_bank_row, group_begin, group_end,
                       w13_bank, w2_bank, bank_rows, hidden_size, intermediate_size, act, nullptr,
                       y_row_ptrs, err_word, stream);
+}
+
+extern "C" int lm_moe_mlp_prefill_wave(const uint16_t* x_perm, int64_t total_rows,
+                                       const int32_t* group_offsets,
+                                       const int32_t* group_bank_row,
+                                       const int32_t* wave_offsets, const int32_t* num_waves,
+                                       int32_t wave, const uint16_t* w13_bank,
+                                       const uint16_t* w2_bank, int64_t bank_rows,
+                                       int32_t hidden_size, int32_t intermediate_size,
+                                       uint16_t* act, uint16_t* y_perm, int32_t* err_word,
+                                       void* stream) {
+  if (wave_offsets == nullptr || num_waves == nullptr || wave < 0)
+    return fail(LM_ERR_INVALID_ARGUMENT, "lm_moe_mlp_prefill_wave: bad wave arguments");
+  // the group range comes from the device plan; [0, 1) only passes the host checks
+  return prefill_impl(x_perm, total_rows, group_offsets, group_bank_row, 0, 1, w13_bank,
+                      w2_bank, bank_rows, hidden_size, intermediate_size, act, y_perm, nullptr,
+                      err_word, stream, wave_offsets, num_waves, wave);
 }

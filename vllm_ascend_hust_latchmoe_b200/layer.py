@@ -76,7 +76,8 @@ def _vllm_cudagraph_mode() -> str | None:
 
 @dataclass
 class StageDecision:
-    mode: str  # "capturing" | "static" | "slots" | "waves" | "resident" | "device" | "passthrough"
+    mode: str  # "capturing" | "static" | "slots" | "waves" | "device_waves" | "resident" |
+    #            "device" | "passthrough"
     active_experts: tuple[int, ...] = ()
     counts: tuple[int, ...] = ()
     prepared: object | None = None
@@ -288,6 +289,8 @@ class SlotBankMoE:
                 raise RuntimeError("prefill-sized calls are not captured under device staging")
             counts = self.active_counts(topk_ids)
             return StageDecision("waves", tuple(e for e, c in enumerate(counts) if c > 0), counts)
+        if self._device_waves(T):
+            return StageDecision("device_waves")
         if capturing or torch.cuda.is_current_stream_capturing():
             if rt.should_use_fixed_slot_plan_for_layer(self.layer_id) and not rt.is_layer_registered(self.layer_id):
                 raise RuntimeError(f"graph capture reached an unregistered fixed-slot MoE layer {self.layer_id}")
@@ -331,6 +334,8 @@ class SlotBankMoE:
         only fixed buffers and makes no host decision for this layer's tier. An HBM-resident
         store reads experts in place; device staging decides slots on the GPU; otherwise the
         slot-bank path reads whatever the eager stage published in log2phy at replay."""
+        if self._device_waves(T):
+            return StageDecision("device_waves")
         if self.resident_tier:
             return StageDecision("resident")
         if self.device_staging:
@@ -338,6 +343,84 @@ class SlotBankMoE:
                 raise RuntimeError("prefill-sized calls are not captured under device staging")
             return StageDecision("device")
         return StageDecision("capturing")
+
+    def _device_waves(self, T: int) -> bool:
+        """Prefill-sized call of a layer whose HBM store is staged wave by wave, with the waves
+        planned and staged on the device (no fused shared lane: its groups sit outside the
+        routed plan)."""
+        cfg = self.runtime.config
+        return (self.resident_tier and cfg.stage_waves_from_hbm_store
+                and cfg.stage_waves_on_device and T > DECODE_MAX_TOKENS
+                and not self.num_fused_shared)
+
+    def forward_waves_device(self, hidden: torch.Tensor, T: int,
+                             out: torch.Tensor | None = None) -> torch.Tensor:
+        """Capacity-bounded waves planned and staged on the device, for an HBM store: histogram
+        -> device wave plan (canonical waves of at most S experts, stage row = position in the
+        wave) -> grouping wave by wave -> row permute -> per wave: a copy kernel on the copy
+        stream fills a double-buffered stage bank with the wave's experts, the grouped MLP runs
+        over the wave's groups read from the device plan, and a release event frees the bank
+        for the wave after next -> one combine. ceil(E / S) waves are launched; the plan
+        decides how many do work. Nothing is read on the host, so it can be captured."""
+        rt = self.runtime
+        store = rt.host_layer(self.layer_id)
+        S = rt.config.num_slots
+        ids = self.topk_ids[:T]
+        _lib.expert_histogram(ids, self.E_total, self.counts, self.err)
+        _lib.plan_waves(self.counts[: self.E], S, self.expert_to_group, self.group_bank_row,
+                        self.wave_offsets, self.num_waves, in_place_rows=False)
+        _lib.build_groups(ids, self.E_total, self.expert_to_group, self.E, self.group_offsets,
+                          self.pair_to_row, self.row_to_pair, self.scratch, self.err)
+        _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
+        self.resident_planned = False
+        self.device_waves_planned = True
+        compute = torch.cuda.current_stream()
+        copy = rt.transfer_engine.stream()
+        capturing = torch.cuda.is_current_stream_capturing()
+        copy.wait_stream(compute)  # the plan and the tables are ready
+        nbuf = rt.config.effective_prefill_buffer_count
+        released: dict[int, torch.cuda.Event] = {}
+        max_waves = -(-self.E // S)
+        for w in range(max_waves):
+            buf = w % nbuf
+            bank = rt.prefill_stage_bank(self.layer_id, buf)
+            prev = released.get(buf)
+            if prev is None and not capturing:
+                # the buffer's last consumer from an earlier call (host-driven or not)
+                prev = rt.prefill_stage_buffer_release_event(self.layer_id, buf)
+            if prev is not None:
+                copy.wait_event(prev)
+            _lib.stage_wave_copy(bank.w13_slots, store.w13, self.expert_to_group,
+                                 self.wave_offsets, self.num_waves, w, stream=copy)
+            _lib.stage_wave_copy(bank.w2_slots, store.w2, self.expert_to_group,
+                                 self.wave_offsets, self.num_waves, w, stream=copy)
+            ready = torch.cuda.Event()
+            ready.record(copy)
+            compute.wait_event(ready)
+            _lib.moe_mlp_prefill_wave(self.x_perm, T * self.k, self.group_offsets,
+                                      self.group_bank_row, self.wave_offsets, self.num_waves, w,
+                                      bank.w13_slots, bank.w2_slots, self.act, self.y_perm,
+                                      self.err)
+            rel = torch.cuda.Event()
+            rel.record(compute)
+            released[buf] = rel
+            if not capturing:
+                rt.remember_prefill_stage_buffer_release(self.layer_id, buf, rel)
+        self.kernel_launches += (2 + group_launches(T * self.k) + 1 + max_waves * 2
+                                 + max_waves * mlp_launches(T) + 1)
+        return self._combine(T, out)
+
+    def device_wave_plan(self) -> tuple[tuple[int, ...], ...]:
+        """The waves (expert ids in group order) of the last device-planned wave call (reads
+        the plan back: synchronises)."""
+        if not getattr(self, "device_waves_planned", False):
+            return ()
+        nw = int(self.num_waves.item())
+        off = self.wave_offsets[: nw + 1].tolist()
+        e2g = self.expert_to_group[: self.E].tolist()
+        by_group = sorted((g, e) for e, g in enumerate(e2g) if g >= 0)
+        order = [e for _, e in by_group]
+        return tuple(tuple(order[off[w]:off[w + 1]]) for w in range(nw))
 
     def _combine(self, T: int, out: torch.Tensor | None) -> torch.Tensor:
         dst = self.out[:T] if out is None else out
@@ -735,6 +818,8 @@ class SlotBankMoE:
         T = int(hidden.shape[0])
         if decision.mode == "device":
             return self.mlp_device(hidden, T, out)
+        if decision.mode == "device_waves":
+            return self.forward_waves_device(hidden, T, out)
         if decision.mode == "waves":
             return self.forward_waves(hidden, T, decision.counts, out)
         if decision.mode == "resident":
@@ -765,10 +850,11 @@ class SlotBankMoE:
         decision = self.stage(ids, phase)
         out = self.run_mlp(hidden, decision)
         resident = decision.mode == "resident"
+        host_waves = decision.mode == "waves"  # device-planned waves are not read back here
         prof.end(start, layer_id=self.layer_id, resident=resident, tokens=T, pairs=T * self.k,
-                 waves=0 if resident else len(self.last_waves.waves),
+                 waves=len(self.last_waves.waves) if host_waves else 0,
                  active=len(decision.active_experts),
-                 h2d_bytes=0 if resident else int(self.last_waves.staged_bytes))
+                 h2d_bytes=int(self.last_waves.staged_bytes) if host_waves else 0)
         return out
 
     def check_device_errors(self, where: str = "SlotBankMoE") -> None:
