@@ -220,3 +220,24 @@ def test_prefill_profile_drives_residency(cuda, tmp_path):
     plan = pr.plan_profile_guided_prefill_residency(num_layers=2, default_offloaded_layer_ids=(1,),
                                                     layer_costs=costs)
     assert plan.reason == "profile_guided_swaps" and plan.offloaded_layer_ids == (0,)
+
+
+def test_waves_reuse_main_bank_slots_device_to_device(cuda):
+    """A staged layer whose main slot bank already holds some of a wave's experts (an earlier
+    call fitted its slots) copies them device to device into the stage bank and stages the rest
+    from the pinned store: the outputs of the slot call and of the wave call both match the
+    oracle, and a slot call after the waves still does."""
+    cfg = syn.LayerConfig("mix", hidden=256, num_experts=16, top_k=2, intermediate=128,
+                          num_slots=8, tokens=128)
+    layer, rt, (w13, w2) = build_layer(cfg)
+    hidden = syn.make_hidden(cfg, seed=3)
+    base = syn.make_router_logits(cfg, seed=3)
+    for n_active in (6, 12, 6, 14):
+        logits = base.clone()
+        logits[:, n_active:] -= 100.0  # route among the first n_active experts only
+        ids_ref, _, ref = _oracle_layer(cfg, hidden, logits, w13, w2)
+        out = layer.forward(hidden.to(cuda), logits.to(cuda))
+        torch.cuda.synchronize()
+        layer.check_device_errors(f"mixed slots / waves, {n_active} experts")
+        assert np.array_equal(layer.topk_ids[: cfg.tokens].cpu().numpy(), ids_ref)
+        _check(out, ref)

@@ -440,6 +440,10 @@ class SlotBankMoE:
         G = self.num_bank_rows
         _lib.build_groups(ids, self.E_total, log2phy, G, self.group_offsets, self.pair_to_row,
                           self.row_to_pair, self.scratch, self.err)
+        if T > DECODE_MAX_TOKENS:
+            # the tcgen05 MLP reads its rows in group order (the decode GEMV gathers them)
+            _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
+            self.kernel_launches += 1
         self._grouped_mlp(hidden, T, self.slot_rows, 0, G, bank.w13_slots, bank.w2_slots)
         self.kernel_launches += group_launches(T * self.k) + mlp_launches(T) + 1  # + combine
         return self._combine(T, out)
