@@ -336,3 +336,22 @@ def test_serve_check_model_config_is_a_qwen3_moe_config():
     assert (cfg.num_hidden_layers, cfg.hidden_size, cfg.moe_intermediate_size) == (4, 2048, 768)
     assert (cfg.num_experts, cfg.num_experts_per_tok, cfg.norm_topk_prob) == (128, 8, True)
     assert (cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim) == (32, 4, 128)
+
+
+def test_foreign_topk_ids_drop_the_routers_grouping():
+    """When the MLP op receives top-k tensors from another router, it copies them into the
+    layer's buffers and the layer groups the pairs again (the one-launch router grouping of
+    the previous route() call no longer describes them)."""
+    from vllm_ascend_hust_latchmoe_b200 import seam_ops
+    from vllm_ascend_hust_latchmoe_b200.layer import SlotBankMoE
+
+    lay = SlotBankMoE.__new__(SlotBankMoE)
+    lay.topk_ids = torch.zeros(4, 2, dtype=torch.int32)
+    lay.topk_w = torch.zeros(4, 2, dtype=torch.bfloat16)
+    lay._grouped_by_router = 4
+    seam_ops._adopt_topk(lay, lay.topk_w[:4], lay.topk_ids[:4])  # the layer's own buffers
+    assert lay._grouped_by_router == 4
+    seam_ops._adopt_topk(lay, torch.ones(4, 2, dtype=torch.bfloat16),
+                         torch.ones(4, 2, dtype=torch.int32))
+    assert lay._grouped_by_router is None and int(lay.topk_ids.sum()) == 8
+

@@ -468,6 +468,7 @@ def cuda_ops(local_moe, *, num_experts: int, top_k: int, renormalize: bool = Tru
         if R == 0:
             return rows.new_empty((0, rows.shape[1]))
         local_moe.topk_ids[:R, 0].copy_(local_ids)
+        local_moe.invalidate_router_grouping()
         local_moe.topk_w[:R].fill_(1.0)
         decision = local_moe.stage(local_moe.topk_ids[:R])
         return local_moe.run_mlp(rows, decision, out)

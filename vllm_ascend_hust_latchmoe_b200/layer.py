@@ -188,6 +188,8 @@ class SlotBankMoE:
         # prefill on the resident tier: order the groups by the device wave plan (as a staged
         # layer's waves would run) instead of by expert id; the results are the same
         self.resident_wave_order = False
+        # tokens of the last route() call whose pairs the router also grouped (None: not)
+        self._grouped_by_router = None
         self.last_waves = WaveReport()
         self.last_fallback_reason: str | None = None
         # Device staging (decode): slot state kept on the GPU, see lm_slot_plan.
@@ -247,6 +249,11 @@ class SlotBankMoE:
                         num_shared=self.num_fused_shared)
         self.kernel_launches += 1
         return self.topk_w[:T], self.topk_ids[:T]
+
+    def invalidate_router_grouping(self) -> None:
+        """The top-k buffers were written by something other than :meth:`route`: the next MLP
+        piece groups the pairs itself instead of using the router's grouping."""
+        self._grouped_by_router = None
 
     def active_counts(self, topk_ids: torch.Tensor) -> tuple[int, ...]:
         """K2 histogram + one small D2H: per-expert pair counts of this call. The layer's

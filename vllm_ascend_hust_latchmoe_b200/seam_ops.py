@@ -162,6 +162,7 @@ def _adopt_topk(layer: SlotBankMoE, topk_weights, topk_ids) -> None:
     T = topk_ids.shape[0]
     if topk_ids.data_ptr() != layer.topk_ids.data_ptr():
         layer.topk_ids[:T].copy_(topk_ids)
+        layer.invalidate_router_grouping()  # ids from another router: the MLP groups them
     if topk_weights.data_ptr() != layer.topk_w.data_ptr():
         layer.topk_w[:T].copy_(topk_weights)
 
