@@ -6,15 +6,23 @@
 // prefix of those counts, and a capacity-strided receive area (source s writes its rows at
 // [s * cap, s * cap + count)), plus the owner's output rows in compacted order.
 //
-//   dispatch (source r):  gather each routed pair's hidden row and store it straight into the
-//                         owner's receive area (plus its owner-local expert id); the last
-//                         block stores the counts and raises r's flag in every owner.
-//   receive  (owner o):   wait for every source's flag (bounded), prefix the counts, compact
-//                         the rows for the local expert MLP.
+//   dispatch (source r):  store each token's hidden row once into every owner holding any of
+//                         its experts (or, per pair, each pair's row), with each pair's
+//                         owner-local expert id and receive-row index; the last block stores
+//                         the counts and raises r's flag in every owner.
+//   receive  (owner o):   wait for every source's flag (bounded), prefix the counts, then
+//                         compact the rows for the local expert MLP, or list only the received
+//                         pairs' receive rows (the MLP gathers from the receive area itself).
+//   outputs  (owner o):   the MLP writes its rows locally (with a pair-row table the sources
+//                         read), or stores each row straight into its source's output area
+//                         through row pointers (lm_ep_output_row_ptrs).
 //   signal   (owner o):   raise o's output flag in every source once its outputs are written.
 //   combine  (source r):  wait for every owner's output flag (bounded), then per token read
-//                         its pairs' output rows from the owners' memory and reduce them in
-//                         fp32 in the original top-k order.
+//                         its pairs' output rows (from the owners' memory, or from its own
+//                         area when the owners pushed them) and reduce them in fp32 in the
+//                         original top-k order.
+// Every kernel here is launched with programmatic dependent launch and waits for its
+// predecessor in the stream (griddepcontrol.wait) before it touches memory.
 // A source only re-dispatches after its combine read every owner's outputs (stream order),
 // and an owner only compacts / overwrites after every source's next dispatch flag, so the
 // areas need no other barrier. Flags carry the call's epoch (the same on every rank).
@@ -101,6 +109,8 @@ __global__ void __launch_bounds__(256)
                        const int32_t* __restrict__ send_offsets, int rank, int G,
                        void* const* __restrict__ peers, Layout L, int cap, long long epoch,
                        int32_t* __restrict__ done, int32_t* __restrict__ err_word) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   // one warp per pair
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -150,6 +160,8 @@ __global__ void __launch_bounds__(1024)
     ep_token_slots_kernel(const int32_t* __restrict__ ids, int64_t num_tokens, int top_k,
                           int per_rank, int G, int32_t* __restrict__ tok_slot,
                           int32_t* __restrict__ tok_count) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   __shared__ int warp_sums[32];
   __shared__ int carry;
   const int o = blockIdx.x;
@@ -202,6 +214,8 @@ __global__ void __launch_bounds__(256)
                               void* const* __restrict__ peers, Layout L, int cap, int tok_cap,
                               long long epoch, int32_t* __restrict__ done,
                               int32_t* __restrict__ err_word) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t w0 = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -257,6 +271,8 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(32)
     ep_receive_wait_kernel(void* region, Layout L, int G, int cap, long long epoch,
                            int32_t* __restrict__ total_out, int32_t* __restrict__ err_word) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
   if (!wait_flags(field<long long>(region, L, F_FLAG_DISPATCH), G, epoch, err_word)) {
     if (threadIdx.x == 0) {
@@ -286,6 +302,8 @@ __global__ void __launch_bounds__(32)
 __global__ void __launch_bounds__(256)
     ep_compact_kernel(void* region, Layout L, int G, int cap, int H,
                       uint16_t* __restrict__ rows_out, int32_t* __restrict__ ids_out) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
   const int32_t* recv_ids = field<int32_t>(region, L, F_RECV_IDS);
   const int32_t* recv_rowidx = field<int32_t>(region, L, F_RECV_ROWIDX);
@@ -315,6 +333,8 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     ep_index_kernel(void* region, Layout L, int G, int cap, int32_t* __restrict__ slot_out,
                     int32_t* __restrict__ ids_out) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
   const int32_t* recv_ids = field<int32_t>(region, L, F_RECV_IDS);
   const int32_t* recv_rowidx = field<int32_t>(region, L, F_RECV_ROWIDX);
@@ -337,6 +357,8 @@ __global__ void __launch_bounds__(256)
                           int cap, int H, int rank, const int32_t* __restrict__ row_to_pair,
                           const int32_t* __restrict__ count_dev, int max_rows,
                           uint16_t** __restrict__ ptrs, int32_t* __restrict__ err_word) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   const int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
   uint16_t* spare = field<uint16_t>(region, L, F_OUT_ROWS) + static_cast<int64_t>(G) * cap * H;
   int n = *count_dev;
@@ -367,6 +389,8 @@ __global__ void ep_stats_kernel(const int32_t* __restrict__ total,
                                 const int32_t* __restrict__ send_offsets,
                                 const int32_t* __restrict__ tok_count, int64_t num_pairs,
                                 int rank, int G, long long* __restrict__ stats) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   if (threadIdx.x != 0) return;
   const long long local = send_offsets[rank + 1] - send_offsets[rank];
   long long stored = num_pairs - local;
@@ -382,6 +406,8 @@ __global__ void ep_stats_kernel(const int32_t* __restrict__ total,
 
 __global__ void ep_signal_kernel(void* const* __restrict__ peers, Layout L, int rank, int G,
                                  long long epoch) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   __threadfence_system();
   for (int o = threadIdx.x; o < G; o += blockDim.x)
     st_release_sys(field<long long>(peers[o], L, F_FLAG_OUT) + rank, epoch);
@@ -391,6 +417,8 @@ __global__ void ep_signal_kernel(void* const* __restrict__ peers, Layout L, int 
 // which the combine reads so that a timed-out call never reads rows that may still change.
 __global__ void __launch_bounds__(32)
     ep_wait_out_kernel(void* region, Layout L, int G, long long epoch, int32_t* err_word) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   const bool ok = wait_flags(field<long long>(region, L, F_FLAG_OUT), G, epoch, err_word);
   if (threadIdx.x == 0) *field<int32_t>(region, L, F_WAIT_STATUS) = ok ? 0 : 1;
 }
@@ -406,6 +434,8 @@ __global__ void ep_combine_kernel(const int32_t* __restrict__ ids,
                                   void* const* __restrict__ peers, const void* local_region,
                                   Layout L, int cap, uint16_t* __restrict__ out,
                                   int32_t* __restrict__ err_word, int pushed) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
   __shared__ const uint16_t* s_src[32];
   __shared__ float s_w[32];
   const int64_t t = blockIdx.x;
@@ -559,10 +589,14 @@ extern "C" int lm_ep_dispatch(const uint16_t* hidden, int64_t num_tokens, int32_
   int64_t blocks = (pairs + 7) / 8;
   if (blocks < 1) blocks = 1;
   if (blocks > 1184) blocks = 1184;
-  ep_dispatch_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      hidden, pairs, top_k, hidden_size, topk_ids, experts_per_rank, pair_to_row, send_offsets,
-      rank, world, peer_regions, make_layout(world, cap, hidden_size), cap, epoch, done_counter,
-      err_word);
+  {
+    const cudaError_t le_ = launch_dependent(ep_dispatch_kernel,
+        dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+        hidden, pairs, top_k, hidden_size, topk_ids, experts_per_rank, pair_to_row, send_offsets,
+        rank, world, peer_regions, make_layout(world, cap, hidden_size), cap, epoch, done_counter,
+        err_word);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_dispatch_kernel");
+  }
   return launch_status("lm_ep_dispatch");
 }
 
@@ -589,17 +623,24 @@ extern "C" int lm_ep_dispatch_tokens(const uint16_t* hidden, int64_t num_tokens,
   // a source's token rows start at rank * tok_cap inside the world * cap receive rows
   const int tok_cap = cap / top_k;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ep_token_slots_kernel<<<world, 1024, 0, s>>>(topk_ids, num_tokens, top_k, experts_per_rank,
-                                               world, tok_slot, tok_count);
+  {
+    const cudaError_t le_ = launch_dependent(ep_token_slots_kernel, dim3(world), dim3(1024), 0, s,
+        topk_ids, num_tokens, top_k, experts_per_rank, world, tok_slot, tok_count);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_token_slots_kernel");
+  }
   rc = launch_status("lm_ep_dispatch_tokens: token slots");
   if (rc) return rc;
   int64_t blocks = (num_tokens * world + 7) / 8;
   if (blocks < 1) blocks = 1;
   if (blocks > 1184) blocks = 1184;
-  ep_dispatch_tokens_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-      hidden, num_tokens, top_k, hidden_size, topk_ids, experts_per_rank, pair_to_row,
-      send_offsets, tok_slot, rank, world, peer_regions, make_layout(world, cap, hidden_size),
-      cap, tok_cap, epoch, done_counter, err_word);
+  {
+    const cudaError_t le_ = launch_dependent(ep_dispatch_tokens_kernel,
+        dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, hidden, num_tokens, top_k,
+        hidden_size, topk_ids, experts_per_rank, pair_to_row, send_offsets, tok_slot, rank, world,
+        peer_regions, make_layout(world, cap, hidden_size), cap, tok_cap, epoch, done_counter,
+        err_word);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_dispatch_tokens_kernel");
+  }
   return launch_status("lm_ep_dispatch_tokens");
 }
 
@@ -613,13 +654,21 @@ extern "C" int lm_ep_receive(void* region, int32_t world, int32_t cap, int32_t h
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_receive: bad arguments");
   const Layout L = make_layout(world, cap, hidden_size);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ep_receive_wait_kernel<<<1, 32, 0, s>>>(region, L, world, cap, epoch, total_out, err_word);
+  {
+    const cudaError_t le_ = launch_dependent(ep_receive_wait_kernel, dim3(1), dim3(32), 0, s,
+        region, L, world, cap, epoch, total_out, err_word);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_receive_wait_kernel");
+  }
   rc = launch_status("lm_ep_receive: wait");
   if (rc) return rc;
   int64_t blocks = (static_cast<int64_t>(world) * cap + 7) / 8;
   if (blocks > 1184) blocks = 1184;
-  ep_compact_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(region, L, world, cap,
-                                                                 hidden_size, rows_out, ids_out);
+  {
+    const cudaError_t le_ = launch_dependent(ep_compact_kernel,
+        dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, region, L, world, cap, hidden_size,
+        rows_out, ids_out);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_compact_kernel");
+  }
   return launch_status("lm_ep_receive: compact");
 }
 
@@ -634,13 +683,20 @@ extern "C" int lm_ep_receive_index(void* region, int32_t world, int32_t cap,
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_receive_index: bad arguments");
   const Layout L = make_layout(world, cap, hidden_size);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ep_receive_wait_kernel<<<1, 32, 0, s>>>(region, L, world, cap, epoch, total_out, err_word);
+  {
+    const cudaError_t le_ = launch_dependent(ep_receive_wait_kernel, dim3(1), dim3(32), 0, s,
+        region, L, world, cap, epoch, total_out, err_word);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_receive_wait_kernel");
+  }
   rc = launch_status("lm_ep_receive_index: wait");
   if (rc) return rc;
   int64_t blocks = (static_cast<int64_t>(world) * cap + 255) / 256;
   if (blocks > 1184) blocks = 1184;
-  ep_index_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(region, L, world, cap,
-                                                                slot_out, ids_out);
+  {
+    const cudaError_t le_ = launch_dependent(ep_index_kernel, dim3(static_cast<unsigned>(blocks)),
+        dim3(256), 0, s, region, L, world, cap, slot_out, ids_out);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_index_kernel");
+  }
   return launch_status("lm_ep_receive_index: index");
 }
 
@@ -672,8 +728,12 @@ extern "C" int lm_ep_signal_outputs(void* const* peer_regions, int32_t rank, int
   if (rc) return rc;
   if (peer_regions == nullptr || rank < 0 || rank >= world || epoch <= 0)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_signal_outputs: bad arguments");
-  ep_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      peer_regions, make_layout(world, cap, hidden_size), rank, world, epoch);
+  {
+    const cudaError_t le_ = launch_dependent(ep_signal_kernel, dim3(1), dim3(32), 0,
+        static_cast<cudaStream_t>(stream), peer_regions, make_layout(world, cap, hidden_size),
+        rank, world, epoch);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_signal_kernel");
+  }
   return launch_status("lm_ep_signal_outputs");
 }
 
@@ -697,15 +757,23 @@ int combine_impl(const int32_t* topk_ids, const uint16_t* topk_weights_bf16, int
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_combine: out must be 16-byte aligned");
   const Layout L = make_layout(world, cap, hidden_size);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ep_wait_out_kernel<<<1, 32, 0, s>>>(local_region, L, world, epoch, err_word);
+  {
+    const cudaError_t le_ = launch_dependent(ep_wait_out_kernel, dim3(1), dim3(32), 0, s,
+        local_region, L, world, epoch, err_word);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_wait_out_kernel");
+  }
   rc = launch_status("lm_ep_combine: wait");
   if (rc || num_tokens == 0) return rc;
   int threads = hidden_size / 8;
   if (threads > 256) threads = 256;
   if (threads < 32) threads = 32;
-  ep_combine_kernel<<<static_cast<unsigned>(num_tokens), threads, 0, s>>>(
-      topk_ids, topk_weights_bf16, top_k, hidden_size, experts_per_rank, pair_to_row,
-      send_offsets, rank, world, peer_regions, local_region, L, cap, out, err_word, pushed);
+  {
+    const cudaError_t le_ = launch_dependent(ep_combine_kernel,
+        dim3(static_cast<unsigned>(num_tokens)), dim3(threads), 0, s, topk_ids, topk_weights_bf16,
+        top_k, hidden_size, experts_per_rank, pair_to_row, send_offsets, rank, world, peer_regions,
+        local_region, L, cap, out, err_word, pushed);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_combine_kernel");
+  }
   return launch_status("lm_ep_combine");
 }
 }  // namespace
@@ -739,9 +807,12 @@ extern "C" int lm_ep_step_stats(const int32_t* total, const int32_t* send_offset
   if (total == nullptr || send_offsets == nullptr || stats == nullptr || rank < 0 ||
       rank >= world || num_pairs < 0)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_step_stats: bad arguments");
-  ep_stats_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      total, send_offsets, tok_count, num_pairs, rank, world,
-      reinterpret_cast<long long*>(stats));
+  {
+    const cudaError_t le_ = launch_dependent(ep_stats_kernel, dim3(1), dim3(32), 0,
+        static_cast<cudaStream_t>(stream), total, send_offsets, tok_count, num_pairs, rank, world,
+        reinterpret_cast<long long*>(stats));
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_stats_kernel");
+  }
   return launch_status("lm_ep_step_stats");
 }
 
@@ -759,8 +830,12 @@ extern "C" int lm_ep_output_row_ptrs(void* region, int32_t world, int32_t cap,
   if (max_rows == 0) return LM_OK;
   int blocks = (max_rows + 255) / 256;
   if (blocks > 1184) blocks = 1184;
-  ep_output_ptrs_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      region, peer_regions, make_layout(world, cap, hidden_size), world, cap, hidden_size, rank,
-      row_to_pair, count_dev, max_rows, row_ptrs_out, err_word);
+  {
+    const cudaError_t le_ = launch_dependent(ep_output_ptrs_kernel, dim3(blocks), dim3(256), 0,
+        static_cast<cudaStream_t>(stream), region, peer_regions,
+        make_layout(world, cap, hidden_size), world, cap, hidden_size, rank, row_to_pair,
+        count_dev, max_rows, row_ptrs_out, err_word);
+    if (le_ != cudaSuccess) return check_cuda(le_, "ep_output_ptrs_kernel");
+  }
   return launch_status("lm_ep_output_row_ptrs");
 }
