@@ -228,24 +228,6 @@ int lm_moe_mlp_decode(const uint16_t* hidden, int32_t top_k, const int32_t* row_
 int lm_decode_counter_sets(int32_t* in_use, int32_t* pinned, int64_t* recycled,
                            int64_t* fallbacks);
 
-/*
- * lm_moe_mlp_decode followed by lm_moe_combine(y_perm, pair_to_row, topk_weights_bf16,
- * num_tokens, top_k, hidden_size, out): the persistent kernel's CTAs wait (bounded) until
- * every down item has stored its rows, then reduce the tokens' pairs in top-k order with the
- * same fp32 arithmetic, so the combine costs no launch of its own. The groups
- * [group_begin, group_end) must hold every pair the combine reads. When the two-kernel decode
- * path runs instead (no counter set free, too many groups), the combine is launched after it.
- */
-int lm_moe_mlp_decode_combine(const uint16_t* hidden, int32_t top_k, const int32_t* row_to_pair,
-                              const int32_t* group_offsets, const int32_t* group_bank_row,
-                              int32_t group_begin, int32_t group_end,
-                              int32_t max_rows_per_group, const uint16_t* w13_bank,
-                              const uint16_t* w2_bank, int64_t bank_rows, int32_t hidden_size,
-                              int32_t intermediate_size, uint16_t* act, uint16_t* y_perm,
-                              const int32_t* pair_to_row, const uint16_t* topk_weights_bf16,
-                              int64_t num_tokens, uint16_t* out, int32_t* err_word,
-                              void* stream);
-
 int lm_moe_mlp_prefill(const uint16_t* x_perm, int64_t total_rows,
                        const int32_t* group_offsets, const int32_t* group_bank_row,
                        int32_t group_begin, int32_t group_end,

@@ -214,41 +214,6 @@ def test_decode_mlp_matches_oracle(cuda, T, k, E, H, I):
     _mlp_case(cuda, T, k, E, H, I, 32, use_prefill=False)
 
 
-@pytest.mark.parametrize("T,k,E,H,I", [(16, 8, 128, 2048, 768), (1, 8, 128, 2048, 768),
-                                       (64, 6, 64, 2048, 1408), (40, 8, 16, 256, 128)])
-def test_decode_mlp_with_fused_combine_equals_two_launches(cuda, T, k, E, H, I):
-    """The combine run inside the persistent decode launch writes exactly what the separate
-    combine launch writes after the decode MLP, call after call (the launch's counters,
-    including the down-item completion count, are reset for the next call)."""
-    g = torch.Generator().manual_seed(T * 7 + k)
-    W13 = to_tiled((torch.randn(E, 2 * I, H, generator=g) * 0.05).to(torch.bfloat16)).to(cuda)
-    W2 = to_tiled((torch.randn(E, H, I, generator=g) * 0.05).to(torch.bfloat16)).to(cuda)
-    ident = torch.arange(E, dtype=torch.int32, device=cuda)
-    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
-    w = torch.rand(T, k, generator=g).to(torch.bfloat16).to(cuda)
-    h = (torch.randn(T, H, generator=g) * 0.5).to(torch.bfloat16).to(cuda)
-    off = torch.empty(E + 1, dtype=torch.int32, device=cuda)
-    p2r = torch.empty(T * k, dtype=torch.int32, device=cuda)
-    r2p = torch.empty(T * k, dtype=torch.int32, device=cuda)
-    scratch = torch.empty(_lib.build_groups_scratch_elems(T * k, E), dtype=torch.int32,
-                          device=cuda)
-    err = torch.zeros(1, dtype=torch.int32, device=cuda)
-    _lib.build_groups(ids.to(cuda), E, ident, E, off, p2r, r2p, scratch, err)
-    act = torch.empty(T * k, I, dtype=torch.bfloat16, device=cuda)
-    y = torch.empty(T * k, H, dtype=torch.bfloat16, device=cuda)
-    ref = torch.empty(T, H, dtype=torch.bfloat16, device=cuda)
-    _lib.moe_mlp_decode(h, k, r2p, off, ident, 0, E, T, W13, W2, act, y, err)
-    _lib.moe_combine(y, p2r, w, ref)
-    for _ in range(3):
-        out = torch.full((T, H), 7.0, dtype=torch.bfloat16, device=cuda)
-        y.zero_()
-        _lib.moe_mlp_decode_combine(h, k, r2p, off, ident, 0, E, T, W13, W2, act, y, p2r, w,
-                                    out, err)
-        torch.cuda.synchronize()
-        assert int(err.item()) == 0
-        assert torch.equal(out, ref)
-
-
 def test_decode_mlp_concurrent_streams(cuda):
     """The persistent decode kernel keeps its work queue and pass counters per stream: two
     layers' decode calls running at the same time on two streams give exactly what each gives

@@ -126,11 +126,6 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _P, _P, _P, _P, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P],
     ),
-    "lm_moe_mlp_decode_combine": (
-        ctypes.c_int,
-        [_P, _I32, _P, _P, _P, _I32, _I32, _I32, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _I64,
-         _P, _P, _P],
-    ),
     "lm_moe_combine": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P, _P]),
     "lm_stage_copy": (
         ctypes.c_int,
@@ -610,27 +605,6 @@ def decode_counter_sets() -> dict:
     _check("lm_decode_counter_sets", lib().lm_decode_counter_sets(
         ctypes.byref(u), ctypes.byref(p), ctypes.byref(r), ctypes.byref(f)))
     return {"in_use": u.value, "pinned": p.value, "recycled": r.value, "fallbacks": f.value}
-
-
-def moe_mlp_decode_combine(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
-                           group_begin, group_end, max_rows_per_group, w13_bank, w2_bank, act,
-                           y_perm, pair_to_row, topk_weights_bf16, out, err_word=None) -> None:
-    """The decode MLP with the weighted combine of ``topk_weights_bf16.shape[0]`` tokens fused
-    into the same persistent launch (``out [T, H]``)."""
-    _require_cuda(hidden, row_to_pair, group_offsets, group_bank_row, w13_bank, w2_bank, act,
-                  y_perm, pair_to_row, topk_weights_bf16, out)
-    H = hidden.shape[-1]
-    I = w2_bank.shape[-1]
-    _check(
-        "lm_moe_mlp_decode_combine",
-        lib().lm_moe_mlp_decode_combine(
-            _ptr(hidden), int(top_k), _ptr(row_to_pair), _ptr(group_offsets),
-            _ptr(group_bank_row), int(group_begin), int(group_end), int(max_rows_per_group),
-            _ptr(w13_bank), _ptr(w2_bank), w13_bank.shape[0], H, I, _ptr(act), _ptr(y_perm),
-            _ptr(pair_to_row), _ptr(topk_weights_bf16), topk_weights_bf16.shape[0], _ptr(out),
-            _ptr(err_word), _stream(),
-        ),
-    )
 
 
 def moe_mlp_decode_offload(hidden, top_k, row_to_pair, group_offsets, group_src, group_expert,

@@ -382,18 +382,7 @@ constexpr int kPdFirst = 1, kPdLast = 2, kPdDown = 4, kPdExit = 8;
 struct PdCounters {
   int32_t work;
   int32_t exited;
-  int32_t down_done;  // consumer-warp completions of down items (fused combine)
   int32_t done[kPdMaxSlots];
-};
-
-// Optional weighted combine fused into the persistent launch: once every down item has
-// stored its outputs, all CTAs reduce out[t] = sum_j w[t, j] * y_perm[pair_to_row[t*k + j]]
-// (fp32 in j order, the arithmetic of combine_kernel).
-struct PdCombine {
-  const int32_t* pair_to_row = nullptr;
-  const uint16_t* w_bf16 = nullptr;
-  uint16_t* out = nullptr;
-  int32_t num_tokens = 0;
 };
 
 __device__ PdCounters g_pd_counters[kPdCounterSets];
@@ -419,10 +408,6 @@ struct PdParams {
   uint16_t* act;
   uint16_t* y_perm;
   int32_t* err_word;
-  const int32_t* c_pair_to_row;  // fused combine (c_out != nullptr)
-  const uint16_t* c_w;
-  uint16_t* c_out;
-  int32_t c_tokens;
   int64_t bank_rows;
   int32_t counter_set;
   int32_t group_begin;
@@ -498,57 +483,6 @@ __device__ __forceinline__ void pd_resolve(const PdParams& p, const int32_t* slo
   for (int j = 0; j < 2 * NC; ++j) {
     const int tok = it.tok0 + j * 4 + (lane >> 3);
     it.xrow[j] = tok >= it.n ? -1 : (it.down ? it.r0 + tok : p.row_to_pair[it.r0 + tok]);
-  }
-}
-
-// The fused combine's share of one CTA (kept out of line so that the streaming loop's
-// register allocation does not change).
-__device__ __noinline__ void pd_fused_combine(const PdParams& p) {
-  const int chunks = p.H >> 3;
-  const int64_t units = static_cast<int64_t>(p.c_tokens) * chunks;
-  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units;
-       u += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t t = u / chunks;
-    const int c = static_cast<int>(u - t * chunks);
-    float acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int j0 = 0; j0 < p.top_k; j0 += 8) {
-      uint4 v[8];
-      bool use[8];
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int row = j0 + jj < p.top_k ? p.c_pair_to_row[t * p.top_k + j0 + jj] : -1;
-        use[jj] = row >= 0;
-        if (use[jj])
-          v[jj] = __ldcg(reinterpret_cast<const uint4*>(p.y_perm +
-                                                        static_cast<int64_t>(row) * p.H) + c);
-      }
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        if (!use[jj]) continue;
-        const float w = bf16_bits_to_f32(p.c_w[t * p.top_k + j0 + jj]);
-        float a, b;
-        unpack_bf16x2(v[jj].x, a, b);
-        acc[0] += w * a;
-        acc[1] += w * b;
-        unpack_bf16x2(v[jj].y, a, b);
-        acc[2] += w * a;
-        acc[3] += w * b;
-        unpack_bf16x2(v[jj].z, a, b);
-        acc[4] += w * a;
-        acc[5] += w * b;
-        unpack_bf16x2(v[jj].w, a, b);
-        acc[6] += w * a;
-        acc[7] += w * b;
-      }
-    }
-    uint4 o;
-    o.x = pack_bf16x2(acc[0], acc[1]);
-    o.y = pack_bf16x2(acc[2], acc[3]);
-    o.z = pack_bf16x2(acc[4], acc[5]);
-    o.w = pack_bf16x2(acc[6], acc[7]);
-    reinterpret_cast<uint4*>(p.c_out + t * p.H)[c] = o;
   }
 }
 
@@ -856,39 +790,10 @@ __global__ void __launch_bounds__(kPdThreads)
         // the warp's activation stores, then one release increment of the pass's counter
         __syncwarp();
         if (lane == 0) red_release_add_gpu(&ctr->done[m.slot], 1);
-      } else if (p.c_out != nullptr) {
-        __syncwarp();
-        if (lane == 0) red_release_add_gpu(&ctr->down_done, 1);
       }
     }
   }
   __syncthreads();
-  if (p.c_out != nullptr) {
-    // fused combine: wait (bounded) until every down item's outputs are stored, then this
-    // CTA reduces its share of the (token, 16-byte chunk) units
-    __shared__ int s_all_done;
-    if (threadIdx.x == 0) {
-      const int slots = min(slot_prefix[G], kPdMaxSlots);
-      const int need = slots <= kPdMaxSlots && slot_prefix[G] <= kPdMaxSlots
-                           ? slots * (p.H >> 6) * kPdConsumers
-                           : 0;
-      int ok = 1;
-      const long long t0 = clock64();
-      while (ld_acquire_gpu(&ctr->down_done) < need) {
-        if (*ab || clock64() - t0 > LM_SPIN_LIMIT_CYCLES) {
-          record_error(p.err_word, LM_DEVERR_WAIT_TIMEOUT);
-          ok = 0;
-          break;
-        }
-      }
-      s_all_done = ok;
-    }
-    __syncthreads();
-    if (s_all_done) {
-      (void)ld_acquire_gpu(&ctr->down_done);
-      pd_fused_combine(p);
-    }
-  }
   if (threadIdx.x == 0) {
     __threadfence();
     if (atomicAdd(&ctr->exited, 1) == static_cast<int>(gridDim.x) - 1) {
@@ -896,7 +801,6 @@ __global__ void __launch_bounds__(kPdThreads)
       const int slots = min(slot_prefix[G], kPdMaxSlots);
       for (int s = 0; s < slots; ++s) atomicExch(&ctr->done[s], 0);
       atomicExch(&ctr->work, 0);
-      atomicExch(&ctr->down_done, 0);
       __threadfence();
       atomicExch(&ctr->exited, 0);
     }
@@ -998,9 +902,7 @@ int launch_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_p
                              int group_begin, int num_groups, int max_rows,
                              const uint16_t* w13_bank, const uint16_t* w2_bank,
                              int64_t bank_rows, int H, int I, uint16_t* act, uint16_t* y_perm,
-                             int32_t* err_word, int per_sm_cap, cudaStream_t s,
-                             const PdCombine* cmb, bool* fused) {
-  *fused = false;
+                             int32_t* err_word, int per_sm_cap, cudaStream_t s) {
   const int max_passes = (max_rows + 8 * NC - 1) / (8 * NC);
   const bool capturing = stream_capturing(s);
   const int set = (num_groups > kPdMaxGroups ||
@@ -1053,12 +955,6 @@ int launch_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_p
   prm.act = act;
   prm.y_perm = y_perm;
   prm.err_word = err_word;
-  if (cmb != nullptr) {
-    prm.c_pair_to_row = cmb->pair_to_row;
-    prm.c_w = cmb->w_bf16;
-    prm.c_out = cmb->out;
-    prm.c_tokens = cmb->num_tokens;
-  }
   prm.bank_rows = bank_rows;
   prm.counter_set = set;
   prm.group_begin = group_begin;
@@ -1071,10 +967,7 @@ int launch_persistent(const uint16_t* hidden, int top_k, const int32_t* row_to_p
                        pd_smem_bytes<NC, S>(num_groups), s, prm);
   if (e != cudaSuccess) return check_cuda(e, "lm_moe_mlp_decode: persistent");
   rc = launch_status("lm_moe_mlp_decode: persistent");
-  if (rc == LM_OK) {
-    pd_counter_set_launched(set, s, capturing);
-    *fused = cmb != nullptr;
-  }
+  if (rc == LM_OK) pd_counter_set_launched(set, s, capturing);
   return rc;
 }
 
@@ -1087,16 +980,15 @@ int launch_decode_persistent(const uint16_t* hidden, int top_k, const int32_t* r
                              int group_begin, int num_groups, int max_rows,
                              const uint16_t* w13_bank, const uint16_t* w2_bank,
                              int64_t bank_rows, int H, int I, uint16_t* act, uint16_t* y_perm,
-                             int32_t* err_word, cudaStream_t s, const PdCombine* cmb,
-                             bool* fused) {
+                             int32_t* err_word, cudaStream_t s) {
   if (static_cast<int64_t>(max_rows) * top_k <= kPdSmallPairs)
     return launch_persistent<NC, 5>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
                                     group_begin, num_groups, max_rows, w13_bank, w2_bank,
-                                    bank_rows, H, I, act, y_perm, err_word, 2, s, cmb, fused);
+                                    bank_rows, H, I, act, y_perm, err_word, 2, s);
   return launch_persistent<NC, pd_stages<NC>()>(hidden, top_k, row_to_pair, group_offsets,
                                                 group_bank_row, group_begin, num_groups,
                                                 max_rows, w13_bank, w2_bank, bank_rows, H, I,
-                                                act, y_perm, err_word, 3, s, cmb, fused);
+                                                act, y_perm, err_word, 3, s);
 }
 
 template <int NC>
@@ -1220,17 +1112,14 @@ extern "C" int lm_decode_counter_sets(int32_t* in_use, int32_t* pinned, int64_t*
   return LM_OK;
 }
 
-namespace {
-int decode_impl(const uint16_t* hidden, int32_t top_k,
+extern "C" int lm_moe_mlp_decode(const uint16_t* hidden, int32_t top_k,
                                  const int32_t* row_to_pair, const int32_t* group_offsets,
                                  const int32_t* group_bank_row, int32_t group_begin,
                                  int32_t group_end, int32_t max_rows_per_group,
                                  const uint16_t* w13_bank, const uint16_t* w2_bank,
                                  int64_t bank_rows, int32_t hidden_size,
                                  int32_t intermediate_size, uint16_t* act, uint16_t* y_perm,
-                                 int32_t* err_word, void* stream, const PdCombine* cmb,
-                                 bool* fused) {
-  *fused = false;
+                                 int32_t* err_word, void* stream) {
   const int H = hidden_size, I = intermediate_size;
   if (H <= 0 || I <= 0 || H % 128 != 0 || I % 64 != 0)
     return fail(LM_ERR_INVALID_ARGUMENT,
@@ -1254,63 +1143,12 @@ int decode_impl(const uint16_t* hidden, int32_t top_k,
   if (max_rows_per_group <= 8)
     return launch_decode_persistent<1>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
                                        group_begin, ng, max_rows_per_group, w13_bank, w2_bank,
-                                       bank_rows, H, I, act, y_perm, err_word, s, cmb,
-                                       fused);
+                                       bank_rows, H, I, act, y_perm, err_word, s);
   if (max_rows_per_group <= 64)
     return launch_decode_persistent<2>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
                                        group_begin, ng, max_rows_per_group, w13_bank, w2_bank,
-                                       bank_rows, H, I, act, y_perm, err_word, s, cmb,
-                                       fused);
+                                       bank_rows, H, I, act, y_perm, err_word, s);
   return launch_decode_persistent<8>(hidden, top_k, row_to_pair, group_offsets, group_bank_row,
                                      group_begin, ng, max_rows_per_group, w13_bank, w2_bank,
-                                     bank_rows, H, I, act, y_perm, err_word, s, cmb,
-                                       fused);
-}
-}  // namespace
-
-extern "C" int lm_moe_mlp_decode(const uint16_t* hidden, int32_t top_k,
-                                 const int32_t* row_to_pair, const int32_t* group_offsets,
-                                 const int32_t* group_bank_row, int32_t group_begin,
-                                 int32_t group_end, int32_t max_rows_per_group,
-                                 const uint16_t* w13_bank, const uint16_t* w2_bank,
-                                 int64_t bank_rows, int32_t hidden_size,
-                                 int32_t intermediate_size, uint16_t* act, uint16_t* y_perm,
-                                 int32_t* err_word, void* stream) {
-  bool fused = false;
-  return decode_impl(hidden, top_k, row_to_pair, group_offsets, group_bank_row, group_begin,
-                     group_end, max_rows_per_group, w13_bank, w2_bank, bank_rows, hidden_size,
-                     intermediate_size, act, y_perm, err_word, stream, nullptr, &fused);
-}
-
-extern "C" int lm_moe_mlp_decode_combine(const uint16_t* hidden, int32_t top_k,
-                                         const int32_t* row_to_pair, const int32_t* group_offsets,
-                                         const int32_t* group_bank_row, int32_t group_begin,
-                                         int32_t group_end, int32_t max_rows_per_group,
-                                         const uint16_t* w13_bank, const uint16_t* w2_bank,
-                                         int64_t bank_rows, int32_t hidden_size,
-                                         int32_t intermediate_size, uint16_t* act,
-                                         uint16_t* y_perm, const int32_t* pair_to_row,
-                                         const uint16_t* topk_weights_bf16, int64_t num_tokens,
-                                         uint16_t* out, int32_t* err_word, void* stream) {
-  if (num_tokens < 0 || num_tokens > 0x7fffffff || top_k > 32 ||
-      (num_tokens > 0 && (pair_to_row == nullptr || topk_weights_bf16 == nullptr ||
-                          out == nullptr)))
-    return fail(LM_ERR_INVALID_ARGUMENT, "lm_moe_mlp_decode_combine: bad combine arguments");
-  if (reinterpret_cast<uintptr_t>(out) & 15)
-    return fail(LM_ERR_INVALID_ARGUMENT,
-                "lm_moe_mlp_decode_combine: out must be 16-byte aligned");
-  PdCombine cmb;
-  cmb.pair_to_row = pair_to_row;
-  cmb.w_bf16 = topk_weights_bf16;
-  cmb.out = out;
-  cmb.num_tokens = static_cast<int32_t>(num_tokens);
-  bool fused = false;
-  int rc = decode_impl(hidden, top_k, row_to_pair, group_offsets, group_bank_row, group_begin,
-                       group_end, max_rows_per_group, w13_bank, w2_bank, bank_rows, hidden_size,
-                       intermediate_size, act, y_perm, err_word, stream,
-                       num_tokens > 0 ? &cmb : nullptr, &fused);
-  if (rc || fused || num_tokens == 0) return rc;
-  // the two-kernel decode path ran (or no group had work): the combine as its own launch
-  return lm_moe_combine(y_perm, pair_to_row, topk_weights_bf16, num_tokens, top_k, hidden_size,
-                        out, stream);
+                                     bank_rows, H, I, act, y_perm, err_word, s);
 }

@@ -451,9 +451,9 @@ class SlotBankMoE:
             # the tcgen05 MLP reads its rows in group order (the decode GEMV gathers them)
             _lib.permute_rows(hidden, self.row_to_pair, self.k, T * self.k, self.x_perm)
             self.kernel_launches += 1
-        self.kernel_launches += group_launches(T * self.k) + mlp_launches(T)
-        return self._grouped_mlp_combine(hidden, T, self.slot_rows, 0, G, bank.w13_slots,
-                                         bank.w2_slots, out)
+        self._grouped_mlp(hidden, T, self.slot_rows, 0, G, bank.w13_slots, bank.w2_slots)
+        self.kernel_launches += group_launches(T * self.k) + mlp_launches(T) + 1  # + combine
+        return self._combine(T, out)
 
     def mlp_device(self, hidden: torch.Tensor, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """Decode MLP piece with the staging decision on the device: slot allocation
@@ -498,13 +498,9 @@ class SlotBankMoE:
                                   self.scratch, self.err)
                 self.kernel_launches += group_launches(T * self.k)
             g_end = self.E_total if self.shared_in_store else self.E
-            if self.shared_in_store or not self.num_fused_shared:
-                # one launch holds every pair: the combine runs inside it
-                self.kernel_launches += mlp_launches(T)
-                return self._grouped_mlp_combine(hidden, T, self.identity_groups, 0, g_end,
-                                                 store.w13, store.w2, out)
             self._grouped_mlp(hidden, T, self.identity_groups, 0, g_end, store.w13, store.w2)
-            self._shared_groups_mlp(hidden, T, self.pinned_rows)
+            if not self.shared_in_store:
+                self._shared_groups_mlp(hidden, T, self.pinned_rows)
             self.kernel_launches += mlp_launches(T) + 1
             return self._combine(T, out)
         if self.resident_wave_order:
@@ -645,21 +641,6 @@ class SlotBankMoE:
         off = self.wave_offsets[: nw + 1].tolist()
         rows = self.group_bank_row.tolist()
         return tuple(tuple(rows[off[w]:off[w + 1]]) for w in range(nw))
-
-    def _grouped_mlp_combine(self, hidden, T, bank_rows_dev, g0, g1, w13_bank, w2_bank,
-                             out: torch.Tensor | None) -> torch.Tensor:
-        """The grouped MLP over groups [g0, g1), which must hold every pair of the call, then
-        the combine; a decode-sized call runs both in the persistent launch."""
-        if T > DECODE_MAX_TOKENS:
-            self._grouped_mlp(hidden, T, bank_rows_dev, g0, g1, w13_bank, w2_bank)
-            self.kernel_launches += 1
-            return self._combine(T, out)
-        dst = self.out[:T] if out is None else out
-        _lib.moe_mlp_decode_combine(hidden, self.k, self.row_to_pair, self.group_offsets,
-                                    bank_rows_dev, g0, g1, T, w13_bank, w2_bank, self.act,
-                                    self.y_perm, self.pair_to_row[: T * self.k],
-                                    self.topk_w[:T], dst, self.err)
-        return dst
 
     def _grouped_mlp(self, hidden, T, bank_rows_dev, g0, g1, w13_bank, w2_bank) -> None:
         if T <= DECODE_MAX_TOKENS:
