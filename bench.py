@@ -666,12 +666,15 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     One step on every rank: route its tokens, store each token's row once into every owner that
     holds any of its experts over NVLink (peer memory), with each pair's owner-local id and
     receive-row index; the owner's grouped MLP gathers its rows from the receive area (the row
-    count stays on the device) and leaves its outputs grouped; signal, and combine every
-    token's pairs from the owners in top-k order. Time = max over ranks; after timing, each rank's first tokens
-    are checked against the torch fp32 restatement of the 1-GPU layer. Also returns the same
-    step from host buffers (``e2e``)."""
+    count stays on the device) and its down GEMM stores every output row into the source's
+    memory; signal, and combine every token's pairs from local memory in top-k order. The
+    rank's step is captured once as a CUDA graph (the exchange's epoch is advanced on the
+    device) and replayed. Time = max over ranks; after timing, each rank's first tokens are
+    checked against the torch fp32 restatement of the 1-GPU layer. Also returns the same step
+    from host buffers (``e2e``)."""
     import torch
 
+    from vllm_ascend_hust_latchmoe_b200.layer import group_launches
     from vllm_ascend_hust_latchmoe_b200 import _lib
     from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
     from vllm_ascend_hust_latchmoe_b200.expert_parallel import (ExpertParallelMoE, PeerExchange,
@@ -689,7 +692,7 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
                              rank=rank, device=dev, max_rows=world * T * k, num_slots=per,
                              store_on_device=True)
     exchange = PeerExchange(world_size=world, rank=rank, max_tokens=T, top_k=k, hidden_size=H,
-                            device=dev)
+                            device=dev, device_epoch=True)
     ep = ExpertParallelMoE(num_experts=E, top_k=k, hidden_size=H, rank=rank, world_size=world,
                            device=dev, exchange=exchange,
                            ops=cuda_ops(local, num_experts=E, top_k=k, max_tokens=T))
@@ -702,14 +705,25 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     torch.cuda.synchronize()
     local.check_device_errors("bench ep value warmup")
     ep.check_exchange_errors()
-    sent0 = ep.stats.bytes_sent
+    # the step captured once as a CUDA graph on every rank (the exchange's epoch lives on the
+    # device, so each replay is a new call) and replayed; the capture executes nothing
     launches0 = local.kernel_launches
+    g_step = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        ep.forward(hidden, logits)
+    owner_launches = local.kernel_launches - launches0
+    for _ in range(2):
+        g_step.replay()
+    torch.cuda.synchronize()
+    local.check_device_errors("bench ep value graph warmup")
+    ep.check_exchange_errors()
+    sent0 = ep.stats.bytes_sent
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         barrier()
         t0.record()
         for _ in range(args.steps):
-            ep.forward(hidden, logits)
+            g_step.replay()
         t1.record()
         barrier()
     local.check_device_errors("bench ep value")
@@ -720,12 +734,12 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
     ms_step = ms_total / args.steps
     value = world * T * args.steps / (ms_total / 1e3)
     nvlink = (ep.stats.bytes_sent - sent0) / args.steps
-    # per step: route, owner grouping, dispatch (token slots + stores when deduplicated),
-    # receive (wait + index), the owner MLP's grouping / row pointers / gather / grouped MLP,
-    # signal, combine (wait + reduce)
+    # per step: route, owner grouping, epoch, dispatch (token slots + stores when
+    # deduplicated), receive (wait + index), the owner MLP's grouping / row pointers / gather /
+    # grouped MLP, signal, combine (wait + reduce), step figures
     dispatch_launches = 2 if ep.dedupe_dispatch else 1
-    launches_per_step = (1 + 1 + dispatch_launches + 2
-                         + (local.kernel_launches - launches0) // args.steps + 1 + 2)
+    launches_per_step = (1 + group_launches(T * k) + 1 + dispatch_launches + 2 + owner_launches
+                         + 1 + 2 + 1)
 
     # correctness of what was timed: one more call, first tokens against the reference
     got = ep.forward(hidden, logits)
@@ -855,6 +869,7 @@ def run_value_ep(args, cfg, dist, dev, rank, world, local_rank, peaks, barrier):
                "dispatch": "token-deduplicated (one row per token and owner)"
                            if ep.dedupe_dispatch else "one row per routed pair",
                "parity": parity}
+    del g_step  # its kernels name the exchange region
     exchange.close()
     del ep, local
     torch.cuda.empty_cache()
@@ -1364,7 +1379,9 @@ def main() -> None:
                                    f"{cfg.num_slots}), all groups in one grouped-MLP pass")
                                   if world == 1 else None,
                    "launch": ("layer step captured once as a CUDA graph, replayed per step"
-                              if world == 1 else "eager (the exchange epochs advance per call)"),
+                              if world == 1 else "the rank's step (route, exchange, owner MLP, "
+                              "combine) captured once as a CUDA graph per rank and replayed; "
+                              "the exchange epoch is advanced on the device"),
                    "parallelism": ("single GPU" if world == 1 else
                                    f"expert-partitioned x{world}: 128 experts over {world} GPUs, "
                                    "4096 tokens per rank, dispatch/combine over NVLink peer "

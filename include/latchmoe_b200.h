@@ -377,7 +377,11 @@ int lm_moe_mlp_decode_offload(const uint16_t* hidden, int32_t top_k,
  * other rank's region (lm_ipc_get_handle -> exchange the 64-byte handles -> lm_ipc_open_handle).
  * peer_regions is a DEVICE array of `world` pointers (entry `rank` = the rank's own region).
  * cap = most routed pairs one source sends to one owner. epoch = a call counter, the same on
- * every rank and increasing by one per layer call (flags hold the last epoch seen).
+ * every rank and increasing by one per layer call (flags hold the last epoch seen). epoch 0
+ * means the counter kept in the rank's own region instead: lm_ep_advance_epoch raises it on
+ * the device at the start of each call, so a step captured in a CUDA graph gets a new epoch
+ * on every replay (every rank advances once per call; do not mix the two forms on one
+ * exchange).
  * Per layer call, in stream order on every rank:
  *   lm_ep_dispatch      pairs grouped by owner (pair_to_row / send_offsets from
  *                       lm_build_groups with expert -> owner); each pair's hidden row and
@@ -456,6 +460,8 @@ int lm_ep_combine_local(const int32_t* topk_ids, const uint16_t* topk_weights_bf
 int lm_ep_step_stats(const int32_t* total, const int32_t* send_offsets, const int32_t* tok_count,
                      int64_t num_pairs, int32_t rank, int32_t world, int64_t* stats,
                      void* stream);
+int lm_ep_advance_epoch(void* region, int32_t world, int32_t cap, int32_t hidden_size,
+                        void* stream);
 int lm_ep_signal_outputs(void* const* peer_regions, int32_t rank, int32_t world, int32_t cap,
                          int32_t hidden_size, int64_t epoch, void* stream);
 int lm_ep_combine(const int32_t* topk_ids, const uint16_t* topk_weights_bf16,

@@ -54,11 +54,12 @@ def _worker(rank, world, port, store_on_device, transport, q):
         exchange = None
         if transport.startswith("peer"):
             exchange = PeerExchange(world_size=world, rank=rank, max_tokens=T, top_k=K,
-                                    hidden_size=H, device=dev)
+                                    hidden_size=H, device=dev,
+                                    device_epoch=transport == "peer_graph")
         ep = ExpertParallelMoE(num_experts=E, top_k=K, hidden_size=H, rank=rank,
                                world_size=world, device=dev, exchange=exchange,
-                               dedupe_dispatch=transport in ("peer", "peer_pull"),
-                               push_outputs=transport == "peer",
+                               dedupe_dispatch=transport in ("peer", "peer_pull", "peer_graph"),
+                               push_outputs=transport in ("peer", "peer_graph"),
                                nccl_rows_per_peer=T * K if transport == "nccl_fixed" else None,
                                ops=cuda_ops(local, num_experts=E, top_k=K, max_tokens=T))
         # a call with other routing first: the checked call reuses every area and flag
@@ -66,13 +67,23 @@ def _worker(rank, world, port, store_on_device, transport, q):
                    syn.make_router_logits(cfg, seed=30 + rank).to(dev))
         hidden = syn.make_hidden(cfg, seed=10 + rank)
         logits = syn.make_router_logits(cfg, seed=10 + rank)
+        h_dev, lg_dev = hidden.to(dev), logits.to(dev)
         for _ in range(2):
-            out = ep.forward(hidden.to(dev), logits.to(dev))
+            out = ep.forward(h_dev, lg_dev)
+        graph = None
+        if transport == "peer_graph":  # the step captured once, replayed as new calls
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = ep.forward(h_dev, lg_dev)
+            for _ in range(2):
+                graph.replay()
         torch.cuda.synchronize()
         local.check_device_errors("ep")
         ep.check_exchange_errors()
         if exchange is not None:
             out = out.clone()
+            del graph
             exchange.close()
         wb, _, ids = orouter.route(logits.numpy(), K)
         ref = omlp.moe_layer(bits(hidden), ids, wb, bits(w13), bits(w2))
@@ -88,13 +99,17 @@ def _worker(rank, world, port, store_on_device, transport, q):
 
 # "peer": token-deduplicated dispatch, owners push outputs into the sources' memory;
 # "peer_pull": the same dispatch, sources read the outputs from the owners;
-# "peer_pairs": one row per routed pair, outputs read from the owners
+# "peer_pairs": one row per routed pair, outputs read from the owners;
+# "peer_graph": as "peer" with the epoch on the device, the step replayed from a CUDA graph
 # "nccl_fixed": fixed-size all-to-all blocks, counts never read on the host
-@pytest.mark.parametrize("transport", ["nccl", "nccl_fixed", "peer", "peer_pull", "peer_pairs"])
+@pytest.mark.parametrize("transport", ["nccl", "nccl_fixed", "peer", "peer_pull", "peer_pairs",
+                                       "peer_graph"])
 @pytest.mark.parametrize("store_on_device", [False, True])
 def test_ep_two_gpus_matches_oracle(store_on_device, transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    if transport == "peer_graph" and not store_on_device:
+        pytest.skip("a staged store reads its received row count on the host: not capturable")
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")

@@ -171,3 +171,86 @@ def test_single_rank_gather_path_matches_oracle(cuda, dedupe, push):
     finally:
         torch.cuda.synchronize()
         _lib.ep_region_free(region)
+
+
+def test_single_rank_device_epoch_step_replays_from_a_graph(cuda):
+    """Epoch 0: every exchange kernel reads the call counter that lm_ep_advance_epoch raised
+    on the device, so the whole step (advance, dispatch by token, index-only receive, gather
+    MLP pushing its outputs, signal, local combine) captured once as a CUDA graph replays as a
+    new call each time, with the oracle's output."""
+    from oracle import router as orouter
+    from vllm_ascend_hust_latchmoe_b200 import synthetic as syn
+    from vllm_ascend_hust_latchmoe_b200.expert_parallel import build_rank_layer
+
+    T2, K2, E2, H2, I2 = 32, 4, 8, 256, 128
+    cap = T2 * K2
+    cfg = syn.LayerConfig("g", hidden=H2, num_experts=E2, top_k=K2, intermediate=I2,
+                          num_slots=E2, tokens=T2)
+    w13, w2 = syn.make_expert_weights(cfg, seed=9)
+    layer = build_rank_layer(w13_owned=w13.to(cuda), w2_owned=w2.to(cuda), rank=0, device=cuda,
+                             max_rows=cap, num_slots=E2, store_on_device=True)
+    region = _lib.ep_region_alloc(_lib.ep_region_bytes(1, cap, H2))
+    g = None
+    try:
+        peers = torch.tensor([region], dtype=torch.int64, device=cuda)
+        recv_rows = torch.as_tensor(_DevicePtrArray(
+            region + _lib.ep_recv_rows_offset(1, cap, H2), (cap, H2), "<i2"),
+            device=cuda).view(torch.bfloat16)
+        slots = torch.empty(cap, dtype=torch.int32, device=cuda)
+        rids = torch.empty(cap, dtype=torch.int32, device=cuda)
+        total = torch.zeros(1, dtype=torch.int32, device=cuda)
+        done = torch.zeros(1, dtype=torch.int32, device=cuda)
+        err = torch.zeros(1, dtype=torch.int32, device=cuda)
+        owner = torch.zeros(E2, dtype=torch.int32, device=cuda)
+        offsets = torch.empty(2, dtype=torch.int32, device=cuda)
+        p2r = torch.empty(cap, dtype=torch.int32, device=cuda)
+        r2p = torch.empty(cap, dtype=torch.int32, device=cuda)
+        scratch = torch.empty(_lib.build_groups_scratch_elems(cap, 1), dtype=torch.int32,
+                              device=cuda)
+        tok_slot = torch.empty(T2, dtype=torch.int32, device=cuda)
+        tok_count = torch.zeros(1, dtype=torch.int32, device=cuda)
+        out = torch.empty(T2, H2, dtype=torch.bfloat16, device=cuda)
+        hidden = syn.make_hidden(cfg, seed=4)
+        wb, _, ids_np = orouter.route(syn.make_router_logits(cfg, seed=4).numpy(), K2)
+        ids = torch.from_numpy(ids_np).to(cuda)
+        w = torch.from_numpy(wb.view(np.int16)).view(torch.bfloat16).to(cuda)
+        h = hidden.to(cuda)
+
+        def row_ptrs(row_to_pair, count, ptrs):
+            _lib.ep_output_row_ptrs(region, 1, cap, H2, 0, peers, row_to_pair, count,
+                                    ptrs.shape[0], ptrs, err)
+
+        def step():
+            _lib.ep_advance_epoch(region, 1, cap, H2)
+            _lib.build_groups(ids, E2, owner, 1, offsets, p2r, r2p, scratch, err)
+            _lib.ep_dispatch_tokens(h, ids, E2, p2r, offsets, 0, 1, peers, cap, 0, tok_slot,
+                                    tok_count, done, err)
+            _lib.ep_receive_index(region, 1, cap, H2, 0, slots, rids, total, err)
+            layer.mlp_rows_gather_push(recv_rows, slots, rids, total, row_ptrs)
+            _lib.ep_signal_outputs(peers, 0, 1, cap, H2, 0)
+            _lib.ep_combine_local(ids, w, E2, p2r, offsets, 0, 1, peers, region, cap, 0, out,
+                                  err)
+
+        ref = omlp.moe_layer(bits(hidden), ids_np, wb, bits(w13), bits(w2))
+        for _ in range(2):  # eager calls, epochs 1 and 2
+            step()
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)
+            assert m["max_rel_err"] <= MAX_REL_ERR and m["cosine"] >= MIN_COSINE, m
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        for _ in range(3):  # epochs 3, 4, 5: each replay waits for its own flags
+            out.fill_(7.0)
+            g.replay()
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            layer.check_device_errors("device epoch graph")
+            m = omlp.compare(bf16_bits_to_f32(bits(out)), ref)
+            assert m["max_rel_err"] <= MAX_REL_ERR and m["cosine"] >= MIN_COSINE, m
+    finally:
+        torch.cuda.synchronize()
+        del g
+        _lib.ep_region_free(region)
+

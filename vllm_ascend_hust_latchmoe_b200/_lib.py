@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lm_ep_recv_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_ep_pair_rows_offset": (ctypes.c_int64, [_I32, _I32, _I32]),
     "lm_permute_rows_gather_count": (ctypes.c_int, [_P, _I32, _P, _P, _I64, _P, _P, _P]),
+    "lm_ep_advance_epoch": (ctypes.c_int, [_P, _I32, _I32, _I32, _P]),
     "lm_ep_step_stats": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P, _P]),
     "lm_ep_output_row_ptrs": (
         ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P]),
@@ -541,6 +542,12 @@ def ep_signal_outputs(peer_regions, rank, world, cap, hidden_size, epoch) -> Non
     _check("lm_ep_signal_outputs", lib().lm_ep_signal_outputs(
         _ptr(peer_regions), int(rank), int(world), int(cap), int(hidden_size), int(epoch),
         _stream()))
+
+
+def ep_advance_epoch(region: int, world, cap, hidden_size) -> None:
+    """Raise the region's device-side call counter (the epoch of calls given epoch 0)."""
+    _check("lm_ep_advance_epoch", lib().lm_ep_advance_epoch(
+        region, int(world), int(cap), int(hidden_size), _stream()))
 
 
 def ep_step_stats(total, send_offsets, tok_count, num_pairs, rank, world, stats) -> None:

@@ -35,9 +35,9 @@
 namespace lm {
 namespace {
 
-constexpr int kLayoutFields = 11;
-enum : int { F_FLAG_DISPATCH = 0, F_FLAG_OUT, F_COUNTS, F_PREFIX, F_WAIT_STATUS, F_RECV_IDS,
-             F_RECV_ROWIDX, F_PAIR_ROW, F_RECV_ROWS, F_OUT_ROWS, F_TOTAL };
+constexpr int kLayoutFields = 12;
+enum : int { F_FLAG_DISPATCH = 0, F_FLAG_OUT, F_COUNTS, F_PREFIX, F_WAIT_STATUS, F_EPOCH,
+             F_RECV_IDS, F_RECV_ROWIDX, F_PAIR_ROW, F_RECV_ROWS, F_OUT_ROWS, F_TOTAL };
 
 int64_t align256(int64_t v) { return (v + 255) & ~static_cast<int64_t>(255); }
 
@@ -53,6 +53,8 @@ void layout(int G, int cap, int H, int64_t* off) {
   o = align256(o + 4ll * (G + 1));
   off[F_WAIT_STATUS] = o;  // this rank's last output wait: 0 every owner answered, 1 timed out
   o = align256(o + 4);
+  off[F_EPOCH] = o;  // the rank's call counter on the device (epoch argument 0 reads it)
+  o = align256(o + 8);
   off[F_RECV_IDS] = o;
   o = align256(o + 4ll * G * cap);
   off[F_RECV_ROWIDX] = o;  // receive-area row of each received pair (rows may be shared)
@@ -73,6 +75,14 @@ struct Layout {
 template <typename T>
 __device__ __forceinline__ T* field(void* region, const Layout& L, int f) {
   return reinterpret_cast<T*>(static_cast<uint8_t*>(region) + L.off[f]);
+}
+
+// The call's epoch: the argument, or, when it is 0, the counter in the rank's own region that
+// lm_ep_advance_epoch raised earlier in the stream (so a captured step replays with a new
+// epoch every time).
+__device__ __forceinline__ long long call_epoch(long long epoch, void* own_region,
+                                                const Layout& L) {
+  return epoch > 0 ? epoch : *field<volatile long long>(own_region, L, F_EPOCH);
 }
 
 __device__ __forceinline__ void st_release_sys(long long* p, long long v) {
@@ -111,6 +121,7 @@ __global__ void __launch_bounds__(256)
                        int32_t* __restrict__ done, int32_t* __restrict__ err_word) {
   pdl_wait();  // launched early (programmatic dependent launch)
   pdl_trigger();
+  epoch = call_epoch(epoch, peers[rank], L);
   // one warp per pair
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -216,6 +227,7 @@ __global__ void __launch_bounds__(256)
                               int32_t* __restrict__ err_word) {
   pdl_wait();  // launched early (programmatic dependent launch)
   pdl_trigger();
+  epoch = call_epoch(epoch, peers[rank], L);
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t w0 = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -273,6 +285,7 @@ __global__ void __launch_bounds__(32)
                            int32_t* __restrict__ total_out, int32_t* __restrict__ err_word) {
   pdl_wait();  // launched early (programmatic dependent launch)
   pdl_trigger();
+  epoch = call_epoch(epoch, region, L);
   int32_t* prefix = field<int32_t>(region, L, F_PREFIX);
   if (!wait_flags(field<long long>(region, L, F_FLAG_DISPATCH), G, epoch, err_word)) {
     if (threadIdx.x == 0) {
@@ -404,10 +417,19 @@ __global__ void ep_stats_kernel(const int32_t* __restrict__ total,
   stats[2] += stored;
 }
 
+// One more call on this rank: raise the region's epoch counter (read by the exchange kernels
+// of the call when they are given epoch 0).
+__global__ void ep_advance_epoch_kernel(void* region, Layout L) {
+  pdl_wait();  // launched early (programmatic dependent launch)
+  pdl_trigger();
+  if (threadIdx.x == 0) *field<long long>(region, L, F_EPOCH) += 1;
+}
+
 __global__ void ep_signal_kernel(void* const* __restrict__ peers, Layout L, int rank, int G,
                                  long long epoch) {
   pdl_wait();  // launched early (programmatic dependent launch)
   pdl_trigger();
+  epoch = call_epoch(epoch, peers[rank], L);
   __threadfence_system();
   for (int o = threadIdx.x; o < G; o += blockDim.x)
     st_release_sys(field<long long>(peers[o], L, F_FLAG_OUT) + rank, epoch);
@@ -419,6 +441,7 @@ __global__ void __launch_bounds__(32)
     ep_wait_out_kernel(void* region, Layout L, int G, long long epoch, int32_t* err_word) {
   pdl_wait();  // launched early (programmatic dependent launch)
   pdl_trigger();
+  epoch = call_epoch(epoch, region, L);
   const bool ok = wait_flags(field<long long>(region, L, F_FLAG_OUT), G, epoch, err_word);
   if (threadIdx.x == 0) *field<int32_t>(region, L, F_WAIT_STATUS) = ok ? 0 : 1;
 }
@@ -576,7 +599,7 @@ extern "C" int lm_ep_dispatch(const uint16_t* hidden, int64_t num_tokens, int32_
   int rc = check_ep("lm_ep_dispatch", world, cap, hidden_size);
   if (rc) return rc;
   if (num_tokens < 0 || top_k <= 0 || experts_per_rank <= 0 || rank < 0 || rank >= world ||
-      epoch <= 0 || done_counter == nullptr || peer_regions == nullptr ||
+      epoch < 0 || done_counter == nullptr || peer_regions == nullptr ||
       send_offsets == nullptr || (num_tokens > 0 && (hidden == nullptr || topk_ids == nullptr ||
                                                      pair_to_row == nullptr)))
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_dispatch: bad arguments");
@@ -610,7 +633,7 @@ extern "C" int lm_ep_dispatch_tokens(const uint16_t* hidden, int64_t num_tokens,
   int rc = check_ep("lm_ep_dispatch_tokens", world, cap, hidden_size);
   if (rc) return rc;
   if (num_tokens < 0 || top_k <= 0 || experts_per_rank <= 0 || rank < 0 || rank >= world ||
-      epoch <= 0 || done_counter == nullptr || peer_regions == nullptr ||
+      epoch < 0 || done_counter == nullptr || peer_regions == nullptr ||
       send_offsets == nullptr || tok_count == nullptr ||
       (num_tokens > 0 && (hidden == nullptr || topk_ids == nullptr || pair_to_row == nullptr ||
                           tok_slot == nullptr)))
@@ -650,7 +673,7 @@ extern "C" int lm_ep_receive(void* region, int32_t world, int32_t cap, int32_t h
   int rc = check_ep("lm_ep_receive", world, cap, hidden_size);
   if (rc) return rc;
   if (region == nullptr || rows_out == nullptr || ids_out == nullptr || total_out == nullptr ||
-      epoch <= 0)
+      epoch < 0)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_receive: bad arguments");
   const Layout L = make_layout(world, cap, hidden_size);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -679,7 +702,7 @@ extern "C" int lm_ep_receive_index(void* region, int32_t world, int32_t cap,
   int rc = check_ep("lm_ep_receive_index", world, cap, hidden_size);
   if (rc) return rc;
   if (region == nullptr || slot_out == nullptr || ids_out == nullptr || total_out == nullptr ||
-      epoch <= 0)
+      epoch < 0)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_receive_index: bad arguments");
   const Layout L = make_layout(world, cap, hidden_size);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -726,7 +749,7 @@ extern "C" int lm_ep_signal_outputs(void* const* peer_regions, int32_t rank, int
                                     void* stream) {
   int rc = check_ep("lm_ep_signal_outputs", world, cap, hidden_size);
   if (rc) return rc;
-  if (peer_regions == nullptr || rank < 0 || rank >= world || epoch <= 0)
+  if (peer_regions == nullptr || rank < 0 || rank >= world || epoch < 0)
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_signal_outputs: bad arguments");
   {
     const cudaError_t le_ = launch_dependent(ep_signal_kernel, dim3(1), dim3(32), 0,
@@ -746,7 +769,7 @@ int combine_impl(const int32_t* topk_ids, const uint16_t* topk_weights_bf16, int
   int rc = check_ep("lm_ep_combine", world, cap, hidden_size);
   if (rc) return rc;
   if (top_k <= 0 || top_k > 32 || num_tokens < 0 || experts_per_rank <= 0 || rank < 0 ||
-      rank >= world || epoch <= 0 || peer_regions == nullptr || local_region == nullptr ||
+      rank >= world || epoch < 0 || peer_regions == nullptr || local_region == nullptr ||
       (num_tokens > 0 && (topk_ids == nullptr || topk_weights_bf16 == nullptr ||
                           pair_to_row == nullptr || send_offsets == nullptr || out == nullptr)))
     return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_combine: bad arguments");
@@ -799,6 +822,18 @@ extern "C" int lm_ep_combine_local(const int32_t* topk_ids, const uint16_t* topk
   return combine_impl(topk_ids, topk_weights_bf16, num_tokens, top_k, hidden_size,
                       experts_per_rank, pair_to_row, send_offsets, rank, world, peer_regions,
                       local_region, cap, epoch, out, err_word, stream, 1);
+}
+
+extern "C" int lm_ep_advance_epoch(void* region, int32_t world, int32_t cap,
+                                   int32_t hidden_size, void* stream) {
+  int rc = check_ep("lm_ep_advance_epoch", world, cap, hidden_size);
+  if (rc) return rc;
+  if (region == nullptr) return fail(LM_ERR_INVALID_ARGUMENT, "lm_ep_advance_epoch: null region");
+  const cudaError_t le_ = launch_dependent(ep_advance_epoch_kernel, dim3(1), dim3(32), 0,
+                                           static_cast<cudaStream_t>(stream), region,
+                                           make_layout(world, cap, hidden_size));
+  if (le_ != cudaSuccess) return check_cuda(le_, "ep_advance_epoch_kernel");
+  return launch_status("lm_ep_advance_epoch");
 }
 
 extern "C" int lm_ep_step_stats(const int32_t* total, const int32_t* send_offsets,

@@ -120,7 +120,8 @@ class PeerExchange:
     spin on flags written by the other ranks' kernels."""
 
     def __init__(self, *, world_size: int, rank: int, max_tokens: int, top_k: int,
-                 hidden_size: int, device: torch.device, group=None) -> None:
+                 hidden_size: int, device: torch.device, group=None,
+                 device_epoch: bool = False) -> None:
         self.G, self.rank, self.H = int(world_size), int(rank), int(hidden_size)
         self.max_tokens = int(max_tokens)
         self.cap = self.max_tokens * int(top_k)
@@ -160,6 +161,9 @@ class PeerExchange:
         self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.epoch = 0
+        # device_epoch: each call raises the region's own counter on the device and the kernels
+        # read it (epoch 0), so a captured step replays with a new epoch every time
+        self.device_epoch = bool(device_epoch)
         self.group = group
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)
@@ -357,7 +361,11 @@ class ExpertParallelMoE:
             raise ValueError(f"{T} tokens exceed the exchange capacity ({x.cap // self.k})")
         w, ids = self.ops.route(router_logits)
         offsets, p2r, _ = self.ops.group_by_owner(ids, self.owner, self.G)
-        x.epoch += 1
+        if x.device_epoch:
+            _lib.ep_advance_epoch(x.region, self.G, x.cap, self.H)
+            x.epoch = 0  # every kernel of the call reads the region's counter
+        else:
+            x.epoch += 1
         if self.dedupe_dispatch:
             _lib.ep_dispatch_tokens(hidden, ids, self.per_rank, p2r, offsets, self.rank, self.G,
                                     x.peers, x.cap, x.epoch, x.tok_slot[: T * self.G],
