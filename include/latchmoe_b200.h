@@ -454,9 +454,9 @@ int lm_ep_combine_local(const int32_t* topk_ids, const uint16_t* topk_weights_bf
                         const int32_t* send_offsets, int32_t rank, int32_t world,
                         void* const* peer_regions, void* local_region, int32_t cap,
                         int64_t epoch, uint16_t* out, int32_t* err_word, void* stream);
-/* Step figures on the device: stats[0] += *total (pairs received), stats[1] += pairs kept
- * local, stats[2] += rows the dispatch stored into other ranks (sum of tok_count over the
- * other ranks, or num_pairs - local when tok_count is NULL). */
+/* Step figures on the device (int64 [4]): stats[0] += *total (pairs received), stats[1] +=
+ * pairs kept local, stats[2] += rows the dispatch stored into other ranks (sum of tok_count
+ * over the other ranks, or num_pairs - local when tok_count is NULL), stats[3] += num_pairs. */
 int lm_ep_step_stats(const int32_t* total, const int32_t* send_offsets, const int32_t* tok_count,
                      int64_t num_pairs, int32_t rank, int32_t world, int64_t* stats,
                      void* stream);

@@ -551,7 +551,7 @@ def ep_advance_epoch(region: int, world, cap, hidden_size) -> None:
 
 
 def ep_step_stats(total, send_offsets, tok_count, num_pairs, rank, world, stats) -> None:
-    """Accumulate one exchange step's figures into ``stats`` (int64 [3], on the device)."""
+    """Accumulate one exchange step's figures into ``stats`` (int64 [4], on the device)."""
     _check("lm_ep_step_stats", lib().lm_ep_step_stats(
         _ptr(total), _ptr(send_offsets), _ptr(tok_count), int(num_pairs), int(rank), int(world),
         _ptr(stats), _stream()))

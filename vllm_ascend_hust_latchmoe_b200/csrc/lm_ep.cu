@@ -397,7 +397,8 @@ __global__ void __launch_bounds__(256)
 
 // Per-step exchange figures kept on the device (one launch instead of several small ones):
 // stats[0] += pairs received, stats[1] += pairs kept local, stats[2] += rows stored into
-// other ranks by the dispatch (token rows when tok_count is given, else remote pairs).
+// other ranks by the dispatch (token rows when tok_count is given, else remote pairs),
+// stats[3] += pairs routed by this rank.
 __global__ void ep_stats_kernel(const int32_t* __restrict__ total,
                                 const int32_t* __restrict__ send_offsets,
                                 const int32_t* __restrict__ tok_count, int64_t num_pairs,
@@ -415,6 +416,7 @@ __global__ void ep_stats_kernel(const int32_t* __restrict__ total,
   stats[0] += *total;
   stats[1] += local;
   stats[2] += stored;
+  stats[3] += num_pairs;
 }
 
 // One more call on this rank: raise the region's epoch counter (read by the exchange kernels

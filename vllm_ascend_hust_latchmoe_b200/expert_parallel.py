@@ -206,9 +206,9 @@ class ExpertParallelMoE:
         self._stats = EPStats()
         # peer steps without a host sync: per-step figures accumulate on the device
         # pairs received, pairs kept local, token rows stored into other ranks
-        self._dev_rows = torch.zeros(3, dtype=torch.int64, device=self.device)
+        # (a captured step adds to them on every replay: the host counts nothing per step)
+        self._dev_rows = torch.zeros(4, dtype=torch.int64, device=self.device)
         self._dev_steps = 0
-        self._dev_pairs = 0
         self.exchange = exchange
         self.transport = "peer" if exchange is not None else "nccl"
         # peer transport: a token's row crosses to an owner once, not once per routed pair
@@ -228,12 +228,12 @@ class ExpertParallelMoE:
         """Exchange totals (reads the device-side part of peer steps: synchronises)."""
         st = EPStats(**vars(self._stats))
         if self._dev_steps:
-            recv, local_rows, token_rows = (int(v) for v in self._dev_rows.tolist())
+            recv, local_rows, token_rows, pairs = (int(v) for v in self._dev_rows.tolist())
             elt = 2  # bf16 rows
-            st.send_rows += self._dev_pairs
+            st.send_rows += pairs
             st.recv_rows += recv
             # dispatch stores (token rows, or one row per remote pair) + outputs read back
-            st.bytes_sent += (token_rows + self._dev_pairs - local_rows) * self.H * elt
+            st.bytes_sent += (token_rows + pairs - local_rows) * self.H * elt
             # counted per pair: an upper bound on the dispatch side when tokens are deduplicated
             st.bytes_received += 2 * (recv - local_rows) * self.H * elt
         return st
@@ -414,7 +414,6 @@ class ExpertParallelMoE:
             _lib.ep_step_stats(x.total, offsets, x.tok_count if self.dedupe_dispatch else None,
                                T * self.k, self.rank, self.G, self._dev_rows)
             self._dev_steps += 1
-            self._dev_pairs += T * self.k
         else:
             counts = (offsets[1:] - offsets[:-1]).tolist()
             st = self._stats
