@@ -62,3 +62,11 @@ def test_ep_exchange_capacity_is_checked_on_the_host():
     rc = lib.lm_ep_combine_local(fake, fake, 10, 8, 2048, 16, fake, fake, 0, 2, fake, fake, 64,
                                  1, fake, None, None)
     assert rc == -1 and b"capacity" in lib.lm_last_error()
+    # epoch 0 selects the region's device-side counter; a negative epoch is refused
+    rc = lib.lm_ep_dispatch_tokens(fake, 4, 8, 2048, fake, 16, fake, fake, 0, 2, fake, 64, -1,
+                                   fake, fake, fake, None, None)
+    assert rc == -1 and b"bad arguments" in lib.lm_last_error()
+    rc = lib.lm_ep_signal_outputs(fake, 0, 2, 64, 2048, -1, None)
+    assert rc == -1
+    rc = lib.lm_ep_advance_epoch(None, 2, 64, 2048, None)
+    assert rc == -1 and b"null region" in lib.lm_last_error()
